@@ -1,0 +1,369 @@
+// common.cuh -- tile layout of repacked GGUF weights, block decoders and PTX
+// helpers shared by the repack, dequant, GEMV and GEMM kernels (sm_100a).
+//
+// TILE LAYOUT ("rowgroup tiles"). A weight tensor of `rows` x `k` is cut into
+// rowgroups of 16 rows (rows padded to 16 with zero blocks) and, along k, into
+// chunks of CHUNK_K weights (128 for Q8_0, one 256-weight superblock for the
+// K-/i-quants; k padded to a whole chunk with zero blocks). Each (rowgroup,
+// chunk) is one contiguous, 16-byte aligned tile of exactly 16 x the GGUF bytes
+// of that piece -- the repack permutes bytes (and, for Q4_K/Q6_K, nibbles and
+// 2-bit fields inside a 32-bit word) but never adds any. Tiles of a rowgroup
+// follow each other along k; rowgroups follow each other.
+//
+// Inside a tile the quant bytes are ordered for the m16n8k16 tensor-core
+// fragment: lane L = 4g + t of a warp owns rows g and g+8 of the rowgroup and a
+// contiguous k-range of each (block t for Q8_0, sub-blocks 2t,2t+1 for Q4_K,
+// quarter-rows (t>>1, t&1) for Q6_K, 32-blocks 2t,2t+1 for the i-quants), and
+// its bytes sit in 16-byte "parts": part p of lane L at tile + 512p + 16L, so
+// one 128-bit load per part by the 32 lanes reads 512 contiguous bytes. Scales
+// follow the parts. Per-type details are next to each scatter/gather below.
+//
+// The GGUF blocks themselves are restated from the reference decoders:
+//   Q8_0 js/kernels.wgsl.js:154-169, Q4_K :227-250 (+scale_min_k4 :94-104),
+//   Q6_K :269-330, IQ2_XXS :368-396, IQ1_S :805-822.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/elffuss_cuda.h"
+
+namespace ef {
+
+// ---------------------------------------------------------------- geometry --
+struct TypeGeo {
+    int block_elems;   // weights per GGUF block
+    int block_bytes;   // bytes per GGUF block
+    int chunk_k;       // weights per tile along k
+    int tile_bytes;    // bytes per (16-row, chunk) tile = 16 * chunk_k / block_elems * block_bytes
+};
+
+__host__ __device__ inline bool geo_of(int type, TypeGeo &g) {
+    switch (type) {
+    case EF_Q8_0: g = {32, 34, 128, 2176}; return true;
+    case EF_Q4_K: g = {256, 144, 256, 2304}; return true;
+    case EF_Q6_K: g = {256, 210, 256, 3360}; return true;
+    case EF_IQ2_XXS: g = {256, 66, 256, 1056}; return true;
+    case EF_IQ1_S: g = {256, 50, 256, 800}; return true;
+    default: return false;
+    }
+}
+
+constexpr int RG_ROWS = 16;   // rows per rowgroup tile
+
+// ------------------------------------------------------------ byte helpers --
+__host__ __device__ inline uint32_t rd32(const uint8_t *p) {
+    return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+__host__ __device__ inline void wr32(uint8_t *p, uint32_t v) {
+    p[0] = (uint8_t)v; p[1] = (uint8_t)(v >> 8); p[2] = (uint8_t)(v >> 16); p[3] = (uint8_t)(v >> 24);
+}
+
+// Nibble permutation of one 32-bit word of 4-bit quants. GGUF byte b_i holds a
+// low nibble (weight i of one group) and a high nibble (weight i of a second
+// group). The repacked word puts the first group's weights i=0,1,2,3 at bits
+// 0,16,4,20 and the second group's at 8,24,12,28, so that
+// (w >> s) & 0x000F000F picks a pair of consecutive weights into the two f16
+// halves of a register (s = 0, 4 for the first group; 8, 12 for the second).
+__host__ __device__ inline uint32_t nib_fwd(uint32_t G) {
+    uint32_t b0 = G & 0xFF, b1 = (G >> 8) & 0xFF, b2 = (G >> 16) & 0xFF, b3 = G >> 24;
+    uint32_t r0 = (b0 & 0xF) | ((b2 & 0xF) << 4);
+    uint32_t r1 = (b0 >> 4) | (b2 & 0xF0);
+    uint32_t r2 = (b1 & 0xF) | ((b3 & 0xF) << 4);
+    uint32_t r3 = (b1 >> 4) | (b3 & 0xF0);
+    return r0 | (r1 << 8) | (r2 << 16) | (r3 << 24);
+}
+__host__ __device__ inline uint32_t nib_inv(uint32_t R) {
+    uint32_t r0 = R & 0xFF, r1 = (R >> 8) & 0xFF, r2 = (R >> 16) & 0xFF, r3 = R >> 24;
+    uint32_t b0 = (r0 & 0xF) | ((r1 & 0xF) << 4);
+    uint32_t b2 = (r0 >> 4) | (r1 & 0xF0);
+    uint32_t b1 = (r2 & 0xF) | ((r3 & 0xF) << 4);
+    uint32_t b3 = (r2 >> 4) | (r3 & 0xF0);
+    return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+}
+
+// Q6_K high-bit word: 16 two-bit fields of one quarter-row, field of weight j
+// at bit 4(j>>2) + 2((j>>1)&1) + 16(j&1), so that weights (j, j+1) with j even
+// sit 16 bits apart and one shift + mask moves a pair under the f16 mantissa.
+__host__ __device__ inline int q6_hpos(int j) { return 4 * (j >> 2) + 2 * ((j >> 1) & 1) + 16 * (j & 1); }
+
+// --------------------------------------------- scatter (GGUF -> tile) -------
+// Write GGUF block `blk` (row r of the rowgroup, block `bic` within the chunk)
+// into tile `T`. Every output byte is written by exactly one block.
+__host__ __device__ inline void scatter_block(int type, const uint8_t *blk, int r, int bic, uint8_t *T) {
+    const int g = r & 7, hs = r >> 3;
+    switch (type) {
+    case EF_Q8_0: {
+        // lane (g, t=bic) owns block bic of rows g and g+8. Parts 2hs, 2hs+1 hold
+        // its 32 quants stored with the sign bit flipped (q ^ 0x80 = q + 128 as
+        // an unsigned byte); the f16 scale goes to 2048 + 4*lane + 2*hs.
+        const int lane = 4 * g + bic;
+        for (int i = 0; i < 32; i++)
+            T[(2 * hs + (i >> 4)) * 512 + lane * 16 + (i & 15)] = blk[2 + i] ^ 0x80;
+        T[2048 + lane * 4 + hs * 2] = blk[0];
+        T[2048 + lane * 4 + hs * 2 + 1] = blk[1];
+    } break;
+    case EF_Q4_K: {
+        // lane (g,t) owns qs bytes [32t, 32t+32) = sub-blocks 2t (low nibbles)
+        // and 2t+1 (high nibbles): 8 words, nibble-permuted, in parts
+        // 2hs + (i>>2). The 16-byte header (d, dmin, 12 scale bytes) is kept
+        // verbatim at 2048 + 16r.
+        for (int t = 0; t < 4; t++) {
+            const int lane = 4 * g + t;
+            for (int i = 0; i < 8; i++)
+                wr32(T + (2 * hs + (i >> 2)) * 512 + lane * 16 + (i & 3) * 4,
+                     nib_fwd(rd32(blk + 16 + 32 * t + 4 * i)));
+        }
+        for (int i = 0; i < 16; i++) T[2048 + r * 16 + i] = blk[i];
+    } break;
+    case EF_Q6_K: {
+        // lane (g,t), n = t>>1, lh = t&1 owns positions 128n + 32i + 16lh + j
+        // (i = quarter 0..3, j = 0..15): GGUF bytes A = ql[64n+16lh+j],
+        // B = ql[64n+32+16lh+j], H = qh[32n+16lh+j]. Part 3hs: A words
+        // nibble-permuted (quarters 0 | 2), part 3hs+1: B words (quarters 1 | 3),
+        // part 3hs+2: one high-bit word per quarter. int8 scales verbatim at
+        // 3072 + 16r, d at 3328 + 4g + 2hs.
+        for (int t = 0; t < 4; t++) {
+            const int n = t >> 1, lh = t & 1, lane = 4 * g + t;
+            const uint8_t *A = blk + 64 * n + 16 * lh, *B = blk + 64 * n + 32 + 16 * lh;
+            const uint8_t *H = blk + 128 + 32 * n + 16 * lh;
+            for (int w = 0; w < 4; w++) {
+                wr32(T + (3 * hs) * 512 + lane * 16 + 4 * w, nib_fwd(rd32(A + 4 * w)));
+                wr32(T + (3 * hs + 1) * 512 + lane * 16 + 4 * w, nib_fwd(rd32(B + 4 * w)));
+            }
+            for (int i = 0; i < 4; i++) {
+                uint32_t hw = 0;
+                for (int j = 0; j < 16; j++) hw |= (uint32_t)((H[j] >> (2 * i)) & 3) << q6_hpos(j);
+                wr32(T + (3 * hs + 2) * 512 + lane * 16 + 4 * i, hw);
+            }
+        }
+        for (int i = 0; i < 16; i++) T[3072 + r * 16 + i] = blk[192 + i];
+        T[3328 + 4 * g + 2 * hs] = blk[208];
+        T[3328 + 4 * g + 2 * hs + 1] = blk[209];
+    } break;
+    case EF_IQ2_XXS: {
+        // lane (g,t) owns 32-blocks 2t, 2t+1: GGUF bytes [2+16t, 2+16t+16) at
+        // part hs. d at 1024 + 4g + 2hs.
+        for (int t = 0; t < 4; t++)
+            for (int i = 0; i < 16; i++) T[hs * 512 + (4 * g + t) * 16 + i] = blk[2 + 16 * t + i];
+        T[1024 + 4 * g + 2 * hs] = blk[0];
+        T[1024 + 4 * g + 2 * hs + 1] = blk[1];
+    } break;
+    case EF_IQ1_S: {
+        // lane (g,t) owns 32-blocks 2t, 2t+1: qs bytes [8t, 8t+8) at
+        // 16*lane + 8hs, qh halves [2t, 2t+2) at 512 + 8*lane + 4hs, d at
+        // 768 + 4g + 2hs.
+        for (int t = 0; t < 4; t++) {
+            const int lane = 4 * g + t;
+            for (int i = 0; i < 8; i++) T[lane * 16 + hs * 8 + i] = blk[2 + 8 * t + i];
+            for (int i = 0; i < 4; i++) T[512 + lane * 8 + hs * 4 + i] = blk[34 + 4 * t + i];
+        }
+        T[768 + 4 * g + 2 * hs] = blk[0];
+        T[768 + 4 * g + 2 * hs + 1] = blk[1];
+    } break;
+    default:
+        break;
+    }
+}
+
+// --------------------------------------------- gather (tile -> GGUF) --------
+// Exact inverse of scatter_block.
+__host__ __device__ inline void gather_block(int type, const uint8_t *T, int r, int bic, uint8_t *blk) {
+    const int g = r & 7, hs = r >> 3;
+    switch (type) {
+    case EF_Q8_0: {
+        const int lane = 4 * g + bic;
+        for (int i = 0; i < 32; i++)
+            blk[2 + i] = T[(2 * hs + (i >> 4)) * 512 + lane * 16 + (i & 15)] ^ 0x80;
+        blk[0] = T[2048 + lane * 4 + hs * 2];
+        blk[1] = T[2048 + lane * 4 + hs * 2 + 1];
+    } break;
+    case EF_Q4_K: {
+        for (int t = 0; t < 4; t++) {
+            const int lane = 4 * g + t;
+            for (int i = 0; i < 8; i++)
+                wr32(blk + 16 + 32 * t + 4 * i,
+                     nib_inv(rd32(T + (2 * hs + (i >> 2)) * 512 + lane * 16 + (i & 3) * 4)));
+        }
+        for (int i = 0; i < 16; i++) blk[i] = T[2048 + r * 16 + i];
+    } break;
+    case EF_Q6_K: {
+        for (int t = 0; t < 4; t++) {
+            const int n = t >> 1, lh = t & 1, lane = 4 * g + t;
+            uint8_t *A = blk + 64 * n + 16 * lh, *B = blk + 64 * n + 32 + 16 * lh;
+            uint8_t *H = blk + 128 + 32 * n + 16 * lh;
+            for (int w = 0; w < 4; w++) {
+                wr32(A + 4 * w, nib_inv(rd32(T + (3 * hs) * 512 + lane * 16 + 4 * w)));
+                wr32(B + 4 * w, nib_inv(rd32(T + (3 * hs + 1) * 512 + lane * 16 + 4 * w)));
+            }
+            for (int j = 0; j < 16; j++) {
+                uint32_t h = 0;
+                for (int i = 0; i < 4; i++)
+                    h |= ((rd32(T + (3 * hs + 2) * 512 + lane * 16 + 4 * i) >> q6_hpos(j)) & 3u) << (2 * i);
+                H[j] = (uint8_t)h;
+            }
+        }
+        for (int i = 0; i < 16; i++) blk[192 + i] = T[3072 + r * 16 + i];
+        blk[208] = T[3328 + 4 * g + 2 * hs];
+        blk[209] = T[3328 + 4 * g + 2 * hs + 1];
+    } break;
+    case EF_IQ2_XXS: {
+        for (int t = 0; t < 4; t++)
+            for (int i = 0; i < 16; i++) blk[2 + 16 * t + i] = T[hs * 512 + (4 * g + t) * 16 + i];
+        blk[0] = T[1024 + 4 * g + 2 * hs];
+        blk[1] = T[1024 + 4 * g + 2 * hs + 1];
+    } break;
+    case EF_IQ1_S: {
+        for (int t = 0; t < 4; t++) {
+            const int lane = 4 * g + t;
+            for (int i = 0; i < 8; i++) blk[2 + 8 * t + i] = T[lane * 16 + hs * 8 + i];
+            for (int i = 0; i < 4; i++) blk[34 + 4 * t + i] = T[512 + lane * 8 + hs * 4 + i];
+        }
+        blk[0] = T[768 + 4 * g + 2 * hs];
+        blk[1] = T[768 + 4 * g + 2 * hs + 1];
+    } break;
+    default:
+        break;
+    }
+}
+
+// ------------------------------------------------ reference decoders --------
+// f16 bits -> f32, exact (WGSL unpack2x16float, kernels.wgsl.js:91-93).
+__device__ __forceinline__ float h2f(uint32_t bits16) {
+    return __half2float(__ushort_as_half((unsigned short)bits16));
+}
+
+__device__ __forceinline__ void scale_min_k4(const uint8_t *sb, int j, int &sc, int &mn) {
+    // kernels.wgsl.js:94-104
+    if (j < 4) { sc = sb[j] & 63; mn = sb[j + 4] & 63; }
+    else { sc = (sb[j + 4] & 0xF) | ((sb[j - 4] >> 6) << 4); mn = (sb[j + 4] >> 4) | ((sb[j] >> 6) << 4); }
+}
+
+// One GGUF block to f32 with the reference's operation order (every product is
+// exact; Q4_K rounds once in d1*q - m1). `grid` = int8 codebook (8 per entry).
+__device__ inline void decode_block(int type, const uint8_t *blk, const int8_t *grid, float *out) {
+    switch (type) {
+    case EF_Q8_0: {
+        const float d = h2f(blk[0] | (blk[1] << 8));
+        for (int i = 0; i < 32; i++) out[i] = __fmul_rn((float)(int8_t)blk[2 + i], d);
+    } break;
+    case EF_Q4_K: {
+        const float d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));
+        for (int j = 0; j < 4; j++) {
+            int s1, m1i, s2, m2i;
+            scale_min_k4(blk + 4, 2 * j, s1, m1i);
+            scale_min_k4(blk + 4, 2 * j + 1, s2, m2i);
+            const float d1 = __fmul_rn(d, (float)s1), m1 = __fmul_rn(dmin, (float)m1i);
+            const float d2 = __fmul_rn(d, (float)s2), m2 = __fmul_rn(dmin, (float)m2i);
+            for (int l = 0; l < 32; l++) {
+                const uint8_t q = blk[16 + 32 * j + l];
+                out[64 * j + l] = __fsub_rn(__fmul_rn(d1, (float)(q & 0xF)), m1);
+                out[64 * j + 32 + l] = __fsub_rn(__fmul_rn(d2, (float)(q >> 4)), m2);
+            }
+        }
+    } break;
+    case EF_Q6_K: {
+        const float d = h2f(blk[208] | (blk[209] << 8));
+        for (int n = 0; n < 2; n++) {
+            const uint8_t *ql = blk + 64 * n, *qh = blk + 128 + 32 * n;
+            const int8_t *sc = (const int8_t *)(blk + 192 + 8 * n);
+            for (int l = 0; l < 32; l++) {
+                const int is = l >> 4;
+                const int q1 = ((ql[l] & 0xF) | (((qh[l] >> 0) & 3) << 4)) - 32;
+                const int q2 = ((ql[32 + l] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+                const int q3 = ((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+                const int q4 = ((ql[32 + l] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+                out[128 * n + l] = __fmul_rn(__fmul_rn(d, (float)sc[is]), (float)q1);
+                out[128 * n + 32 + l] = __fmul_rn(__fmul_rn(d, (float)sc[is + 2]), (float)q2);
+                out[128 * n + 64 + l] = __fmul_rn(__fmul_rn(d, (float)sc[is + 4]), (float)q3);
+                out[128 * n + 96 + l] = __fmul_rn(__fmul_rn(d, (float)sc[is + 6]), (float)q4);
+            }
+        }
+    } break;
+    case EF_IQ2_XXS: {
+        const float d = h2f(blk[0] | (blk[1] << 8));
+        for (int ib = 0; ib < 8; ib++) {
+            const uint32_t a0 = rd32(blk + 2 + 8 * ib), a1 = rd32(blk + 6 + 8 * ib);
+            const float db = __fmul_rn(__fmul_rn(d, __fadd_rn(0.5f, (float)(a1 >> 28))), 0.25f);
+            for (int l = 0; l < 4; l++) {
+                const uint32_t gi = (a0 >> (8 * l)) & 0xFF;
+                const uint32_t bits = (a1 >> (7 * l)) & 127u;
+                const uint32_t signs = bits | ((uint32_t)(__popc(bits) & 1) << 7);
+                for (int j = 0; j < 8; j++) {
+                    const float gv = (float)(uint8_t)grid[8 * gi + j];
+                    const float sg = (signs & (1u << j)) ? -1.0f : 1.0f;
+                    out[32 * ib + 8 * l + j] = __fmul_rn(__fmul_rn(db, gv), sg);
+                }
+            }
+        }
+    } break;
+    case EF_IQ1_S: {
+        const float d = h2f(blk[0] | (blk[1] << 8));
+        for (int ib = 0; ib < 8; ib++) {
+            const uint32_t qh = blk[34 + 2 * ib] | (blk[35 + 2 * ib] << 8);
+            const float dl = __fmul_rn(d, (float)(2u * ((qh >> 12) & 7u) + 1u));
+            const float delta = (qh & 0x8000u) ? -0.125f : 0.125f;
+            for (int l = 0; l < 4; l++) {
+                const uint32_t gi = blk[2 + 4 * ib + l] | (((qh >> (3 * l)) & 7u) << 8);
+                for (int j = 0; j < 8; j++)
+                    out[32 * ib + 8 * l + j] = __fmul_rn(dl, __fadd_rn((float)grid[8 * gi + j], delta));
+            }
+        }
+    } break;
+    default:
+        break;
+    }
+}
+
+// ------------------------------------------------------------ PTX helpers --
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+    // (a & b) | c
+    uint32_t d;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+    uint32_t d;
+    asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+    return d;
+}
+__device__ __forceinline__ uint32_t hsub2u(uint32_t a, uint32_t b) {
+    __half2 r = __hsub2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
+    __half2 r = __hmul2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
+    __half2 r = __hfma2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b),
+                        *reinterpret_cast<__half2 *>(&c));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t hadd2u(uint32_t a, uint32_t b) {
+    __half2 r = __hadd2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
+    return *reinterpret_cast<uint32_t *>(&r);
+}
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+// D (+)= A(16x16 f16, row) * B(16x8 f16, col), f32 accumulate.
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};\n"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Streaming 128-bit load of weights: read-only path, not kept in L1.
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+}  // namespace ef

@@ -1,0 +1,168 @@
+/*
+ * elffuss_cuda.h -- C ABI of the B200 (sm_100a) quantized matrix-product path.
+ *
+ * This library replaces, for the GGUF block-quantized GEMV (decode) and GEMM
+ * (prefill), the WebGPU objects and WGSL kernels behind the reference's
+ * operator API `createQuantOps(device, {ctx, ...})` (js/ops.js:748-1142):
+ *   device + context + buffer pool   js/device.js:66-165, js/ops.js:134-469
+ *   load-time repack                 js/repack.js:153-306
+ *   dequant / matmul / gemv / gemm2  js/ops.js:813-1101, js/ops.gemv.js:148-215,
+ *                                    js/ops.gemm2.js:266-302
+ * Plain pointers, sizes and opaque handles only; no C++ or torch types.
+ *
+ * Conventions
+ *   - Every call returns an int status: EF_OK (0), EF_NOT_APPLICABLE (1, the
+ *     reference's `null` return from gemv/gemm2: "this path does not apply,
+ *     the caller falls back", js/ops.gemv.js:13-21, js/ops.gemm2.js:5-8), or a
+ *     negative error (the reference's `throw new Error(...)`). The message of
+ *     the last error is kept per context: ef_last_error().
+ *   - All device work is asynchronous and ordered on the context's stream
+ *     (the reference records into one command batch and syncs only at
+ *     readback, js/ops.js:665-679, js/device.js:165). ef_stream_sync waits.
+ *   - Activations are token-major f32 [tokens][k]; outputs f32 [tokens][rows]
+ *     (js/ops.js:827-829, 1085-1100).
+ *   - Device pointers passed in (x, y, dev_out) must be 16-byte aligned.
+ */
+#ifndef ELFFUSS_CUDA_H
+#define ELFFUSS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EF_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define EF_API __attribute__((visibility("default")))
+#else
+#define EF_API
+#endif
+
+/* Status codes. */
+enum {
+    EF_OK = 0,
+    EF_NOT_APPLICABLE = 1,   /* path does not apply; caller falls back (reference `null`) */
+    EF_ERR_INVALID = -1,     /* null handle / pointer, negative or zero size */
+    EF_ERR_TYPE = -2,        /* unsupported quant type (js/ops.js:769-770) */
+    EF_ERR_SHAPE = -3,       /* k not a multiple of the block, bad rows/tokens (js/ops.js:850-852) */
+    EF_ERR_CUDA = -4,        /* CUDA runtime failure; message in ef_last_error */
+    EF_ERR_OOM = -5,         /* device allocation failed */
+    EF_ERR_MISMATCH = -6,    /* weight handle does not match the call (js/repack.js:268-286) */
+    EF_ERR_RANGE = -7        /* offset/size outside a buffer, or a slice outside a tensor */
+};
+
+/* GGUF tensor types (ggml ids, js/gguf.js:48-64). */
+enum {
+    EF_F32 = 0, EF_F16 = 1, EF_Q4_0 = 2, EF_Q8_0 = 8, EF_Q4_K = 12, EF_Q6_K = 14,
+    EF_IQ2_XXS = 16, EF_IQ1_S = 19
+};
+
+typedef struct ef_ctx ef_ctx;        /* device + stream + buffer pool (js/ops.js:134 createContext) */
+typedef struct ef_buf ef_buf;        /* device allocation (a GPUBuffer of the reference) */
+typedef struct ef_weight ef_weight;  /* a weight tensor repacked on the device (creaBufferR) */
+
+/* ---- library / context ---------------------------------------------------- */
+
+/* ABI version of the loaded library (EF_ABI_VERSION). */
+EF_API int ef_version(void);
+
+/* Block geometry of a type: elements and bytes per GGUF block (js/kernels.wgsl.js:886-892
+ * QUANT_TYPES). EF_ERR_TYPE for a type without a decoder here. */
+EF_API int ef_type_info(int type, int *block_elems, int *block_bytes);
+
+/* Create a context on CUDA device `device` with its own stream.
+ * Replaces requestDevice() + createContext() (js/device.js:66, js/ops.js:134). */
+EF_API int ef_ctx_create(int device, ef_ctx **out);
+EF_API int ef_ctx_destroy(ef_ctx *ctx);
+
+/* Run subsequent work on a caller-owned cudaStream_t (e.g. torch's current
+ * stream); NULL selects the CUDA default stream. Until the first call the
+ * context uses a stream of its own. */
+EF_API int ef_ctx_set_stream(ef_ctx *ctx, void *cuda_stream);
+EF_API void *ef_ctx_stream(const ef_ctx *ctx);
+
+/* Wait for all work queued on the context's stream (the readback sync point,
+ * js/device.js:165). */
+EF_API int ef_stream_sync(ef_ctx *ctx);
+
+/* Message of the last failing call on this context ("" if none). */
+EF_API const char *ef_last_error(const ef_ctx *ctx);
+
+/* ---- buffers (ctx.alloc / recycle / upload, js/ops.js:242-307,1129-1133) --- */
+
+EF_API int ef_alloc(ef_ctx *ctx, size_t bytes, ef_buf **out);
+EF_API int ef_free(ef_ctx *ctx, ef_buf *buf);
+EF_API void *ef_buf_ptr(const ef_buf *buf);
+EF_API size_t ef_buf_size(const ef_buf *buf);
+/* Host <-> device copies, ordered on the context stream; ef_download waits. */
+EF_API int ef_upload(ef_ctx *ctx, ef_buf *buf, size_t offset, const void *host, size_t n);
+EF_API int ef_download(ef_ctx *ctx, const ef_buf *buf, size_t offset, void *host, size_t n);
+/* Pool marks: every ef_alloc after `mark` that is not in `live` is freed by
+ * ef_scratch_release (ctx.recycleDesde(mark, ...live), js/ops.js:295-307). */
+EF_API int ef_scratch_mark(ef_ctx *ctx, uint64_t *mark);
+EF_API int ef_scratch_release(ef_ctx *ctx, uint64_t mark, ef_buf *const *live, int nlive);
+
+/* ---- weights (load-time repack, js/repack.js:153-306, js/model.js:312-329) --- */
+
+/* Upload a row-major GGUF tensor (rows x k weights, raw block bytes) and repack
+ * it on the device into the tile layout the kernels read. Replaces
+ * reordena/creaBufferR/marcaBufferR (js/repack.js:187,241,293). */
+EF_API int ef_weight_load(ef_ctx *ctx, int type, const void *host_gguf, int64_t rows, int64_t k,
+                   ef_weight **out);
+/* The same from GGUF bytes already in device memory (not modified). */
+EF_API int ef_weight_load_device(ef_ctx *ctx, int type, const void *dev_gguf, int64_t rows,
+                          int64_t k, ef_weight **out);
+/* Load the sub-matrix rows [row0, row0+nrows) x columns [k0, k0+nk) of a host
+ * GGUF tensor of rows x k: the shard of one tensor-parallel rank (column-
+ * parallel: a row range; row-parallel: a k range, k0 and nk multiples of the
+ * block). No reference counterpart: the reference is single-device. */
+EF_API int ef_weight_load_slice(ef_ctx *ctx, int type, const void *host_gguf, int64_t rows, int64_t k,
+                         int64_t row0, int64_t nrows, int64_t k0, int64_t nk, ef_weight **out);
+EF_API int ef_weight_free(ef_ctx *ctx, ef_weight *w);
+EF_API int ef_weight_info(const ef_weight *w, int *type, int64_t *rows, int64_t *k, size_t *dev_bytes);
+/* Inverse repack: write the original GGUF bytes (rows * k/elems * bytes) to
+ * `dev_gguf_out`. The round-trip hook of vuelveAlGGUF (js/repack.js:201-219). */
+EF_API int ef_weight_unpack(ef_ctx *ctx, const ef_weight *w, void *dev_gguf_out);
+
+/* ---- operators ------------------------------------------------------------- */
+
+/* Rows [row0, row0+nrows) of dequant(W) to f32 [nrows][k], bit-exact with the
+ * reference decoders. quant.dequant (js/ops.js:813-823, kernels.wgsl.js:903). */
+EF_API int ef_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows, float *dev_out);
+
+/* Decode GEMV, 1 <= M <= 16 tokens: y[M][rows] = x[M][k] . dequant(W)^T.
+ * quant.gemv.matmul / quant.matmul for few tokens (js/ops.gemv.js:148-165,
+ * js/ops.js:834-837). EF_NOT_APPLICABLE for M > 16. */
+EF_API int ef_gemv(ef_ctx *ctx, const ef_weight *w, const float *x, int M, float *y);
+
+/* Fused gate/up GEMV with the SwiGLU epilogue: y = silu(Wg.x) * (Wu.x),
+ * silu(v) = v / (1 + exp(-v)). quant.gemv.gateUp (js/ops.gemv.js:166-190,
+ * kernels.gemv.wgsl.js:434-437). Wg and Wu share type, rows and k. */
+EF_API int ef_gemv_swiglu(ef_ctx *ctx, const ef_weight *wg, const ef_weight *wu, const float *x, int M,
+                   float *y);
+
+/* 1..4 matrices with the same x and k, each to its own output (Q/K/V/gate in
+ * one launch). quant.gemv.secciones (js/ops.gemv.js:192-215). */
+EF_API int ef_gemv_sections(ef_ctx *ctx, const ef_weight *const *ws, int n, const float *x, int M,
+                     float *const *ys);
+
+/* Prefill GEMM, M >= 1 tokens (tuned for M >= 128): y[M][rows] with x given as
+ * f16 (x_type EF_F16, [M][k]) or f32 (EF_F32, converted to f16 with round to
+ * nearest even first, js/ops.gemm2.js:175-196). W is dequantised to f16 and
+ * multiplied on the tcgen05 tensor cores with f32 accumulation
+ * (gemm2.matmul, js/ops.gemm2.js:266-289, kernels.gemm2.wgsl.js:174-240).
+ * `flags` is reserved (0). */
+EF_API int ef_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y,
+            uint32_t flags);
+
+/* The dispatcher of quant.matmul (js/ops.js:827-1101): GEMV for tokens <= 16,
+ * GEMM above, same contract and output. */
+EF_API int ef_matmul(ef_ctx *ctx, const ef_weight *w, const float *x, int tokens, float *y);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ELFFUSS_CUDA_H */

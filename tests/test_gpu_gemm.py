@@ -1,0 +1,49 @@
+"""Prefill GEMM parity: f16 activations, f32 accumulate, against the oracle's
+GEMM2 contract (X rounded to f16; W rounded to f16 as the reference tile does,
+kernels.gemm2.wgsl.js:12-23), within max|err| <= 1e-3 * ||row|| * ||x||."""
+import numpy as np
+import pytest
+import torch
+
+from elffuss_engine_b200 import formats
+
+pytestmark = pytest.mark.gpu
+REL = 1e-3
+
+
+@pytest.mark.parametrize("t,rows,k", [("Q8_0", 256, 512), ("Q8_0", 48, 2048), ("Q4_K", 128, 1024),
+                                      ("Q6_K", 64, 512)])
+@pytest.mark.parametrize("M", [17, 64, 130])
+def test_gemm_f16x_vs_oracle(ops, oracle_mod, t, rows, k, M):
+    raw = formats.synth(t, rows, k, seed=M + rows)
+    w = ops.load_weight(t, raw, rows, k)
+    x = np.random.default_rng(M).standard_normal((M, k)).astype(np.float32)
+    xh = oracle_mod.f32_to_f16_bits(x)
+    y = ops.gemm2.matmul(t, w, torch.from_numpy(xh.view(np.float16)).cuda(), rows, k, M, x_f16=True)
+    y = y.cpu().numpy()
+    want = oracle_mod.matmul_f64(t, raw, rows, k, xh=xh, tokens=M, w16=True)
+    tol = oracle_mod.tolerance(t, raw, rows, k, xh.view(np.float16).astype(np.float32), rel=REL)
+    assert np.all(np.abs(y - want) <= tol)
+
+
+@pytest.mark.parametrize("M,k,rows", [(512, 2048, 8192), (2048, 8192, 2048)])
+def test_gemm_config2_vs_torch(ops, M, k, rows):
+    raw = formats.synth("Q8_0", rows, k, seed=2)
+    w = ops.load_weight("Q8_0", raw, rows, k)
+    wd = ops.dequant("Q8_0", w, rows * k // 32).reshape(rows, k)
+    x = torch.randn(M, k, device="cuda").half()
+    y = ops.gemm2.matmul("Q8_0", w, x, rows, k, M, x_f16=True)
+    ref = x.float() @ wd.half().float().T
+    tol = REL * torch.linalg.norm(x.float(), dim=1)[:, None] * torch.linalg.norm(wd, dim=1)[None, :]
+    assert bool(torch.all((y - ref).abs() <= tol))
+
+
+def test_cola_matches_batch_row(ops):
+    rows, k, lote = 256, 1024, 64
+    raw = formats.synth("Q8_0", rows, k, seed=4)
+    w = ops.load_weight("Q8_0", raw, rows, k)
+    x = torch.randn(lote, k, device="cuda")
+    yb = ops.gemm2.matmul("Q8_0", w, x, rows, k, lote)
+    y1 = ops.gemm2.cola("Q8_0", w, x[-1:].clone(), rows, k, lote)
+    assert ops.gemm2.reproducible("Q8_0", rows, k, lote)
+    torch.testing.assert_close(y1[0], yb[-1], rtol=0, atol=0)

@@ -1,0 +1,108 @@
+"""Decode GEMV parity on the GPU: every hot-path type, 1..16 tokens, ragged
+shapes, fused SwiGLU and sections, against the f64 CPU oracle within the
+acceptance bound max|err| <= 1e-3 * ||row||_2 * ||x||_2.
+At full benchmark sizes the check is against a torch f32 product of the
+bit-exact dequantised weights with the same bound."""
+import numpy as np
+import pytest
+import torch
+
+from elffuss_engine_b200 import formats
+
+pytestmark = pytest.mark.gpu
+REL = 1e-3   # acceptance tolerance (north_star)
+
+
+def _check(oracle_mod, t, raw, rows, k, x, y):
+    yr = oracle_mod.matmul_f64(t, raw, rows, k, x=x, tokens=x.shape[0])
+    tol = oracle_mod.tolerance(t, raw, rows, k, x, rel=REL)
+    err = np.abs(y.astype(np.float64) - yr)
+    assert np.all(err <= tol), f"max err/tol = {(err / tol).max():.3f}"
+    return (err / tol).max()
+
+
+SHAPES = [("Q8_0", 128, 2048), ("Q8_0", 40, 96), ("Q4_K", 256, 1024), ("Q4_K", 36, 4096),
+          ("Q6_K", 128, 1024), ("Q6_K", 20, 2304), ("IQ2_XXS", 64, 1024), ("IQ1_S", 64, 1024)]
+
+
+@pytest.mark.parametrize("t,rows,k", SHAPES)
+@pytest.mark.parametrize("M", [1, 2, 3, 4, 8, 9, 16])
+def test_gemv_vs_oracle(ops, oracle_mod, t, rows, k, M):
+    raw = formats.synth(t, rows, k, seed=M * 131 + rows)
+    w = ops.load_weight(t, raw, rows, k)
+    x = np.random.default_rng(M).standard_normal((M, k)).astype(np.float32)
+    y = ops.matmul(t, w, torch.from_numpy(x).cuda(), rows, k, M).cpu().numpy()
+    assert y.shape == (M, rows)
+    _check(oracle_mod, t, raw, rows, k, x, y)
+
+
+@pytest.mark.parametrize("t", formats.HOT_TYPES)
+def test_gemv_is_deterministic(ops, t):
+    rows, k = 512, 4096
+    raw = formats.synth(t, rows, k, seed=1)
+    w = ops.load_weight(t, raw, rows, k)
+    x = torch.randn(3, k, device="cuda")
+    a = ops.matmul(t, w, x, rows, k, 3)
+    b = ops.matmul(t, w, x, rows, k, 3)
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("t", ["Q8_0", "Q4_K", "Q6_K"])
+@pytest.mark.parametrize("M", [1, 16])
+def test_swiglu_vs_oracle(ops, oracle_mod, t, M):
+    rows, k = 160, 1024
+    rg, ru = formats.synth(t, rows, k, seed=5), formats.synth(t, rows, k, seed=6)
+    wg, wu = ops.load_weight(t, rg, rows, k), ops.load_weight(t, ru, rows, k)
+    x = np.random.default_rng(2).standard_normal((M, k)).astype(np.float32)
+    y = ops.gemv.gateUp(t, wg, wu, torch.from_numpy(x).cuda(), rows, k, M).cpu().numpy()
+    g = oracle_mod.matmul_f64(t, rg, rows, k, x=x, tokens=M)
+    u = oracle_mod.matmul_f64(t, ru, rows, k, x=x, tokens=M)
+    want = oracle_mod.swiglu_f64(g, u)
+    # error propagation of silu(g)*u from the two GEMV bounds
+    tg = oracle_mod.tolerance(t, rg, rows, k, x, rel=REL)
+    tu = oracle_mod.tolerance(t, ru, rows, k, x, rel=REL)
+    dsilu = 1.1 * np.abs(u) + 1e-30
+    tol = dsilu * tg + (np.abs(g) + 1.0) * tu
+    assert np.all(np.abs(y - want) <= tol)
+
+
+@pytest.mark.parametrize("t", ["Q8_0", "Q4_K"])
+def test_sections_equal_single(ops, t):
+    k = 1024
+    shapes = [512, 128, 128, 32]
+    raws = [formats.synth(t, r, k, seed=i) for i, r in enumerate(shapes)]
+    ws = [ops.load_weight(t, raw, r, k) for raw, r in zip(raws, shapes)]
+    x = torch.randn(2, k, device="cuda")
+    ys = ops.gemv.secciones(t, ws, x, shapes, k, 2)
+    for w, r, y in zip(ws, shapes, ys):
+        single = ops.gemv.matmul(t, w, x, r, k, 2)
+        torch.testing.assert_close(y, single, rtol=0, atol=0)
+    assert ops.gemv.despachados()["secciones"] >= 1
+
+
+@pytest.mark.parametrize("t,rows,k", [("Q8_0", 8192, 2048), ("Q4_K", 14336, 4096), ("Q4_K", 4096, 14336),
+                                      ("Q6_K", 14336, 4096), ("Q6_K", 4096, 14336)])
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_full_size_vs_torch_f32(ops, t, rows, k, M):
+    """Benchmark shapes: GEMV vs a torch f32 product of the bit-exact dequant."""
+    raw = formats.synth(t, rows, k, seed=42)
+    w = ops.load_weight(t, raw, rows, k)
+    be, _ = formats.block_info(t)
+    wd = ops.dequant(t, w, rows * k // be).reshape(rows, k)
+    x = torch.randn(M, k, device="cuda")
+    y = ops.matmul(t, w, x, rows, k, M)
+    ref = (x.double() @ wd.double().T)
+    tol = REL * torch.linalg.norm(x.double(), dim=1)[:, None] * torch.linalg.norm(wd.double(), dim=1)[None, :]
+    assert bool(torch.all((y.double() - ref).abs() <= tol))
+
+
+def test_wrong_weight_raises(ops):
+    from elffuss_engine_b200 import EfError
+    raw = formats.synth("Q4_K", 16, 256, seed=0)
+    w = ops.load_weight("Q4_K", raw, 16, 256)
+    with pytest.raises(EfError):
+        ops.matmul("Q6_K", w, torch.randn(1, 256, device="cuda"), 16, 256, 1)
+    with pytest.raises(EfError):
+        ops.matmul("Q4_K", w, torch.randn(1, 256, device="cuda"), 32, 256, 1)
+    with pytest.raises(EfError):
+        ops.matmul("Q4_0X", w, torch.randn(1, 256, device="cuda"), 16, 256, 1)
