@@ -7,12 +7,15 @@ each on its OWN copy of its weight tensor, so a step streams 486 MB of weights
 inputs with the BASELINE.json distributions (no dataset exists).
 
   value  = algorithmic bytes of all 12 GEMVs (weights + x + y) / device time
-           of the step, CUDA events on the launching stream, inputs resident;
-  e2e    = the same bytes through the public operator (QuantOps.gemv) with x
-           copied from pinned host memory and y read back to pinned host memory
-           inside the timed region, every GEMV;
-  roofline: the GEMV kernel's algorithmic bytes / its own event-timed duration
-           against the measured HBM copy bandwidth (MEASURED_PEAKS.json).
+           of the step: the step (12 x ef_gemv, each = activation prep kernel +
+           GEMV kernel) is captured once as a CUDA graph and replayed K times
+           back to back; CUDA events around the K replays, inputs resident;
+  e2e    = the same bytes through the public operator (QuantOps.gemv.matmul)
+           with x copied from pinned host memory and y copied back to pinned
+           host memory inside every step (captured and replayed the same way);
+  roofline: the GEMV's algorithmic bytes / its own duration (CUDA events
+           recorded between the kernels inside a captured step) against the
+           measured HBM copy bandwidth (MEASURED_PEAKS.json).
 
 N > 1 (torchrun, one rank per GPU): weak scaling -- every rank runs the same
 sweep on its own weights (independent tensors, no collective on the data path);
@@ -208,25 +211,26 @@ def run_ours(args):
         work.append((t, n, k, m, w, x, y, xh, yh, alg_bytes(t, n, k, m)))
     del raw
     step_bytes = sum(wk[-1] for wk in work)
-    h = ops.ctx.bind()
     L = lib()
 
-    def step_device(evs=None):
-        for j, (t, n, k, m, w, x, y, xh, yh, b) in enumerate(work):
-            if evs is not None:
-                evs[j][0].record(stream)
+    def step_device():
+        h = ops.ctx.bind()
+        for (t, n, k, m, w, x, y, xh, yh, b) in work:
             check(L.ef_gemv(h, w.h, _ptr(x), m, _ptr(y)), h)
-            if evs is not None:
-                evs[j][1].record(stream)
 
-    def step_e2e_real():
-        outs = []
+    def step_device_evs(evs):
+        h = ops.ctx.bind()
+        s = torch.cuda.current_stream()
+        for j, (t, n, k, m, w, x, y, xh, yh, b) in enumerate(work):
+            evs[j][0].record(s)
+            check(L.ef_gemv(h, w.h, _ptr(x), m, _ptr(y)), h)
+            evs[j][1].record(s)
+
+    def step_e2e():
         for (t, n, k, m, w, x, y, xh, yh, b) in work:
             x.copy_(xh, non_blocking=True)
-            yo = ops.gemv.matmul(t, w, x, n, k, m)
+            yo = ops.gemv.matmul(t, w, x, n, k, m)   # public operator (allocates its output)
             yh.copy_(yo, non_blocking=True)
-            outs.append(yo)
-        return outs
 
     def barrier():
         torch.cuda.synchronize()
@@ -241,40 +245,64 @@ def run_ours(args):
         dist.all_reduce(tv, op=dist.ReduceOp.MAX)
         return float(tv.item())
 
-    # ---- device-resident timing ----
+    def capture(fn, *a):
+        g = torch.cuda.CUDAGraph()
+        cs = torch.cuda.Stream()
+        cs.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cs):
+            fn(*a)          # warm this stream (first-use attribute setup, scratch sizing)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g, stream=cs):
+            fn(*a)
+        torch.cuda.synchronize()
+        return g
+
+    def timed_replays(g, steps):
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        ev0.record()
+        for _ in range(steps):
+            g.replay()
+        ev1.record()
+        barrier()
+        return max_over_ranks(ev0.elapsed_time(ev1))
+
+    # eager warm-up: kernel attributes and scratch sized before any capture
     for _ in range(args.warmup):
         step_device()
+        step_e2e()
     barrier()
-    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in work]
-           for _ in range(args.steps)]
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    # ---- device-resident timing: one captured step (12 GEMVs), replayed ----
+    g_dev = capture(step_device)
+    for _ in range(args.warmup):
+        g_dev.replay()
     with Clocks(local) as clk:
-        barrier()
-        e0.record(stream)
-        for s in range(args.steps):
-            step_device(evs[s])
-        e1.record(stream)
-        barrier()
-    t_ms = max_over_ranks(e0.elapsed_time(e1))
-    kern_ms = [sum(evs[s][j][0].elapsed_time(evs[s][j][1]) for s in range(args.steps)) / args.steps
-               for j in range(len(work))]
+        t_ms = timed_replays(g_dev, args.steps)
     ms_step = t_ms / args.steps
     value = world * step_bytes / (ms_step * 1e-3) / 1e9
 
-    # ---- end to end through the public operator, host buffers ----
-    for _ in range(max(1, args.warmup)):
-        step_e2e_real()
-    barrier()
-    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    f0.record(stream)
-    for _ in range(args.steps):
-        step_e2e_real()
-    f1.record(stream)
-    barrier()
-    e2e_ms = max_over_ranks(f0.elapsed_time(f1)) / args.steps
+    # ---- per-kernel durations: events between the kernels of the step ----
+    evs = [(torch.cuda.Event(enable_timing=True, external=True),
+            torch.cuda.Event(enable_timing=True, external=True)) for _ in work]
+    g_ker = capture(step_device_evs, evs)
+    reps = max(3, min(args.steps, 20))
+    kern_ms = [0.0] * len(work)
+    for _ in range(reps):
+        g_ker.replay()
+        torch.cuda.synchronize()
+        for j in range(len(work)):
+            kern_ms[j] += evs[j][0].elapsed_time(evs[j][1]) / reps
+
+    # ---- end to end through the public operator, pinned host buffers ----
+    g_e2e = capture(step_e2e)
+    for _ in range(args.warmup):
+        g_e2e.replay()
+    e2e_ms = timed_replays(g_e2e, args.steps) / args.steps
     e2e_val = world * step_bytes / (e2e_ms * 1e-3) / 1e9
     h2d = sum(4 * m * k for (t, n, k, m, *_r) in work)
     d2h = sum(4 * m * n for (t, n, k, m, *_r) in work)
+    del g_dev, g_ker, g_e2e
 
     # ---- roofline of the dominant kernel (the GEMV) ----
     peak, peak_kind = peaks()
@@ -306,7 +334,7 @@ def run_ours(args):
                          "traffic": profile_traffic(), "kernel": "gemv_kernel (all 12 launches)"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
-            "gpu_launches": args.steps * len(work),
+            "gpu_launches": args.steps * len(work) * 2,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "per_call": per_call,

@@ -30,19 +30,19 @@ int check_cuda(ef_ctx *ctx, cudaError_t e, const char *what) {
                    cudaGetErrorString(e), cudaGetErrorName(e));
 }
 
-int ensure_scratch(ef_ctx *ctx, size_t bytes) {
-    if (ctx->scratch_bytes >= bytes) return EF_OK;
-    if (ctx->scratch) {
+int ensure_scratch(ef_ctx *ctx, int slot, size_t bytes) {
+    if (ctx->scratch_bytes[slot] >= bytes) return EF_OK;
+    if (ctx->scratch[slot]) {
         // the old scratch may still be read by queued work
         cudaStreamSynchronize(ctx->stream);
-        cudaFree(ctx->scratch);
-        ctx->scratch = nullptr;
-        ctx->scratch_bytes = 0;
+        cudaFree(ctx->scratch[slot]);
+        ctx->scratch[slot] = nullptr;
+        ctx->scratch_bytes[slot] = 0;
     }
     size_t sz = std::max(bytes, (size_t)1 << 20);
-    int rc = check_cuda(ctx, cudaMalloc(&ctx->scratch, sz), "scratch alloc");
+    int rc = check_cuda(ctx, cudaMalloc(&ctx->scratch[slot], sz), "scratch alloc");
     if (rc) return rc;
-    ctx->scratch_bytes = sz;
+    ctx->scratch_bytes[slot] = sz;
     return EF_OK;
 }
 
@@ -92,7 +92,8 @@ int ef_ctx_destroy(ef_ctx *ctx) {
         cudaFree(b->ptr);
         delete b;
     }
-    if (ctx->scratch) cudaFree(ctx->scratch);
+    for (int i = 0; i < 2; i++)
+        if (ctx->scratch[i]) cudaFree(ctx->scratch[i]);
     if (ctx->own) cudaStreamDestroy(ctx->own);
     delete ctx;
     return EF_OK;

@@ -21,12 +21,12 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
     const float *xf = (const float *)x;
     if (x_type == EF_F16) {
         const int64_t n = (int64_t)M * w->k;
-        if (int rc = ensure_scratch(ctx, (size_t)n * 4)) return rc;
+        if (int rc = ensure_scratch(ctx, 1, (size_t)n * 4)) return rc;
         int64_t blocks = (n + 255) / 256;
         if (blocks > 148 * 32) blocks = 148 * 32;
-        f16_to_f32_kernel<<<(int)blocks, 256, 0, ctx->stream>>>((const __half *)x, (float *)ctx->scratch, n);
+        f16_to_f32_kernel<<<(int)blocks, 256, 0, ctx->stream>>>((const __half *)x, (float *)ctx->scratch[1], n);
         if (int rc = check_cuda(ctx, cudaGetLastError(), "gemm f16->f32")) return rc;
-        xf = (const float *)ctx->scratch;
+        xf = (const float *)ctx->scratch[1];
     }
     for (int t0 = 0; t0 < M; t0 += 16) {
         const int mt = M - t0 < 16 ? M - t0 : 16;

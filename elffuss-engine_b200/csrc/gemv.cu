@@ -4,32 +4,41 @@
 //   swiglu:  y = silu(Wg.x) * (Wu.x)                   (kernels.gemv.wgsl.js:434-437)
 //   sections: several W sharing x and k, one output each (js/ops.gemv.js:192-215)
 //
-// Design (B200): the GEMV is HBM-bound, so every weight byte is read once with
-// 128-bit streaming loads and turned into f16 operands IN REGISTERS, which feed
-// the tensor cores through mma.sync.m16n8k16 (A = 16 weight rows x 16 k, B =
-// 16 k x 8 tokens, f32 accumulate). Register-sourced MMA is the right tensor
-// instruction here: tcgen05.mma takes A from shared or tensor memory, which
-// would add a store + read of every dequantised weight for a kernel whose only
-// job is to stream weights; with register operands a 16-token GEMV costs two
-// MMAs per 256 weights and the dequant stays the only per-weight work.
+// Design (B200). The GEMV is HBM-bound: every weight byte is read once and
+// must be turned into tensor-core operands with as few instructions as
+// possible, and enough bytes must be in flight to cover DRAM latency.
 //
-// Work split: CTA = 8 warps = one "rowblock" of 8 rowgroups (128 rows); a warp
-// owns one rowgroup. Along k the chunks are cut into `kslices` slices, one CTA
-// each; the slices of a rowblock form one thread-block cluster and their
-// partial sums are added through distributed shared memory in rank order
-// (deterministic, no atomics, no global scratch). Activations of the CTA's
-// k-slice are converted once to f16 and staged in shared memory already in
-// B-fragment order, so a fragment is one conflict-free 64-bit shared load.
+//  * Weights: each warp owns one 16-row rowgroup and streams its tiles through
+//    a private ring of cp.async (LDGSTS, L2-only) shared-memory slots, several
+//    tiles ahead of the math. The hardware wait (cp.async.wait_group) needs no
+//    spin loop.
+//  * Math: quants are expanded IN REGISTERS to f16 A fragments of
+//    mma.sync.m16n8k16 (A = 16 weight rows x 16 k, B = 16 k x 8 tokens, f32
+//    accumulate). Register-sourced MMA is the right tensor instruction for a
+//    GEMV: tcgen05.mma reads A from shared or tensor memory, which would add a
+//    store and a read of every dequantised weight.
+//  * Activations: a small prep kernel converts x once per call into f16 B
+//    fragments (zero-padded to 8/16 tokens) plus, for Q4_K, the per-sub-block
+//    sums needed by the "-m*sum(x)" term; each CTA copies its k-slice of that
+//    buffer into shared memory with cp.async. The GEMV is launched with
+//    programmatic dependent launch, so its weight prefetch overlaps the prep.
+//  * Work split: CTA = WARPS rowgroups x one k-slice; the k-slices of a
+//    rowblock form one thread-block cluster whose partial sums are added
+//    through distributed shared memory in rank order (deterministic, no
+//    atomics). A small cost model picks WARPS and the k-split for load
+//    balance over the 148 SMs.
 //
-// Numerics: quants are exact small integers in f16; the block scales are
-// applied in f16 (Q8_0: f16(d*q); Q4_K: f16(f16(d*sc)*q - f16(dmin*m));
-// IQ2_XXS: f16(db)*grid*sign; IQ1_S: f16(dl)*(grid + delta); one rounding
-// each) because the 16 k-columns of one MMA come from four different blocks;
-// only a scale shared by the whole tile row (Q6_K's superblock d) is applied in
-// f32 on the accumulator. x is rounded to f16. The products are exact and
-// summed in f32 by the tensor cores.
+// Numerics: quants are exact small integers in f16 and the per-block scales
+// are applied in f16 with one rounding per weight -- Q8_0: f16(d*q); Q4_K:
+// f16(f16(d*sc)*q) with -f16(dmin*m)*sum(x) as one more MMA; IQ2_XXS:
+// f16(db)*grid*sign; IQ1_S: f16(dl)*(grid+delta) -- because the 16 k-columns of
+// one MMA belong to four different blocks. Q6_K: sc*(q-32) is exact in f16 and
+// the superblock d is applied in f32 on the accumulator. x is rounded to f16.
+// Products are exact and summed in f32 by the tensor cores.
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "gen/iq_grids.h"
@@ -42,11 +51,12 @@ namespace ef {
 __device__ const __align__(16) uint16_t g_grid_iq2xxs_f16[EF_GRID_IQ2XXS_ENTRIES * 8] = {EF_GRID_IQ2XXS_F16_INIT};
 __device__ const __align__(16) uint16_t g_grid_iq1s_f16[EF_GRID_IQ1S_ENTRIES * 8] = {EF_GRID_IQ1S_F16_INIT};
 
+constexpr uint32_t H2_64 = 0x54005400u;     // half2(64, 64)
 constexpr uint32_t H2_1024 = 0x64006400u;   // half2(1024, 1024)
 constexpr uint32_t H2_1152 = 0x64806480u;   // half2(1152, 1152)
 constexpr uint32_t H2_2080 = 0x68106810u;   // half2(2080, 2080)
-constexpr int WARPS = 8;                    // warps (rowgroups) per CTA
-constexpr int MAX_XS_BYTES = 96 * 1024;     // shared memory for staged activations
+constexpr int MAX_XS_BYTES = 32 * 1024;     // shared memory for one phase of x fragments
+constexpr int RING_PER_WARP = 7 * 1024;     // bytes of weight tiles per warp ring
 
 struct GemvArgs {
     const uint8_t *w[4];      // repacked tiles of each section
@@ -56,48 +66,67 @@ struct GemvArgs {
     int64_t rowgroups[4];
     int rb_end[4];            // cumulative rowblocks per section
     int nmat;
-    const float *x;
+    const uint8_t *xf;        // x fragments from gemv_xprep: nchunks x FB bytes
     int M;
-    int64_t K;
     int64_t nchunks;
     int cps;                  // chunks per k-slice
     int kslices;
-    int phase_chunks;         // chunks staged in shared memory at a time
+    int phase_chunks;         // chunks of x fragments in shared memory at a time
 };
 
 // ---------------------------------------------------------------- traits ---
 // STEPS = k16 steps per chunk; inv maps a k-quad (4 consecutive weights of the
-// chunk) to the lane column t and the step s that consume it.
+// chunk) to the lane column t and the step s that consume it; MINF = the chunk
+// carries one extra "-m*sum(x)" fragment (Q4_K).
 template <int TYPE> struct Tr;
 template <> struct Tr<EF_Q8_0> {
-    static constexpr int CHUNK = 128, STEPS = 8, TILE = 2176;
+    static constexpr int CHUNK = 128, STEPS = 8, TILE = 2176, MINF = 0;
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 3; s = kq & 7; }
 };
 template <> struct Tr<EF_Q4_K> {
-    static constexpr int CHUNK = 256, STEPS = 16, TILE = 2304;
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 2304, MINF = 1;
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 4; s = 2 * (kq & 7) + ((kq >> 3) & 1); }
 };
 template <> struct Tr<EF_Q6_K> {
-    static constexpr int CHUNK = 256, STEPS = 16, TILE = 3360;
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 3360, MINF = 0;
     __device__ static void inv(int kq, int &t, int &s) {
         t = 2 * (kq >> 5) + ((kq >> 2) & 1);
         s = 4 * ((kq >> 3) & 3) + (kq & 3);
     }
 };
 template <> struct Tr<EF_IQ2_XXS> {
-    static constexpr int CHUNK = 256, STEPS = 16, TILE = 1056;
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 1056, MINF = 0;
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 4; s = kq & 15; }
 };
 template <> struct Tr<EF_IQ1_S> {
-    static constexpr int CHUNK = 256, STEPS = 16, TILE = 800;
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 800, MINF = 0;
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 4; s = kq & 15; }
+};
+// bytes of x fragments per chunk: STEPS x NT x 32 lanes x 8 B (+ NT x 32 x 4 B)
+template <int TYPE, int NT> struct FragBytes {
+    static constexpr int v = Tr<TYPE>::STEPS * NT * 256 + Tr<TYPE>::MINF * NT * 128;
 };
 
 __device__ __forceinline__ uint32_t wsel(const uint4 &v, int i) {
     return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
-__device__ __forceinline__ uint32_t ldg32(const void *p) { return __ldg((const unsigned int *)p); }
-__device__ __forceinline__ uint2 ldg64(const void *p) { return __ldg((const uint2 *)p); }
+// Tile reads: the tiles sit in the warp's shared-memory ring (see the kernel).
+__device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
+__device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *reinterpret_cast<const uint2 *>(p); }
+__device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+
+// Asynchronous global -> shared copies (LDGSTS, L2 only).
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+template <int TILE>
+__device__ __forceinline__ void copy_tile(uint8_t *dst, const uint8_t *src, int lane) {
+#pragma unroll
+    for (int p = lane; p < TILE / 16; p += 32) cp_async16(dst + 16 * p, src + 16 * p);
+}
 
 template <int NT>
 __device__ __forceinline__ void mma_step(float (&acc)[NT][4], const uint2 *xsc, int s, int lane, uint32_t a0,
@@ -109,24 +138,18 @@ __device__ __forceinline__ void mma_step(float (&acc)[NT][4], const uint2 *xsc, 
     }
 }
 
-template <int NT>
-__device__ __forceinline__ void scale_acc(float (&acc)[NT][4], float (&tmp)[NT][4], float sg, float sg8) {
-#pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-        acc[nt][0] = fmaf(sg, tmp[nt][0], acc[nt][0]);
-        acc[nt][1] = fmaf(sg, tmp[nt][1], acc[nt][1]);
-        acc[nt][2] = fmaf(sg8, tmp[nt][2], acc[nt][2]);
-        acc[nt][3] = fmaf(sg8, tmp[nt][3], acc[nt][3]);
-        tmp[nt][0] = tmp[nt][1] = tmp[nt][2] = tmp[nt][3] = 0.f;
-    }
+__device__ __forceinline__ uint32_t dup_h2(float v) {
+    const uint32_t b = __half_as_ushort(__float2half_rn(v));
+    return b | (b << 16);
 }
 
 // ------------------------------------------------------------------ Q8_0 ---
+// lane (g,t) holds block t of rows g and g+8 (biased bytes q+128) and their f16 d.
 struct RawQ8 { uint4 q[4]; uint32_t sc; };
 __device__ __forceinline__ void load_raw(RawQ8 &r, const uint8_t *T, int lane) {
 #pragma unroll
-    for (int p = 0; p < 4; p++) r.q[p] = ldg_stream(T + p * 512 + lane * 16);
-    r.sc = ldg32(T + 2048 + lane * 4);
+    for (int p = 0; p < 4; p++) r.q[p] = lds128(T + p * 512 + lane * 16);
+    r.sc = lds32(T + 2048 + lane * 4);
 }
 template <int NT>
 __device__ __forceinline__ void compute(const RawQ8 &r, const uint2 *xsc, float (&acc)[NT][4], int lane,
@@ -135,6 +158,7 @@ __device__ __forceinline__ void compute(const RawQ8 &r, const uint2 *xsc, float 
 #pragma unroll
     for (int s = 0; s < 8; s++) {
         const uint32_t wg = wsel(r.q[s >> 2], s & 3), wg8 = wsel(r.q[2 + (s >> 2)], s & 3);
+        // (1024 + q + 128) - 1152 = q exactly; then one rounding of d*q
         const uint32_t a0 = hmul2u(hsub2u(prmt(wg, 0x64646464u, 0x5140), H2_1152), dg);
         const uint32_t a2 = hmul2u(hsub2u(prmt(wg, 0x64646464u, 0x7362), H2_1152), dg);
         const uint32_t a1 = hmul2u(hsub2u(prmt(wg8, 0x64646464u, 0x5140), H2_1152), dg8);
@@ -147,74 +171,79 @@ __device__ __forceinline__ void compute(const RawQ8 &r, const uint2 *xsc, float 
 struct RawQ4K { uint4 q[4]; uint4 hg, hg8; };
 __device__ __forceinline__ void load_raw(RawQ4K &r, const uint8_t *T, int lane) {
 #pragma unroll
-    for (int p = 0; p < 4; p++) r.q[p] = ldg_stream(T + p * 512 + lane * 16);
+    for (int p = 0; p < 4; p++) r.q[p] = lds128(T + p * 512 + lane * 16);
     const int g = lane >> 2;
-    r.hg = ldg_stream(T + 2048 + g * 16);
-    r.hg8 = ldg_stream(T + 2048 + (g + 8) * 16);
+    r.hg = lds128(T + 2048 + g * 16);
+    r.hg8 = lds128(T + 2048 + (g + 8) * 16);
 }
-// (d*sc_a, d*sc_b, -dmin*m_a, -dmin*m_b) as duplicated half2 for lane column t
-// (sub-blocks 2t, 2t+1), from a verbatim 16-byte Q4_K header: scale_min_k4
-// (kernels.wgsl.js:94-104) for j = 2t, 2t+1 without divergence.
-__device__ __forceinline__ void q4k_scales(const uint4 &h, int t, uint32_t &d1a, uint32_t &d1b, uint32_t &nm1a,
-                                           uint32_t &nm1b) {
+// Scales of lane column t (sub-blocks 2t, 2t+1) from a verbatim 16-byte Q4_K
+// header: scale_min_k4 (kernels.wgsl.js:94-104) for j = 2t, 2t+1, as f16:
+// d1 = f16(d*sc) duplicated in both halves, and (-f16(dmin*m_a), -f16(dmin*m_b)).
+__device__ __forceinline__ void q4k_scales(const uint4 &h, int t, uint32_t &d1a, uint32_t &d1b, uint32_t &nm) {
     const uint32_t dd = prmt(h.x, 0, 0x1010), nmm = prmt(h.x, 0, 0x3232) ^ 0x80008000u;
     const int sh = 16 * (t & 1);
     const uint32_t p0 = (h.y >> sh) & 0xFFFF, p1 = (h.z >> sh) & 0xFFFF, p2 = (h.w >> sh) & 0xFFFF;
-    uint32_t scp, mp;
-    if (t < 2) {
-        scp = p0 & 0x3F3F;
-        mp = p1 & 0x3F3F;
-    } else {
-        scp = (p2 & 0x0F0F) | ((p0 >> 2) & 0x3030);
-        mp = ((p2 >> 4) & 0x0F0F) | ((p1 >> 2) & 0x3030);
-    }
+    const uint32_t scl = p0 & 0x3F3F, mpl = p1 & 0x3F3F;
+    const uint32_t sch = (p2 & 0x0F0F) | ((p0 >> 2) & 0x3030), mph = ((p2 >> 4) & 0x0F0F) | ((p1 >> 2) & 0x3030);
+    const uint32_t scp = t < 2 ? scl : sch, mp = t < 2 ? mpl : mph;
     d1a = hmul2u(hsub2u(prmt(scp, 0x64646464u, 0x4040), H2_1024), dd);
     d1b = hmul2u(hsub2u(prmt(scp, 0x64646464u, 0x4141), H2_1024), dd);
-    nm1a = hmul2u(hsub2u(prmt(mp, 0x64646464u, 0x4040), H2_1024), nmm);
-    nm1b = hmul2u(hsub2u(prmt(mp, 0x64646464u, 0x4141), H2_1024), nmm);
+    nm = hmul2u(hsub2u(prmt(mp, 0x64646464u, 0x4140), H2_1024), nmm);   // (m_a, m_b) * -dmin
 }
 template <int NT>
 __device__ __forceinline__ void compute(const RawQ4K &r, const uint2 *xsc, float (&acc)[NT][4], int lane,
                                         const uint4 *, const uint4 *) {
     const int t = lane & 3;
-    uint32_t ga, gb, gna, gnb, ha, hb, hna, hnb;
-    q4k_scales(r.hg, t, ga, gb, gna, gnb);
-    q4k_scales(r.hg8, t, ha, hb, hna, hnb);
+    uint32_t ga, gb, gnm, ha, hb, hnm;
+    q4k_scales(r.hg, t, ga, gb, gnm);
+    q4k_scales(r.hg8, t, ha, hb, hnm);
+    // (M + q) * d1 - M * d1 = q * d1 with ONE rounding (fused, -M*d1 exact):
+    // M = 1024 for a nibble at bits 0-3 of a half, M = 64 at bits 4-7.
+    const uint32_t ga10 = hmul2u(ga, 0xE400E400u), ga6 = hmul2u(ga, 0xD400D400u);   // -1024 d1, -64 d1
+    const uint32_t gb10 = hmul2u(gb, 0xE400E400u), gb6 = hmul2u(gb, 0xD400D400u);
+    const uint32_t ha10 = hmul2u(ha, 0xE400E400u), ha6 = hmul2u(ha, 0xD400D400u);
+    const uint32_t hb10 = hmul2u(hb, 0xE400E400u), hb6 = hmul2u(hb, 0xD400D400u);
 #pragma unroll
     for (int i = 0; i < 8; i++) {
         const uint32_t wg = wsel(r.q[i >> 2], i & 3), wg8 = wsel(r.q[2 + (i >> 2)], i & 3);
+        const uint32_t vg = wg >> 8, vg8 = wg8 >> 8;
         {   // sub-block 2t: weights 64t + 4i .. +3
-            const uint32_t a0 = hfma2u(hsub2u(lop3_and_or(wg, 0x000F000Fu, H2_1024), H2_1024), ga, gna);
-            const uint32_t a2 = hfma2u(hsub2u(lop3_and_or(wg >> 4, 0x000F000Fu, H2_1024), H2_1024), ga, gna);
-            const uint32_t a1 = hfma2u(hsub2u(lop3_and_or(wg8, 0x000F000Fu, H2_1024), H2_1024), ha, hna);
-            const uint32_t a3 = hfma2u(hsub2u(lop3_and_or(wg8 >> 4, 0x000F000Fu, H2_1024), H2_1024), ha, hna);
+            const uint32_t a0 = hfma2u(lop3_and_or(wg, 0x000F000Fu, H2_1024), ga, ga10);
+            const uint32_t a2 = hfma2u(lop3_and_or(wg, 0x00F000F0u, H2_64), ga, ga6);
+            const uint32_t a1 = hfma2u(lop3_and_or(wg8, 0x000F000Fu, H2_1024), ha, ha10);
+            const uint32_t a3 = hfma2u(lop3_and_or(wg8, 0x00F000F0u, H2_64), ha, ha6);
             mma_step<NT>(acc, xsc, 2 * i, lane, a0, a1, a2, a3);
         }
         {   // sub-block 2t+1: weights 64t + 32 + 4i .. +3
-            const uint32_t a0 = hfma2u(hsub2u(lop3_and_or(wg >> 8, 0x000F000Fu, H2_1024), H2_1024), gb, gnb);
-            const uint32_t a2 = hfma2u(hsub2u(lop3_and_or(wg >> 12, 0x000F000Fu, H2_1024), H2_1024), gb, gnb);
-            const uint32_t a1 = hfma2u(hsub2u(lop3_and_or(wg8 >> 8, 0x000F000Fu, H2_1024), H2_1024), hb, hnb);
-            const uint32_t a3 = hfma2u(hsub2u(lop3_and_or(wg8 >> 12, 0x000F000Fu, H2_1024), H2_1024), hb, hnb);
+            const uint32_t a0 = hfma2u(lop3_and_or(vg, 0x000F000Fu, H2_1024), gb, gb10);
+            const uint32_t a2 = hfma2u(lop3_and_or(vg, 0x00F000F0u, H2_64), gb, gb6);
+            const uint32_t a1 = hfma2u(lop3_and_or(vg8, 0x000F000Fu, H2_1024), hb, hb10);
+            const uint32_t a3 = hfma2u(lop3_and_or(vg8, 0x00F000F0u, H2_64), hb, hb6);
             mma_step<NT>(acc, xsc, 2 * i + 1, lane, a0, a1, a2, a3);
         }
     }
+    // -m * sum(x): A = (-m_2t, -m_2t+1) per row in columns (2t, 2t+1), B = the
+    // sub-block sums of x (prep kernel); columns 2t+8.. are zero.
+    const uint32_t *mf = reinterpret_cast<const uint32_t *>(xsc + 16 * NT * 32);
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) mma16816(acc[nt], gnm, hnm, 0u, 0u, mf[nt * 32 + lane], 0u);
 }
 
 // ------------------------------------------------------------------ Q6_K ---
 struct RawQ6K { uint4 q[6]; uint2 scg, scg8; uint32_t d; };
 __device__ __forceinline__ void load_raw(RawQ6K &r, const uint8_t *T, int lane) {
 #pragma unroll
-    for (int p = 0; p < 6; p++) r.q[p] = ldg_stream(T + p * 512 + lane * 16);
+    for (int p = 0; p < 6; p++) r.q[p] = lds128(T + p * 512 + lane * 16);
     const int g = lane >> 2, n = (lane & 3) >> 1;
-    r.scg = ldg64(T + 3072 + g * 16 + 8 * n);
-    r.scg8 = ldg64(T + 3072 + (g + 8) * 16 + 8 * n);
-    r.d = ldg32(T + 3328 + 4 * g);
+    r.scg = lds64(T + 3072 + g * 16 + 8 * n);
+    r.scg8 = lds64(T + 3072 + (g + 8) * 16 + 8 * n);
+    r.d = lds32(T + 3328 + 4 * g);
 }
 __device__ __forceinline__ uint32_t q6_pair(uint32_t nw, int nsh, uint32_t hw, int hsh, uint32_t sc2) {
     const uint32_t lo = lop3_and_or(nw >> nsh, 0x000F000Fu, H2_1024);
     const uint32_t hs = hsh >= 0 ? (hw >> hsh) : (hw << -hsh);
     const uint32_t hi = lop3_and_or(hs, 0x00300030u, H2_1024);
-    // (1024 + lo) - (2080 - (1024 + 16 hi)) = lo + 16 hi - 32, all exact
+    // (1024 + lo) - (2080 - (1024 + 16 hi)) = lo + 16 hi - 32; times sc: all exact
     return hmul2u(hsub2u(lo, hsub2u(H2_2080, hi)), sc2);
 }
 template <int NT>
@@ -246,22 +275,23 @@ __device__ __forceinline__ void compute(const RawQ6K &r, const uint2 *xsc, float
             mma_step<NT>(tmp, xsc, 4 * i + jj, lane, a0, a1, a2, a3);
         }
     }
-    scale_acc<NT>(acc, tmp, h2f(r.d & 0xFFFF), h2f(r.d >> 16));
+    // the superblock d is common to the 4 lane columns of a row: apply in f32
+    const float dg = h2f(r.d & 0xFFFF), dg8 = h2f(r.d >> 16);
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) {
+        acc[nt][0] = fmaf(dg, tmp[nt][0], acc[nt][0]);
+        acc[nt][1] = fmaf(dg, tmp[nt][1], acc[nt][1]);
+        acc[nt][2] = fmaf(dg8, tmp[nt][2], acc[nt][2]);
+        acc[nt][3] = fmaf(dg8, tmp[nt][3], acc[nt][3]);
+    }
 }
 
 // --------------------------------------------------------------- IQ2_XXS ---
-// The 32-block scales (db, dl) differ between the four lane columns t of one
-// MMA step, so they are applied to the f16 operand before the MMA.
-__device__ __forceinline__ uint32_t dup_h2(float v) {
-    const __half h = __float2half_rn(v);
-    const uint32_t b = __half_as_ushort(h);
-    return b | (b << 16);
-}
 struct RawIQ2 { uint4 q[2]; uint32_t d; };
 __device__ __forceinline__ void load_raw(RawIQ2 &r, const uint8_t *T, int lane) {
-    r.q[0] = ldg_stream(T + lane * 16);
-    r.q[1] = ldg_stream(T + 512 + lane * 16);
-    r.d = ldg32(T + 1024 + 4 * (lane >> 2));
+    r.q[0] = lds128(T + lane * 16);
+    r.q[1] = lds128(T + 512 + lane * 16);
+    r.d = lds32(T + 1024 + 4 * (lane >> 2));
 }
 template <int NT>
 __device__ __forceinline__ void compute(const RawIQ2 &r, const uint2 *xsc, float (&acc)[NT][4], int lane,
@@ -289,9 +319,9 @@ __device__ __forceinline__ void compute(const RawIQ2 &r, const uint2 *xsc, float
 // ----------------------------------------------------------------- IQ1_S ---
 struct RawIQ1 { uint4 qs; uint2 qh; uint32_t d; };
 __device__ __forceinline__ void load_raw(RawIQ1 &r, const uint8_t *T, int lane) {
-    r.qs = ldg_stream(T + lane * 16);
-    r.qh = ldg64(T + 512 + lane * 8);
-    r.d = ldg32(T + 768 + 4 * (lane >> 2));
+    r.qs = lds128(T + lane * 16);
+    r.qh = lds64(T + 512 + lane * 8);
+    r.d = lds32(T + 768 + 4 * (lane >> 2));
 }
 template <int NT>
 __device__ __forceinline__ void compute(const RawIQ1 &r, const uint2 *xsc, float (&acc)[NT][4], int lane,
@@ -332,6 +362,53 @@ template <int TYPE> struct TableBytes { static constexpr int v = 0; };
 template <> struct TableBytes<EF_IQ2_XXS> { static constexpr int v = 256 * 16 + 128 * 16; };
 template <> struct TableBytes<EF_IQ1_S> { static constexpr int v = 2048 * 16; };
 
+// ------------------------------------------------------------- x prep ------
+// x f32 [M][K] -> per chunk: f16 B fragments [STEPS][NT][32 lanes] (tokens >= M
+// and k >= K are zero), then for Q4_K the sub-block sums of the f16-rounded x,
+// as f16 pairs (sum of sub-block 2t, 2t+1) per (nt, lane = 4g + t).
+template <int TYPE, int NT>
+__global__ void gemv_xprep(const float *__restrict__ x, int M, int64_t K, int64_t nchunks, uint8_t *__restrict__ xf) {
+    using TR = Tr<TYPE>;
+    constexpr int QPC = TR::CHUNK / 4;
+    constexpr int FB = FragBytes<TYPE, NT>::v;
+    // let the dependent GEMV start its weight prefetch now
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    const int64_t total = nchunks * QPC * (8 * NT);
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int token = (int)(i % (8 * NT));
+        const int64_t q = i / (8 * NT);
+        const int64_t c = q / QPC;
+        const int kq = (int)(q % QPC);
+        const int64_t k = c * TR::CHUNK + 4 * kq;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (token < M && k < K) v = *reinterpret_cast<const float4 *>(x + token * K + k);
+        int t, s;
+        TR::inv(kq, t, s);
+        uint2 *dst = reinterpret_cast<uint2 *>(xf + c * FB);
+        dst[(s * NT + (token >> 3)) * 32 + 4 * (token & 7) + t] = make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
+    }
+    if (TR::MINF) {
+        const int64_t total2 = nchunks * 4 * (8 * NT);
+        for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total2;
+             i += (int64_t)gridDim.x * blockDim.x) {
+            const int token = (int)(i % (8 * NT));
+            const int t = (int)((i / (8 * NT)) % 4);
+            const int64_t c = i / (8 * NT * 4);
+            float sa = 0.f, sb = 0.f;
+            if (token < M) {
+                const int64_t k0 = c * TR::CHUNK + 64 * t;
+                for (int j = 0; j < 32; j++) {
+                    if (k0 + j < K) sa += __half2float(__float2half_rn(x[token * K + k0 + j]));
+                    if (k0 + 32 + j < K) sb += __half2float(__float2half_rn(x[token * K + k0 + 32 + j]));
+                }
+            }
+            uint32_t *mf = reinterpret_cast<uint32_t *>(xf + c * FB + TR::STEPS * NT * 256);
+            mf[(token >> 3) * 32 + 4 * (token & 7) + t] = pack_h2(sa, sb);
+        }
+    }
+}
+
 // ------------------------------------------------------------- epilogue ----
 template <int NT, bool SWIGLU>
 __device__ __forceinline__ void write_out(const float (&acc)[NT][4], const float (&acc2)[NT][4], float *y,
@@ -363,12 +440,22 @@ __device__ __forceinline__ void write_out(const float (&acc)[NT][4], const float
 }
 
 // ---------------------------------------------------------------- kernel ---
-template <int TYPE, int NT, bool SWIGLU>
-__global__ void __launch_bounds__(WARPS * 32) gemv_kernel(const GemvArgs a) {
+// Shared memory: [weight rings: WARPS x NMAT x ST tiles][x fragments of one
+// phase][codebooks][cluster partial sums].
+template <int TYPE, bool SW> struct Stages {
+    static constexpr int raw = RING_PER_WARP / ((SW ? 2 : 1) * Tr<TYPE>::TILE);
+    static constexpr int v = raw < 2 ? 2 : raw > 6 ? 6 : raw;
+};
+template <int WARPS> struct MinBlocks { static constexpr int v = WARPS == 8 ? 2 : 4; };
+
+template <int TYPE, int NT, bool SWIGLU, int WARPS>
+__global__ void __launch_bounds__(WARPS * 32, MinBlocks<WARPS>::v) gemv_kernel(const GemvArgs a) {
     using TR = Tr<TYPE>;
     using Raw = typename RawOf<TYPE>::T;
-    constexpr int QPC = TR::CHUNK / 4;          // k-quads per chunk
     constexpr int NMAT = SWIGLU ? 2 : 1;
+    constexpr int ST = Stages<TYPE, SWIGLU>::v;
+    constexpr int TILE = TR::TILE;
+    constexpr int FB = FragBytes<TYPE, NT>::v;
     extern __shared__ __align__(16) uint8_t smem[];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -381,11 +468,28 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(const GemvArgs a) {
     const int c0 = ks * a.cps;
     const int nc = (int)min((int64_t)a.cps, a.nchunks - c0);
 
-    uint2 *xs = reinterpret_cast<uint2 *>(smem);
-    const int xs_bytes = a.phase_chunks * TR::STEPS * NT * 32 * 8;
-    uint4 *grid = reinterpret_cast<uint4 *>(smem + xs_bytes);
+    constexpr int RING = WARPS * NMAT * ST * TILE;
+    uint8_t *ring = smem + warp * NMAT * ST * TILE;
+    uint8_t *xs = smem + RING;
+    const int xs_bytes = a.phase_chunks * FB;
+    uint4 *grid = reinterpret_cast<uint4 *>(smem + RING + xs_bytes);
     uint4 *sgn = grid + 256;
-    float *red = reinterpret_cast<float *>(smem + xs_bytes + TableBytes<TYPE>::v);
+    float *red = reinterpret_cast<float *>(smem + RING + xs_bytes + TableBytes<TYPE>::v);
+
+    // Weight stream: chunk cc of this warp goes to ring slot cc % ST by
+    // cp.async; one commit group per chunk (empty groups keep the count).
+    const int64_t tile0 = active ? (rg * a.nchunks + c0) * (int64_t)TILE : 0;
+    const uint8_t *Tm = a.w[m] + tile0;
+    const uint8_t *Tu = SWIGLU ? a.w_up + tile0 : nullptr;
+    auto issue = [&](int cc) {
+        if (active && cc < nc) {
+            copy_tile<TILE>(ring + (cc % ST) * TILE, Tm + (int64_t)cc * TILE, lane);
+            if (SWIGLU) copy_tile<TILE>(ring + (ST + cc % ST) * TILE, Tu + (int64_t)cc * TILE, lane);
+        }
+        cp_commit();
+    };
+#pragma unroll
+    for (int s0 = 0; s0 < ST - 1; s0++) issue(s0);
 
     // codebooks -> shared memory (f16 entries; IQ2_XXS also the sign masks:
     // 7 stored sign bits + even parity -> XOR masks on f16 pairs)
@@ -410,53 +514,36 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(const GemvArgs a) {
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[nt][j] = acc2[nt][j] = 0.f;
 
-    const uint8_t *Wm = a.w[m];
-    const uint8_t *Wu = a.w_up;
+    // x fragments are written by the prep kernel launched just before.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int p0 = 0; p0 < nc; p0 += a.phase_chunks) {
         const int pc = min(a.phase_chunks, nc - p0);
-        if (p0) __syncthreads();   // previous phase done with xs
-        // stage x[:, chunks c0+p0 .. +pc) as f16 B fragments
-        const int per_tok = pc * QPC;
-        for (int idx = threadIdx.x; idx < 8 * NT * per_tok; idx += blockDim.x) {
-            const int token = idx / per_tok, rem = idx - token * per_tok;
-            const int cc = rem / QPC, kq = rem - cc * QPC;
-            const int64_t kg = (int64_t)(c0 + p0 + cc) * TR::CHUNK + 4 * kq;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (token < a.M && kg < a.K) v = __ldg(reinterpret_cast<const float4 *>(a.x + token * a.K + kg));
-            int t, s;
-            TR::inv(kq, t, s);
-            xs[((cc * TR::STEPS + s) * NT + (token >> 3)) * 32 + 4 * (token & 7) + t] =
-                make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
-        }
+        if (p0) __syncthreads();   // every warp is done with the previous phase
+        const uint8_t *src = a.xf + (int64_t)(c0 + p0) * FB;
+        for (int i = threadIdx.x; i < pc * FB / 16; i += blockDim.x) cp_async16(xs + 16 * i, src + 16 * i);
+        cp_commit();
+        cp_wait<0>();   // the x phase (and the weight tiles issued before it)
         __syncthreads();
-        if (active && pc > 0) {
-            const int64_t tile0 = (rg * a.nchunks + c0 + p0) * (int64_t)TR::TILE;
-            const uint8_t *Tm = Wm + tile0;
-            const uint8_t *Tu = SWIGLU ? Wu + tile0 : nullptr;
-            Raw ra, rb2, ua, ub;
-            load_raw(ra, Tm, lane);
-            if (SWIGLU) load_raw(ua, Tu, lane);
-            for (int cc = 0; cc < pc; cc += 2) {
-                const bool more = cc + 1 < pc;
-                if (more) {
-                    load_raw(rb2, Tm + (cc + 1) * TR::TILE, lane);
-                    if (SWIGLU) load_raw(ub, Tu + (cc + 1) * TR::TILE, lane);
-                }
-                const uint2 *xc = xs + cc * TR::STEPS * NT * 32;
-                compute<NT>(ra, xc, acc, lane, grid, sgn);
-                if (SWIGLU) compute<NT>(ua, xc, acc2, lane, grid, sgn);
-                if (more) {
-                    if (cc + 2 < pc) {
-                        load_raw(ra, Tm + (cc + 2) * TR::TILE, lane);
-                        if (SWIGLU) load_raw(ua, Tu + (cc + 2) * TR::TILE, lane);
-                    }
-                    const uint2 *xd = xc + TR::STEPS * NT * 32;
-                    compute<NT>(rb2, xd, acc, lane, grid, sgn);
-                    if (SWIGLU) compute<NT>(ub, xd, acc2, lane, grid, sgn);
+        for (int cl = 0; cl < pc; cl++) {
+            const int cc = p0 + cl;
+            __syncwarp();          // every lane is done reading the slot refilled next
+            issue(cc + ST - 1);
+            cp_wait<ST - 1>();     // this thread's copies of chunk cc have landed
+            __syncwarp();          // ... and every other lane's
+            if (active) {
+                const uint2 *xc = reinterpret_cast<const uint2 *>(xs + cl * FB);
+                Raw r;
+                load_raw(r, ring + (cc % ST) * TILE, lane);
+                compute<NT>(r, xc, acc, lane, grid, sgn);
+                if (SWIGLU) {
+                    Raw u;
+                    load_raw(u, ring + (ST + cc % ST) * TILE, lane);
+                    compute<NT>(u, xc, acc2, lane, grid, sgn);
                 }
             }
         }
     }
+    cp_wait<0>();
 
     if (a.kslices == 1) {
         if (active) write_out<NT, SWIGLU>(acc, acc2, a.y[m], a.rows[m], a.M, rg, lane);
@@ -496,92 +583,144 @@ __global__ void __launch_bounds__(WARPS * 32) gemv_kernel(const GemvArgs a) {
 }
 
 // ------------------------------------------------------------------ host ---
-GemvPlan gemv_plan(int sm_count, int64_t rowgroups, int64_t nchunks, int M) {
-    GemvPlan p;
-    p.nt = M <= 8 ? 1 : 2;
-    p.rowblocks = (int)((rowgroups + WARPS - 1) / WARPS);
-    const int64_t target = 2LL * sm_count;
-    int64_t ks = (target + p.rowblocks - 1) / p.rowblocks;
-    if (ks > 8) ks = 8;
-    if (ks > nchunks) ks = nchunks;
-    if (ks < 1) ks = 1;
-    p.cps = (int)((nchunks + ks - 1) / ks);
-    p.kslices = (int)((nchunks + p.cps - 1) / p.cps);
-    return p;
+// Pick the CTA width (4 or 8 rowgroups) and the k-split (a cluster of at most
+// 8 CTAs) that minimise the busiest SM's work: per-SM CTAs x (warps x chunks +
+// a per-CTA start cost), given how many CTAs of that shape fit on one SM.
+GemvPlan gemv_plan(int sm_count, int64_t rowgroups, int64_t nchunks, int M, const int ctas_per_sm[2]) {
+    GemvPlan best = {};
+    double best_cost = 1e300;
+    const int widths[2] = {8, 4};
+    for (int wi = 0; wi < 2; wi++) {
+        const int W = widths[wi];
+        const int64_t rowblocks = (rowgroups + W - 1) / W;
+        for (int64_t ks = 1; ks <= 8 && ks <= nchunks; ks++) {
+            const int64_t cps = (nchunks + ks - 1) / ks;
+            const int64_t ks2 = (nchunks + cps - 1) / cps;
+            if (ks2 != ks) continue;
+            const int64_t n = rowblocks * ks2;
+            const int64_t per_sm = (n + sm_count - 1) / sm_count;
+            double cost = (double)per_sm * (W * cps + 0.75 * W);
+            // too few warps resident to cover latency
+            const int64_t resident_warps = std::min<int64_t>(per_sm, ctas_per_sm[wi]) * W;
+            if (resident_warps < 12) cost *= 1.0 + (12 - resident_warps) / 12.0;
+            if (cost < best_cost - 1e-9) {
+                best_cost = cost;
+                best.warps = W;
+                best.kslices = (int)ks2;
+                best.cps = (int)cps;
+                best.rowblocks = (int)rowblocks;
+            }
+        }
+    }
+    best.nt = M <= 8 ? 1 : 2;
+    return best;
 }
 
-template <int TYPE, int NT, bool SWIGLU>
-static int launch_t(ef_ctx *ctx, GemvArgs &a, int total_rowblocks) {
-    using TR = Tr<TYPE>;
-    const int per_chunk = TR::STEPS * NT * 32 * 8;
-    a.phase_chunks = a.cps;
-    if (a.phase_chunks * per_chunk > MAX_XS_BYTES) a.phase_chunks = MAX_XS_BYTES / per_chunk;
-    const int nmat = SWIGLU ? 2 : 1;
-    const size_t smem = (size_t)a.phase_chunks * per_chunk + TableBytes<TYPE>::v +
-                        (a.kslices > 1 ? (size_t)WARPS * nmat * NT * 32 * 16 : 0);
-    auto kern = gemv_kernel<TYPE, NT, SWIGLU>;
+template <int TYPE, int NT, bool SWIGLU, int WARPS>
+static size_t smem_bytes(int phase_chunks, int kslices) {
+    constexpr int NMAT = SWIGLU ? 2 : 1;
+    return (size_t)WARPS * NMAT * Stages<TYPE, SWIGLU>::v * Tr<TYPE>::TILE +
+           (size_t)phase_chunks * FragBytes<TYPE, NT>::v + TableBytes<TYPE>::v +
+           (kslices > 1 ? (size_t)WARPS * NMAT * NT * 32 * 16 : 0);
+}
+
+template <int TYPE, int NT, bool SWIGLU, int WARPS>
+static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int grid_y) {
+    auto kern = gemv_kernel<TYPE, NT, SWIGLU, WARPS>;
     static unsigned long long configured = 0;   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
         if (e != cudaSuccess) return check_cuda(ctx, e, "gemv smem attribute");
         configured |= 1ull << ctx->device;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.kslices, total_rowblocks, 1);
+    cfg.gridDim = dim3(a.kslices, grid_y, 1);
     cfg.blockDim = dim3(WARPS * 32, 1, 1);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = smem_bytes<TYPE, NT, SWIGLU, WARPS>(a.phase_chunks, a.kslices);
     cfg.stream = ctx->stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = a.kslices;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    na++;
+    if (a.kslices > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = a.kslices;
+        attr[na].val.clusterDim.y = 1;
+        attr[na].val.clusterDim.z = 1;
+        na++;
+    }
     cfg.attrs = attr;
-    cfg.numAttrs = a.kslices > 1 ? 1 : 0;
+    cfg.numAttrs = na;
     return check_cuda(ctx, cudaLaunchKernelEx(&cfg, kern, a), "gemv launch");
 }
 
-template <int TYPE>
-static int launch_type(ef_ctx *ctx, GemvArgs &a, int nt, bool swiglu, int total_rowblocks) {
-    if (swiglu)
-        return nt == 1 ? launch_t<TYPE, 1, true>(ctx, a, total_rowblocks)
-                       : launch_t<TYPE, 2, true>(ctx, a, total_rowblocks);
-    return nt == 1 ? launch_t<TYPE, 1, false>(ctx, a, total_rowblocks)
-                   : launch_t<TYPE, 2, false>(ctx, a, total_rowblocks);
+template <int TYPE, int NT, bool SWIGLU>
+static int launch_t(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n, const float *x) {
+    using TR = Tr<TYPE>;
+    constexpr int FB = FragBytes<TYPE, NT>::v;
+    // x fragments for all chunks -> context scratch (prep kernel)
+    const size_t xbytes = (size_t)a.nchunks * FB;
+    if (int rc = ensure_scratch(ctx, 0, xbytes)) return rc;
+    a.xf = (const uint8_t *)ctx->scratch[0];
+    {
+        const int64_t work = a.nchunks * (TR::CHUNK / 4) * 8 * NT;
+        int64_t blocks = (work + 255) / 256;
+        if (blocks > 4LL * ctx->sm_count) blocks = 4LL * ctx->sm_count;
+        gemv_xprep<TYPE, NT><<<(int)blocks, 256, 0, ctx->stream>>>(x, a.M, ws[0]->k, a.nchunks,
+                                                                   (uint8_t *)ctx->scratch[0]);
+        if (int rc = check_cuda(ctx, cudaGetLastError(), "gemv xprep launch")) return rc;
+    }
+    // how many CTAs of each width fit on one SM, then the cost model
+    const int fit8 = (int)std::min<size_t>(2, 227 * 1024 / (smem_bytes<TYPE, NT, SWIGLU, 8>(8, 2) + 1024));
+    const int fit4 = (int)std::min<size_t>(4, 227 * 1024 / (smem_bytes<TYPE, NT, SWIGLU, 4>(8, 2) + 1024));
+    const int fits[2] = {std::max(fit8, 1), std::max(fit4, 1)};
+    int64_t total_rg = 0;
+    for (int i = 0; i < n; i++) total_rg += ws[i]->rowgroups;
+    GemvPlan p = gemv_plan(ctx->sm_count, total_rg, a.nchunks, a.M, fits);
+    a.cps = p.cps;
+    a.kslices = p.kslices;
+    a.phase_chunks = std::min(a.cps, MAX_XS_BYTES / FB);
+    if (a.phase_chunks < 1) a.phase_chunks = 1;
+    int grid_y = 0;
+    for (int i = 0; i < n; i++) {
+        grid_y += (int)((ws[i]->rowgroups + p.warps - 1) / p.warps);
+        a.rb_end[i] = grid_y;
+    }
+    return p.warps == 8 ? launch_kernel<TYPE, NT, SWIGLU, 8>(ctx, a, grid_y)
+                        : launch_kernel<TYPE, NT, SWIGLU, 4>(ctx, a, grid_y);
 }
 
-int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight *w_up, const float *x,
-                int M, float *const *ys) {
+template <int TYPE>
+static int launch_type(ef_ctx *ctx, GemvArgs &a, int nt, bool swiglu, const ef_weight *const *ws, int n,
+                       const float *x) {
+    if (swiglu)
+        return nt == 1 ? launch_t<TYPE, 1, true>(ctx, a, ws, n, x) : launch_t<TYPE, 2, true>(ctx, a, ws, n, x);
+    return nt == 1 ? launch_t<TYPE, 1, false>(ctx, a, ws, n, x) : launch_t<TYPE, 2, false>(ctx, a, ws, n, x);
+}
+
+int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight *w_up, const float *x, int M,
+                float *const *ys) {
     GemvArgs a = {};
     const ef_weight *w0 = ws[0];
     a.nmat = n;
-    int64_t max_rg = 0;
-    int total_rb = 0;
     for (int i = 0; i < n; i++) {
         a.w[i] = ws[i]->dev;
         a.y[i] = ys[i];
         a.rows[i] = ws[i]->rows;
         a.rowgroups[i] = ws[i]->rowgroups;
-        total_rb += (int)((ws[i]->rowgroups + WARPS - 1) / WARPS);
-        a.rb_end[i] = total_rb;
-        if (ws[i]->rowgroups > max_rg) max_rg = ws[i]->rowgroups;
     }
     a.w_up = w_up ? w_up->dev : nullptr;
-    a.x = x;
     a.M = M;
-    a.K = w0->k;
     a.nchunks = w0->nchunks;
-    // the plan sees the total rowblocks of all sections as one matrix
-    GemvPlan p = gemv_plan(ctx->sm_count, (int64_t)total_rb * WARPS, w0->nchunks, M);
-    a.cps = p.cps;
-    a.kslices = p.kslices;
     const bool sw = w_up != nullptr;
+    const int nt = M <= 8 ? 1 : 2;
     switch (w0->type) {
-    case EF_Q8_0: return launch_type<EF_Q8_0>(ctx, a, p.nt, sw, total_rb);
-    case EF_Q4_K: return launch_type<EF_Q4_K>(ctx, a, p.nt, sw, total_rb);
-    case EF_Q6_K: return launch_type<EF_Q6_K>(ctx, a, p.nt, sw, total_rb);
-    case EF_IQ2_XXS: return launch_type<EF_IQ2_XXS>(ctx, a, p.nt, sw, total_rb);
-    case EF_IQ1_S: return launch_type<EF_IQ1_S>(ctx, a, p.nt, sw, total_rb);
+    case EF_Q8_0: return launch_type<EF_Q8_0>(ctx, a, nt, sw, ws, n, x);
+    case EF_Q4_K: return launch_type<EF_Q4_K>(ctx, a, nt, sw, ws, n, x);
+    case EF_Q6_K: return launch_type<EF_Q6_K>(ctx, a, nt, sw, ws, n, x);
+    case EF_IQ2_XXS: return launch_type<EF_IQ2_XXS>(ctx, a, nt, sw, ws, n, x);
+    case EF_IQ1_S: return launch_type<EF_IQ1_S>(ctx, a, nt, sw, ws, n, x);
     default: return set_err(ctx, EF_ERR_TYPE, "gemv: unsupported type %d", w0->type);
     }
 }

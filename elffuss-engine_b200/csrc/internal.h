@@ -31,17 +31,19 @@ struct ef_ctx {
     std::string err;
     std::vector<ef_buf *> pool;       // live ef_alloc buffers, in allocation order
     uint64_t seq = 0;
-    // Persistent device scratch owned by the context (grown on demand): the
-    // f16 copy of f32 GEMM activations.
-    void *scratch = nullptr;
-    size_t scratch_bytes = 0;
+    // Persistent device scratch owned by the context (grown on demand):
+    // slot 0 holds the GEMV's f16 activation fragments, slot 1 the GEMM's
+    // converted activations. A first call of a new, larger shape grows them
+    // (cudaMalloc), so that call must come before any stream capture.
+    void *scratch[2] = {nullptr, nullptr};
+    size_t scratch_bytes[2] = {0, 0};
 };
 
 namespace ef {
 
 int set_err(ef_ctx *ctx, int code, const char *fmt, ...);
 int check_cuda(ef_ctx *ctx, cudaError_t e, const char *what);
-int ensure_scratch(ef_ctx *ctx, size_t bytes);
+int ensure_scratch(ef_ctx *ctx, int slot, size_t bytes);
 
 // weights.cu
 int launch_repack(ef_ctx *ctx, int type, const uint8_t *dev_gguf, int64_t rows, int64_t k,
@@ -55,8 +57,9 @@ struct GemvPlan {
     int cps;        // chunks per k-slice
     int rowblocks;  // CTAs along rows (8 rowgroups = 128 rows each)
     int nt;         // 8-token tiles (1 or 2)
+    int warps;      // rowgroups (warps) per CTA
 };
-GemvPlan gemv_plan(int sm_count, int64_t rowgroups, int64_t nchunks, int M);
+GemvPlan gemv_plan(int sm_count, int64_t rowgroups, int64_t nchunks, int M, const int ctas_per_sm[2]);
 int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight *w_up,
                 const float *x, int M, float *const *ys);
 
