@@ -66,6 +66,7 @@ _SIGS = {
     "ef_gemv_sections": ([_P, _PP, _I, _P, _I, _PP], _I),
     "ef_gemm": ([_P, _P, _P, _I, _I, _P, ctypes.c_uint32], _I),
     "ef_matmul": ([_P, _P, _P, _I, _P], _I),
+    "ef_gemv_noalloc": ([_P, _P, _I, _P, _P], _I),
 }
 
 

@@ -726,3 +726,73 @@ int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight 
 }
 
 }  // namespace ef
+
+// ------------------------------------------------------ allocation-free GEMV --
+// ef_gemv_noalloc: the decode GEMV for callers that must not allocate device
+// memory. Its per-call activation fragments live in this file-scope array
+// (NOALLOC_SCRATCH_BYTES, held by every GPU that loads the library until the
+// process exits) instead of the context scratch that ef_gemv grows with
+// cudaMalloc. Host code cannot use `g_noalloc_scratch` as an address (the name
+// is a host-side shadow); the device address is looked up once per device with
+// cudaGetSymbolAddress on the first call on that device.
+namespace ef {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = (size_t)1 << 20;   // 1 MiB
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+// Bytes of activation fragments one GEMV call writes and reads (the same
+// amount launch_t sizes its scratch for).
+static size_t gemv_xfrag_bytes(int type, int64_t nchunks, int M) {
+    const bool two = M > 8;
+    size_t fb = 0;
+    switch (type) {
+    case EF_Q8_0: fb = two ? FragBytes<EF_Q8_0, 2>::v : FragBytes<EF_Q8_0, 1>::v; break;
+    case EF_Q4_K: fb = two ? FragBytes<EF_Q4_K, 2>::v : FragBytes<EF_Q4_K, 1>::v; break;
+    case EF_Q6_K: fb = two ? FragBytes<EF_Q6_K, 2>::v : FragBytes<EF_Q6_K, 1>::v; break;
+    case EF_IQ2_XXS: fb = two ? FragBytes<EF_IQ2_XXS, 2>::v : FragBytes<EF_IQ2_XXS, 1>::v; break;
+    case EF_IQ1_S: fb = two ? FragBytes<EF_IQ1_S, 2>::v : FragBytes<EF_IQ1_S, 1>::v; break;
+    default: return 0;
+    }
+    return (size_t)nchunks * fb;
+}
+
+}  // namespace ef
+
+#include <mutex>
+
+extern "C" int ef_gemv_noalloc(const ef_weight *w, const float *x, int M, float *y, void *cuda_stream) {
+    using namespace ef;
+    if (!w || !x || !y) return EF_ERR_INVALID;
+    if (M < 1) return EF_ERR_SHAPE;
+    if (M > 16) return EF_NOT_APPLICABLE;
+    if (((uintptr_t)x & 15) != 0) return EF_ERR_INVALID;
+    const size_t need = gemv_xfrag_bytes(w->type, w->nchunks, M);
+    if (need == 0) return EF_ERR_TYPE;
+    if (need > NOALLOC_SCRATCH_BYTES) return EF_ERR_RANGE;   // k too large for the static array
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return EF_ERR_CUDA;
+    // once per device: the device address of the static array
+    static std::mutex mu;
+    static void *addr[64] = {nullptr};
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!addr[dev]) {
+            void *p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return EF_ERR_CUDA;
+            addr[dev] = p;
+        }
+    }
+    // A context on the stack whose scratch slot 0 IS the static array (large
+    // enough, checked above), so the shared launch path never allocates.
+    ef_ctx tmp;
+    tmp.device = dev;
+    tmp.stream = (cudaStream_t)cuda_stream;
+    if (cudaDeviceGetAttribute(&tmp.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+        return EF_ERR_CUDA;
+    tmp.scratch[0] = addr[dev];
+    tmp.scratch_bytes[0] = NOALLOC_SCRATCH_BYTES;
+    float *ys[1] = {y};
+    const int rc = launch_gemv(&tmp, &w, 1, nullptr, x, M, ys);
+    tmp.scratch[0] = nullptr;   // not the context's to free
+    return rc;
+}

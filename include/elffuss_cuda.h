@@ -158,6 +158,28 @@ EF_API int ef_gemv_sections(ef_ctx *ctx, const ef_weight *const *ws, int n, cons
 EF_API int ef_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y,
             uint32_t flags);
 
+/* Decode GEMV that allocates nothing (no counterpart in the reference, which
+ * is single-device and allocates through its own buffer pool). ef_gemv keeps
+ * its per-call activation fragments in context scratch that it grows with
+ * cudaMalloc on the first call of a larger shape; some callers cannot allow
+ * that: code that runs while a stream is being captured into a CUDA graph
+ * (cudaFree synchronizes and is not allowed there), decode loops that cannot
+ * take the implicit device synchronization of an allocation, and hosts whose
+ * device memory is owned entirely by another allocator (a framework's caching
+ * allocator or a fixed arena). This variant uses a file-scope device array of
+ * 1 MiB instead, held by every GPU that loads the library until the process
+ * exits; it supports k up to the point where the fragments exceed 1 MiB
+ * (about 31,000 for 9-16 tokens, 63,000 for 1-8 tokens) and returns
+ * EF_ERR_RANGE beyond that. No context is needed: work is queued on
+ * `cuda_stream` (NULL = default stream) of the current device, which must be
+ * the device `w` was loaded on. The first call on a device looks up the
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture. All calls share the one array: calls that overlap on the
+ * GPU (other streams, other threads) race; each call overwrites the whole part
+ * of the array it reads, so nothing needs clearing. Same arguments, result and
+ * status codes as ef_gemv (no per-call error message). */
+EF_API int ef_gemv_noalloc(const ef_weight *w, const float *x, int M, float *y, void *cuda_stream);
+
 /* The dispatcher of quant.matmul (js/ops.js:827-1101): GEMV for tokens <= 16,
  * GEMM above, same contract and output. */
 EF_API int ef_matmul(ef_ctx *ctx, const ef_weight *w, const float *x, int tokens, float *y);
