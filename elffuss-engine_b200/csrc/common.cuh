@@ -103,15 +103,21 @@ __host__ __device__ inline void scatter_block(int type, const uint8_t *blk, int 
         T[2048 + lane * 4 + hs * 2 + 1] = blk[1];
     } break;
     case EF_Q4_K: {
-        // lane (g,t) owns qs bytes [32t, 32t+32) = sub-blocks 2t (low nibbles)
-        // and 2t+1 (high nibbles): 8 words, nibble-permuted, in parts
-        // 2hs + (i>>2). The 16-byte header (d, dmin, 12 scale bytes) is kept
-        // verbatim at 2048 + 16r.
+        // lane (g,t) owns, in each 32-byte qs group j, the bytes [4t, 4t+4)
+        // and [16+4t, 16+4t+4): their low nibbles are weights of sub-block 2j,
+        // their high nibbles of sub-block 2j+1, at the k positions of the
+        // lane's 8-bit MMA fragment. Group j of row g/g+8 is 8 bytes at part
+        // 2hs + (j>>1), offset 8*(j&1). The 16-byte header (d, dmin, 12 scale
+        // bytes) is kept verbatim at 2048 + 16r.
         for (int t = 0; t < 4; t++) {
             const int lane = 4 * g + t;
-            for (int i = 0; i < 8; i++)
-                wr32(T + (2 * hs + (i >> 2)) * 512 + lane * 16 + (i & 3) * 4,
-                     nib_fwd(rd32(blk + 16 + 32 * t + 4 * i)));
+            for (int j = 0; j < 4; j++) {
+                uint8_t *d = T + (2 * hs + (j >> 1)) * 512 + lane * 16 + (j & 1) * 8;
+                for (int b = 0; b < 4; b++) {
+                    d[b] = blk[16 + 32 * j + 4 * t + b];
+                    d[4 + b] = blk[16 + 32 * j + 16 + 4 * t + b];
+                }
+            }
         }
         for (int i = 0; i < 16; i++) T[2048 + r * 16 + i] = blk[i];
     } break;
@@ -180,9 +186,13 @@ __host__ __device__ inline void gather_block(int type, const uint8_t *T, int r, 
     case EF_Q4_K: {
         for (int t = 0; t < 4; t++) {
             const int lane = 4 * g + t;
-            for (int i = 0; i < 8; i++)
-                wr32(blk + 16 + 32 * t + 4 * i,
-                     nib_inv(rd32(T + (2 * hs + (i >> 2)) * 512 + lane * 16 + (i & 3) * 4)));
+            for (int j = 0; j < 4; j++) {
+                const uint8_t *d = T + (2 * hs + (j >> 1)) * 512 + lane * 16 + (j & 1) * 8;
+                for (int b = 0; b < 4; b++) {
+                    blk[16 + 32 * j + 4 * t + b] = d[b];
+                    blk[16 + 32 * j + 16 + 4 * t + b] = d[4 + b];
+                }
+            }
         }
         for (int i = 0; i < 16; i++) blk[i] = T[2048 + r * 16 + i];
     } break;

@@ -38,6 +38,9 @@
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
+#include <stdio.h>
+#include <stdlib.h>
+
 #include <algorithm>
 
 #include "common.cuh"
@@ -51,7 +54,6 @@ namespace ef {
 __device__ const __align__(16) uint16_t g_grid_iq2xxs_f16[EF_GRID_IQ2XXS_ENTRIES * 8] = {EF_GRID_IQ2XXS_F16_INIT};
 __device__ const __align__(16) uint16_t g_grid_iq1s_f16[EF_GRID_IQ1S_ENTRIES * 8] = {EF_GRID_IQ1S_F16_INIT};
 
-constexpr uint32_t H2_64 = 0x54005400u;     // half2(64, 64)
 constexpr uint32_t H2_1024 = 0x64006400u;   // half2(1024, 1024)
 constexpr uint32_t H2_1152 = 0x64806480u;   // half2(1152, 1152)
 constexpr uint32_t H2_2080 = 0x68106810u;   // half2(2080, 2080)
@@ -66,46 +68,52 @@ struct GemvArgs {
     int64_t rowgroups[4];
     int rb_end[4];            // cumulative rowblocks per section
     int nmat;
-    const uint8_t *xf;        // x fragments from gemv_xprep: nchunks x FB bytes
+    const uint8_t *xf;        // x data from gemv_xprep: nchunks x xb bytes (5..16 tokens)
     int M;
     int64_t nchunks;
     int cps;                  // chunks per k-slice
     int kslices;
     int phase_chunks;         // chunks of x fragments in shared memory at a time
+    int xb;                   // bytes of x data per chunk (f16_xbytes / i8_xbytes)
+    const float *x;           // f32 activations [M][K] (fused staging)
+    int64_t K;
 };
 
 // ---------------------------------------------------------------- traits ---
 // STEPS = k16 steps per chunk; inv maps a k-quad (4 consecutive weights of the
-// chunk) to the lane column t and the step s that consume it; MINF = the chunk
-// carries one extra "-m*sum(x)" fragment (Q4_K).
+// chunk) to the lane column t and the step s that consume it; I8 = the type
+// runs on the 8-bit tensor cores with 8-bit activation planes (Q4_K).
 template <int TYPE> struct Tr;
 template <> struct Tr<EF_Q8_0> {
-    static constexpr int CHUNK = 128, STEPS = 8, TILE = 2176, MINF = 0;
+    static constexpr int CHUNK = 128, STEPS = 8, TILE = 2176, I8 = 0;
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 3; s = kq & 7; }
 };
 template <> struct Tr<EF_Q4_K> {
-    static constexpr int CHUNK = 256, STEPS = 16, TILE = 2304, MINF = 1;
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 2304, I8 = 1;
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 4; s = 2 * (kq & 7) + ((kq >> 3) & 1); }
 };
 template <> struct Tr<EF_Q6_K> {
-    static constexpr int CHUNK = 256, STEPS = 16, TILE = 3360, MINF = 0;
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 3360, I8 = 0;
     __device__ static void inv(int kq, int &t, int &s) {
         t = 2 * (kq >> 5) + ((kq >> 2) & 1);
         s = 4 * ((kq >> 3) & 3) + (kq & 3);
     }
 };
 template <> struct Tr<EF_IQ2_XXS> {
-    static constexpr int CHUNK = 256, STEPS = 16, TILE = 1056, MINF = 0;
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 1056, I8 = 0;
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 4; s = kq & 15; }
 };
 template <> struct Tr<EF_IQ1_S> {
-    static constexpr int CHUNK = 256, STEPS = 16, TILE = 800, MINF = 0;
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 800, I8 = 0;
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 4; s = kq & 15; }
 };
-// bytes of x fragments per chunk: STEPS x NT x 32 lanes x 8 B (+ NT x 32 x 4 B)
-template <int TYPE, int NT> struct FragBytes {
-    static constexpr int v = Tr<TYPE>::STEPS * NT * 256 + Tr<TYPE>::MINF * NT * 128;
-};
+// bytes of f16 x fragments per chunk for M tokens: STEPS x M x 4 lanes x 8 B
+template <int TYPE> __host__ __device__ inline int f16_xbytes(int M) { return Tr<TYPE>::STEPS * M * 32; }
+// bytes of 8-bit x data per 256-weight chunk for M tokens (I8 types):
+// two int8 planes (high and residual) of B fragments, each
+// [8 sub-blocks][M tokens][4 lanes][8 B]; [M][4] f16 pairs of sub-block sums;
+// [M] f32 scales; rounded up to 16.
+__host__ __device__ inline int i8_xbytes(int M) { return (532 * M + 15) & ~15; }
 
 __device__ __forceinline__ uint32_t wsel(const uint4 &v, int i) {
     return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
@@ -128,12 +136,28 @@ __device__ __forceinline__ void copy_tile(uint8_t *dst, const uint8_t *src, int 
     for (int p = lane; p < TILE / 16; p += 32) cp_async16(dst + 16 * p, src + 16 * p);
 }
 
+// x data of one chunk for the f16 types: B fragments [step][token][lane t]
+// (8 B each), tokens 0..M-1 only; lanes whose token is >= M feed zeros.
+struct XF {
+    const uint8_t *xc;
+    int M;
+    uint32_t vmask;   // bit nt: token nt*8 + g of this lane exists
+};
 template <int NT>
-__device__ __forceinline__ void mma_step(float (&acc)[NT][4], const uint2 *xsc, int s, int lane, uint32_t a0,
+__device__ __forceinline__ XF make_xf(const uint8_t *xc, int M, int lane) {
+    uint32_t v = 0;
+#pragma unroll
+    for (int nt = 0; nt < NT; nt++) v |= (uint32_t)(nt * 8 + (lane >> 2) < M) << nt;
+    return XF{xc, M, v};
+}
+template <int NT>
+__device__ __forceinline__ void mma_step(float (&acc)[NT][4], const XF &xf, int s, int lane, uint32_t a0,
                                          uint32_t a1, uint32_t a2, uint32_t a3) {
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
-        const uint2 b = xsc[(s * NT + nt) * 32 + lane];
+        const uint2 b = (xf.vmask >> nt) & 1
+                            ? *reinterpret_cast<const uint2 *>(xf.xc + (s * xf.M + nt * 8) * 32 + lane * 8)
+                            : make_uint2(0u, 0u);
         mma16816(acc[nt], a0, a1, a2, a3, b.x, b.y);
     }
 }
@@ -152,8 +176,9 @@ __device__ __forceinline__ void load_raw(RawQ8 &r, const uint8_t *T, int lane) {
     r.sc = lds32(T + 2048 + lane * 4);
 }
 template <int NT>
-__device__ __forceinline__ void compute(const RawQ8 &r, const uint2 *xsc, float (&acc)[NT][4], int lane,
+__device__ __forceinline__ void compute(const RawQ8 &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
                                         const uint4 *, const uint4 *) {
+    const XF xsc = make_xf<NT>(xc, M, lane);
     const uint32_t dg = prmt(r.sc, 0, 0x1010), dg8 = prmt(r.sc, 0, 0x3232);
 #pragma unroll
     for (int s = 0; s < 8; s++) {
@@ -176,57 +201,93 @@ __device__ __forceinline__ void load_raw(RawQ4K &r, const uint8_t *T, int lane) 
     r.hg = lds128(T + 2048 + g * 16);
     r.hg8 = lds128(T + 2048 + (g + 8) * 16);
 }
-// Scales of lane column t (sub-blocks 2t, 2t+1) from a verbatim 16-byte Q4_K
-// header: scale_min_k4 (kernels.wgsl.js:94-104) for j = 2t, 2t+1, as f16:
-// d1 = f16(d*sc) duplicated in both halves, and (-f16(dmin*m_a), -f16(dmin*m_b)).
-__device__ __forceinline__ void q4k_scales(const uint4 &h, int t, uint32_t &d1a, uint32_t &d1b, uint32_t &nm) {
-    const uint32_t dd = prmt(h.x, 0, 0x1010), nmm = prmt(h.x, 0, 0x3232) ^ 0x80008000u;
+// 8-bit tensor-core MMA: D = A(16x32 u8, row) * B(32x8 s8, col), s32.
+__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%10,%10,%10,%10};\n"
+        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+// (-f16(dmin*m_2t), -f16(dmin*m_2t+1)) of lane column t from a verbatim 16-byte
+// Q4_K header (scale_min_k4, kernels.wgsl.js:94-104, for j = 2t, 2t+1).
+__device__ __forceinline__ uint32_t q4k_negmin(const uint4 &h, int t) {
+    const uint32_t nmm = prmt(h.x, 0, 0x3232) ^ 0x80008000u;
     const int sh = 16 * (t & 1);
     const uint32_t p0 = (h.y >> sh) & 0xFFFF, p1 = (h.z >> sh) & 0xFFFF, p2 = (h.w >> sh) & 0xFFFF;
-    const uint32_t scl = p0 & 0x3F3F, mpl = p1 & 0x3F3F;
-    const uint32_t sch = (p2 & 0x0F0F) | ((p0 >> 2) & 0x3030), mph = ((p2 >> 4) & 0x0F0F) | ((p1 >> 2) & 0x3030);
-    const uint32_t scp = t < 2 ? scl : sch, mp = t < 2 ? mpl : mph;
-    d1a = hmul2u(hsub2u(prmt(scp, 0x64646464u, 0x4040), H2_1024), dd);
-    d1b = hmul2u(hsub2u(prmt(scp, 0x64646464u, 0x4141), H2_1024), dd);
-    nm = hmul2u(hsub2u(prmt(mp, 0x64646464u, 0x4140), H2_1024), nmm);   // (m_a, m_b) * -dmin
+    const uint32_t mp = t < 2 ? (p1 & 0x3F3F) : (((p2 >> 4) & 0x0F0F) | ((p1 >> 2) & 0x3030));
+    (void)p0;
+    return hmul2u(hsub2u(prmt(mp, 0x64646464u, 0x4140), H2_1024), nmm);
 }
+// Q4_K on the 8-bit tensor cores. The prep kernel writes x per 256-weight
+// chunk and token as x = dx * (qh + ql / 256) with two int8 planes (qh =
+// round(x/dx), dx = max|x|/127; ql = round(256 * residual)), i.e. about 16
+// significant bits, finer than f16. Per 32-weight sub-block: the raw nibbles
+// are the A operand (one LOP3 per 4 weights), one m16n8k32 MMA per plane, and
+// the 6-bit sub-block scale is applied to the exact integer results; d*dx once
+// per superblock in f32; -dmin*m*sum(x) is one f16 MMA per superblock.
 template <int NT>
-__device__ __forceinline__ void compute(const RawQ4K &r, const uint2 *xsc, float (&acc)[NT][4], int lane,
+__device__ __forceinline__ void compute(const RawQ4K &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
                                         const uint4 *, const uint4 *) {
-    const int t = lane & 3;
-    uint32_t ga, gb, gnm, ha, hb, hnm;
-    q4k_scales(r.hg, t, ga, gb, gnm);
-    q4k_scales(r.hg8, t, ha, hb, hnm);
-    // (M + q) * d1 - M * d1 = q * d1 with ONE rounding (fused, -M*d1 exact):
-    // M = 1024 for a nibble at bits 0-3 of a half, M = 64 at bits 4-7.
-    const uint32_t ga10 = hmul2u(ga, 0xE400E400u), ga6 = hmul2u(ga, 0xD400D400u);   // -1024 d1, -64 d1
-    const uint32_t gb10 = hmul2u(gb, 0xE400E400u), gb6 = hmul2u(gb, 0xD400D400u);
-    const uint32_t ha10 = hmul2u(ha, 0xE400E400u), ha6 = hmul2u(ha, 0xD400D400u);
-    const uint32_t hb10 = hmul2u(hb, 0xE400E400u), hb6 = hmul2u(hb, 0xD400D400u);
+    const int g = lane >> 2, t = lane & 3;
+    // 6-bit scales of sub-blocks 0..7 of rows g and g+8, one byte each
+    const uint32_t sgl = r.hg.y & 0x3F3F3F3Fu, sgh = (r.hg.w & 0x0F0F0F0Fu) | ((r.hg.y >> 2) & 0x30303030u);
+    const uint32_t shl = r.hg8.y & 0x3F3F3F3Fu, shh = (r.hg8.w & 0x0F0F0F0Fu) | ((r.hg8.y >> 2) & 0x30303030u);
+    int si[NT][4], sl[NT][4];
+    bool tv[NT];
 #pragma unroll
-    for (int i = 0; i < 8; i++) {
-        const uint32_t wg = wsel(r.q[i >> 2], i & 3), wg8 = wsel(r.q[2 + (i >> 2)], i & 3);
-        const uint32_t vg = wg >> 8, vg8 = wg8 >> 8;
-        {   // sub-block 2t: weights 64t + 4i .. +3
-            const uint32_t a0 = hfma2u(lop3_and_or(wg, 0x000F000Fu, H2_1024), ga, ga10);
-            const uint32_t a2 = hfma2u(lop3_and_or(wg, 0x00F000F0u, H2_64), ga, ga6);
-            const uint32_t a1 = hfma2u(lop3_and_or(wg8, 0x000F000Fu, H2_1024), ha, ha10);
-            const uint32_t a3 = hfma2u(lop3_and_or(wg8, 0x00F000F0u, H2_64), ha, ha6);
-            mma_step<NT>(acc, xsc, 2 * i, lane, a0, a1, a2, a3);
-        }
-        {   // sub-block 2t+1: weights 64t + 32 + 4i .. +3
-            const uint32_t a0 = hfma2u(lop3_and_or(vg, 0x000F000Fu, H2_1024), gb, gb10);
-            const uint32_t a2 = hfma2u(lop3_and_or(vg, 0x00F000F0u, H2_64), gb, gb6);
-            const uint32_t a1 = hfma2u(lop3_and_or(vg8, 0x000F000Fu, H2_1024), hb, hb10);
-            const uint32_t a3 = hfma2u(lop3_and_or(vg8, 0x00F000F0u, H2_64), hb, hb6);
-            mma_step<NT>(acc, xsc, 2 * i + 1, lane, a0, a1, a2, a3);
+    for (int nt = 0; nt < NT; nt++) {
+        si[nt][0] = si[nt][1] = si[nt][2] = si[nt][3] = 0;
+        sl[nt][0] = sl[nt][1] = sl[nt][2] = sl[nt][3] = 0;
+        tv[nt] = nt * 8 + g < M;
+    }
+    const uint8_t *fr = xc + g * 32 + t * 8;
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        const uint4 &pg = r.q[j >> 1], &ph = r.q[2 + (j >> 1)];
+        const uint32_t g0 = (j & 1) ? pg.z : pg.x, g1 = (j & 1) ? pg.w : pg.y;
+        const uint32_t h0 = (j & 1) ? ph.z : ph.x, h1 = (j & 1) ? ph.w : ph.y;
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+            const int sub = 2 * j + hf;
+            const uint32_t a0 = (hf ? g0 >> 4 : g0) & 0x0F0F0F0Fu, a2 = (hf ? g1 >> 4 : g1) & 0x0F0F0F0Fu;
+            const uint32_t a1 = (hf ? h0 >> 4 : h0) & 0x0F0F0F0Fu, a3 = (hf ? h1 >> 4 : h1) & 0x0F0F0F0Fu;
+            const int scg = (int)(((sub < 4 ? sgl : sgh) >> (8 * (sub & 3))) & 0xFF);
+            const int sch = (int)(((sub < 4 ? shl : shh) >> (8 * (sub & 3))) & 0xFF);
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                const uint8_t *f = fr + (sub * M + nt * 8) * 32;
+                const uint2 b = tv[nt] ? *reinterpret_cast<const uint2 *>(f) : make_uint2(0u, 0u);
+                const uint2 bl = tv[nt] ? *reinterpret_cast<const uint2 *>(f + 256 * M) : make_uint2(0u, 0u);
+                int d[4], e[4];
+                imma16832(d, a0, a1, a2, a3, b.x, b.y);
+                imma16832(e, a0, a1, a2, a3, bl.x, bl.y);
+                si[nt][0] += scg * d[0];
+                si[nt][1] += scg * d[1];
+                si[nt][2] += sch * d[2];
+                si[nt][3] += sch * d[3];
+                sl[nt][0] += scg * e[0];
+                sl[nt][1] += scg * e[1];
+                sl[nt][2] += sch * e[2];
+                sl[nt][3] += sch * e[3];
+            }
         }
     }
-    // -m * sum(x): A = (-m_2t, -m_2t+1) per row in columns (2t, 2t+1), B = the
-    // sub-block sums of x (prep kernel); columns 2t+8.. are zero.
-    const uint32_t *mf = reinterpret_cast<const uint32_t *>(xsc + 16 * NT * 32);
+    const float dg = h2f(r.hg.x & 0xFFFF), dh = h2f(r.hg8.x & 0xFFFF);
+    const float *dxp = reinterpret_cast<const float *>(xc + 528 * M);
+    const uint32_t gnm = q4k_negmin(r.hg, t), hnm = q4k_negmin(r.hg8, t);
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) mma16816(acc[nt], gnm, hnm, 0u, 0u, mf[nt * 32 + lane], 0u);
+    for (int nt = 0; nt < NT; nt++) {
+        const int tk0 = nt * 8 + 2 * t, tk1 = tk0 + 1;
+        const float dx0 = tk0 < M ? dxp[tk0] : 0.f, dx1 = tk1 < M ? dxp[tk1] : 0.f;
+        acc[nt][0] = fmaf(dg * dx0, fmaf((float)sl[nt][0], 1.f / 256.f, (float)si[nt][0]), acc[nt][0]);
+        acc[nt][1] = fmaf(dg * dx1, fmaf((float)sl[nt][1], 1.f / 256.f, (float)si[nt][1]), acc[nt][1]);
+        acc[nt][2] = fmaf(dh * dx0, fmaf((float)sl[nt][2], 1.f / 256.f, (float)si[nt][2]), acc[nt][2]);
+        acc[nt][3] = fmaf(dh * dx1, fmaf((float)sl[nt][3], 1.f / 256.f, (float)si[nt][3]), acc[nt][3]);
+        const uint32_t mf = tv[nt] ? *reinterpret_cast<const uint32_t *>(xc + 512 * M + (nt * 8 + g) * 16 + t * 4) : 0u;
+        mma16816(acc[nt], gnm, hnm, 0u, 0u, mf, 0u);
+    }
 }
 
 // ------------------------------------------------------------------ Q6_K ---
@@ -247,8 +308,9 @@ __device__ __forceinline__ uint32_t q6_pair(uint32_t nw, int nsh, uint32_t hw, i
     return hmul2u(hsub2u(lo, hsub2u(H2_2080, hi)), sc2);
 }
 template <int NT>
-__device__ __forceinline__ void compute(const RawQ6K &r, const uint2 *xsc, float (&acc)[NT][4], int lane,
+__device__ __forceinline__ void compute(const RawQ6K &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
                                         const uint4 *, const uint4 *) {
+    const XF xsc = make_xf<NT>(xc, M, lane);
     const int lh = lane & 1;
     float tmp[NT][4];
 #pragma unroll
@@ -294,8 +356,9 @@ __device__ __forceinline__ void load_raw(RawIQ2 &r, const uint8_t *T, int lane) 
     r.d = lds32(T + 1024 + 4 * (lane >> 2));
 }
 template <int NT>
-__device__ __forceinline__ void compute(const RawIQ2 &r, const uint2 *xsc, float (&acc)[NT][4], int lane,
+__device__ __forceinline__ void compute(const RawIQ2 &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
                                         const uint4 *grid, const uint4 *sgn) {
+    const XF xsc = make_xf<NT>(xc, M, lane);
     const float dg = h2f(r.d & 0xFFFF), dg8 = h2f(r.d >> 16);
 #pragma unroll
     for (int u = 0; u < 2; u++) {
@@ -324,8 +387,9 @@ __device__ __forceinline__ void load_raw(RawIQ1 &r, const uint8_t *T, int lane) 
     r.d = lds32(T + 768 + 4 * (lane >> 2));
 }
 template <int NT>
-__device__ __forceinline__ void compute(const RawIQ1 &r, const uint2 *xsc, float (&acc)[NT][4], int lane,
+__device__ __forceinline__ void compute(const RawIQ1 &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
                                         const uint4 *grid, const uint4 *) {
+    const XF xsc = make_xf<NT>(xc, M, lane);
     const float dg = h2f(r.d & 0xFFFF), dg8 = h2f(r.d >> 16);
 #pragma unroll
     for (int u = 0; u < 2; u++) {
@@ -362,51 +426,104 @@ template <int TYPE> struct TableBytes { static constexpr int v = 0; };
 template <> struct TableBytes<EF_IQ2_XXS> { static constexpr int v = 256 * 16 + 128 * 16; };
 template <> struct TableBytes<EF_IQ1_S> { static constexpr int v = 2048 * 16; };
 
-// ------------------------------------------------------------- x prep ------
-// x f32 [M][K] -> per chunk: f16 B fragments [STEPS][NT][32 lanes] (tokens >= M
-// and k >= K are zero), then for Q4_K the sub-block sums of the f16-rounded x,
-// as f16 pairs (sum of sub-block 2t, 2t+1) per (nt, lane = 4g + t).
-template <int TYPE, int NT>
-__global__ void gemv_xprep(const float *__restrict__ x, int M, int64_t K, int64_t nchunks, uint8_t *__restrict__ xf) {
+// ------------------------------------------------------------- x staging ---
+// Chunks [c, c + n) of x (f32 [M][K]) are written as the activation data the
+// compute functions read, to `dst` (chunk i at dst + i * xb), by the threads
+// [tid, tid + nthreads) -- either one CTA (the fused, single-kernel path used
+// for up to 4 tokens) or the whole grid of the prep kernel (5..16 tokens).
+//
+// f16 types: per chunk, B fragments [step][token][lane t] (8 B: the pairs
+// (k, k+1), (k+2, k+3) of the k-quad that (t, step) consumes), tokens 0..M-1.
+template <int TYPE>
+__device__ __forceinline__ void stage_f16(const float *__restrict__ x, int M, int64_t K, int64_t c, int n,
+                                          uint8_t *dst, int xb, int tid, int nthreads) {
     using TR = Tr<TYPE>;
     constexpr int QPC = TR::CHUNK / 4;
-    constexpr int FB = FragBytes<TYPE, NT>::v;
-    // let the dependent GEMV start its weight prefetch now
-    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-    const int64_t total = nchunks * QPC * (8 * NT);
-    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int token = (int)(i % (8 * NT));
-        const int64_t q = i / (8 * NT);
-        const int64_t c = q / QPC;
-        const int kq = (int)(q % QPC);
-        const int64_t k = c * TR::CHUNK + 4 * kq;
+    const int per_chunk = M * QPC;
+    for (int i = tid; i < n * per_chunk; i += nthreads) {
+        const int cc = i / per_chunk, rem = i - cc * per_chunk;
+        const int token = rem / QPC, kq = rem - token * QPC;
+        const int64_t k = (c + cc) * TR::CHUNK + 4 * kq;
         float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (token < M && k < K) v = *reinterpret_cast<const float4 *>(x + token * K + k);
-        int t, s;
-        TR::inv(kq, t, s);
-        uint2 *dst = reinterpret_cast<uint2 *>(xf + c * FB);
-        dst[(s * NT + (token >> 3)) * 32 + 4 * (token & 7) + t] = make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
+        if (k < K) v = __ldg(reinterpret_cast<const float4 *>(x + token * K + k));
+        int t, st;
+        TR::inv(kq, t, st);
+        *reinterpret_cast<uint2 *>(dst + (int64_t)cc * xb + ((st * M + token) * 4 + t) * 8) =
+            make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
     }
-    if (TR::MINF) {
-        const int64_t total2 = nchunks * 4 * (8 * NT);
-        for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total2;
-             i += (int64_t)gridDim.x * blockDim.x) {
-            const int token = (int)(i % (8 * NT));
-            const int t = (int)((i / (8 * NT)) % 4);
-            const int64_t c = i / (8 * NT * 4);
-            float sa = 0.f, sb = 0.f;
-            if (token < M) {
-                const int64_t k0 = c * TR::CHUNK + 64 * t;
-                for (int j = 0; j < 32; j++) {
-                    if (k0 + j < K) sa += __half2float(__float2half_rn(x[token * K + k0 + j]));
-                    if (k0 + 32 + j < K) sb += __half2float(__float2half_rn(x[token * K + k0 + 32 + j]));
-                }
-            }
-            uint32_t *mf = reinterpret_cast<uint32_t *>(xf + c * FB + TR::STEPS * NT * 256);
-            mf[(token >> 3) * 32 + 4 * (token & 7) + t] = pack_h2(sa, sb);
+}
+// Q4_K (8-bit MMA): per 256-weight chunk and token x = dx * (qh + ql/256),
+// dx = max|x|/127, qh = rne(x/dx), ql = rne(256 * (x/dx - qh)), both int8, as
+// B fragments [plane][sub-block][token][lane t][b0 b1]; then the f16 sums of x
+// over each 32-weight sub-block as pairs (2t, 2t+1) per (token, t); then dx per
+// token. One warp per (chunk, token); lane l holds weights 8l .. 8l+7.
+__device__ __forceinline__ void stage_i8(const float *__restrict__ x, int M, int64_t K, int64_t c, int n,
+                                         uint8_t *dst, int xb, int tid, int nthreads) {
+    const int lane = tid & 31;
+    for (int w = tid >> 5; w < n * M; w += nthreads >> 5) {
+        const int cc = w / M, token = w - cc * M;
+        const int64_t k0 = (c + cc) * 256 + 8 * lane;
+        float v[8];
+        if (k0 < K) {
+            const float4 p = __ldg(reinterpret_cast<const float4 *>(x + token * K + k0));
+            const float4 q = __ldg(reinterpret_cast<const float4 *>(x + token * K + k0 + 4));
+            v[0] = p.x; v[1] = p.y; v[2] = p.z; v[3] = p.w; v[4] = q.x; v[5] = q.y; v[6] = q.z; v[7] = q.w;
+        } else {
+            for (int i = 0; i < 8; i++) v[i] = 0.f;
         }
+        float amax = 0.f, sum = 0.f;
+        for (int i = 0; i < 8; i++) {
+            amax = fmaxf(amax, fabsf(v[i]));
+            sum += v[i];
+        }
+        for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        const float dx = amax / 127.f, inv = amax > 0.f ? 127.f / amax : 0.f;
+        uint32_t wq[2], wl[2];
+        for (int h = 0; h < 2; h++) {
+            uint32_t word = 0, wlo = 0;
+            for (int i = 0; i < 4; i++) {
+                const float u = v[4 * h + i] * inv;
+                const float qh = fminf(fmaxf(rintf(u), -127.f), 127.f);
+                const int ql = (int)fminf(fmaxf(rintf((u - qh) * 256.f), -127.f), 127.f);
+                word |= (uint32_t)((int)qh & 0xFF) << (8 * i);
+                wlo |= (uint32_t)(ql & 0xFF) << (8 * i);
+            }
+            wq[h] = word;
+            wl[h] = wlo;
+        }
+        uint8_t *base = dst + (int64_t)cc * xb;
+        const int sub = lane >> 2, kk = 8 * (lane & 3);                  // k within the sub-block
+        const int tA = (kk & 15) >> 2, off = kk >= 16 ? 4 : 0;          // fragment lane and half
+        uint8_t *fr = base + (sub * M + token) * 32;
+        *reinterpret_cast<uint32_t *>(fr + tA * 8 + off) = wq[0];
+        *reinterpret_cast<uint32_t *>(fr + (tA + 1) * 8 + off) = wq[1];
+        *reinterpret_cast<uint32_t *>(fr + 256 * M + tA * 8 + off) = wl[0];
+        *reinterpret_cast<uint32_t *>(fr + 256 * M + (tA + 1) * 8 + off) = wl[1];
+        if ((lane & 3) == 0)
+            *reinterpret_cast<__half *>(base + 512 * M + token * 16 + (sub >> 1) * 4 + (sub & 1) * 2) =
+                __float2half_rn(sum);
+        if (lane == 0) *reinterpret_cast<float *>(base + 528 * M + token * 4) = dx;
     }
+}
+template <int TYPE>
+__device__ __forceinline__ void stage_x(const float *x, int M, int64_t K, int64_t c, int n, uint8_t *dst, int xb,
+                                        int tid, int nthreads) {
+    if (Tr<TYPE>::I8) stage_i8(x, M, K, c, n, dst, xb, tid, nthreads);
+    else stage_f16<TYPE>(x, M, K, c, n, dst, xb, tid, nthreads);
+}
+
+// Prep kernel (5..16 tokens): all chunks into global scratch. Launched with
+// programmatic dependent launch: it lets the GEMV that follows start (and
+// prefetch weights) at once, and waits for the kernel before it (which may
+// have produced x, or still read the scratch) before touching memory.
+template <int TYPE>
+__global__ void gemv_xprep(const float *__restrict__ x, int M, int64_t K, int64_t nchunks, int xb,
+                           uint8_t *__restrict__ xf) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    stage_x<TYPE>(x, M, K, 0, (int)nchunks, xf, xb, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
 }
 
 // ------------------------------------------------------------- epilogue ----
@@ -448,14 +565,16 @@ template <int TYPE, bool SW> struct Stages {
 };
 template <int WARPS> struct MinBlocks { static constexpr int v = WARPS == 8 ? 2 : 4; };
 
-template <int TYPE, int NT, bool SWIGLU, int WARPS>
+// FUSED: the CTA stages its own x slice from f32 x (up to 4 tokens: one
+// kernel per call); otherwise it copies the slice the prep kernel wrote.
+template <int TYPE, int NT, bool SWIGLU, int WARPS, bool FUSED>
 __global__ void __launch_bounds__(WARPS * 32, MinBlocks<WARPS>::v) gemv_kernel(const GemvArgs a) {
     using TR = Tr<TYPE>;
     using Raw = typename RawOf<TYPE>::T;
     constexpr int NMAT = SWIGLU ? 2 : 1;
     constexpr int ST = Stages<TYPE, SWIGLU>::v;
     constexpr int TILE = TR::TILE;
-    constexpr int FB = FragBytes<TYPE, NT>::v;
+    const int FB = a.xb;
     extern __shared__ __align__(16) uint8_t smem[];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -514,15 +633,20 @@ __global__ void __launch_bounds__(WARPS * 32, MinBlocks<WARPS>::v) gemv_kernel(c
 #pragma unroll
         for (int j = 0; j < 4; j++) acc[nt][j] = acc2[nt][j] = 0.f;
 
-    // x fragments are written by the prep kernel launched just before.
+    // x is produced by the kernel before this one (the prep kernel, or the
+    // caller's previous kernel): wait for it only now, after the weight prefetch.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     for (int p0 = 0; p0 < nc; p0 += a.phase_chunks) {
         const int pc = min(a.phase_chunks, nc - p0);
         if (p0) __syncthreads();   // every warp is done with the previous phase
-        const uint8_t *src = a.xf + (int64_t)(c0 + p0) * FB;
-        for (int i = threadIdx.x; i < pc * FB / 16; i += blockDim.x) cp_async16(xs + 16 * i, src + 16 * i);
-        cp_commit();
-        cp_wait<0>();   // the x phase (and the weight tiles issued before it)
+        if (FUSED) {
+            stage_x<TYPE>(a.x, a.M, a.K, c0 + p0, pc, xs, FB, threadIdx.x, blockDim.x);
+        } else {
+            const uint8_t *src = a.xf + (int64_t)(c0 + p0) * FB;
+            for (int i = threadIdx.x; i < pc * FB / 16; i += blockDim.x) cp_async16(xs + 16 * i, src + 16 * i);
+            cp_commit();
+            cp_wait<0>();   // the x phase (and the weight tiles issued before it)
+        }
         __syncthreads();
         for (int cl = 0; cl < pc; cl++) {
             const int cc = p0 + cl;
@@ -531,19 +655,24 @@ __global__ void __launch_bounds__(WARPS * 32, MinBlocks<WARPS>::v) gemv_kernel(c
             cp_wait<ST - 1>();     // this thread's copies of chunk cc have landed
             __syncwarp();          // ... and every other lane's
             if (active) {
-                const uint2 *xc = reinterpret_cast<const uint2 *>(xs + cl * FB);
+                const uint8_t *xc = xs + cl * FB;
                 Raw r;
                 load_raw(r, ring + (cc % ST) * TILE, lane);
-                compute<NT>(r, xc, acc, lane, grid, sgn);
+                compute<NT>(r, xc, a.M, acc, lane, grid, sgn);
                 if (SWIGLU) {
                     Raw u;
                     load_raw(u, ring + (ST + cc % ST) * TILE, lane);
-                    compute<NT>(u, xc, acc2, lane, grid, sgn);
+                    compute<NT>(u, xc, a.M, acc2, lane, grid, sgn);
                 }
             }
         }
     }
     cp_wait<0>();
+    // The weight stream is done: the next kernel in the stream may launch now
+    // (programmatic dependent launch) and prefetch its weights while this one
+    // reduces and writes y. Triggering earlier lets waiting CTAs of the next
+    // kernel hold SM resources that this kernel still needs.
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
     if (a.kslices == 1) {
         if (active) write_out<NT, SWIGLU>(acc, acc2, a.y[m], a.rows[m], a.M, rg, lane);
@@ -583,50 +712,50 @@ __global__ void __launch_bounds__(WARPS * 32, MinBlocks<WARPS>::v) gemv_kernel(c
 }
 
 // ------------------------------------------------------------------ host ---
-// Pick the CTA width (4 or 8 rowgroups) and the k-split (a cluster of at most
-// 8 CTAs) that minimise the busiest SM's work: per-SM CTAs x (warps x chunks +
-// a per-CTA start cost), given how many CTAs of that shape fit on one SM.
+// Pick the CTA shape. Measured on B200 (sweeps over width x k-split for the
+// benchmark shapes): long-lived warps that stream many tiles beat short CTAs
+// even when some SMs stay idle, because every CTA pays a pipeline start, an
+// activation staging and a cluster reduction. So: 8 rowgroups per CTA and the
+// smallest k-split that puts at least 3/4 of the SMs to work (4 rowgroups
+// when the rows are too few even for that).
 GemvPlan gemv_plan(int sm_count, int64_t rowgroups, int64_t nchunks, int M, const int ctas_per_sm[2]) {
+    (void)ctas_per_sm;
     GemvPlan best = {};
-    double best_cost = 1e300;
-    const int widths[2] = {8, 4};
-    for (int wi = 0; wi < 2; wi++) {
-        const int W = widths[wi];
-        const int64_t rowblocks = (rowgroups + W - 1) / W;
-        for (int64_t ks = 1; ks <= 8 && ks <= nchunks; ks++) {
-            const int64_t cps = (nchunks + ks - 1) / ks;
-            const int64_t ks2 = (nchunks + cps - 1) / cps;
-            if (ks2 != ks) continue;
-            const int64_t n = rowblocks * ks2;
-            const int64_t per_sm = (n + sm_count - 1) / sm_count;
-            double cost = (double)per_sm * (W * cps + 0.75 * W);
-            // too few warps resident to cover latency
-            const int64_t resident_warps = std::min<int64_t>(per_sm, ctas_per_sm[wi]) * W;
-            if (resident_warps < 12) cost *= 1.0 + (12 - resident_warps) / 12.0;
-            if (cost < best_cost - 1e-9) {
-                best_cost = cost;
-                best.warps = W;
-                best.kslices = (int)ks2;
-                best.cps = (int)cps;
-                best.rowblocks = (int)rowblocks;
-            }
-        }
+    const int64_t want = (3LL * sm_count + 3) / 4;
+    best.warps = 8;
+    int64_t rowblocks = (rowgroups + 7) / 8;
+    if (rowblocks * std::min<int64_t>(8, nchunks) < want) {
+        best.warps = 4;
+        rowblocks = (rowgroups + 3) / 4;
     }
+    int64_t ks = 1;
+    while (ks < 8 && ks < nchunks && rowblocks * ks < want) ks++;
+    best.cps = (int)((nchunks + ks - 1) / ks);
+    best.kslices = (int)((nchunks + best.cps - 1) / best.cps);
+    best.rowblocks = (int)rowblocks;
     best.nt = M <= 8 ? 1 : 2;
     return best;
 }
 
-template <int TYPE, int NT, bool SWIGLU, int WARPS>
-static size_t smem_bytes(int phase_chunks, int kslices) {
-    constexpr int NMAT = SWIGLU ? 2 : 1;
-    return (size_t)WARPS * NMAT * Stages<TYPE, SWIGLU>::v * Tr<TYPE>::TILE +
-           (size_t)phase_chunks * FragBytes<TYPE, NT>::v + TableBytes<TYPE>::v +
-           (kslices > 1 ? (size_t)WARPS * NMAT * NT * 32 * 16 : 0);
+// Programmatic dependent launch between consecutive kernels: off by default
+// (measured on B200 over the mixed-shape benchmark sequence: the early-
+// launched CTAs of the next GEMV hold shared memory and registers that the
+// current one still needs, a net loss); EF_GEMV_PDL=1 turns it on.
+static bool gemv_pdl() {
+    const char *v = getenv("EF_GEMV_PDL");
+    return v && v[0] == '1';
 }
 
 template <int TYPE, int NT, bool SWIGLU, int WARPS>
+static size_t smem_bytes(int phase_chunks, int xb, int kslices) {
+    constexpr int NMAT = SWIGLU ? 2 : 1;
+    return (size_t)WARPS * NMAT * Stages<TYPE, SWIGLU>::v * Tr<TYPE>::TILE + (size_t)phase_chunks * xb +
+           TableBytes<TYPE>::v + (kslices > 1 ? (size_t)WARPS * NMAT * NT * 32 * 16 : 0);
+}
+
+template <int TYPE, int NT, bool SWIGLU, int WARPS, bool FUSED>
 static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int grid_y) {
-    auto kern = gemv_kernel<TYPE, NT, SWIGLU, WARPS>;
+    auto kern = gemv_kernel<TYPE, NT, SWIGLU, WARPS, FUSED>;
     static unsigned long long configured = 0;   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
@@ -636,13 +765,15 @@ static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int grid_y) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.kslices, grid_y, 1);
     cfg.blockDim = dim3(WARPS * 32, 1, 1);
-    cfg.dynamicSmemBytes = smem_bytes<TYPE, NT, SWIGLU, WARPS>(a.phase_chunks, a.kslices);
+    cfg.dynamicSmemBytes = smem_bytes<TYPE, NT, SWIGLU, WARPS>(a.phase_chunks, a.xb, a.kslices);
     cfg.stream = ctx->stream;
     cudaLaunchAttribute attr[2];
     int na = 0;
-    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[na].val.programmaticStreamSerializationAllowed = 1;
-    na++;
+    if (gemv_pdl()) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
     if (a.kslices > 1) {
         attr[na].id = cudaLaunchAttributeClusterDimension;
         attr[na].val.clusterDim.x = a.kslices;
@@ -655,40 +786,75 @@ static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int grid_y) {
     return check_cuda(ctx, cudaLaunchKernelEx(&cfg, kern, a), "gemv launch");
 }
 
+// Up to this many tokens each CTA stages its own x slice (one kernel per
+// call); above it a prep kernel writes the slices once into context scratch.
+constexpr int FUSED_MAX_TOKENS = 2;
+
+template <int TYPE> static int x_bytes_per_chunk(int M) {
+    return Tr<TYPE>::I8 ? i8_xbytes(M) : f16_xbytes<TYPE>(M);
+}
+
 template <int TYPE, int NT, bool SWIGLU>
 static int launch_t(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n, const float *x) {
-    using TR = Tr<TYPE>;
-    constexpr int FB = FragBytes<TYPE, NT>::v;
-    // x fragments for all chunks -> context scratch (prep kernel)
-    const size_t xbytes = (size_t)a.nchunks * FB;
-    if (int rc = ensure_scratch(ctx, 0, xbytes)) return rc;
-    a.xf = (const uint8_t *)ctx->scratch[0];
-    {
-        const int64_t work = a.nchunks * (TR::CHUNK / 4) * 8 * NT;
+    a.xb = x_bytes_per_chunk<TYPE>(a.M);
+    a.x = x;
+    a.K = ws[0]->k;
+    const bool fused = NT == 1 && a.M <= FUSED_MAX_TOKENS;
+    if (!fused) {
+        // x data for all chunks -> context scratch slot 0 (prep kernel, PDL)
+        const size_t xbytes = (size_t)a.nchunks * a.xb;
+        if (int rc = ensure_scratch(ctx, 0, xbytes)) return rc;
+        a.xf = (const uint8_t *)ctx->scratch[0];
+        const int64_t work = Tr<TYPE>::I8 ? a.nchunks * a.M * 32 : a.nchunks * a.M * (Tr<TYPE>::CHUNK / 4);
         int64_t blocks = (work + 255) / 256;
-        if (blocks > 4LL * ctx->sm_count) blocks = 4LL * ctx->sm_count;
-        gemv_xprep<TYPE, NT><<<(int)blocks, 256, 0, ctx->stream>>>(x, a.M, ws[0]->k, a.nchunks,
-                                                                   (uint8_t *)ctx->scratch[0]);
-        if (int rc = check_cuda(ctx, cudaGetLastError(), "gemv xprep launch")) return rc;
+        if (blocks > 2LL * ctx->sm_count) blocks = 2LL * ctx->sm_count;
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((unsigned)blocks, 1, 1);
+        cfg.blockDim = dim3(256, 1, 1);
+        cfg.stream = ctx->stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = gemv_pdl() ? 1 : 0;
+        if (int rc = check_cuda(ctx, cudaLaunchKernelEx(&cfg, gemv_xprep<TYPE>, x, a.M, a.K, a.nchunks, a.xb,
+                                                        (uint8_t *)ctx->scratch[0]), "gemv xprep launch"))
+            return rc;
+    } else {
+        a.xf = nullptr;
     }
     // how many CTAs of each width fit on one SM, then the cost model
-    const int fit8 = (int)std::min<size_t>(2, 227 * 1024 / (smem_bytes<TYPE, NT, SWIGLU, 8>(8, 2) + 1024));
-    const int fit4 = (int)std::min<size_t>(4, 227 * 1024 / (smem_bytes<TYPE, NT, SWIGLU, 4>(8, 2) + 1024));
+    const int ph = std::max(1, std::min(8, MAX_XS_BYTES / a.xb));
+    const int fit8 = (int)std::min<size_t>(2, 227 * 1024 / (smem_bytes<TYPE, NT, SWIGLU, 8>(ph, a.xb, 2) + 1024));
+    const int fit4 = (int)std::min<size_t>(4, 227 * 1024 / (smem_bytes<TYPE, NT, SWIGLU, 4>(ph, a.xb, 2) + 1024));
     const int fits[2] = {std::max(fit8, 1), std::max(fit4, 1)};
     int64_t total_rg = 0;
     for (int i = 0; i < n; i++) total_rg += ws[i]->rowgroups;
     GemvPlan p = gemv_plan(ctx->sm_count, total_rg, a.nchunks, a.M, fits);
+    // Tuning override for sweeps: EF_GEMV_PLAN="W:ks" (W = 4 or 8 rowgroups per
+    // CTA, ks = k-slices, 1..8); ignored when it does not fit the shape.
+    if (const char *ov = getenv("EF_GEMV_PLAN")) {
+        int W = 0, ks = 0;
+        if (sscanf(ov, "%d:%d", &W, &ks) == 2 && (W == 4 || W == 8) && ks >= 1 && ks <= 8 && ks <= a.nchunks) {
+            p.warps = W;
+            p.cps = (int)((a.nchunks + ks - 1) / ks);
+            p.kslices = (int)((a.nchunks + p.cps - 1) / p.cps);
+        }
+    }
     a.cps = p.cps;
     a.kslices = p.kslices;
-    a.phase_chunks = std::min(a.cps, MAX_XS_BYTES / FB);
+    a.phase_chunks = std::min(a.cps, MAX_XS_BYTES / a.xb);
     if (a.phase_chunks < 1) a.phase_chunks = 1;
     int grid_y = 0;
     for (int i = 0; i < n; i++) {
         grid_y += (int)((ws[i]->rowgroups + p.warps - 1) / p.warps);
         a.rb_end[i] = grid_y;
     }
-    return p.warps == 8 ? launch_kernel<TYPE, NT, SWIGLU, 8>(ctx, a, grid_y)
-                        : launch_kernel<TYPE, NT, SWIGLU, 4>(ctx, a, grid_y);
+    if (fused)
+        return p.warps == 8 ? launch_kernel<TYPE, NT, SWIGLU, 8, true>(ctx, a, grid_y)
+                            : launch_kernel<TYPE, NT, SWIGLU, 4, true>(ctx, a, grid_y);
+    return p.warps == 8 ? launch_kernel<TYPE, NT, SWIGLU, 8, false>(ctx, a, grid_y)
+                        : launch_kernel<TYPE, NT, SWIGLU, 4, false>(ctx, a, grid_y);
 }
 
 template <int TYPE>
@@ -740,20 +906,20 @@ namespace ef {
 constexpr size_t NOALLOC_SCRATCH_BYTES = (size_t)1 << 20;   // 1 MiB
 static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
 
-// Bytes of activation fragments one GEMV call writes and reads (the same
-// amount launch_t sizes its scratch for).
+// Bytes of activation data one GEMV call keeps in scratch (the same amount
+// launch_t sizes its scratch for; calls of up to FUSED_MAX_TOKENS tokens keep
+// it in shared memory and need none).
 static size_t gemv_xfrag_bytes(int type, int64_t nchunks, int M) {
-    const bool two = M > 8;
     size_t fb = 0;
     switch (type) {
-    case EF_Q8_0: fb = two ? FragBytes<EF_Q8_0, 2>::v : FragBytes<EF_Q8_0, 1>::v; break;
-    case EF_Q4_K: fb = two ? FragBytes<EF_Q4_K, 2>::v : FragBytes<EF_Q4_K, 1>::v; break;
-    case EF_Q6_K: fb = two ? FragBytes<EF_Q6_K, 2>::v : FragBytes<EF_Q6_K, 1>::v; break;
-    case EF_IQ2_XXS: fb = two ? FragBytes<EF_IQ2_XXS, 2>::v : FragBytes<EF_IQ2_XXS, 1>::v; break;
-    case EF_IQ1_S: fb = two ? FragBytes<EF_IQ1_S, 2>::v : FragBytes<EF_IQ1_S, 1>::v; break;
+    case EF_Q8_0: fb = (size_t)f16_xbytes<EF_Q8_0>(M); break;
+    case EF_Q4_K: fb = (size_t)i8_xbytes(M); break;
+    case EF_Q6_K: fb = (size_t)f16_xbytes<EF_Q6_K>(M); break;
+    case EF_IQ2_XXS: fb = (size_t)f16_xbytes<EF_IQ2_XXS>(M); break;
+    case EF_IQ1_S: fb = (size_t)f16_xbytes<EF_IQ1_S>(M); break;
     default: return 0;
     }
-    return (size_t)nchunks * fb;
+    return M <= FUSED_MAX_TOKENS ? 1 : (size_t)nchunks * fb;
 }
 
 }  // namespace ef

@@ -168,9 +168,9 @@ EF_API int ef_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, i
  * device memory is owned entirely by another allocator (a framework's caching
  * allocator or a fixed arena). This variant uses a file-scope device array of
  * 1 MiB instead, held by every GPU that loads the library until the process
- * exits; it supports k up to the point where the fragments exceed 1 MiB
- * (about 31,000 for 9-16 tokens, 63,000 for 1-8 tokens) and returns
- * EF_ERR_RANGE beyond that. No context is needed: work is queued on
+ * exits; it supports k up to the point where the activation data exceeds
+ * 1 MiB (k up to about 31,000 for 9-16 tokens and 63,000 for 1-8 tokens)
+ * and returns EF_ERR_RANGE beyond that. No context is needed: work is queued on
  * `cuda_stream` (NULL = default stream) of the current device, which must be
  * the device `w` was loaded on. The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before

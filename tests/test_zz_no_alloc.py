@@ -49,9 +49,9 @@ def test_noalloc_matches_gemv_on_two_calls(ops):
 
 
 def test_noalloc_refuses_k_beyond_its_array(ops):
-    rows, k = 16, 256 * 160          # 16 tokens need ~33 B per k: 40960 k > 1 MiB of fragments
-    raw = formats.synth("Q4_K", rows, k, seed=1)
-    w = ops.load_weight("Q4_K", raw, rows, k)
+    rows, k = 16, 256 * 160          # Q6_K, 16 tokens: 32 B per k -> 40960 k > 1 MiB of fragments
+    raw = formats.synth("Q6_K", rows, k, seed=1)
+    w = ops.load_weight("Q6_K", raw, rows, k)
     x = torch.randn(16, k, device="cuda")
     y = torch.empty(16, rows, device="cuda")
     assert _noalloc(w, x, 16, y) == EF_ERR_RANGE
