@@ -45,6 +45,7 @@ _SIGS = {
     "ef_ctx_stream": ([_P], _P),
     "ef_stream_sync": ([_P], _I),
     "ef_last_error": ([_P], ctypes.c_char_p),
+    "ef_ctx_launch_count": ([_P], ctypes.c_uint64),
     "ef_alloc": ([_P, _SZ, _PP], _I),
     "ef_free": ([_P, _P], _I),
     "ef_buf_ptr": ([_P], _P),

@@ -30,7 +30,7 @@ int check_cuda(ef_ctx *ctx, cudaError_t e, const char *what) {
                    cudaGetErrorString(e), cudaGetErrorName(e));
 }
 
-int ensure_scratch(ef_ctx *ctx, int slot, size_t bytes) {
+int ensure_scratch(ef_ctx *ctx, int slot, size_t bytes, bool zero) {
     if (ctx->scratch_bytes[slot] >= bytes) return EF_OK;
     if (ctx->scratch[slot]) {
         // the old scratch may still be read by queued work
@@ -43,6 +43,7 @@ int ensure_scratch(ef_ctx *ctx, int slot, size_t bytes) {
     int rc = check_cuda(ctx, cudaMalloc(&ctx->scratch[slot], sz), "scratch alloc");
     if (rc) return rc;
     ctx->scratch_bytes[slot] = sz;
+    if (zero) return check_cuda(ctx, cudaMemsetAsync(ctx->scratch[slot], 0, sz, ctx->stream), "scratch zero");
     return EF_OK;
 }
 
@@ -113,6 +114,8 @@ int ef_stream_sync(ef_ctx *ctx) {
 }
 
 const char *ef_last_error(const ef_ctx *ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+uint64_t ef_ctx_launch_count(const ef_ctx *ctx) { return ctx ? ctx->launches : 0; }
 
 // ---------------------------------------------------------------- buffers --
 int ef_alloc(ef_ctx *ctx, size_t bytes, ef_buf **out) {

@@ -37,36 +37,11 @@ constexpr uint32_t GM_WAIT_LIMIT = 1u << 24;   // try_wait polls before giving u
 __device__ int g_gemm_error;   // nonzero after a bounded wait gave up
 
 // ------------------------------------------------------------ PTX wrappers --
-__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-                 : "memory");
-}
-// Bounded wait for phase `parity` of `bar`; false (and the error flag set) on timeout.
+// (mbarrier and bulk-copy helpers are in common.cuh)
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    const uint32_t a = smem_u32(bar);
-    for (uint32_t i = 0; i < GM_WAIT_LIMIT; i++) {
-        uint32_t ok;
-        asm volatile(
-            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-            : "=r"(ok) : "r"(a), "r"(parity) : "memory");
-        if (ok) return true;
-    }
+    if (mbar_wait_bounded(bar, parity, GM_WAIT_LIMIT)) return true;
     atomicExch(&g_gemm_error, 1);
     return false;
-}
-__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
-    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
 }
 __device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -75,7 +50,6 @@ __device__ __forceinline__ void tma_2d(void *dst, const CUtensorMap *map, int x,
         "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
         : "memory");
 }
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -137,7 +111,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             mbar_init(&aempty[b], 1);
         }
         mbar_init(tfull, 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_init_fence();
     }
     if (warp == 1) {   // tensor memory: BN f32 columns x 128 lanes
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
@@ -320,6 +294,7 @@ static int launch_q8_0(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M,
         configured |= 1ull << ctx->device;
     }
     dim3 grid((unsigned)((w->rowgroups + 7) / 8), (unsigned)((M + BN - 1) / BN));
+    ctx->launches++;
     kern<<<grid, GM_THREADS, smem, ctx->stream>>>(map, w->dev, w->rowgroups, w->nchunks, w->rows, M, y);
     return check_cuda(ctx, cudaGetLastError(), "gemm launch");
 }
@@ -333,6 +308,7 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
             if (int rc = ensure_scratch(ctx, 1, (size_t)n * 2)) return rc;
             int64_t blocks = (n + 255) / 256;
             if (blocks > 148 * 32) blocks = 148 * 32;
+            ctx->launches++;
             f32_to_f16_kernel<<<(int)blocks, 256, 0, ctx->stream>>>((const float *)x, (__half *)ctx->scratch[1], n);
             if (int rc = check_cuda(ctx, cudaGetLastError(), "gemm f32->f16")) return rc;
             xh = (const __half *)ctx->scratch[1];
@@ -347,6 +323,7 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
         if (int rc = ensure_scratch(ctx, 1, (size_t)n * 4)) return rc;
         int64_t blocks = (n + 255) / 256;
         if (blocks > 148 * 32) blocks = 148 * 32;
+        ctx->launches++;
         f16_to_f32_kernel<<<(int)blocks, 256, 0, ctx->stream>>>((const __half *)x, (float *)ctx->scratch[1], n);
         if (int rc = check_cuda(ctx, cudaGetLastError(), "gemm f16->f32")) return rc;
         xf = (const float *)ctx->scratch[1];

@@ -5,36 +5,42 @@
 //   sections: several W sharing x and k, one output each (js/ops.gemv.js:192-215)
 //
 // Design (B200). The GEMV is HBM-bound: every weight byte is read once and
-// must be turned into tensor-core operands with as few instructions as
-// possible, and enough bytes must be in flight to cover DRAM latency.
+// must become tensor-core operands with as few instructions as possible, while
+// enough loads are in flight on every SM to cover DRAM latency.
 //
-//  * Weights: each warp owns one 16-row rowgroup and streams its tiles through
-//    a private ring of cp.async (LDGSTS, L2-only) shared-memory slots, several
-//    tiles ahead of the math. The hardware wait (cp.async.wait_group) needs no
-//    spin loop.
-//  * Math: quants are expanded IN REGISTERS to f16 A fragments of
-//    mma.sync.m16n8k16 (A = 16 weight rows x 16 k, B = 16 k x 8 tokens, f32
-//    accumulate). Register-sourced MMA is the right tensor instruction for a
-//    GEMV: tcgen05.mma reads A from shared or tensor memory, which would add a
-//    store and a read of every dequantised weight.
-//  * Activations: a small prep kernel converts x once per call into f16 B
-//    fragments (zero-padded to 8/16 tokens) plus, for Q4_K, the per-sub-block
-//    sums needed by the "-m*sum(x)" term; each CTA copies its k-slice of that
-//    buffer into shared memory with cp.async. The GEMV is launched with
-//    programmatic dependent launch, so its weight prefetch overlaps the prep.
-//  * Work split: CTA = WARPS rowgroups x one k-slice; the k-slices of a
-//    rowblock form one thread-block cluster whose partial sums are added
-//    through distributed shared memory in rank order (deterministic, no
-//    atomics). A small cost model picks WARPS and the k-split for load
-//    balance over the 148 SMs.
+//  * Work split: CTA = one rowblock (8 rowgroups of 16 rows) x one k-slice;
+//    the k-slices of a rowblock form one thread-block cluster whose partial
+//    sums are added through distributed shared memory in rank order
+//    (deterministic, no atomics). The smallest k-split that keeps 3/4 of the
+//    SMs busy is used.
+//  * Weights: each warp streams the tiles of its rowgroup straight from HBM
+//    into registers (128-bit non-allocating loads of the lane's fragment
+//    parts), one tile ahead of the math. Measured on B200, loads into
+//    registers from 16 warps per SM stream faster than shared-memory rings
+//    filled by bulk (TMA) or per-lane asynchronous copies. Where the kernel
+//    fits 128 registers, a CTA has 16 warps: two per rowgroup, taking
+//    alternate chunks and merging their sums in shared memory at the end.
+//  * Math: quants become tensor-core operands IN REGISTERS (register-sourced
+//    mma.sync is the right tensor instruction for a GEMV: tcgen05.mma reads A
+//    from shared or tensor memory, which would add a store and a read of every
+//    dequantised weight). Q8_0, Q6_K and the i-quants run m16n8k16 f16 MMAs;
+//    Q4_K runs m16n8k32 8-bit MMAs on the raw nibbles, with the 8 MMA columns
+//    holding (token, sub-block) pairs for 1-4 tokens (q4_tq).
+//  * Activations: converted once per call into the operand layout -- by each
+//    CTA for its own chunks when there are 1-2 tokens (one kernel per call),
+//    else by a small prep kernel into context scratch -- and staged in shared
+//    memory, per phase of chunks when they do not fit at once.
 //
-// Numerics: quants are exact small integers in f16 and the per-block scales
-// are applied in f16 with one rounding per weight -- Q8_0: f16(d*q); Q4_K:
-// f16(f16(d*sc)*q) with -f16(dmin*m)*sum(x) as one more MMA; IQ2_XXS:
-// f16(db)*grid*sign; IQ1_S: f16(dl)*(grid+delta) -- because the 16 k-columns of
-// one MMA belong to four different blocks. Q6_K: sc*(q-32) is exact in f16 and
-// the superblock d is applied in f32 on the accumulator. x is rounded to f16.
-// Products are exact and summed in f32 by the tensor cores.
+// Numerics. f16 types: quants are exact small integers in f16 and the
+// per-block scales are applied in f16 with one rounding per weight (Q8_0:
+// f16(d*q); IQ2_XXS: f16(db)*grid*sign; IQ1_S: f16(dl)*(grid+delta)), because
+// the 16 k-columns of one MMA belong to four different blocks; Q6_K:
+// sc*(q-32) is exact in f16 and d is applied in f32 on the accumulator. x is
+// rounded to f16. Products are exact and summed in f32 by the tensor cores.
+// Q4_K: x per 256-weight chunk and token is x = dx*(xh + xl/256) with two int8
+// planes (about 16 significant bits); the nibble products are exact integer
+// sums, the 6-bit sub-block scales are applied to them in integers, and d*dx,
+// dmin*m*sum(x) in f32.
 #include <cooperative_groups.h>
 #include <cuda_runtime.h>
 
@@ -57,8 +63,9 @@ __device__ const __align__(16) uint16_t g_grid_iq1s_f16[EF_GRID_IQ1S_ENTRIES * 8
 constexpr uint32_t H2_1024 = 0x64006400u;   // half2(1024, 1024)
 constexpr uint32_t H2_1152 = 0x64806480u;   // half2(1152, 1152)
 constexpr uint32_t H2_2080 = 0x68106810u;   // half2(2080, 2080)
-constexpr int MAX_XS_BYTES = 32 * 1024;     // shared memory for one phase of x fragments
-constexpr int RING_PER_WARP = 7 * 1024;     // bytes of weight tiles per warp ring
+constexpr int GV_WARPS = 8;                 // rowgroups (warps) per CTA = one rowblock
+constexpr int MAX_XS_BYTES = 64 * 1024;     // shared memory for activation data
+
 
 struct GemvArgs {
     const uint8_t *w[4];      // repacked tiles of each section
@@ -68,21 +75,22 @@ struct GemvArgs {
     int64_t rowgroups[4];
     int rb_end[4];            // cumulative rowblocks per section
     int nmat;
-    const uint8_t *xf;        // x data from gemv_xprep: nchunks x xb bytes (5..16 tokens)
     int M;
     int64_t nchunks;
-    int cps;                  // chunks per k-slice
-    int kslices;
-    int phase_chunks;         // chunks of x fragments in shared memory at a time
-    int xb;                   // bytes of x data per chunk (f16_xbytes / i8_xbytes)
-    const float *x;           // f32 activations [M][K] (fused staging)
+    int kslices;              // CTAs (one cluster) per rowblock
+    int phase_chunks;         // chunks of activation data in shared memory at a time
+    int whole;                // the k-slice's chunks staged once (else phases)
+    int xs_bytes;             // shared memory for activation data
+    int xs_half;              // offset of the second phase buffer
+    int xb;                   // bytes of activation data per chunk
+    const uint8_t *xf;        // activation data from gemv_xprep (3..16 tokens)
+    const float *x;           // f32 activations [M][K] (1..2 tokens: staged by each CTA)
     int64_t K;
 };
 
 // ---------------------------------------------------------------- traits ---
 // STEPS = k16 steps per chunk; inv maps a k-quad (4 consecutive weights of the
-// chunk) to the lane column t and the step s that consume it; I8 = the type
-// runs on the 8-bit tensor cores with 8-bit activation planes (Q4_K).
+// chunk) to the lane column t and the step s that consume it (f16 types).
 template <int TYPE> struct Tr;
 template <> struct Tr<EF_Q8_0> {
     static constexpr int CHUNK = 128, STEPS = 8, TILE = 2176, I8 = 0;
@@ -109,32 +117,71 @@ template <> struct Tr<EF_IQ1_S> {
 };
 // bytes of f16 x fragments per chunk for M tokens: STEPS x M x 4 lanes x 8 B
 template <int TYPE> __host__ __device__ inline int f16_xbytes(int M) { return Tr<TYPE>::STEPS * M * 32; }
-// bytes of 8-bit x data per 256-weight chunk for M tokens (I8 types):
-// two int8 planes (high and residual) of B fragments, each
-// [8 sub-blocks][M tokens][4 lanes][8 B]; [M][4] f16 pairs of sub-block sums;
-// [M] f32 scales; rounded up to 16.
-__host__ __device__ inline int i8_xbytes(int M) { return (532 * M + 15) & ~15; }
+
+// Q4_K activation layout. The 8 columns of the m16n8k32 MMA hold TQ tokens x
+// (8 / TQ) sub-blocks: TQ = 1, 2, 4 for 1, 2, 3-4 tokens (several sub-blocks
+// share one MMA, each in its own columns, so the integer sub-block scales are
+// applied once per 8/TQ MMAs), TQ = 8 for 5-16 tokens in NT tiles of 8.
+__host__ __device__ inline int q4_tq(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
+__host__ __device__ inline int q4_nt(int M) { return M > 8 ? 2 : 1; }
+// Per chunk: B fragments [ntile][TQ][lane][16 B: xh b0 b1, xl b0 b1]; then the
+// f32 sums of x over each 32-weight sub-block [8][MP]; then dx [MP]
+// (MP = NT * TQ padded tokens); rounded up to 16 bytes.
+__host__ __device__ inline int i8_xbytes(int M) {
+    const int tq = q4_tq(M), nt = q4_nt(M), mp = tq * nt;
+    return (512 * tq * nt + 36 * mp + 15) & ~15;
+}
 
 __device__ __forceinline__ uint32_t wsel(const uint4 &v, int i) {
     return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
 }
-// Tile reads: the tiles sit in the warp's shared-memory ring (see the kernel).
+// Shared-memory reads (activation data).
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
 __device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *reinterpret_cast<const uint2 *>(p); }
 __device__ __forceinline__ uint32_t lds32(const uint8_t *p) { return *reinterpret_cast<const uint32_t *>(p); }
+// Tile reads, straight from global memory into registers: quant parts are
+// streamed (read once: no L1 allocation); scale bytes that the 4 lanes of a
+// group share go through L1.
+__device__ __forceinline__ uint4 ldq128(const uint8_t *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ldq64(const uint8_t *p) {
+    uint2 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldq32(const uint8_t *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.L1::no_allocate.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint4 ldh128(const uint8_t *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint2 ldh64(const uint8_t *p) {
+    uint2 v;
+    asm volatile("ld.global.nc.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ uint32_t ldh32(const uint8_t *p) {
+    uint32_t v;
+    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(v) : "l"(p));
+    return v;
+}
 
-// Asynchronous global -> shared copies (LDGSTS, L2 only).
+// Asynchronous 16-byte global -> shared copies (LDGSTS, L2 only), for the
+// activation phases.
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
 }
 __device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-template <int TILE>
-__device__ __forceinline__ void copy_tile(uint8_t *dst, const uint8_t *src, int lane) {
-#pragma unroll
-    for (int p = lane; p < TILE / 16; p += 32) cp_async16(dst + 16 * p, src + 16 * p);
-}
 
 // x data of one chunk for the f16 types: B fragments [step][token][lane t]
 // (8 B each), tokens 0..M-1 only; lanes whose token is >= M feed zeros.
@@ -172,8 +219,8 @@ __device__ __forceinline__ uint32_t dup_h2(float v) {
 struct RawQ8 { uint4 q[4]; uint32_t sc; };
 __device__ __forceinline__ void load_raw(RawQ8 &r, const uint8_t *T, int lane) {
 #pragma unroll
-    for (int p = 0; p < 4; p++) r.q[p] = lds128(T + p * 512 + lane * 16);
-    r.sc = lds32(T + 2048 + lane * 4);
+    for (int p = 0; p < 4; p++) r.q[p] = ldq128(T + p * 512 + lane * 16);
+    r.sc = ldq32(T + 2048 + lane * 4);
 }
 template <int NT>
 __device__ __forceinline__ void compute(const RawQ8 &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
@@ -193,100 +240,188 @@ __device__ __forceinline__ void compute(const RawQ8 &r, const uint8_t *xc, int M
 }
 
 // ------------------------------------------------------------------ Q4_K ---
+// lane (g,t): for each 64-weight group j the bytes l = 4t..4t+3 and
+// 16+4t..16+4t+3 of rows g and g+8 (low nibble: sub-block 2j, high nibble:
+// sub-block 2j+1), and the verbatim 16-byte headers of rows g and g+8.
 struct RawQ4K { uint4 q[4]; uint4 hg, hg8; };
 __device__ __forceinline__ void load_raw(RawQ4K &r, const uint8_t *T, int lane) {
 #pragma unroll
-    for (int p = 0; p < 4; p++) r.q[p] = lds128(T + p * 512 + lane * 16);
+    for (int p = 0; p < 4; p++) r.q[p] = ldq128(T + p * 512 + lane * 16);
     const int g = lane >> 2;
-    r.hg = lds128(T + 2048 + g * 16);
-    r.hg8 = lds128(T + 2048 + (g + 8) * 16);
+    r.hg = ldh128(T + 2048 + g * 16);
+    r.hg8 = ldh128(T + 2048 + (g + 8) * 16);
 }
-// 8-bit tensor-core MMA: D = A(16x32 u8, row) * B(32x8 s8, col), s32.
-__device__ __forceinline__ void imma16832(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                          uint32_t b0, uint32_t b1) {
-    asm volatile(
-        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-        "{%10,%10,%10,%10};\n"
-        : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+// 6-bit scales (sc) and mins (m) of one row, one per byte: sub-blocks 0..3
+// and 4..7 (scale_min_k4, kernels.wgsl.js:94-104).
+struct Q4Scales { uint32_t scl, sch, ml, mh; };
+__device__ __forceinline__ Q4Scales q4k_scales(const uint4 &h) {
+    Q4Scales s;
+    s.scl = h.y & 0x3F3F3F3Fu;
+    s.sch = (h.w & 0x0F0F0F0Fu) | ((h.y >> 2) & 0x30303030u);
+    s.ml = h.z & 0x3F3F3F3Fu;
+    s.mh = ((h.w >> 4) & 0x0F0F0F0Fu) | ((h.z >> 2) & 0x30303030u);
+    return s;
 }
-// (-f16(dmin*m_2t), -f16(dmin*m_2t+1)) of lane column t from a verbatim 16-byte
-// Q4_K header (scale_min_k4, kernels.wgsl.js:94-104, for j = 2t, 2t+1).
-__device__ __forceinline__ uint32_t q4k_negmin(const uint4 &h, int t) {
-    const uint32_t nmm = prmt(h.x, 0, 0x3232) ^ 0x80008000u;
-    const int sh = 16 * (t & 1);
-    const uint32_t p0 = (h.y >> sh) & 0xFFFF, p1 = (h.z >> sh) & 0xFFFF, p2 = (h.w >> sh) & 0xFFFF;
-    const uint32_t mp = t < 2 ? (p1 & 0x3F3F) : (((p2 >> 4) & 0x0F0F) | ((p1 >> 2) & 0x3030));
-    (void)p0;
-    return hmul2u(hsub2u(prmt(mp, 0x64646464u, 0x4140), H2_1024), nmm);
+// byte `b` of w as an integer
+__device__ __forceinline__ int byte_of(uint32_t w, int b) { return (int)prmt(w, 0u, 0x4440u | (uint32_t)b); }
+
+// A fragment of sub-block s (m16n8k32, u8): rows g, g+8; k = 4t.., 16+4t..
+// The high-nibble sub-blocks (odd s) are taken as 16*q (mask 0xF0), so every
+// integer product sum carries a factor 16 once even sub-blocks' scales are
+// shifted by 4.
+__device__ __forceinline__ void q4k_afrag(const RawQ4K &r, int s, uint32_t &a0, uint32_t &a1, uint32_t &a2,
+                                          uint32_t &a3) {
+    const int j = s >> 1;
+    const uint4 &pg = r.q[j >> 1], &ph = r.q[2 + (j >> 1)];
+    const uint32_t mask = (s & 1) ? 0xF0F0F0F0u : 0x0F0F0F0Fu;
+    a0 = ((j & 1) ? pg.z : pg.x) & mask;
+    a1 = ((j & 1) ? ph.z : ph.x) & mask;
+    a2 = ((j & 1) ? pg.w : pg.y) & mask;
+    a3 = ((j & 1) ? ph.w : ph.y) & mask;
 }
-// Q4_K on the 8-bit tensor cores. The prep kernel writes x per 256-weight
-// chunk and token as x = dx * (qh + ql / 256) with two int8 planes (qh =
-// round(x/dx), dx = max|x|/127; ql = round(256 * residual)), i.e. about 16
-// significant bits, finer than f16. Per 32-weight sub-block: the raw nibbles
-// are the A operand (one LOP3 per 4 weights), one m16n8k32 MMA per plane, and
-// the 6-bit sub-block scale is applied to the exact integer results; d*dx once
-// per superblock in f32; -dmin*m*sum(x) is one f16 MMA per superblock.
-template <int NT>
-__device__ __forceinline__ void compute(const RawQ4K &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
-                                        const uint4 *, const uint4 *) {
+
+// Q4_K tile: acc[nt][i] (row g or g+8 by i>>1; lane column 2t + (i&1)) +=
+//   d*dx*(sum_sub sc*sum_k q*(xh + xl/256)) - dmin*sum_sub m*S_sub
+// with the column -> (sub-block, token) mapping of TQ (see q4_tq).
+template <int TQ, int NT>
+__device__ __forceinline__ void compute_q4k(const RawQ4K &r, const uint8_t *xc, float (&acc)[NT][4], int lane) {
+    constexpr int FL = 8 / TQ;   // sub-blocks per MMA group (flush)
+    constexpr int MP = NT * TQ;
     const int g = lane >> 2, t = lane & 3;
-    // 6-bit scales of sub-blocks 0..7 of rows g and g+8, one byte each
-    const uint32_t sgl = r.hg.y & 0x3F3F3F3Fu, sgh = (r.hg.w & 0x0F0F0F0Fu) | ((r.hg.y >> 2) & 0x30303030u);
-    const uint32_t shl = r.hg8.y & 0x3F3F3F3Fu, shh = (r.hg8.w & 0x0F0F0F0Fu) | ((r.hg8.y >> 2) & 0x30303030u);
-    int si[NT][4], sl[NT][4];
-    bool tv[NT];
+    const Q4Scales sg = q4k_scales(r.hg), sh = q4k_scales(r.hg8);
+    const float *S = reinterpret_cast<const float *>(xc + 512 * TQ * NT);
+    const float *DX = S + 8 * MP;
+    int ih[NT][4], il[NT][4];
+    float ms[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-        si[nt][0] = si[nt][1] = si[nt][2] = si[nt][3] = 0;
-        sl[nt][0] = sl[nt][1] = sl[nt][2] = sl[nt][3] = 0;
-        tv[nt] = nt * 8 + g < M;
-    }
-    const uint8_t *fr = xc + g * 32 + t * 8;
+    for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-    for (int j = 0; j < 4; j++) {
-        const uint4 &pg = r.q[j >> 1], &ph = r.q[2 + (j >> 1)];
-        const uint32_t g0 = (j & 1) ? pg.z : pg.x, g1 = (j & 1) ? pg.w : pg.y;
-        const uint32_t h0 = (j & 1) ? ph.z : ph.x, h1 = (j & 1) ? ph.w : ph.y;
+        for (int i = 0; i < 4; i++) {
+            ih[nt][i] = il[nt][i] = 0;
+            ms[nt][i] = 0.f;
+        }
+    if constexpr (TQ == 8) {
+        // one sub-block per MMA, all 8 columns are tokens
 #pragma unroll
-        for (int hf = 0; hf < 2; hf++) {
-            const int sub = 2 * j + hf;
-            const uint32_t a0 = (hf ? g0 >> 4 : g0) & 0x0F0F0F0Fu, a2 = (hf ? g1 >> 4 : g1) & 0x0F0F0F0Fu;
-            const uint32_t a1 = (hf ? h0 >> 4 : h0) & 0x0F0F0F0Fu, a3 = (hf ? h1 >> 4 : h1) & 0x0F0F0F0Fu;
-            const int scg = (int)(((sub < 4 ? sgl : sgh) >> (8 * (sub & 3))) & 0xFF);
-            const int sch = (int)(((sub < 4 ? shl : shh) >> (8 * (sub & 3))) & 0xFF);
+        for (int s = 0; s < 8; s++) {
+            uint32_t a0, a1, a2, a3;
+            q4k_afrag(r, s, a0, a1, a2, a3);
+            const int shl = (s & 1) ? 0 : 4;
+            const int scg = byte_of(s < 4 ? sg.scl : sg.sch, s & 3) << shl;
+            const int sch = byte_of(s < 4 ? sh.scl : sh.sch, s & 3) << shl;
+            const float mg = (float)byte_of(s < 4 ? sg.ml : sg.mh, s & 3);
+            const float mh = (float)byte_of(s < 4 ? sh.ml : sh.mh, s & 3);
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                const uint8_t *f = fr + (sub * M + nt * 8) * 32;
-                const uint2 b = tv[nt] ? *reinterpret_cast<const uint2 *>(f) : make_uint2(0u, 0u);
-                const uint2 bl = tv[nt] ? *reinterpret_cast<const uint2 *>(f + 256 * M) : make_uint2(0u, 0u);
-                int d[4], e[4];
-                imma16832(d, a0, a1, a2, a3, b.x, b.y);
-                imma16832(e, a0, a1, a2, a3, bl.x, bl.y);
-                si[nt][0] += scg * d[0];
-                si[nt][1] += scg * d[1];
-                si[nt][2] += sch * d[2];
-                si[nt][3] += sch * d[3];
-                sl[nt][0] += scg * e[0];
-                sl[nt][1] += scg * e[1];
-                sl[nt][2] += sch * e[2];
-                sl[nt][3] += sch * e[3];
+                const uint4 b = lds128(xc + ((nt * 8 + s) * 32 + lane) * 16);
+                int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0};
+                imma16832(dh, a0, a1, a2, a3, b.x, b.y);
+                imma16832(dl, a0, a1, a2, a3, b.z, b.w);
+                ih[nt][0] += scg * dh[0];
+                ih[nt][1] += scg * dh[1];
+                ih[nt][2] += sch * dh[2];
+                ih[nt][3] += sch * dh[3];
+                il[nt][0] += scg * dl[0];
+                il[nt][1] += scg * dl[1];
+                il[nt][2] += sch * dl[2];
+                il[nt][3] += sch * dl[3];
+                const float2 sv = *reinterpret_cast<const float2 *>(S + s * MP + nt * 8 + 2 * t);
+                ms[nt][0] = fmaf(mg, sv.x, ms[nt][0]);
+                ms[nt][1] = fmaf(mg, sv.y, ms[nt][1]);
+                ms[nt][2] = fmaf(mh, sv.x, ms[nt][2]);
+                ms[nt][3] = fmaf(mh, sv.y, ms[nt][3]);
             }
         }
+    } else {
+        // B column g of this lane carries token g % TQ of sub-blocks with
+        // s % FL == g / TQ: one 16-byte fragment per flush, zero otherwise.
+        const int sgb = g / TQ;
+#pragma unroll
+        for (int f = 0; f < TQ; f++) {
+            const uint4 xb = lds128(xc + (f * 32 + lane) * 16);
+            // two independent MMA chains (even / odd steps) for latency; the
+            // columns they fill are disjoint, so their sum is exact
+            int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0}, eh[4] = {0, 0, 0, 0}, el[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int q = 0; q < FL; q++) {
+                uint32_t a0, a1, a2, a3;
+                q4k_afrag(r, f * FL + q, a0, a1, a2, a3);
+                const uint32_t mk = q == sgb ? 0xFFFFFFFFu : 0u;
+                if (q & 1) {
+                    imma16832(eh, a0, a1, a2, a3, xb.x & mk, xb.y & mk);
+                    imma16832(el, a0, a1, a2, a3, xb.z & mk, xb.w & mk);
+                } else {
+                    imma16832(dh, a0, a1, a2, a3, xb.x & mk, xb.y & mk);
+                    imma16832(dl, a0, a1, a2, a3, xb.z & mk, xb.w & mk);
+                }
+            }
+            if (FL > 1)
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    dh[i] += eh[i];
+                    dl[i] += el[i];
+                }
+            // accumulator column 2t + c now holds sub-block f*FL + (2t+c)/TQ
+            // of token (2t+c) % TQ
+            int s0, s1, tok0;
+            if (TQ == 1) {
+                s0 = 2 * t;
+                s1 = 2 * t + 1;
+                tok0 = 0;
+            } else if (TQ == 2) {
+                s0 = s1 = 4 * f + t;
+                tok0 = 0;
+            } else {
+                s0 = s1 = 2 * f + (t >> 1);
+                tok0 = 2 * (t & 1);
+            }
+            const int sh0 = (s0 & 1) ? 0 : 4, sh1 = (s1 & 1) ? 0 : 4;
+            const uint32_t wsg = s0 < 4 ? sg.scl : sg.sch, wsh = s0 < 4 ? sh.scl : sh.sch;
+            const uint32_t wmg = s0 < 4 ? sg.ml : sg.mh, wmh = s0 < 4 ? sh.ml : sh.mh;
+            const int scg0 = byte_of(wsg, s0 & 3) << sh0, scg1 = byte_of(wsg, s1 & 3) << sh1;
+            const int sch0 = byte_of(wsh, s0 & 3) << sh0, sch1 = byte_of(wsh, s1 & 3) << sh1;
+            ih[0][0] += scg0 * dh[0];
+            ih[0][1] += scg1 * dh[1];
+            ih[0][2] += sch0 * dh[2];
+            ih[0][3] += sch1 * dh[3];
+            il[0][0] += scg0 * dl[0];
+            il[0][1] += scg1 * dl[1];
+            il[0][2] += sch0 * dl[2];
+            il[0][3] += sch1 * dl[3];
+            const float mg0 = (float)byte_of(wmg, s0 & 3), mg1 = (float)byte_of(wmg, s1 & 3);
+            const float mh0 = (float)byte_of(wmh, s0 & 3), mh1 = (float)byte_of(wmh, s1 & 3);
+            float2 sv;
+            if (TQ == 1) sv = *reinterpret_cast<const float2 *>(S + s0);               // S[s0][0], S[s1][0]
+            else sv = *reinterpret_cast<const float2 *>(S + s0 * MP + tok0);          // S[s][tok0], S[s][tok0+1]
+            ms[0][0] = fmaf(mg0, sv.x, ms[0][0]);
+            ms[0][1] = fmaf(mg1, sv.y, ms[0][1]);
+            ms[0][2] = fmaf(mh0, sv.x, ms[0][2]);
+            ms[0][3] = fmaf(mh1, sv.y, ms[0][3]);
+        }
     }
-    const float dg = h2f(r.hg.x & 0xFFFF), dh = h2f(r.hg8.x & 0xFFFF);
-    const float *dxp = reinterpret_cast<const float *>(xc + 528 * M);
-    const uint32_t gnm = q4k_negmin(r.hg, t), hnm = q4k_negmin(r.hg8, t);
+    // d*dx/16 and dmin per row, dx per lane column
+    const float dg = h2f(r.hg.x & 0xFFFF), mng = h2f(r.hg.x >> 16);
+    const float dh8 = h2f(r.hg8.x & 0xFFFF), mnh = h2f(r.hg8.x >> 16);
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
-        const int tk0 = nt * 8 + 2 * t, tk1 = tk0 + 1;
-        const float dx0 = tk0 < M ? dxp[tk0] : 0.f, dx1 = tk1 < M ? dxp[tk1] : 0.f;
-        acc[nt][0] = fmaf(dg * dx0, fmaf((float)sl[nt][0], 1.f / 256.f, (float)si[nt][0]), acc[nt][0]);
-        acc[nt][1] = fmaf(dg * dx1, fmaf((float)sl[nt][1], 1.f / 256.f, (float)si[nt][1]), acc[nt][1]);
-        acc[nt][2] = fmaf(dh * dx0, fmaf((float)sl[nt][2], 1.f / 256.f, (float)si[nt][2]), acc[nt][2]);
-        acc[nt][3] = fmaf(dh * dx1, fmaf((float)sl[nt][3], 1.f / 256.f, (float)si[nt][3]), acc[nt][3]);
-        const uint32_t mf = tv[nt] ? *reinterpret_cast<const uint32_t *>(xc + 512 * M + (nt * 8 + g) * 16 + t * 4) : 0u;
-        mma16816(acc[nt], gnm, hnm, 0u, 0u, mf, 0u);
+        float dx0, dx1;
+        if (TQ == 1) {
+            dx0 = dx1 = DX[0];
+        } else {
+            const int tk = TQ == 2 ? 0 : TQ == 4 ? 2 * (t & 1) : nt * 8 + 2 * t;
+            const float2 d2 = *reinterpret_cast<const float2 *>(DX + tk);
+            dx0 = d2.x;
+            dx1 = d2.y;
+        }
+        const float k0 = dx0 * (1.f / 16.f), k1 = dx1 * (1.f / 16.f);
+        const float v0 = fmaf((float)il[nt][0], 1.f / 256.f, (float)ih[nt][0]);
+        const float v1 = fmaf((float)il[nt][1], 1.f / 256.f, (float)ih[nt][1]);
+        const float v2 = fmaf((float)il[nt][2], 1.f / 256.f, (float)ih[nt][2]);
+        const float v3 = fmaf((float)il[nt][3], 1.f / 256.f, (float)ih[nt][3]);
+        acc[nt][0] = fmaf(-mng, ms[nt][0], fmaf(dg * k0, v0, acc[nt][0]));
+        acc[nt][1] = fmaf(-mng, ms[nt][1], fmaf(dg * k1, v1, acc[nt][1]));
+        acc[nt][2] = fmaf(-mnh, ms[nt][2], fmaf(dh8 * k0, v2, acc[nt][2]));
+        acc[nt][3] = fmaf(-mnh, ms[nt][3], fmaf(dh8 * k1, v3, acc[nt][3]));
     }
 }
 
@@ -294,11 +429,11 @@ __device__ __forceinline__ void compute(const RawQ4K &r, const uint8_t *xc, int 
 struct RawQ6K { uint4 q[6]; uint2 scg, scg8; uint32_t d; };
 __device__ __forceinline__ void load_raw(RawQ6K &r, const uint8_t *T, int lane) {
 #pragma unroll
-    for (int p = 0; p < 6; p++) r.q[p] = lds128(T + p * 512 + lane * 16);
+    for (int p = 0; p < 6; p++) r.q[p] = ldq128(T + p * 512 + lane * 16);
     const int g = lane >> 2, n = (lane & 3) >> 1;
-    r.scg = lds64(T + 3072 + g * 16 + 8 * n);
-    r.scg8 = lds64(T + 3072 + (g + 8) * 16 + 8 * n);
-    r.d = lds32(T + 3328 + 4 * g);
+    r.scg = ldh64(T + 3072 + g * 16 + 8 * n);
+    r.scg8 = ldh64(T + 3072 + (g + 8) * 16 + 8 * n);
+    r.d = ldh32(T + 3328 + 4 * g);
 }
 __device__ __forceinline__ uint32_t q6_pair(uint32_t nw, int nsh, uint32_t hw, int hsh, uint32_t sc2) {
     const uint32_t lo = lop3_and_or(nw >> nsh, 0x000F000Fu, H2_1024);
@@ -351,9 +486,9 @@ __device__ __forceinline__ void compute(const RawQ6K &r, const uint8_t *xc, int 
 // --------------------------------------------------------------- IQ2_XXS ---
 struct RawIQ2 { uint4 q[2]; uint32_t d; };
 __device__ __forceinline__ void load_raw(RawIQ2 &r, const uint8_t *T, int lane) {
-    r.q[0] = lds128(T + lane * 16);
-    r.q[1] = lds128(T + 512 + lane * 16);
-    r.d = lds32(T + 1024 + 4 * (lane >> 2));
+    r.q[0] = ldq128(T + lane * 16);
+    r.q[1] = ldq128(T + 512 + lane * 16);
+    r.d = ldh32(T + 1024 + 4 * (lane >> 2));
 }
 template <int NT>
 __device__ __forceinline__ void compute(const RawIQ2 &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
@@ -382,9 +517,9 @@ __device__ __forceinline__ void compute(const RawIQ2 &r, const uint8_t *xc, int 
 // ----------------------------------------------------------------- IQ1_S ---
 struct RawIQ1 { uint4 qs; uint2 qh; uint32_t d; };
 __device__ __forceinline__ void load_raw(RawIQ1 &r, const uint8_t *T, int lane) {
-    r.qs = lds128(T + lane * 16);
-    r.qh = lds64(T + 512 + lane * 8);
-    r.d = lds32(T + 768 + 4 * (lane >> 2));
+    r.qs = ldq128(T + lane * 16);
+    r.qh = ldq64(T + 512 + lane * 8);
+    r.d = ldh32(T + 768 + 4 * (lane >> 2));
 }
 template <int NT>
 __device__ __forceinline__ void compute(const RawIQ1 &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
@@ -429,8 +564,8 @@ template <> struct TableBytes<EF_IQ1_S> { static constexpr int v = 2048 * 16; };
 // ------------------------------------------------------------- x staging ---
 // Chunks [c, c + n) of x (f32 [M][K]) are written as the activation data the
 // compute functions read, to `dst` (chunk i at dst + i * xb), by the threads
-// [tid, tid + nthreads) -- either one CTA (the fused, single-kernel path used
-// for up to 4 tokens) or the whole grid of the prep kernel (5..16 tokens).
+// [tid, tid + nthreads) -- either one CTA (1-2 tokens) or the whole grid of
+// the prep kernel (3..16 tokens).
 //
 // f16 types: per chunk, B fragments [step][token][lane t] (8 B: the pairs
 // (k, k+1), (k+2, k+3) of the k-quad that (t, step) consumes), tokens 0..M-1.
@@ -452,19 +587,20 @@ __device__ __forceinline__ void stage_f16(const float *__restrict__ x, int M, in
             make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
     }
 }
-// Q4_K (8-bit MMA): per 256-weight chunk and token x = dx * (qh + ql/256),
-// dx = max|x|/127, qh = rne(x/dx), ql = rne(256 * (x/dx - qh)), both int8, as
-// B fragments [plane][sub-block][token][lane t][b0 b1]; then the f16 sums of x
-// over each 32-weight sub-block as pairs (2t, 2t+1) per (token, t); then dx per
-// token. One warp per (chunk, token); lane l holds weights 8l .. 8l+7.
+// Q4_K: per 256-weight chunk and token x = dx * (xh + xl/256), dx =
+// max|x|/127, xh = rne(x/dx), xl = rne(256 * (x/dx - xh)), both int8, as the
+// B fragments of the column layout of q4_tq (tokens M..MP-1 are zero); the f32
+// sums of x over each 32-weight sub-block; dx. One warp per (chunk, token);
+// lane l holds weights 8l .. 8l+7.
 __device__ __forceinline__ void stage_i8(const float *__restrict__ x, int M, int64_t K, int64_t c, int n,
                                          uint8_t *dst, int xb, int tid, int nthreads) {
     const int lane = tid & 31;
-    for (int w = tid >> 5; w < n * M; w += nthreads >> 5) {
-        const int cc = w / M, token = w - cc * M;
+    const int tq = q4_tq(M), ntl = q4_nt(M), mp = tq * ntl, fl = 8 / tq;
+    for (int w = tid >> 5; w < n * mp; w += nthreads >> 5) {
+        const int cc = w / mp, token = w - cc * mp;
         const int64_t k0 = (c + cc) * 256 + 8 * lane;
         float v[8];
-        if (k0 < K) {
+        if (token < M && k0 < K) {
             const float4 p = __ldg(reinterpret_cast<const float4 *>(x + token * K + k0));
             const float4 q = __ldg(reinterpret_cast<const float4 *>(x + token * K + k0 + 4));
             v[0] = p.x; v[1] = p.y; v[2] = p.z; v[3] = p.w; v[4] = q.x; v[5] = q.y; v[6] = q.z; v[7] = q.w;
@@ -494,17 +630,20 @@ __device__ __forceinline__ void stage_i8(const float *__restrict__ x, int M, int
             wl[h] = wlo;
         }
         uint8_t *base = dst + (int64_t)cc * xb;
-        const int sub = lane >> 2, kk = 8 * (lane & 3);                  // k within the sub-block
-        const int tA = (kk & 15) >> 2, off = kk >= 16 ? 4 : 0;          // fragment lane and half
-        uint8_t *fr = base + (sub * M + token) * 32;
-        *reinterpret_cast<uint32_t *>(fr + tA * 8 + off) = wq[0];
-        *reinterpret_cast<uint32_t *>(fr + (tA + 1) * 8 + off) = wq[1];
-        *reinterpret_cast<uint32_t *>(fr + 256 * M + tA * 8 + off) = wl[0];
-        *reinterpret_cast<uint32_t *>(fr + 256 * M + (tA + 1) * 8 + off) = wl[1];
-        if ((lane & 3) == 0)
-            *reinterpret_cast<__half *>(base + 512 * M + token * 16 + (sub >> 1) * 4 + (sub & 1) * 2) =
-                __float2half_rn(sum);
-        if (lane == 0) *reinterpret_cast<float *>(base + 528 * M + token * 4) = dx;
+        const int sub = lane >> 2, kk = 8 * (lane & 3);       // k within the sub-block
+        const int nt = token >> 3, tk = token & 7;            // n-tile, token within it
+        const int n_col = (sub % fl) * tq + (tq == 8 ? tk : token);   // B column
+        const int f = sub / fl;                               // fragment index of that lane
+        const int tb = (kk & 15) >> 2, reg = kk >> 4;         // lane t of the B fragment, b0 or b1
+        uint8_t *fr0 = base + ((nt * tq + f) * 32 + 4 * n_col + tb) * 16 + reg * 4;
+        uint8_t *fr1 = fr0 + 16;
+        *reinterpret_cast<uint32_t *>(fr0) = wq[0];
+        *reinterpret_cast<uint32_t *>(fr0 + 8) = wl[0];
+        *reinterpret_cast<uint32_t *>(fr1) = wq[1];
+        *reinterpret_cast<uint32_t *>(fr1 + 8) = wl[1];
+        float *S = reinterpret_cast<float *>(base + 512 * tq * ntl);
+        if ((lane & 3) == 0) S[sub * mp + token] = sum;
+        if (lane == 0) S[8 * mp + token] = dx;
     }
 }
 template <int TYPE>
@@ -514,10 +653,10 @@ __device__ __forceinline__ void stage_x(const float *x, int M, int64_t K, int64_
     else stage_f16<TYPE>(x, M, K, c, n, dst, xb, tid, nthreads);
 }
 
-// Prep kernel (5..16 tokens): all chunks into global scratch. Launched with
-// programmatic dependent launch: it lets the GEMV that follows start (and
-// prefetch weights) at once, and waits for the kernel before it (which may
-// have produced x, or still read the scratch) before touching memory.
+// Prep kernel (3..16 tokens): all chunks into global scratch. When launched
+// with programmatic dependent launch it lets the GEMV that follows start at
+// once, and waits for the kernel before it (which may have produced x, or
+// still read the scratch) before touching memory.
 template <int TYPE>
 __global__ void gemv_xprep(const float *__restrict__ x, int M, int64_t K, int64_t nchunks, int xb,
                            uint8_t *__restrict__ xf) {
@@ -526,92 +665,103 @@ __global__ void gemv_xprep(const float *__restrict__ x, int M, int64_t K, int64_
     stage_x<TYPE>(x, M, K, 0, (int)nchunks, xf, xb, blockIdx.x * blockDim.x + threadIdx.x, gridDim.x * blockDim.x);
 }
 
-// ------------------------------------------------------------- epilogue ----
-template <int NT, bool SWIGLU>
-__device__ __forceinline__ void write_out(const float (&acc)[NT][4], const float (&acc2)[NT][4], float *y,
-                                          int64_t rows, int M, int64_t rg, int lane) {
-    const int g = lane >> 2, t = lane & 3;
-    const int64_t r0 = rg * 16 + g, r1 = r0 + 8;
+// ------------------------------------------------------- result columns ----
+// After a segment, the accumulators of the 4 lanes t of a group are reduced
+// over the lanes that hold the same token (q4_tq column layouts); then
+// for_owned visits each (row, token) value exactly once, on its owner lane:
+// f(nt, i, row within the rowgroup, token).
+template <int TQ, int NT>
+__device__ __forceinline__ void reduce_cols(float (&acc)[NT][4]) {
+    if constexpr (TQ == 1) {
+        acc[0][0] += acc[0][1];
+        acc[0][2] += acc[0][3];
+        acc[0][0] += __shfl_xor_sync(0xffffffffu, acc[0][0], 1);
+        acc[0][2] += __shfl_xor_sync(0xffffffffu, acc[0][2], 1);
+        acc[0][0] += __shfl_xor_sync(0xffffffffu, acc[0][0], 2);
+        acc[0][2] += __shfl_xor_sync(0xffffffffu, acc[0][2], 2);
+    } else if constexpr (TQ == 2) {
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) {
-        const int tk0 = nt * 8 + 2 * t, tk1 = tk0 + 1;
-        float v[4];
+        for (int i = 0; i < 4; i++) {
+            acc[0][i] += __shfl_xor_sync(0xffffffffu, acc[0][i], 1);
+            acc[0][i] += __shfl_xor_sync(0xffffffffu, acc[0][i], 2);
+        }
+    } else if constexpr (TQ == 4) {
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            if (SWIGLU) {
-                const float gt = acc[nt][j];
-                v[j] = gt / (1.0f + expf(-gt)) * acc2[nt][j];   // silu(g) * u
-            } else {
-                v[j] = acc[nt][j];
-            }
-        }
-        if (r0 < rows) {
-            if (tk0 < M) y[(int64_t)tk0 * rows + r0] = v[0];
-            if (tk1 < M) y[(int64_t)tk1 * rows + r0] = v[1];
-        }
-        if (r1 < rows) {
-            if (tk0 < M) y[(int64_t)tk0 * rows + r1] = v[2];
-            if (tk1 < M) y[(int64_t)tk1 * rows + r1] = v[3];
-        }
+        for (int i = 0; i < 4; i++) acc[0][i] += __shfl_xor_sync(0xffffffffu, acc[0][i], 2);
     }
+}
+template <int TQ, int NT, typename F>
+__device__ __forceinline__ void for_owned(int lane, F &&f) {
+    const int g = lane >> 2, t = lane & 3;
+    if constexpr (TQ == 1) {
+        if (t == 0) {
+            f(0, 0, g, 0);
+            f(0, 2, g + 8, 0);
+        }
+    } else if constexpr (TQ == 2) {
+        if (t == 0)
+#pragma unroll
+            for (int i = 0; i < 4; i++) f(0, i, g + 8 * (i >> 1), i & 1);
+    } else if constexpr (TQ == 4) {
+        if (t < 2)
+#pragma unroll
+            for (int i = 0; i < 4; i++) f(0, i, g + 8 * (i >> 1), 2 * t + (i & 1));
+    } else {
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) f(nt, i, g + 8 * (i >> 1), nt * 8 + 2 * t + (i & 1));
+    }
+}
+template <bool SWIGLU> __device__ __forceinline__ float out_value(float gate, float up) {
+    if (SWIGLU) return gate / (1.0f + expf(-gate)) * up;   // silu(g) * u
+    return gate;
 }
 
 // ---------------------------------------------------------------- kernel ---
-// Shared memory: [weight rings: WARPS x NMAT x ST tiles][x fragments of one
-// phase][codebooks][cluster partial sums].
-template <int TYPE, bool SW> struct Stages {
-    static constexpr int raw = RING_PER_WARP / ((SW ? 2 : 1) * Tr<TYPE>::TILE);
-    static constexpr int v = raw < 2 ? 2 : raw > 6 ? 6 : raw;
+// CTA = one rowblock (8 rowgroups) x one k-slice [c0, c1) of its chunks; the
+// ks k-slices of a rowblock form one thread-block cluster and add their sums
+// through distributed shared memory, in rank order (deterministic, no
+// atomics). KH = warps per rowgroup: with KH = 2 a CTA has 16 warps and the
+// two warps of a rowgroup take alternate chunks, merging their sums through
+// shared memory at the end.
+template <int NT, int KH> struct CombineBytes {
+    static constexpr int v = KH == 2 ? GV_WARPS * 32 * NT * 4 * 4 : 0;
 };
-template <int WARPS> struct MinBlocks { static constexpr int v = WARPS == 8 ? 2 : 4; };
+// cluster reduction: [rowgroup slot][matrix][token][16 rows] f32
+template <bool SW> struct ReduceBytes { static constexpr int v = GV_WARPS * (SW ? 2 : 1) * 16 * 16 * 4; };
+// Shared memory: [activation data: the slice's chunks, or one or two phase
+// buffers][codebooks][pair-combine buffer][cluster-reduction buffer].
+template <int TYPE, int NT, bool SWIGLU, int KH>
+static size_t gemv_smem(int xs_bytes, bool cluster) {
+    return (size_t)xs_bytes + TableBytes<TYPE>::v + CombineBytes<NT, KH>::v + (cluster ? ReduceBytes<SWIGLU>::v : 0);
+}
 
-// FUSED: the CTA stages its own x slice from f32 x (up to 4 tokens: one
-// kernel per call); otherwise it copies the slice the prep kernel wrote.
-template <int TYPE, int NT, bool SWIGLU, int WARPS, bool FUSED>
-__global__ void __launch_bounds__(WARPS * 32, MinBlocks<WARPS>::v) gemv_kernel(const GemvArgs a) {
+// TQ: Q4_K column layout (8 for the f16 types); NT: 8-token tiles; FUSED: the
+// CTA stages its own activation data from f32 x (1-2 tokens); KH: warps per
+// rowgroup (1 or 2).
+template <int TYPE, int TQ, int NT, bool SWIGLU, bool FUSED, int KH>
+__global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) gemv_kernel(const GemvArgs a) {
     using TR = Tr<TYPE>;
     using Raw = typename RawOf<TYPE>::T;
+    constexpr int W = GV_WARPS;
     constexpr int NMAT = SWIGLU ? 2 : 1;
-    constexpr int ST = Stages<TYPE, SWIGLU>::v;
     constexpr int TILE = TR::TILE;
-    const int FB = a.xb;
-    extern __shared__ __align__(16) uint8_t smem[];
+    static_assert(KH == 1 || !SWIGLU, "SwiGLU runs one warp per rowgroup");
+    extern __shared__ __align__(128) uint8_t smem[];
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int ks = blockIdx.x, rb = blockIdx.y;
-    int m = 0;
-    while (m + 1 < a.nmat && rb >= a.rb_end[m]) m++;
-    const int rb_local = rb - (m ? a.rb_end[m - 1] : 0);
-    const int64_t rg = (int64_t)rb_local * WARPS + warp;
-    const bool active = rg < a.rowgroups[m];
-    const int c0 = ks * a.cps;
-    const int nc = (int)min((int64_t)a.cps, a.nchunks - c0);
-
-    constexpr int RING = WARPS * NMAT * ST * TILE;
-    uint8_t *ring = smem + warp * NMAT * ST * TILE;
-    uint8_t *xs = smem + RING;
-    const int xs_bytes = a.phase_chunks * FB;
-    uint4 *grid = reinterpret_cast<uint4 *>(smem + RING + xs_bytes);
+    const int wr = warp % W, kh = warp / W;   // rowgroup slot, k-half
+    const int FB = a.xb;
+    uint8_t *xs = smem;
+    uint4 *grid = reinterpret_cast<uint4 *>(xs + a.xs_bytes);
     uint4 *sgn = grid + 256;
-    float *red = reinterpret_cast<float *>(smem + RING + xs_bytes + TableBytes<TYPE>::v);
-
-    // Weight stream: chunk cc of this warp goes to ring slot cc % ST by
-    // cp.async; one commit group per chunk (empty groups keep the count).
-    const int64_t tile0 = active ? (rg * a.nchunks + c0) * (int64_t)TILE : 0;
-    const uint8_t *Tm = a.w[m] + tile0;
-    const uint8_t *Tu = SWIGLU ? a.w_up + tile0 : nullptr;
-    auto issue = [&](int cc) {
-        if (active && cc < nc) {
-            copy_tile<TILE>(ring + (cc % ST) * TILE, Tm + (int64_t)cc * TILE, lane);
-            if (SWIGLU) copy_tile<TILE>(ring + (ST + cc % ST) * TILE, Tu + (int64_t)cc * TILE, lane);
-        }
-        cp_commit();
-    };
-#pragma unroll
-    for (int s0 = 0; s0 < ST - 1; s0++) issue(s0);
+    float *comb = reinterpret_cast<float *>(xs + a.xs_bytes + TableBytes<TYPE>::v);
+    float *red = reinterpret_cast<float *>(xs + a.xs_bytes + TableBytes<TYPE>::v + CombineBytes<NT, KH>::v);
 
     // codebooks -> shared memory (f16 entries; IQ2_XXS also the sign masks:
-    // 7 stored sign bits + even parity -> XOR masks on f16 pairs)
+    // 7 stored sign bits + even parity -> XOR masks on f16 pairs). Visible to
+    // all warps after the first activation barrier.
     if (TYPE == EF_IQ2_XXS) {
         const uint4 *src = reinterpret_cast<const uint4 *>(g_grid_iq2xxs_f16);
         for (int i = threadIdx.x; i < 256; i += blockDim.x) grid[i] = src[i];
@@ -627,114 +777,194 @@ __global__ void __launch_bounds__(WARPS * 32, MinBlocks<WARPS>::v) gemv_kernel(c
         for (int i = threadIdx.x; i < 2048; i += blockDim.x) grid[i] = src[i];
     }
 
+    const int nc = (int)a.nchunks, ks = a.kslices;
+    const int rb = blockIdx.x / ks, ksi = blockIdx.x - rb * ks;
+    const int c0 = (int)((int64_t)ksi * nc / ks), c1 = (int)((int64_t)(ksi + 1) * nc / ks);
+    int m = 0;
+    while (m + 1 < a.nmat && rb >= a.rb_end[m]) m++;
+    int64_t rg = (int64_t)(rb - (m ? a.rb_end[m - 1] : 0)) * W + wr;
+    const bool active = rg < a.rowgroups[m];
+
+    // ---- weight stream: this warp's chunks c0+kh, c0+kh+KH, ... < c1, each
+    // tile loaded into registers one tile ahead of the math
+    const int64_t tile0 = active ? (rg * nc + c0 + kh) * (int64_t)TILE : 0;
+    const uint8_t *ip = a.w[m] + tile0;
+    const uint8_t *ipu = SWIGLU ? a.w_up + tile0 : nullptr;
+    int ic = c0 + kh;
+    auto fetch = [&](Raw &r, Raw &ru) {
+        if (ic < c1 && active) {
+            load_raw(r, ip, lane);
+            if (SWIGLU) load_raw(ru, ipu, lane);
+            ip += KH * TILE;
+            if (SWIGLU) ipu += KH * TILE;
+        }
+        ic += KH;
+    };
+    Raw q0, q0u;
+    fetch(q0, q0u);
+
+    // ---- activation data ---------------------------------------------------
+    // whole: the slice's chunks staged once (1-2 tokens, when they fit); else
+    // phases of at most phase_chunks chunks, copied from the prep kernel's
+    // buffer one phase ahead into two alternating buffers (or, FUSED, staged
+    // in place). x is produced by the kernel before this one: with
+    // programmatic dependent launch, wait for it only now.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
+    auto copy_phase = [&](int c, uint8_t *dst) {   // prep buffer -> shared, async
+        const int len = min(a.phase_chunks, c1 - c);
+        const uint8_t *src = a.xf + (int64_t)c * FB;
+        for (int i = threadIdx.x; i < len * FB / 16; i += blockDim.x) cp_async16(dst + 16 * i, src + 16 * i);
+    };
+    int ph_i = 0;
+    if (a.whole) {
+        stage_x<TYPE>(a.x, a.M, a.K, c0, c1 - c0, xs, FB, threadIdx.x, blockDim.x);
+        __syncthreads();
+    } else if (!FUSED) {
+        copy_phase(c0, xs);
+        cp_commit();
+    }
+
     float acc[NT][4], acc2[NT][4];
 #pragma unroll
     for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-        for (int j = 0; j < 4; j++) acc[nt][j] = acc2[nt][j] = 0.f;
+        for (int i = 0; i < 4; i++) acc[nt][i] = acc2[nt][i] = 0.f;
 
-    // x is produced by the kernel before this one (the prep kernel, or the
-    // caller's previous kernel): wait for it only now, after the weight prefetch.
-    asm volatile("griddepcontrol.wait;" ::: "memory");
-    for (int p0 = 0; p0 < nc; p0 += a.phase_chunks) {
-        const int pc = min(a.phase_chunks, nc - p0);
-        if (p0) __syncthreads();   // every warp is done with the previous phase
-        if (FUSED) {
-            stage_x<TYPE>(a.x, a.M, a.K, c0 + p0, pc, xs, FB, threadIdx.x, blockDim.x);
+#pragma unroll 1
+    for (int p0 = c0; p0 < c1;) {    // activation phases
+        int p1;
+        const uint8_t *xbase;        // activation data of chunk p0
+        if (a.whole) {
+            p1 = c1;
+            xbase = xs;
         } else {
-            const uint8_t *src = a.xf + (int64_t)(c0 + p0) * FB;
-            for (int i = threadIdx.x; i < pc * FB / 16; i += blockDim.x) cp_async16(xs + 16 * i, src + 16 * i);
-            cp_commit();
-            cp_wait<0>();   // the x phase (and the weight tiles issued before it)
+            p1 = min(c1, p0 + a.phase_chunks);
+            __syncthreads();         // every warp is done with the previous phase
+            if (FUSED) {
+                stage_x<TYPE>(a.x, a.M, a.K, p0, p1 - p0, xs, FB, threadIdx.x, blockDim.x);
+                xbase = xs;
+            } else {
+                if (p1 < c1) copy_phase(p1, xs + ((ph_i + 1) & 1) * a.xs_half);
+                cp_commit();
+                cp_wait<1>();        // this thread's copies of this phase have landed
+                xbase = xs + (ph_i & 1) * a.xs_half;
+                ph_i++;
+            }
+            __syncthreads();
         }
-        __syncthreads();
-        for (int cl = 0; cl < pc; cl++) {
-            const int cc = p0 + cl;
-            __syncwarp();          // every lane is done reading the slot refilled next
-            issue(cc + ST - 1);
-            cp_wait<ST - 1>();     // this thread's copies of chunk cc have landed
-            __syncwarp();          // ... and every other lane's
+        // this warp's chunks of the phase: c = c0 + kh (mod KH)
+        int c = p0;
+        if (KH > 1) c += ((c0 + kh - p0) % KH + KH) % KH;
+#pragma unroll 1
+        for (; c < p1; c += KH) {
+            Raw r = q0, ru = q0u;
+            fetch(q0, q0u);          // the next tile's loads go out before this tile's math
             if (active) {
-                const uint8_t *xc = xs + cl * FB;
-                Raw r;
-                load_raw(r, ring + (cc % ST) * TILE, lane);
-                compute<NT>(r, xc, a.M, acc, lane, grid, sgn);
+                const uint8_t *xc = xbase + (c - (a.whole ? c0 : p0)) * FB;
+                if constexpr (TYPE == EF_Q4_K) compute_q4k<TQ, NT>(r, xc, acc, lane);
+                else compute<NT>(r, xc, a.M, acc, lane, grid, sgn);
                 if (SWIGLU) {
-                    Raw u;
-                    load_raw(u, ring + (ST + cc % ST) * TILE, lane);
-                    compute<NT>(u, xc, a.M, acc2, lane, grid, sgn);
+                    if constexpr (TYPE == EF_Q4_K) compute_q4k<TQ, NT>(ru, xc, acc2, lane);
+                    else compute<NT>(ru, xc, a.M, acc2, lane, grid, sgn);
                 }
             }
         }
+        p0 = p1;
     }
-    cp_wait<0>();
-    // The weight stream is done: the next kernel in the stream may launch now
-    // (programmatic dependent launch) and prefetch its weights while this one
-    // reduces and writes y. Triggering earlier lets waiting CTAs of the next
-    // kernel hold SM resources that this kernel still needs.
+    if (!FUSED) cp_wait<0>();
+    // The weight stream is done: with programmatic dependent launch the next
+    // kernel may start now.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
-    if (a.kslices == 1) {
-        if (active) write_out<NT, SWIGLU>(acc, acc2, a.y[m], a.rows[m], a.M, rg, lane);
-        return;
-    }
-    // k-slices of this rowblock are one cluster: add partials in rank order.
-    float *mine = red + ((warp * NMAT) * NT * 32 + lane) * 4;
+    // ---- the two warps of a rowgroup ----
+    if constexpr (KH == 2) {
+        float4 *cb = reinterpret_cast<float4 *>(comb) + (wr * 32 + lane) * NT;
+        if (kh == 1) {
 #pragma unroll
-    for (int mm = 0; mm < NMAT; mm++)
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) mine[((mm * NT + nt) * 32) * 4 + j] = mm ? acc2[nt][j] : acc[nt][j];
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    if (warp % a.kslices == ks && active) {
-        float s1[NT][4], s2[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; nt++)
-#pragma unroll
-            for (int j = 0; j < 4; j++) s1[nt][j] = s2[nt][j] = 0.f;
-        for (int rk = 0; rk < a.kslices; rk++) {
-            const float *src = cluster.map_shared_rank(mine, rk);
+            for (int nt = 0; nt < NT; nt++) cb[nt] = make_float4(acc[nt][0], acc[nt][1], acc[nt][2], acc[nt][3]);
+        }
+        asm volatile("bar.sync %0, 64;" ::"r"(1 + wr) : "memory");
+        if (kh == 0) {
 #pragma unroll
             for (int nt = 0; nt < NT; nt++) {
-                const float4 v = *reinterpret_cast<const float4 *>(src + (nt * 32) * 4);
-                s1[nt][0] += v.x; s1[nt][1] += v.y; s1[nt][2] += v.z; s1[nt][3] += v.w;
-                if (SWIGLU) {
-                    const float4 u = *reinterpret_cast<const float4 *>(src + ((NT + nt) * 32) * 4);
-                    s2[nt][0] += u.x; s2[nt][1] += u.y; s2[nt][2] += u.z; s2[nt][3] += u.w;
-                }
+                const float4 o = cb[nt];
+                acc[nt][0] += o.x;
+                acc[nt][1] += o.y;
+                acc[nt][2] += o.z;
+                acc[nt][3] += o.w;
             }
         }
-        write_out<NT, SWIGLU>(s1, s2, a.y[m], a.rows[m], a.M, rg, lane);
     }
-    cluster.sync();   // keep this CTA's shared memory alive until all ranks have read it
+    const int M = a.M;
+    const int64_t rows = a.rows[m];
+    float *y = a.y[m];
+    if (kh == 0 && active) {
+        reduce_cols<TQ, NT>(acc);
+        if (SWIGLU) reduce_cols<TQ, NT>(acc2);
+    }
+    if (ks == 1) {
+        if (kh == 0 && active)
+            for_owned<TQ, NT>(lane, [&](int nt, int i, int row, int tok) {
+                const int64_t r = rg * 16 + row;
+                if (tok < M && r < rows) y[(int64_t)tok * rows + r] = out_value<SWIGLU>(acc[nt][i], acc2[nt][i]);
+            });
+        return;
+    }
+    // ---- k-slices of this rowblock: one cluster, added in rank order ----
+    float *mine = red + wr * NMAT * 16 * 16;
+    if (kh == 0 && active)
+        for_owned<TQ, NT>(lane, [&](int nt, int i, int row, int tok) {
+            if (tok < M) {
+                mine[tok * 16 + row] = acc[nt][i];
+                if (SWIGLU) mine[256 + tok * 16 + row] = acc2[nt][i];
+            }
+        });
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    if (kh == 0 && active && wr % ks == ksi) {   // rowgroup wr is finished by rank wr % ks
+        for (int i = lane; i < 16 * M; i += 32) {
+            float s1 = 0.f, s2 = 0.f;
+            for (int rk = 0; rk < ks; rk++) {
+                const float *src = cluster.map_shared_rank(mine, rk);
+                s1 += src[i];
+                if (SWIGLU) s2 += src[256 + i];
+            }
+            const int64_t r = rg * 16 + (i & 15);
+            if (r < rows) y[(int64_t)(i >> 4) * rows + r] = out_value<SWIGLU>(s1, s2);
+        }
+    }
+    cluster.sync();                  // keep this CTA's shared memory alive until all ranks have read it
 }
 
 // ------------------------------------------------------------------ host ---
-// Pick the CTA shape. Measured on B200 (sweeps over width x k-split for the
-// benchmark shapes): long-lived warps that stream many tiles beat short CTAs
-// even when some SMs stay idle, because every CTA pays a pipeline start, an
-// activation staging and a cluster reduction. So: 8 rowgroups per CTA and the
-// smallest k-split that puts at least 3/4 of the SMs to work (4 rowgroups
-// when the rows are too few even for that).
-GemvPlan gemv_plan(int sm_count, int64_t rowgroups, int64_t nchunks, int M, const int ctas_per_sm[2]) {
-    (void)ctas_per_sm;
-    GemvPlan best = {};
+// Work split: CTA = 8 rowgroups (one rowblock) x one k-slice; the smallest
+// k-split that puts at least 3/4 of the SMs to work (at most 8, one cluster).
+// Measured on B200: splitting rowblocks further (stream-K over all SMs) or
+// adding rows per SM loses more to the cross-CTA reduction and the shorter
+// weight streams than it gains from the idle SMs. Activation data: with 1-2
+// tokens the slice's chunks at once when they fit, else phases (two buffers
+// when a prep kernel supplies the data).
+GemvPlan gemv_plan(int sm_count, int64_t rowblocks, int64_t nchunks, int xb, bool fused) {
+    GemvPlan p = {};
     const int64_t want = (3LL * sm_count + 3) / 4;
-    best.warps = 8;
-    int64_t rowblocks = (rowgroups + 7) / 8;
-    if (rowblocks * std::min<int64_t>(8, nchunks) < want) {
-        best.warps = 4;
-        rowblocks = (rowgroups + 3) / 4;
-    }
-    int64_t ks = 1;
+    int ks = 1;
     while (ks < 8 && ks < nchunks && rowblocks * ks < want) ks++;
-    best.cps = (int)((nchunks + ks - 1) / ks);
-    best.kslices = (int)((nchunks + best.cps - 1) / best.cps);
-    best.rowblocks = (int)rowblocks;
-    best.nt = M <= 8 ? 1 : 2;
-    return best;
+    p.kslices = ks;
+    p.ctas = rowblocks * ks;
+    const int64_t slice = (nchunks + ks - 1) / ks;
+    if (fused && slice * xb <= MAX_XS_BYTES) {
+        p.whole = 1;
+        p.phase_chunks = (int)slice;
+        p.xs_bytes = (int)(slice * xb);
+        p.xs_half = 0;
+    } else {
+        const int budget = fused ? MAX_XS_BYTES : MAX_XS_BYTES / 2;
+        p.whole = 0;
+        p.phase_chunks = (int)std::max<int64_t>(1, std::min<int64_t>(slice, budget / xb));
+        p.xs_half = p.phase_chunks * xb;
+        p.xs_bytes = fused ? p.xs_half : 2 * p.xs_half;
+    }
+    return p;
 }
 
 // Programmatic dependent launch between consecutive kernels: off by default
@@ -746,26 +976,28 @@ static bool gemv_pdl() {
     return v && v[0] == '1';
 }
 
-template <int TYPE, int NT, bool SWIGLU, int WARPS>
-static size_t smem_bytes(int phase_chunks, int xb, int kslices) {
-    constexpr int NMAT = SWIGLU ? 2 : 1;
-    return (size_t)WARPS * NMAT * Stages<TYPE, SWIGLU>::v * Tr<TYPE>::TILE + (size_t)phase_chunks * xb +
-           TableBytes<TYPE>::v + (kslices > 1 ? (size_t)WARPS * NMAT * NT * 32 * 16 : 0);
+// Warps per rowgroup: two (16-warp CTAs) where the kernel fits 128 registers
+// per thread, else one.
+template <int TYPE, int TQ, int NT, bool SWIGLU> constexpr int kh_of() {
+    return !SWIGLU && (NT == 1 || TYPE == EF_Q8_0) ? 2 : 1;
 }
 
-template <int TYPE, int NT, bool SWIGLU, int WARPS, bool FUSED>
-static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int grid_y) {
-    auto kern = gemv_kernel<TYPE, NT, SWIGLU, WARPS, FUSED>;
+template <int TYPE, int TQ, int NT, bool SWIGLU, bool FUSED>
+static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int64_t ctas) {
+    constexpr int KH = kh_of<TYPE, TQ, NT, SWIGLU>();
+    auto kern = gemv_kernel<TYPE, TQ, NT, SWIGLU, FUSED, KH>;
     static unsigned long long configured = 0;   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return check_cuda(ctx, e, "gemv smem attribute");
         configured |= 1ull << ctx->device;
     }
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.kslices, grid_y, 1);
-    cfg.blockDim = dim3(WARPS * 32, 1, 1);
-    cfg.dynamicSmemBytes = smem_bytes<TYPE, NT, SWIGLU, WARPS>(a.phase_chunks, a.xb, a.kslices);
+    cfg.gridDim = dim3((unsigned)ctas, 1, 1);
+    cfg.blockDim = dim3(GV_WARPS * KH * 32, 1, 1);
+    cfg.dynamicSmemBytes = gemv_smem<TYPE, NT, SWIGLU, KH>(a.xs_bytes, a.kslices > 1);
+    if (cfg.dynamicSmemBytes > 227 * 1024)
+        return set_err(ctx, EF_ERR_RANGE, "gemv: %zu bytes of shared memory needed", cfg.dynamicSmemBytes);
     cfg.stream = ctx->stream;
     cudaLaunchAttribute attr[2];
     int na = 0;
@@ -783,29 +1015,31 @@ static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int grid_y) {
     }
     cfg.attrs = attr;
     cfg.numAttrs = na;
+    ctx->launches++;
     return check_cuda(ctx, cudaLaunchKernelEx(&cfg, kern, a), "gemv launch");
 }
 
-// Up to this many tokens each CTA stages its own x slice (one kernel per
-// call); above it a prep kernel writes the slices once into context scratch.
+// Up to this many tokens each CTA stages its own activation data (one kernel
+// per call); above it a prep kernel writes the data once into context scratch.
 constexpr int FUSED_MAX_TOKENS = 2;
 
 template <int TYPE> static int x_bytes_per_chunk(int M) {
     return Tr<TYPE>::I8 ? i8_xbytes(M) : f16_xbytes<TYPE>(M);
 }
 
-template <int TYPE, int NT, bool SWIGLU>
+template <int TYPE, int TQ, int NT, bool SWIGLU>
 static int launch_t(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n, const float *x) {
     a.xb = x_bytes_per_chunk<TYPE>(a.M);
     a.x = x;
     a.K = ws[0]->k;
-    const bool fused = NT == 1 && a.M <= FUSED_MAX_TOKENS;
+    const bool fused = a.M <= FUSED_MAX_TOKENS;
     if (!fused) {
-        // x data for all chunks -> context scratch slot 0 (prep kernel, PDL)
+        // activation data for all chunks -> context scratch slot 0
         const size_t xbytes = (size_t)a.nchunks * a.xb;
         if (int rc = ensure_scratch(ctx, 0, xbytes)) return rc;
         a.xf = (const uint8_t *)ctx->scratch[0];
-        const int64_t work = Tr<TYPE>::I8 ? a.nchunks * a.M * 32 : a.nchunks * a.M * (Tr<TYPE>::CHUNK / 4);
+        const int64_t work = Tr<TYPE>::I8 ? a.nchunks * q4_tq(a.M) * q4_nt(a.M) * 32
+                                          : a.nchunks * a.M * (Tr<TYPE>::CHUNK / 4);
         int64_t blocks = (work + 255) / 256;
         if (blocks > 2LL * ctx->sm_count) blocks = 2LL * ctx->sm_count;
         cudaLaunchConfig_t cfg = {};
@@ -817,52 +1051,45 @@ static int launch_t(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n,
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
         cfg.numAttrs = gemv_pdl() ? 1 : 0;
+        ctx->launches++;
         if (int rc = check_cuda(ctx, cudaLaunchKernelEx(&cfg, gemv_xprep<TYPE>, x, a.M, a.K, a.nchunks, a.xb,
                                                         (uint8_t *)ctx->scratch[0]), "gemv xprep launch"))
             return rc;
     } else {
         a.xf = nullptr;
     }
-    // how many CTAs of each width fit on one SM, then the cost model
-    const int ph = std::max(1, std::min(8, MAX_XS_BYTES / a.xb));
-    const int fit8 = (int)std::min<size_t>(2, 227 * 1024 / (smem_bytes<TYPE, NT, SWIGLU, 8>(ph, a.xb, 2) + 1024));
-    const int fit4 = (int)std::min<size_t>(4, 227 * 1024 / (smem_bytes<TYPE, NT, SWIGLU, 4>(ph, a.xb, 2) + 1024));
-    const int fits[2] = {std::max(fit8, 1), std::max(fit4, 1)};
-    int64_t total_rg = 0;
-    for (int i = 0; i < n; i++) total_rg += ws[i]->rowgroups;
-    GemvPlan p = gemv_plan(ctx->sm_count, total_rg, a.nchunks, a.M, fits);
-    // Tuning override for sweeps: EF_GEMV_PLAN="W:ks" (W = 4 or 8 rowgroups per
-    // CTA, ks = k-slices, 1..8); ignored when it does not fit the shape.
-    if (const char *ov = getenv("EF_GEMV_PLAN")) {
-        int W = 0, ks = 0;
-        if (sscanf(ov, "%d:%d", &W, &ks) == 2 && (W == 4 || W == 8) && ks >= 1 && ks <= 8 && ks <= a.nchunks) {
-            p.warps = W;
-            p.cps = (int)((a.nchunks + ks - 1) / ks);
-            p.kslices = (int)((a.nchunks + p.cps - 1) / p.cps);
-        }
-    }
-    a.cps = p.cps;
-    a.kslices = p.kslices;
-    a.phase_chunks = std::min(a.cps, MAX_XS_BYTES / a.xb);
-    if (a.phase_chunks < 1) a.phase_chunks = 1;
-    int grid_y = 0;
+    int rowblocks = 0;
     for (int i = 0; i < n; i++) {
-        grid_y += (int)((ws[i]->rowgroups + p.warps - 1) / p.warps);
-        a.rb_end[i] = grid_y;
+        rowblocks += (int)((ws[i]->rowgroups + GV_WARPS - 1) / GV_WARPS);
+        a.rb_end[i] = rowblocks;
     }
-    if (fused)
-        return p.warps == 8 ? launch_kernel<TYPE, NT, SWIGLU, 8, true>(ctx, a, grid_y)
-                            : launch_kernel<TYPE, NT, SWIGLU, 4, true>(ctx, a, grid_y);
-    return p.warps == 8 ? launch_kernel<TYPE, NT, SWIGLU, 8, false>(ctx, a, grid_y)
-                        : launch_kernel<TYPE, NT, SWIGLU, 4, false>(ctx, a, grid_y);
+    const GemvPlan p = gemv_plan(ctx->sm_count, rowblocks, a.nchunks, a.xb, fused);
+    a.kslices = p.kslices;
+    a.phase_chunks = p.phase_chunks;
+    a.whole = p.whole;
+    a.xs_bytes = p.xs_bytes;
+    a.xs_half = p.xs_half;
+    // (1-2 tokens run TQ <= 2 for Q4_K and one 8-token tile for the others)
+    if constexpr (NT == 1 && (TYPE != EF_Q4_K || TQ <= 2))
+        if (fused) return launch_kernel<TYPE, TQ, NT, SWIGLU, true>(ctx, a, p.ctas);
+    return launch_kernel<TYPE, TQ, NT, SWIGLU, false>(ctx, a, p.ctas);
+}
+
+template <int TYPE, bool SWIGLU>
+static int launch_type(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n, const float *x) {
+    const int M = a.M;
+    if constexpr (TYPE == EF_Q4_K) {
+        if (M <= 1) return launch_t<TYPE, 1, 1, SWIGLU>(ctx, a, ws, n, x);
+        if (M <= 2) return launch_t<TYPE, 2, 1, SWIGLU>(ctx, a, ws, n, x);
+        if (M <= 4) return launch_t<TYPE, 4, 1, SWIGLU>(ctx, a, ws, n, x);
+    }
+    if (M <= 8) return launch_t<TYPE, 8, 1, SWIGLU>(ctx, a, ws, n, x);
+    return launch_t<TYPE, 8, 2, SWIGLU>(ctx, a, ws, n, x);
 }
 
 template <int TYPE>
-static int launch_type(ef_ctx *ctx, GemvArgs &a, int nt, bool swiglu, const ef_weight *const *ws, int n,
-                       const float *x) {
-    if (swiglu)
-        return nt == 1 ? launch_t<TYPE, 1, true>(ctx, a, ws, n, x) : launch_t<TYPE, 2, true>(ctx, a, ws, n, x);
-    return nt == 1 ? launch_t<TYPE, 1, false>(ctx, a, ws, n, x) : launch_t<TYPE, 2, false>(ctx, a, ws, n, x);
+static int launch_sw(ef_ctx *ctx, GemvArgs &a, bool sw, const ef_weight *const *ws, int n, const float *x) {
+    return sw ? launch_type<TYPE, true>(ctx, a, ws, n, x) : launch_type<TYPE, false>(ctx, a, ws, n, x);
 }
 
 int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight *w_up, const float *x, int M,
@@ -880,16 +1107,16 @@ int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight 
     a.M = M;
     a.nchunks = w0->nchunks;
     const bool sw = w_up != nullptr;
-    const int nt = M <= 8 ? 1 : 2;
     switch (w0->type) {
-    case EF_Q8_0: return launch_type<EF_Q8_0>(ctx, a, nt, sw, ws, n, x);
-    case EF_Q4_K: return launch_type<EF_Q4_K>(ctx, a, nt, sw, ws, n, x);
-    case EF_Q6_K: return launch_type<EF_Q6_K>(ctx, a, nt, sw, ws, n, x);
-    case EF_IQ2_XXS: return launch_type<EF_IQ2_XXS>(ctx, a, nt, sw, ws, n, x);
-    case EF_IQ1_S: return launch_type<EF_IQ1_S>(ctx, a, nt, sw, ws, n, x);
+    case EF_Q8_0: return launch_sw<EF_Q8_0>(ctx, a, sw, ws, n, x);
+    case EF_Q4_K: return launch_sw<EF_Q4_K>(ctx, a, sw, ws, n, x);
+    case EF_Q6_K: return launch_sw<EF_Q6_K>(ctx, a, sw, ws, n, x);
+    case EF_IQ2_XXS: return launch_sw<EF_IQ2_XXS>(ctx, a, sw, ws, n, x);
+    case EF_IQ1_S: return launch_sw<EF_IQ1_S>(ctx, a, sw, ws, n, x);
     default: return set_err(ctx, EF_ERR_TYPE, "gemv: unsupported type %d", w0->type);
     }
 }
+
 
 }  // namespace ef
 

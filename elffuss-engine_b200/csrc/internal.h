@@ -32,18 +32,19 @@ struct ef_ctx {
     std::vector<ef_buf *> pool;       // live ef_alloc buffers, in allocation order
     uint64_t seq = 0;
     // Persistent device scratch owned by the context (grown on demand):
-    // slot 0 holds the GEMV's f16 activation fragments, slot 1 the GEMM's
-    // converted activations. A first call of a new, larger shape grows them
+    // slot 0 holds the GEMV's activation data, slot 1 the GEMM's converted
+    // activations. A first call of a new, larger shape grows them
     // (cudaMalloc), so that call must come before any stream capture.
     void *scratch[2] = {nullptr, nullptr};
     size_t scratch_bytes[2] = {0, 0};
+    uint64_t launches = 0;            // kernels this context has launched (diagnostic counter)
 };
 
 namespace ef {
 
 int set_err(ef_ctx *ctx, int code, const char *fmt, ...);
 int check_cuda(ef_ctx *ctx, cudaError_t e, const char *what);
-int ensure_scratch(ef_ctx *ctx, int slot, size_t bytes);
+int ensure_scratch(ef_ctx *ctx, int slot, size_t bytes, bool zero = false);
 
 // weights.cu
 int launch_repack(ef_ctx *ctx, int type, const uint8_t *dev_gguf, int64_t rows, int64_t k,
@@ -53,13 +54,14 @@ int launch_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows,
 
 // gemv.cu
 struct GemvPlan {
-    int kslices;    // CTAs along k (one thread-block cluster)
-    int cps;        // chunks per k-slice
-    int rowblocks;  // CTAs along rows (8 rowgroups = 128 rows each)
-    int nt;         // 8-token tiles (1 or 2)
-    int warps;      // rowgroups (warps) per CTA
+    int64_t ctas;      // rowblocks x kslices
+    int kslices;       // CTAs (one cluster) per rowblock, each a contiguous k-slice
+    int phase_chunks;  // chunks of activation data staged in shared memory at a time
+    int whole;         // 1: the slice's chunks staged once at the start
+    int xs_bytes;      // shared memory for activation data
+    int xs_half;       // bytes of one phase buffer
 };
-GemvPlan gemv_plan(int sm_count, int64_t rowgroups, int64_t nchunks, int M, const int ctas_per_sm[2]);
+GemvPlan gemv_plan(int sm_count, int64_t rowblocks, int64_t nchunks, int xb, bool fused);
 int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight *w_up,
                 const float *x, int M, float *const *ys);
 

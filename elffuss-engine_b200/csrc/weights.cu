@@ -92,6 +92,7 @@ int launch_repack(ef_ctx *ctx, int type, const uint8_t *dev_gguf, int64_t rows, 
     const int bpc = geo.chunk_k / geo.block_elems;
     const int64_t bpr = k / geo.block_elems;
     const int64_t total = w->rowgroups * RG_ROWS * w->nchunks * bpc;
+    ctx->launches++;
     repack_kernel<<<grid_for(total), 256, 0, ctx->stream>>>(type, dev_gguf, rows, bpr, w->rowgroups,
                                                             w->nchunks, bpc, geo.block_bytes,
                                                             geo.tile_bytes, w->dev);
@@ -103,6 +104,7 @@ int launch_unpack(ef_ctx *ctx, const ef_weight *w, uint8_t *dev_gguf) {
     geo_of(w->type, geo);
     const int bpc = geo.chunk_k / geo.block_elems;
     const int64_t bpr = w->k / geo.block_elems;
+    ctx->launches++;
     unpack_kernel<<<grid_for(w->rows * bpr), 256, 0, ctx->stream>>>(
         w->type, w->dev, w->rows, bpr, w->nchunks, bpc, geo.block_bytes, geo.tile_bytes, dev_gguf);
     return check_cuda(ctx, cudaGetLastError(), "unpack launch");
@@ -114,6 +116,7 @@ int launch_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows,
     const int bpc = geo.chunk_k / geo.block_elems;
     const int64_t bpr = w->k / geo.block_elems;
     // 256 f32 + 256 bytes of local state per thread: keep blocks small.
+    ctx->launches++;
     dequant_kernel<<<grid_for(nrows * bpr), 128, 0, ctx->stream>>>(
         w->type, w->dev, row0, nrows, bpr, w->nchunks, bpc, geo.block_bytes, geo.block_elems,
         geo.tile_bytes, w->k, out);

@@ -91,6 +91,11 @@ EF_API int ef_stream_sync(ef_ctx *ctx);
 /* Message of the last failing call on this context ("" if none). */
 EF_API const char *ef_last_error(const ef_ctx *ctx);
 
+/* Number of kernels this context has launched so far (host-side counter,
+ * incremented at every launch; launches recorded into a CUDA graph count once,
+ * at capture). Diagnostic only: no counterpart in the reference. */
+EF_API uint64_t ef_ctx_launch_count(const ef_ctx *ctx);
+
 /* ---- buffers (ctx.alloc / recycle / upload, js/ops.js:242-307,1129-1133) --- */
 
 EF_API int ef_alloc(ef_ctx *ctx, size_t bytes, ef_buf **out);
@@ -169,8 +174,9 @@ EF_API int ef_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, i
  * allocator or a fixed arena). This variant uses a file-scope device array of
  * 1 MiB instead, held by every GPU that loads the library until the process
  * exits; it supports k up to the point where the activation data exceeds
- * 1 MiB (k up to about 31,000 for 9-16 tokens and 63,000 for 1-8 tokens)
- * and returns EF_ERR_RANGE beyond that. No context is needed: work is queued on
+ * 1 MiB (k up to about 30,000 for 9-16 tokens and 61,000 for 3-8 tokens;
+ * 1-2 tokens keep it in shared memory and have no limit) and returns
+ * EF_ERR_RANGE beyond that. No context is needed: work is queued on
  * `cuda_stream` (NULL = default stream) of the current device, which must be
  * the device `w` was loaded on. The first call on a device looks up the
  * array's device address (cudaGetSymbolAddress); make that first call before
