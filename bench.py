@@ -65,11 +65,11 @@ def peaks():
 
 
 def profile_traffic():
-    """dram read+write bytes per GEMV launch from the committed ncu summary."""
-    path = os.path.join(ROOT, "profiles", "gemv_ksweep_ncu.md")
+    """DRAM read+write bytes of one step's 12 GEMV launches, from the committed ncu launch list."""
+    path = os.path.join(ROOT, "profiles", "gemv_ksweep_launches.md")
     try:
         for line in open(path):
-            if line.startswith("traffic_bytes_per_launch:"):
+            if line.startswith("traffic_bytes_per_step:"):
                 return float(line.split(":", 1)[1])
     except OSError:
         pass
@@ -341,7 +341,9 @@ def run_ours(args):
                        "parallelism": f"weak x{world} (independent tensors per rank)"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "traffic": profile_traffic(), "kernel": "gemv_kernel (all 12 launches)"},
+                         "traffic": profile_traffic(), "algorithmic_bytes": step_bytes,
+                         "per": "one step = the 12 gemv_kernel launches (sum of bytes / sum of launch times)",
+                         "kernel": "gemv_kernel"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps * launches_per_step,
