@@ -3,21 +3,27 @@
 //   y[t][r] = sum_k f16(dequant(W)[r][k]) * f16(x[t][k])      f32 accumulate
 //
 // The reference's prefill kernel (GEMM2 "exacto", js/kernels.gemm2.wgsl.js:
-// 12-23,174-240) dequantises a tile of W to f16 in shared memory and
-// multiplies it with f16 activations, accumulating in f32. Here the same
-// contract runs as a tcgen05 pipeline:
+// 12-23,174-240) dequantises a tile of W to f16 and multiplies it with f16
+// activations, accumulating in f32. Here the same contract runs as a tcgen05
+// pipeline. CTA tile: 128 weight rows (MMA M) x 256 tokens (MMA N).
 //
 //   producer (1 thread):  cp.async.bulk of the repacked weight tiles (8
-//                         rowgroup tiles of 2176 B = 128 rows x 128 k) and a
-//                         TMA load (128B swizzle, no multicast) of the f16
-//                         activation tile, completing on one mbarrier;
-//   dequant (4 warps):    one thread per weight row expands its 128 quants to
-//                         f16(d*q) and writes them in the K-major 128B-swizzle
-//                         layout the MMA reads (A operand, double-buffered);
-//   MMA (1 thread):       tcgen05.mma.kind::f16, M=128 (weight rows) x N=BN
-//                         (tokens) x K=16, accumulator in tensor memory;
+//                         rowgroup tiles of 2176 B = 128 rows x 128 k, 2
+//                         stages) and TMA loads (128B swizzle, no multicast)
+//                         of the f16 activations, 64 k x 256 tokens per stage
+//                         (4 stages);
+//   dequant (4 warps):    thread = weight row = tensor-memory lane; expands
+//                         its 128 quants per weight tile to f16(d*q) and
+//                         stores them into tensor memory (tcgen05.st), where
+//                         the MMA reads the A operand (double-buffered);
+//   MMA (1 thread):       tcgen05.mma.kind::f16, A from tensor memory, B from
+//                         shared memory, M=128 x N=256 x K=16, accumulator in
+//                         tensor memory (256 columns);
 //   epilogue (4 warps):   tcgen05.ld of the accumulator, coalesced f32 stores
 //                         of y[token][row].
+// Keeping A out of shared memory leaves shared-memory bandwidth to the TMA
+// writes and the MMA's B reads: about 160 B/clock per SM at full tensor rate
+// against 420 for an A operand staged in shared memory at N=128.
 // Every wait on an mbarrier is bounded: past the limit the kernel records an
 // error code, stops issuing work and still releases its tensor memory.
 #include <cuda.h>
@@ -30,7 +36,11 @@
 namespace ef {
 
 constexpr int GM_BM = 128;     // weight rows per CTA tile (MMA M)
-constexpr int GM_BK = 128;     // k per pipeline step (one Q8_0 rowgroup tile)
+constexpr int GM_BN = 256;     // tokens per CTA tile (MMA N)
+constexpr int GM_BKW = 128;    // k per weight stage (one Q8_0 rowgroup tile)
+constexpr int GM_BKX = 64;     // k per activation stage (one 128-byte swizzle atom)
+constexpr int GM_SW = 2;       // weight stages
+constexpr int GM_SX = 4;       // activation stages
 constexpr int GM_THREADS = 192;
 constexpr uint32_t GM_WAIT_LIMIT = 1u << 24;   // try_wait polls before giving up (about a second)
 
@@ -76,35 +86,59 @@ __device__ __forceinline__ void umma_commit(uint64_t *bar) {
                  : "memory");
 }
 
-template <int BN>
+__device__ __forceinline__ void umma_f16_ts(uint32_t dtmem, uint32_t atmem, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(dtmem),
+        "r"(atmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// 16 consecutive 32-bit tensor-memory columns of this thread's lane
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+        "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+        : "memory");
+}
+
+// Tensor memory: accumulator in columns [0, 256), A buffers in [256, 320) and
+// [320, 384) (128 k of f16 pairs each); 512 columns allocated.
+constexpr uint32_t GM_TMEM_COLS = 512;
+constexpr uint32_t GM_TMEM_A = 256;
+
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_q8_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
-    constexpr int S = 3;                                 // raw (W + X) pipeline stages
     constexpr int WRAW = 8 * 2176;                       // 8 rowgroup tiles
-    constexpr int XBYTES = 2 * BN * 128;                 // two 64-k boxes of BN rows x 128 B
-    constexpr int ABYTES = 2 * GM_BM * 128;              // two 64-k atoms of 128 rows x 128 B
-    constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
+    constexpr int XBYTES = GM_BN * 128;                  // one 64-k box of 256 rows x 128 B
+    constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(GM_BN >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    // 1024-byte alignment for the swizzled operand tiles
+    // 1024-byte alignment for the swizzled activation tiles
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint8_t *xs = smem;                                  // S x XBYTES
-    uint8_t *as = xs + S * XBYTES;                       // 2 x ABYTES
-    uint8_t *ws = as + 2 * ABYTES;                       // S x WRAW
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ws + S * WRAW);
-    uint64_t *full = bars, *empty = bars + S, *afull = bars + 2 * S, *aempty = bars + 2 * S + 2;
-    uint64_t *tfull = bars + 2 * S + 4;
-    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
+    uint8_t *xs = smem;                                  // GM_SX x XBYTES
+    uint8_t *ws = xs + GM_SX * XBYTES;                   // GM_SW x WRAW
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ws + GM_SW * WRAW);
+    uint64_t *xfull = bars, *xempty = bars + GM_SX;
+    uint64_t *wfull = bars + 2 * GM_SX, *wempty = bars + 2 * GM_SX + GM_SW;
+    uint64_t *afull = bars + 2 * GM_SX + 2 * GM_SW, *aempty = afull + 2, *tfull = afull + 4;
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(tfull + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t rb = blockIdx.x;                       // 8 rowgroups = 128 rows
-    const int n0 = blockIdx.y * BN;                      // first token
-    const int nk = (int)nchunks;
+    const int n0 = blockIdx.y * GM_BN;                   // first token
+    const int nk = (int)nchunks;                         // weight tiles along k
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < S; s++) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+        for (int s = 0; s < GM_SX; s++) {
+            mbar_init(&xfull[s], 1);
+            mbar_init(&xempty[s], 1);
+        }
+        for (int s = 0; s < GM_SW; s++) {
+            mbar_init(&wfull[s], 1);
+            mbar_init(&wempty[s], 128);
         }
         for (int b = 0; b < 2; b++) {
             mbar_init(&afull[b], 128);
@@ -113,9 +147,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         mbar_init(tfull, 1);
         mbar_init_fence();
     }
-    if (warp == 1) {   // tensor memory: BN f32 columns x 128 lanes
+    if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tslot)),
-                     "r"(BN)
+                     "r"(GM_TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -128,87 +162,123 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     if (warp == 0) {
         if (lane == 0) {   // ---------------------------------------- producer
             const int64_t nrg = rowgroups - rb * 8 < 8 ? rowgroups - rb * 8 : 8;
-            const uint32_t tx = (uint32_t)(nrg * 2176 + XBYTES);
-            for (int ks = 0; ks < nk && ok; ks++) {
-                const int s = ks % S;
-                if (ks >= S) ok = mbar_wait(&empty[s], ((ks / S) - 1) & 1);
+            int wi = 0, xi = 0;                          // copies issued
+            for (int kk = 0; kk < nk && ok; kk++) {
+                const int sw = kk % GM_SW;
+                if (kk >= GM_SW) ok = mbar_wait(&wempty[sw], ((kk / GM_SW) - 1) & 1);
                 if (!ok) break;
-                mbar_expect_tx(&full[s], tx);
+                mbar_expect_tx(&wfull[sw], (uint32_t)(nrg * 2176));
                 for (int i = 0; i < nrg; i++)
-                    bulk_g2s(ws + s * WRAW + i * 2176, W + ((rb * 8 + i) * nchunks + ks) * 2176, 2176, &full[s]);
-                tma_2d(xs + s * XBYTES, &xmap, ks * GM_BK, n0, &full[s]);
-                tma_2d(xs + s * XBYTES + BN * 128, &xmap, ks * GM_BK + 64, n0, &full[s]);
+                    bulk_g2s(ws + sw * WRAW + i * 2176, W + ((rb * 8 + i) * nchunks + kk) * 2176, 2176, &wfull[sw]);
+                wi++;
+                for (int h = 0; h < 2 && ok; h++) {
+                    const int xsi = 2 * kk + h, sx = xsi % GM_SX;
+                    if (xsi >= GM_SX) ok = mbar_wait(&xempty[sx], ((xsi / GM_SX) - 1) & 1);
+                    if (!ok) break;
+                    mbar_expect_tx(&xfull[sx], XBYTES);
+                    tma_2d(xs + sx * XBYTES, &xmap, kk * GM_BKW + h * GM_BKX, n0, &xfull[sx]);
+                    xi++;
+                }
+            }
+            if (!ok) {   // a wait gave up: let this thread's copies still in flight land first
+                for (int j = wi > GM_SW ? wi - GM_SW : 0; j < wi; j++)
+                    mbar_wait_bounded(&wfull[j % GM_SW], (j / GM_SW) & 1, GM_WAIT_LIMIT);
+                for (int j = xi > GM_SX ? xi - GM_SX : 0; j < xi; j++)
+                    mbar_wait_bounded(&xfull[j % GM_SX], (j / GM_SX) & 1, GM_WAIT_LIMIT);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {   // --------------------------------------------- MMA
-            for (int ks = 0; ks < nk && ok; ks++) {
-                const int s = ks % S, b = ks & 1;
-                ok = mbar_wait(&full[s], (ks / S) & 1) && mbar_wait(&afull[b], (ks >> 1) & 1);
+            for (int kk = 0; kk < nk && ok; kk++) {
+                const int b = kk & 1;
+                ok = mbar_wait(&afull[b], (kk >> 1) & 1);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(as + b * ABYTES), b0 = smem_u32(xs + s * XBYTES);
+                const uint32_t abuf = tmem + GM_TMEM_A + 64 * b;
+                for (int h = 0; h < 2 && ok; h++) {
+                    const int xsi = 2 * kk + h, sx = xsi % GM_SX;
+                    ok = mbar_wait(&xfull[sx], (xsi / GM_SX) & 1);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t b0 = smem_u32(xs + sx * XBYTES);
 #pragma unroll
-                for (int j = 0; j < GM_BK / 16; j++) {
-                    const uint32_t ao = (j >> 2) * (GM_BM * 128) + (j & 3) * 32;
-                    const uint32_t bo = (j >> 2) * (BN * 128) + (j & 3) * 32;
-                    umma_f16(tmem, sw128_desc(a0 + ao), sw128_desc(b0 + bo), IDESC, (ks | j) != 0);
+                    for (int j = 0; j < GM_BKX / 16; j++)
+                        umma_f16_ts(tmem, abuf + 32 * h + 8 * j, sw128_desc(b0 + 32 * j), IDESC, (kk | h | j) != 0);
+                    umma_commit(&xempty[sx]);   // activation stage reusable when these MMAs finish
                 }
-                umma_commit(&empty[s]);    // X (and W raw) stage reusable when these MMAs finish
-                umma_commit(&aempty[b]);   // A buffer reusable
+                umma_commit(&aempty[b]);       // A buffer reusable
             }
-            umma_commit(tfull);            // accumulator complete
+            umma_commit(tfull);                // accumulator complete
         }
     } else {
-        // ------------------------------------------------ dequant (128 threads)
-        const int r = threadIdx.x - 64;                  // weight row within the tile
+        // ---------------------------------------- dequant (4 warps = 128 rows)
+        // Thread = weight row r = tensor-memory lane: warp w owns lanes
+        // 32*(w%4) .. +31. Row r of the tile is row g + 8hs of rowgroup r>>4;
+        // its block t (32 quants) is two 16-byte parts of fragment lane 4g+t
+        // and its f16 scale sits at 2048 + 4(4g+t) + 2hs. The four blocks are
+        // read in a lane-staggered order, so one 128-bit shared load by the 32
+        // lanes touches each bank group four times (no conflicts).
+        const int quad = warp & 3;
+        const int r = quad * 32 + lane;
         const int rl = r & 15, g = rl & 7, hs = rl >> 3, rg_in = r >> 4;
         const bool have = rb * 8 + rg_in < rowgroups;
-        for (int ks = 0; ks < nk && ok; ks++) {
-            const int s = ks % S, b = ks & 1;
-            ok = mbar_wait(&full[s], (ks / S) & 1);
-            if (ok && ks >= 2) ok = mbar_wait(&aempty[b], ((ks >> 1) - 1) & 1);
+        const uint32_t tlane = (uint32_t)(quad * 32) << 16;
+        for (int kk = 0; kk < nk && ok; kk++) {
+            const int sw = kk % GM_SW, b = kk & 1;
+            ok = mbar_wait(&wfull[sw], (kk / GM_SW) & 1);
+            if (ok && kk >= 2) ok = mbar_wait(&aempty[b], ((kk >> 1) - 1) & 1);
             if (!ok) break;
-            const uint8_t *T = ws + s * WRAW + rg_in * 2176;
-            uint8_t *A = as + b * ABYTES;
+            tc_fence_after();
+            const uint8_t *T = ws + sw * WRAW + rg_in * 2176;
+            uint4 q0[4], q1[4];
+            uint32_t sc[4];
 #pragma unroll
-            for (int t = 0; t < 4; t++) {   // block t of the row: k = 32t .. 32t+31
-                uint4 q0 = make_uint4(0, 0, 0, 0), q1 = q0;
-                uint32_t dd = 0;
+            for (int i = 0; i < 4; i++) {
+                const int t = (i + (lane >> 1)) & 3;
                 if (have) {
-                    q0 = *reinterpret_cast<const uint4 *>(T + (2 * hs) * 512 + (4 * g + t) * 16);
-                    q1 = *reinterpret_cast<const uint4 *>(T + (2 * hs + 1) * 512 + (4 * g + t) * 16);
-                    const uint32_t sc = *reinterpret_cast<const uint32_t *>(T + 2048 + (4 * g + t) * 4);
-                    dd = prmt(sc, 0, hs ? 0x3232 : 0x1010);   // (d, d)
-                }
-                const uint32_t w[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
-                uint32_t h[16];
-#pragma unroll
-                for (int i = 0; i < 8; i++) {   // 4 quants (biased by 128) -> 2 x half2 f16(d*q)
-                    h[2 * i] = hmul2u(hsub2u(prmt(w[i], 0x64646464u, 0x5140), 0x64806480u), dd);
-                    h[2 * i + 1] = hmul2u(hsub2u(prmt(w[i], 0x64646464u, 0x7362), 0x64806480u), dd);
-                }
-                // 32 f16 = four 16-byte chunks at k = 32t .. 32t+31: atom t>>1,
-                // chunk (4*(t&1) + c) XOR (row & 7) of the row's 128 bytes
-                uint8_t *rowp = A + (t >> 1) * (GM_BM * 128) + (r >> 3) * 1024 + (r & 7) * 128;
-#pragma unroll
-                for (int c = 0; c < 4; c++) {
-                    const int chunk = (4 * (t & 1) + c) ^ (r & 7);
-                    *reinterpret_cast<uint4 *>(rowp + chunk * 16) =
-                        make_uint4(h[4 * c], h[4 * c + 1], h[4 * c + 2], h[4 * c + 3]);
+                    q0[i] = *reinterpret_cast<const uint4 *>(T + (2 * hs) * 512 + (4 * g + t) * 16);
+                    q1[i] = *reinterpret_cast<const uint4 *>(T + (2 * hs + 1) * 512 + (4 * g + t) * 16);
+                    sc[i] = *reinterpret_cast<const uint32_t *>(T + 2048 + (4 * g + t) * 4);
+                } else {
+                    q0[i] = q1[i] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
+                    sc[i] = 0;
                 }
             }
-            fence_proxy_async();   // generic-proxy writes -> visible to the tensor core
+            mbar_arrive(&wempty[sw]);          // raw tile consumed (in registers)
+            const uint32_t abuf = tmem + tlane + GM_TMEM_A + 64 * b;
+            // tcgen05.st takes one column address for the whole warp: block t
+            // is stored by all lanes at once, each picking it from the slot
+            // its staggered load order put it in (i = (t - stagger) mod 4).
+            const int stg = (lane >> 1) & 3;
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                uint4 a0 = q0[t & 3], a1 = q1[t & 3];
+                uint32_t sct = sc[t & 3];
+                if (stg == 1) { a0 = q0[(t + 3) & 3]; a1 = q1[(t + 3) & 3]; sct = sc[(t + 3) & 3]; }
+                if (stg == 2) { a0 = q0[(t + 2) & 3]; a1 = q1[(t + 2) & 3]; sct = sc[(t + 2) & 3]; }
+                if (stg == 3) { a0 = q0[(t + 1) & 3]; a1 = q1[(t + 1) & 3]; sct = sc[(t + 1) & 3]; }
+                const uint32_t dd = prmt(sct, 0, hs ? 0x3232 : 0x1010);   // (d, d)
+                const uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+                uint32_t h[16];
+#pragma unroll
+                for (int j = 0; j < 8; j++) {   // 4 quants (biased by 128) -> 2 x half2 f16(d*q)
+                    h[2 * j] = hmul2u(hsub2u(prmt(w[j], 0x64646464u, 0x5140), 0x64806480u), dd);
+                    h[2 * j + 1] = hmul2u(hsub2u(prmt(w[j], 0x64646464u, 0x7362), 0x64806480u), dd);
+                }
+                tmem_st16(abuf + 16 * t, h);   // k = 32t .. 32t+31 as 16 f16 pairs
+            }
+            asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+            tc_fence_before();
             mbar_arrive(&afull[b]);
         }
         // ------------------------------------------------------------ epilogue
         if (ok) ok = mbar_wait(tfull, 0);
         tc_fence_after();
         if (ok) {
-            const int quad = warp & 3;                   // TMEM lanes 32*quad .. +31
             const int64_t row = rb * GM_BM + quad * 32 + lane;
 #pragma unroll 1
-            for (int c0 = 0; c0 < BN; c0 += 32) {
+            for (int c0 = 0; c0 < GM_BN; c0 += 32) {
+                if (n0 + c0 >= M) break;
                 uint32_t v[32];
                 asm volatile(
                     "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
@@ -218,7 +288,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                       "=r"(v[14]), "=r"(v[15]), "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]),
                       "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]),
                       "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-                    : "r"(tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)c0));
+                    : "r"(tmem + tlane + (uint32_t)c0));
                 asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
                 if (row < rows) {
 #pragma unroll
@@ -234,7 +304,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(GM_TMEM_COLS) : "memory");
     }
 }
 
@@ -265,27 +335,24 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-template <int BN> static size_t gemm_smem() {
-    static_assert(BN == 128, "the 256-token tile does not fit 227 KB of shared memory with this pipeline");
-    constexpr int S = 3;
-    return 1024 + (size_t)S * (2 * BN * 128) + 2 * (2 * GM_BM * 128) + (size_t)S * 8 * 2176 + 256;
+static size_t gemm_smem() {
+    return 1024 + (size_t)GM_SX * (GM_BN * 128) + (size_t)GM_SW * 8 * 2176 + 256;
 }
 
-template <int BN>
 static int launch_q8_0(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, float *y) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return set_err(ctx, EF_ERR_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
     CUtensorMap map;
     const cuuint64_t dims[2] = {(cuuint64_t)w->k, (cuuint64_t)M};
     const cuuint64_t strides[1] = {(cuuint64_t)w->k * 2};
-    const cuuint32_t box[2] = {64, (cuuint32_t)BN};
+    const cuuint32_t box[2] = {GM_BKX, (cuuint32_t)GM_BN};
     const cuuint32_t estr[2] = {1, 1};
     CUresult cr = enc(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)xh, dims, strides, box, estr,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return set_err(ctx, EF_ERR_CUDA, "gemm: tensor map encode failed (%d)", (int)cr);
-    auto kern = gemm_q8_0_kernel<BN>;
-    const size_t smem = gemm_smem<BN>();
+    auto kern = gemm_q8_0_kernel;
+    const size_t smem = gemm_smem();
     static unsigned long long configured = 0;
     if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
         if (int rc = check_cuda(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
@@ -293,7 +360,7 @@ static int launch_q8_0(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M,
             return rc;
         configured |= 1ull << ctx->device;
     }
-    dim3 grid((unsigned)((w->rowgroups + 7) / 8), (unsigned)((M + BN - 1) / BN));
+    dim3 grid((unsigned)((w->rowgroups + 7) / 8), (unsigned)((M + GM_BN - 1) / GM_BN));
     ctx->launches++;
     kern<<<grid, GM_THREADS, smem, ctx->stream>>>(map, w->dev, w->rowgroups, w->nchunks, w->rows, M, y);
     return check_cuda(ctx, cudaGetLastError(), "gemm launch");
@@ -313,7 +380,7 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
             if (int rc = check_cuda(ctx, cudaGetLastError(), "gemm f32->f16")) return rc;
             xh = (const __half *)ctx->scratch[1];
         }
-        return launch_q8_0<128>(ctx, w, xh, M, y);
+        return launch_q8_0(ctx, w, xh, M, y);
     }
     // Other types: the token dimension in groups of 16 through the GEMV
     // kernel (same numerics contract: f16 activations, f32 accumulation).
