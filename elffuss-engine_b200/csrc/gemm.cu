@@ -8,19 +8,20 @@
 // pipeline. CTA tile: 128 weight rows (MMA M) x 256 tokens (MMA N).
 //
 //   producer (1 thread):  cp.async.bulk of the repacked weight tiles (8
-//                         rowgroup tiles of 2176 B = 128 rows x 128 k, 2
+//                         rowgroup tiles of 2176 B = 128 rows x 128 k, 4
 //                         stages) and TMA loads (128B swizzle, no multicast)
 //                         of the f16 activations, 64 k x 256 tokens per stage
 //                         (4 stages);
-//   dequant (4 warps):    thread = weight row = tensor-memory lane; expands
-//                         its 128 quants per weight tile to f16(d*q) and
-//                         stores them into tensor memory (tcgen05.st), where
-//                         the MMA reads the A operand (double-buffered);
+//   dequant (2 x 4 warps): thread = weight row = tensor-memory lane; the two
+//                         groups take alternate weight tiles, expand the 128
+//                         quants of their row to f16(d*q) and store them into
+//                         tensor memory (tcgen05.st), where the MMA reads the
+//                         A operand (one buffer per group);
 //   MMA (1 thread):       tcgen05.mma.kind::f16, A from tensor memory, B from
 //                         shared memory, M=128 x N=256 x K=16, accumulator in
 //                         tensor memory (256 columns);
-//   epilogue (4 warps):   tcgen05.ld of the accumulator, coalesced f32 stores
-//                         of y[token][row].
+//   epilogue (8 warps):   tcgen05.ld of the accumulator, coalesced f32 stores
+//                         of y[token][row] (each group half of the tokens).
 // Keeping A out of shared memory leaves shared-memory bandwidth to the TMA
 // writes and the MMA's B reads: about 160 B/clock per SM at full tensor rate
 // against 420 for an A operand staged in shared memory at N=128.
@@ -39,9 +40,9 @@ constexpr int GM_BM = 128;     // weight rows per CTA tile (MMA M)
 constexpr int GM_BN = 256;     // tokens per CTA tile (MMA N)
 constexpr int GM_BKW = 128;    // k per weight stage (one Q8_0 rowgroup tile)
 constexpr int GM_BKX = 64;     // k per activation stage (one 128-byte swizzle atom)
-constexpr int GM_SW = 2;       // weight stages
+constexpr int GM_SW = 4;       // weight stages
 constexpr int GM_SX = 4;       // activation stages
-constexpr int GM_THREADS = 192;
+constexpr int GM_THREADS = 320;   // producer, MMA, 2 x 4 dequant/epilogue warps
 constexpr uint32_t GM_WAIT_LIMIT = 1u << 24;   // try_wait polls before giving up (about a second)
 
 __device__ int g_gemm_error;   // nonzero after a bounded wait gave up
@@ -163,14 +164,19 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         if (lane == 0) {   // ---------------------------------------- producer
             const int64_t nrg = rowgroups - rb * 8 < 8 ? rowgroups - rb * 8 : 8;
             int wi = 0, xi = 0;                          // copies issued
-            for (int kk = 0; kk < nk && ok; kk++) {
+            // weight tile kk -> stage kk % GM_SW (refilled once the dequant
+            // warps have read tile kk - GM_SW)
+            auto issue_w = [&](int kk) {
                 const int sw = kk % GM_SW;
                 if (kk >= GM_SW) ok = mbar_wait(&wempty[sw], ((kk / GM_SW) - 1) & 1);
-                if (!ok) break;
+                if (!ok) return;
                 mbar_expect_tx(&wfull[sw], (uint32_t)(nrg * 2176));
                 for (int i = 0; i < nrg; i++)
                     bulk_g2s(ws + sw * WRAW + i * 2176, W + ((rb * 8 + i) * nchunks + kk) * 2176, 2176, &wfull[sw]);
                 wi++;
+            };
+            for (int kk = 0; kk < GM_SW && kk < nk && ok; kk++) issue_w(kk);
+            for (int kk = 0; kk < nk && ok; kk++) {
                 for (int h = 0; h < 2 && ok; h++) {
                     const int xsi = 2 * kk + h, sx = xsi % GM_SX;
                     if (xsi >= GM_SX) ok = mbar_wait(&xempty[sx], ((xsi / GM_SX) - 1) & 1);
@@ -179,6 +185,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                     tma_2d(xs + sx * XBYTES, &xmap, kk * GM_BKW + h * GM_BKX, n0, &xfull[sx]);
                     xi++;
                 }
+                if (ok && kk + GM_SW < nk) issue_w(kk + GM_SW);
             }
             if (!ok) {   // a wait gave up: let this thread's copies still in flight land first
                 for (int j = wi > GM_SW ? wi - GM_SW : 0; j < wi; j++)
@@ -211,19 +218,20 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             umma_commit(tfull);                // accumulator complete
         }
     } else {
-        // ---------------------------------------- dequant (4 warps = 128 rows)
-        // Thread = weight row r = tensor-memory lane: warp w owns lanes
-        // 32*(w%4) .. +31. Row r of the tile is row g + 8hs of rowgroup r>>4;
+        // ------------------------ dequant (2 groups of 4 warps = 128 rows each)
+        // Group G = (warp - 2) / 4 handles the weight tiles kk = G, G+2, ...
+        // (A buffer G). Thread = weight row r = tensor-memory lane: warp w
+        // owns lanes 32*(w%4) .. +31. Row r of the tile is row g + 8hs of rowgroup r>>4;
         // its block t (32 quants) is two 16-byte parts of fragment lane 4g+t
         // and its f16 scale sits at 2048 + 4(4g+t) + 2hs. The four blocks are
         // read in a lane-staggered order, so one 128-bit shared load by the 32
         // lanes touches each bank group four times (no conflicts).
-        const int quad = warp & 3;
+        const int quad = warp & 3, grp = (warp - 2) >> 2;
         const int r = quad * 32 + lane;
         const int rl = r & 15, g = rl & 7, hs = rl >> 3, rg_in = r >> 4;
         const bool have = rb * 8 + rg_in < rowgroups;
         const uint32_t tlane = (uint32_t)(quad * 32) << 16;
-        for (int kk = 0; kk < nk && ok; kk++) {
+        for (int kk = grp; kk < nk && ok; kk += 2) {
             const int sw = kk % GM_SW, b = kk & 1;
             ok = mbar_wait(&wfull[sw], (kk / GM_SW) & 1);
             if (ok && kk >= 2) ok = mbar_wait(&aempty[b], ((kk >> 1) - 1) & 1);
@@ -277,7 +285,7 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
         if (ok) {
             const int64_t row = rb * GM_BM + quad * 32 + lane;
 #pragma unroll 1
-            for (int c0 = 0; c0 < GM_BN; c0 += 32) {
+            for (int c0 = grp * (GM_BN / 2); c0 < (grp + 1) * (GM_BN / 2); c0 += 32) {
                 if (n0 + c0 >= M) break;
                 uint32_t v[32];
                 asm volatile(
