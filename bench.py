@@ -176,6 +176,59 @@ def run_reference(args):
     return 0
 
 
+GEMM_SHAPES = [(512, 2048, 8192), (2048, 8192, 2048)]   # (tokens M, k, weight rows N)
+
+
+def bench_gemm(ops, L, args, capture, timed_replays, rank):
+    """Config 2: f16 activations x Q8_0 weights through ef_gemm, graph-replayed;
+    8 distinct weight tensors per shape (more than L2 per replay)."""
+    import torch
+
+    from elffuss_engine_b200 import formats
+    from elffuss_engine_b200._lib import check
+    from elffuss_engine_b200.ops import _ptr
+    peak = 1611.6
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+        src = "measured (dense bf16 burst)"
+    except Exception:
+        src = "fallback"
+    per_shape, tot_flop, tot_ms = [], 0.0, 0.0
+    for si, (m, k, n) in enumerate(GEMM_SHAPES):
+        raw = formats.synth("Q8_0", n, k, seed=500 + si + 10 * rank)
+        ws = [ops.load_weight("Q8_0", raw, n, k) for _ in range(8)]
+        del raw
+        x = torch.randn(m, k, device="cuda", generator=torch.Generator("cuda").manual_seed(si)).half()
+        y = torch.empty(m, n, device="cuda")
+
+        def step():
+            h = ops.ctx.bind()
+            for w in ws:
+                check(L.ef_gemm(h, w.h, _ptr(x), 1, m, _ptr(y), 0), h)
+        step()
+        g = capture(step)
+        for _ in range(args.warmup):
+            g.replay()
+        reps = max(3, min(args.steps, 10))
+        ms = timed_replays(g, reps) / (reps * len(ws))
+        del g
+        flop = 2.0 * m * n * k
+        tot_flop += flop
+        tot_ms += ms
+        per_shape.append({"M": m, "K": k, "N": n, "us": round(ms * 1e3, 2),
+                          "TFLOPs": round(flop / (ms * 1e-3) / 1e12, 1),
+                          "frac": round(flop / (ms * 1e-3) / 1e12 / peak, 4)})
+        del ws, x, y
+    torch.cuda.empty_cache()
+    ach = tot_flop / (tot_ms * 1e-3) / 1e12
+    return {"workload": "config2 Q8_0 prefill GEMM (tcgen05): M=512,K=2048,N=8192 and M=2048,K=8192,N=2048; "
+                        "f16 activations, f32 out; 8 distinct weight tensors per shape",
+            "per_shape": per_shape,
+            "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(ach / peak, 4), "peak_source": src, "kernel": "gemm_q8_0_kernel"}}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -314,6 +367,9 @@ def run_ours(args):
     d2h = sum(4 * m * n for (t, n, k, m, *_r) in work)
     del g_dev, g_ker, g_e2e
 
+    # ---- config 2: Q8_0 prefill GEMM on tcgen05 (tensor roofline) ----
+    gemm = None if args.no_gemm else bench_gemm(ops, L, args, capture, timed_replays, rank)
+
     # ---- roofline of the dominant kernel (the GEMV) ----
     peak, peak_kind = peaks()
     kern_total_ms = sum(kern_ms)
@@ -349,6 +405,7 @@ def run_ours(args):
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "gemm": gemm,
             "per_call": per_call,
         }
         print(json.dumps(line), flush=True)
@@ -365,6 +422,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--no-gemm", action="store_true", help="skip the config-2 GEMM measurement")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ncu-step", action="store_true",
                     help="profiling mode for ncu: eager warm-up steps plus one eager step, no timing")

@@ -416,7 +416,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
     }
     return false;
 }
-// Contiguous global -> shared copy (TMA engine, no tensor map, no multicast);
+// Contiguous global -> shared copy (TMA engine, no tensor map, this CTA only);
 // completes `bytes` of transaction count on `bar`. Both addresses and the
 // size must be multiples of 16 bytes.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

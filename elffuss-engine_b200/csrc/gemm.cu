@@ -9,7 +9,7 @@
 //
 //   producer (1 thread):  cp.async.bulk of the repacked weight tiles (8
 //                         rowgroup tiles of 2176 B = 128 rows x 128 k, 4
-//                         stages) and TMA loads (128B swizzle, no multicast)
+//                         stages) and TMA loads (128B swizzle, into this CTA only)
 //                         of the f16 activations, 64 k x 256 tokens per stage
 //                         (4 stages);
 //   dequant (2 x 4 warps): thread = weight row = tensor-memory lane; the two
