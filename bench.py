@@ -293,8 +293,8 @@ def run_ours(args):
 
     def step_e2e():
         x_all.copy_(xh_all, non_blocking=True)                      # the step's inputs, host -> device
-        outs = [ops.gemv.matmul(t, w, xv, n, k, m)                   # public operator (allocates its output)
-                for (t, n, k, m, *_r), xv in zip(work, x_views)]
+        outs = [ops.gemv.matmul(t, wt, xv, n, k, m)                  # public operator (allocates its output)
+                for (t, n, k, m, wt, *_r), xv in zip(work, x_views)]
         torch.cat([o.view(-1) for o in outs], out=y_all)
         yh_all.copy_(y_all, non_blocking=True)                       # the step's results, device -> host
 

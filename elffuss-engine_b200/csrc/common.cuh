@@ -6,17 +6,18 @@
 // chunks of CHUNK_K weights (128 for Q8_0, one 256-weight superblock for the
 // K-/i-quants; k padded to a whole chunk with zero blocks). Each (rowgroup,
 // chunk) is one contiguous, 16-byte aligned tile of exactly 16 x the GGUF bytes
-// of that piece -- the repack permutes bytes (and, for Q4_K/Q6_K, nibbles and
-// 2-bit fields inside a 32-bit word) but never adds any. Tiles of a rowgroup
+// of that piece -- the repack permutes bytes (and, for Q6_K, nibbles and 2-bit
+// fields) but never adds any. Tiles of a rowgroup
 // follow each other along k; rowgroups follow each other.
 //
-// Inside a tile the quant bytes are ordered for the m16n8k16 tensor-core
-// fragment: lane L = 4g + t of a warp owns rows g and g+8 of the rowgroup and a
-// contiguous k-range of each (block t for Q8_0, sub-blocks 2t,2t+1 for Q4_K,
-// quarter-rows (t>>1, t&1) for Q6_K, 32-blocks 2t,2t+1 for the i-quants), and
-// its bytes sit in 16-byte "parts": part p of lane L at tile + 512p + 16L, so
-// one 128-bit load per part by the 32 lanes reads 512 contiguous bytes. Scales
-// follow the parts. Per-type details are next to each scatter/gather below.
+// Inside a tile the quant bytes are ordered for the tensor-core fragments: lane
+// L = 4g + t of a warp owns rows g and g+8 of the rowgroup and, per row, the k
+// positions of its A fragment (block t for Q8_0 / m16n8k16; positions 4t..4t+3
+// and 16+4t..16+4t+3 of every 32 for Q4_K and Q6_K / m16n8k32 8-bit;
+// 32-blocks 2t,2t+1 for the i-quants), and its bytes sit in 16-byte "parts":
+// part p of lane L at tile + 512p + 16L, so one 128-bit load per part by the
+// 32 lanes reads 512 contiguous bytes. Scales follow the parts. Per-type
+// details are next to each scatter/gather below.
 //
 // The GGUF blocks themselves are restated from the reference decoders:
 //   Q8_0 js/kernels.wgsl.js:154-169, Q4_K :227-250 (+scale_min_k4 :94-104),
@@ -58,33 +59,17 @@ __host__ __device__ inline void wr32(uint8_t *p, uint32_t v) {
     p[0] = (uint8_t)v; p[1] = (uint8_t)(v >> 8); p[2] = (uint8_t)(v >> 16); p[3] = (uint8_t)(v >> 24);
 }
 
-// Nibble permutation of one 32-bit word of 4-bit quants. GGUF byte b_i holds a
-// low nibble (weight i of one group) and a high nibble (weight i of a second
-// group). The repacked word puts the first group's weights i=0,1,2,3 at bits
-// 0,16,4,20 and the second group's at 8,24,12,28, so that
-// (w >> s) & 0x000F000F picks a pair of consecutive weights into the two f16
-// halves of a register (s = 0, 4 for the first group; 8, 12 for the second).
-__host__ __device__ inline uint32_t nib_fwd(uint32_t G) {
-    uint32_t b0 = G & 0xFF, b1 = (G >> 8) & 0xFF, b2 = (G >> 16) & 0xFF, b3 = G >> 24;
-    uint32_t r0 = (b0 & 0xF) | ((b2 & 0xF) << 4);
-    uint32_t r1 = (b0 >> 4) | (b2 & 0xF0);
-    uint32_t r2 = (b1 & 0xF) | ((b3 & 0xF) << 4);
-    uint32_t r3 = (b1 >> 4) | (b3 & 0xF0);
-    return r0 | (r1 << 8) | (r2 << 16) | (r3 << 24);
+// Q6_K weight p of a GGUF block (kernels.wgsl.js:269-330): p = 128n + 32i + l,
+// low 4 bits from ql[64n + 32(i&1) + l] (low nibble for i < 2, high for
+// i >= 2), high 2 bits from qh[32n + l] >> 2i.
+__host__ __device__ inline int q6_lo4(const uint8_t *blk, int p) {
+    const int n = p >> 7, i = (p >> 5) & 3, l = p & 31;
+    return (blk[64 * n + 32 * (i & 1) + l] >> (4 * (i >> 1))) & 15;
 }
-__host__ __device__ inline uint32_t nib_inv(uint32_t R) {
-    uint32_t r0 = R & 0xFF, r1 = (R >> 8) & 0xFF, r2 = (R >> 16) & 0xFF, r3 = R >> 24;
-    uint32_t b0 = (r0 & 0xF) | ((r1 & 0xF) << 4);
-    uint32_t b2 = (r0 >> 4) | (r1 & 0xF0);
-    uint32_t b1 = (r2 & 0xF) | ((r3 & 0xF) << 4);
-    uint32_t b3 = (r2 >> 4) | (r3 & 0xF0);
-    return b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+__host__ __device__ inline int q6_hi2(const uint8_t *blk, int p) {
+    const int n = p >> 7, i = (p >> 5) & 3, l = p & 31;
+    return (blk[128 + 32 * n + l] >> (2 * i)) & 3;
 }
-
-// Q6_K high-bit word: 16 two-bit fields of one quarter-row, field of weight j
-// at bit 4(j>>2) + 2((j>>1)&1) + 16(j&1), so that weights (j, j+1) with j even
-// sit 16 bits apart and one shift + mask moves a pair under the f16 mantissa.
-__host__ __device__ inline int q6_hpos(int j) { return 4 * (j >> 2) + 2 * ((j >> 1) & 1) + 16 * (j & 1); }
 
 // --------------------------------------------- scatter (GGUF -> tile) -------
 // Write GGUF block `blk` (row r of the rowgroup, block `bic` within the chunk)
@@ -122,25 +107,29 @@ __host__ __device__ inline void scatter_block(int type, const uint8_t *blk, int 
         for (int i = 0; i < 16; i++) T[2048 + r * 16 + i] = blk[i];
     } break;
     case EF_Q6_K: {
-        // lane (g,t), n = t>>1, lh = t&1 owns positions 128n + 32i + 16lh + j
-        // (i = quarter 0..3, j = 0..15): GGUF bytes A = ql[64n+16lh+j],
-        // B = ql[64n+32+16lh+j], H = qh[32n+16lh+j]. Part 3hs: A words
-        // nibble-permuted (quarters 0 | 2), part 3hs+1: B words (quarters 1 | 3),
-        // part 3hs+2: one high-bit word per quarter. int8 scales verbatim at
+        // 8-bit MMA layout. Weight position p = 32s + 16h + 4t + b (step s =
+        // 0..7, half h, lane column t, byte b) of row g + 8hs: lane (g,t) holds
+        // for each step one word of low nibbles (byte b: position 32s+4t+b in
+        // bits 0-3, 32s+16+4t+b in bits 4-7) at part 2hs + (s>>2), offset
+        // 4(s&3); and for each pair of steps one word of 2-bit high fields
+        // (byte b: step 2sp half 0 | half 1 | step 2sp+1 half 0 | half 1, two
+        // bits each) at part 4 + hs, offset 4sp. int8 scales verbatim at
         // 3072 + 16r, d at 3328 + 4g + 2hs.
         for (int t = 0; t < 4; t++) {
-            const int n = t >> 1, lh = t & 1, lane = 4 * g + t;
-            const uint8_t *A = blk + 64 * n + 16 * lh, *B = blk + 64 * n + 32 + 16 * lh;
-            const uint8_t *H = blk + 128 + 32 * n + 16 * lh;
-            for (int w = 0; w < 4; w++) {
-                wr32(T + (3 * hs) * 512 + lane * 16 + 4 * w, nib_fwd(rd32(A + 4 * w)));
-                wr32(T + (3 * hs + 1) * 512 + lane * 16 + 4 * w, nib_fwd(rd32(B + 4 * w)));
-            }
-            for (int i = 0; i < 4; i++) {
-                uint32_t hw = 0;
-                for (int j = 0; j < 16; j++) hw |= (uint32_t)((H[j] >> (2 * i)) & 3) << q6_hpos(j);
-                wr32(T + (3 * hs + 2) * 512 + lane * 16 + 4 * i, hw);
-            }
+            const int lane = 4 * g + t;
+            for (int st = 0; st < 8; st++)
+                for (int b = 0; b < 4; b++) {
+                    const int p0 = 32 * st + 4 * t + b, p1 = p0 + 16;
+                    T[(2 * hs + (st >> 2)) * 512 + lane * 16 + 4 * (st & 3) + b] =
+                        (uint8_t)(q6_lo4(blk, p0) | (q6_lo4(blk, p1) << 4));
+                }
+            for (int sp = 0; sp < 4; sp++)
+                for (int b = 0; b < 4; b++) {
+                    const int p0 = 64 * sp + 4 * t + b;
+                    T[(4 + hs) * 512 + lane * 16 + 4 * sp + b] =
+                        (uint8_t)(q6_hi2(blk, p0) | (q6_hi2(blk, p0 + 16) << 2) | (q6_hi2(blk, p0 + 32) << 4) |
+                                  (q6_hi2(blk, p0 + 48) << 6));
+                }
         }
         for (int i = 0; i < 16; i++) T[3072 + r * 16 + i] = blk[192 + i];
         T[3328 + 4 * g + 2 * hs] = blk[208];
@@ -197,20 +186,15 @@ __host__ __device__ inline void gather_block(int type, const uint8_t *T, int r, 
         for (int i = 0; i < 16; i++) blk[i] = T[2048 + r * 16 + i];
     } break;
     case EF_Q6_K: {
-        for (int t = 0; t < 4; t++) {
-            const int n = t >> 1, lh = t & 1, lane = 4 * g + t;
-            uint8_t *A = blk + 64 * n + 16 * lh, *B = blk + 64 * n + 32 + 16 * lh;
-            uint8_t *H = blk + 128 + 32 * n + 16 * lh;
-            for (int w = 0; w < 4; w++) {
-                wr32(A + 4 * w, nib_inv(rd32(T + (3 * hs) * 512 + lane * 16 + 4 * w)));
-                wr32(B + 4 * w, nib_inv(rd32(T + (3 * hs + 1) * 512 + lane * 16 + 4 * w)));
-            }
-            for (int j = 0; j < 16; j++) {
-                uint32_t h = 0;
-                for (int i = 0; i < 4; i++)
-                    h |= ((rd32(T + (3 * hs + 2) * 512 + lane * 16 + 4 * i) >> q6_hpos(j)) & 3u) << (2 * i);
-                H[j] = (uint8_t)h;
-            }
+        for (int i = 0; i < 192; i++) blk[i] = 0;
+        for (int p = 0; p < 256; p++) {
+            const int st = p >> 5, h = (p >> 4) & 1, lane = 4 * g + ((p >> 2) & 3), b = p & 3;
+            const uint8_t nb = T[(2 * hs + (st >> 2)) * 512 + lane * 16 + 4 * (st & 3) + b];
+            const uint8_t hb = T[(4 + hs) * 512 + lane * 16 + 4 * (st >> 1) + b];
+            const int lo = h ? nb >> 4 : nb & 15, hi = (hb >> (2 * (2 * (st & 1) + h))) & 3;
+            const int n = p >> 7, qi = (p >> 5) & 3, l = p & 31;
+            blk[64 * n + 32 * (qi & 1) + l] |= (uint8_t)(lo << (4 * (qi >> 1)));
+            blk[128 + 32 * n + l] |= (uint8_t)(hi << (2 * qi));
         }
         for (int i = 0; i < 16; i++) blk[192 + i] = T[3072 + r * 16 + i];
         blk[208] = T[3328 + 4 * g + 2 * hs];

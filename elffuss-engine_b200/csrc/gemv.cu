@@ -25,7 +25,7 @@
 //    from shared or tensor memory, which would add a store and a read of every
 //    dequantised weight). Q8_0, Q6_K and the i-quants run m16n8k16 f16 MMAs;
 //    Q4_K runs m16n8k32 8-bit MMAs on the raw nibbles, with the 8 MMA columns
-//    holding (token, sub-block) pairs for 1-4 tokens (q4_tq).
+//    holding (token, sub-block) pairs for 1-4 tokens (i8_tq).
 //  * Activations: converted once per call into the operand layout -- by each
 //    CTA for its own chunks when there are 1-2 tokens (one kernel per call),
 //    else by a small prep kernel into context scratch -- and staged in shared
@@ -60,9 +60,7 @@ namespace ef {
 __device__ const __align__(16) uint16_t g_grid_iq2xxs_f16[EF_GRID_IQ2XXS_ENTRIES * 8] = {EF_GRID_IQ2XXS_F16_INIT};
 __device__ const __align__(16) uint16_t g_grid_iq1s_f16[EF_GRID_IQ1S_ENTRIES * 8] = {EF_GRID_IQ1S_F16_INIT};
 
-constexpr uint32_t H2_1024 = 0x64006400u;   // half2(1024, 1024)
 constexpr uint32_t H2_1152 = 0x64806480u;   // half2(1152, 1152)
-constexpr uint32_t H2_2080 = 0x68106810u;   // half2(2080, 2080)
 constexpr int GV_WARPS = 8;                 // rowgroups (warps) per CTA = one rowblock
 constexpr int MAX_XS_BYTES = 64 * 1024;     // shared memory for activation data
 
@@ -101,7 +99,7 @@ template <> struct Tr<EF_Q4_K> {
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 4; s = 2 * (kq & 7) + ((kq >> 3) & 1); }
 };
 template <> struct Tr<EF_Q6_K> {
-    static constexpr int CHUNK = 256, STEPS = 16, TILE = 3360, I8 = 0;
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 3360, I8 = 1;
     __device__ static void inv(int kq, int &t, int &s) {
         t = 2 * (kq >> 5) + ((kq >> 2) & 1);
         s = 4 * ((kq >> 3) & 3) + (kq & 3);
@@ -118,18 +116,27 @@ template <> struct Tr<EF_IQ1_S> {
 // bytes of f16 x fragments per chunk for M tokens: STEPS x M x 4 lanes x 8 B
 template <int TYPE> __host__ __device__ inline int f16_xbytes(int M) { return Tr<TYPE>::STEPS * M * 32; }
 
-// Q4_K activation layout. The 8 columns of the m16n8k32 MMA hold TQ tokens x
-// (8 / TQ) sub-blocks: TQ = 1, 2, 4 for 1, 2, 3-4 tokens (several sub-blocks
-// share one MMA, each in its own columns, so the integer sub-block scales are
-// applied once per 8/TQ MMAs), TQ = 8 for 5-16 tokens in NT tiles of 8.
-__host__ __device__ inline int q4_tq(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
-__host__ __device__ inline int q4_nt(int M) { return M > 8 ? 2 : 1; }
-// Per chunk: B fragments [ntile][TQ][lane][16 B: xh b0 b1, xl b0 b1]; then the
-// f32 sums of x over each 32-weight sub-block [8][MP]; then dx [MP]
-// (MP = NT * TQ padded tokens); rounded up to 16 bytes.
-__host__ __device__ inline int i8_xbytes(int M) {
-    const int tq = q4_tq(M), nt = q4_nt(M), mp = tq * nt;
-    return (512 * tq * nt + 36 * mp + 15) & ~15;
+// Activation layout of the 8-bit types (Q4_K, Q6_K). The 8 columns of the
+// 8-bit MMA hold TQ tokens x (8 / TQ) sub-blocks: TQ = 1, 2, 4 for 1, 2, 3-4
+// tokens (several sub-blocks share one MMA, each in its own columns, so the
+// integer sub-block scales are applied once per group of MMAs), TQ = 8 for
+// 5-16 tokens in NT tiles of 8.
+__host__ __device__ inline int i8_tq(int M) { return M <= 1 ? 1 : M <= 2 ? 2 : M <= 4 ? 4 : 8; }
+__host__ __device__ inline int i8_nt(int M) { return M > 8 ? 2 : 1; }
+// Per chunk: B fragments [..][lane][16 B: xh b0 b1, xl b0 b1] -- Q4_K:
+// [ntile][TQ][lane] (32-weight sub-blocks); Q6_K: [2 TQ flushes][lane] for TQ
+// <= 4, [ntile][8 steps][lane] for TQ = 8 (16-weight sub-blocks), then for TQ
+// = 8 the f16 m16n8k16 B fragments of S/dx [ntile][lane][8 B]; then the f32
+// sums of x over each sub-block [8 or 16][MP]; then dx [MP] (MP = NT * TQ
+// padded tokens); rounded up to 16 bytes.
+template <int TYPE> __host__ __device__ inline int i8_frag_bytes(int M) {
+    const int tq = i8_tq(M), nt = i8_nt(M);
+    if (TYPE == EF_Q6_K) return tq <= 4 ? 1024 * tq : 4352 * nt;   // tq = 8: + f16 sums S/dx as MMA B
+    return 512 * tq * nt;
+}
+template <int TYPE> __host__ __device__ inline int i8_xbytes(int M) {
+    const int mp = i8_tq(M) * i8_nt(M), subs = TYPE == EF_Q6_K ? 16 : 8;
+    return (i8_frag_bytes<TYPE>(M) + 4 * (subs + 1) * mp + 15) & ~15;
 }
 
 __device__ __forceinline__ uint32_t wsel(const uint4 &v, int i) {
@@ -282,7 +289,7 @@ __device__ __forceinline__ void q4k_afrag(const RawQ4K &r, int s, uint32_t &a0, 
 
 // Q4_K tile: acc[nt][i] (row g or g+8 by i>>1; lane column 2t + (i&1)) +=
 //   d*dx*(sum_sub sc*sum_k q*(xh + xl/256)) - dmin*sum_sub m*S_sub
-// with the column -> (sub-block, token) mapping of TQ (see q4_tq).
+// with the column -> (sub-block, token) mapping of TQ (see i8_tq).
 template <int TQ, int NT>
 __device__ __forceinline__ void compute_q4k(const RawQ4K &r, const uint8_t *xc, float (&acc)[NT][4], int lane) {
     constexpr int FL = 8 / TQ;   // sub-blocks per MMA group (flush)
@@ -426,60 +433,187 @@ __device__ __forceinline__ void compute_q4k(const RawQ4K &r, const uint8_t *xc, 
 }
 
 // ------------------------------------------------------------------ Q6_K ---
-struct RawQ6K { uint4 q[6]; uint2 scg, scg8; uint32_t d; };
+// lane (g,t): parts 0,1 = low-nibble words of row g for steps 0-3, 4-7;
+// parts 2,3 = the same for row g+8; parts 4,5 = high-bit words (one per pair
+// of steps) of rows g and g+8; the rows' 16 int8 scales; d of both rows.
+struct RawQ6K { uint4 q[6]; uint4 scg, scg8; uint32_t d; };
 __device__ __forceinline__ void load_raw(RawQ6K &r, const uint8_t *T, int lane) {
 #pragma unroll
     for (int p = 0; p < 6; p++) r.q[p] = ldq128(T + p * 512 + lane * 16);
-    const int g = lane >> 2, n = (lane & 3) >> 1;
-    r.scg = ldh64(T + 3072 + g * 16 + 8 * n);
-    r.scg8 = ldh64(T + 3072 + (g + 8) * 16 + 8 * n);
+    const int g = lane >> 2;
+    r.scg = ldh128(T + 3072 + g * 16);
+    r.scg8 = ldh128(T + 3072 + (g + 8) * 16);
     r.d = ldh32(T + 3328 + 4 * g);
 }
-__device__ __forceinline__ uint32_t q6_pair(uint32_t nw, int nsh, uint32_t hw, int hsh, uint32_t sc2) {
-    const uint32_t lo = lop3_and_or(nw >> nsh, 0x000F000Fu, H2_1024);
-    const uint32_t hs = hsh >= 0 ? (hw >> hsh) : (hw << -hsh);
-    const uint32_t hi = lop3_and_or(hs, 0x00300030u, H2_1024);
-    // (1024 + lo) - (2080 - (1024 + 16 hi)) = lo + 16 hi - 32; times sc: all exact
-    return hmul2u(hsub2u(lo, hsub2u(H2_2080, hi)), sc2);
+// D (+)= A(16x16 u8, row) * B(16x8 s8, col), s32 accumulate (one 16-weight sub-block).
+__device__ __forceinline__ void imma16816(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(b0));
 }
-template <int NT>
-__device__ __forceinline__ void compute(const RawQ6K &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
-                                        const uint4 *, const uint4 *) {
-    const XF xsc = make_xf<NT>(xc, M, lane);
-    const int lh = lane & 1;
-    float tmp[NT][4];
+// u8 A fragment of 32-weight step s: 6-bit q = low nibble | high 2 bits << 4
+// for rows g (a0: k 4t.., a2: k 16+4t..) and g+8 (a1, a3).
+__device__ __forceinline__ void q6k_afrag(const RawQ6K &r, int s, uint32_t &a0, uint32_t &a1, uint32_t &a2,
+                                          uint32_t &a3) {
+    const uint32_t ng = wsel(r.q[s >> 2], s & 3), nh = wsel(r.q[2 + (s >> 2)], s & 3);
+    const uint32_t hg = wsel(r.q[4], s >> 1), hh = wsel(r.q[5], s >> 1);
+    // high fields per byte: bits 0-1 / 2-3 = even step halves 0 / 1, 4-5 / 6-7 = odd step
+    const uint32_t g0 = (s & 1) ? hg : hg << 4, g1 = (s & 1) ? hg >> 2 : hg << 2;
+    const uint32_t h0 = (s & 1) ? hh : hh << 4, h1 = (s & 1) ? hh >> 2 : hh << 2;
+    a0 = lop3_and_or(g0, 0x30303030u, ng & 0x0F0F0F0Fu);
+    a2 = lop3_and_or(g1, 0x30303030u, (ng >> 4) & 0x0F0F0F0Fu);
+    a1 = lop3_and_or(h0, 0x30303030u, nh & 0x0F0F0F0Fu);
+    a3 = lop3_and_or(h1, 0x30303030u, (nh >> 4) & 0x0F0F0F0Fu);
+}
+// signed int8 scale `i` (runtime) of a row's 16 scale bytes
+__device__ __forceinline__ int q6_sc(const uint4 &v, int i) {
+    const uint32_t b = (uint32_t)(i & 3), sgn = 8u | b;
+    return (int)prmt(wsel(v, i >> 2), 0u, b | (sgn << 4) | (sgn << 8) | (sgn << 12));
+}
+
+// Q6_K tile: w = d * sc * (q - 32) over 16-weight sub-blocks:
+//   acc += d * (dx * sum_sub sc * sum_k q * (xh + xl/256) - 32 * sum_sub sc * S_sub)
+// TQ <= 4: the 8 MMA columns hold 8/TQ sub-blocks x TQ tokens; a lane's B
+// fragment is nonzero in one step of each group (one of b0/b1). TQ = 8: one
+// 16-k MMA per sub-block.
+template <int TQ, int NT>
+__device__ __forceinline__ void compute_q6k(const RawQ6K &r, const uint8_t *xc, float (&acc)[NT][4], int lane) {
+    constexpr int MP = NT * TQ;
+    const int g = lane >> 2, t = lane & 3;
+    const float *S = reinterpret_cast<const float *>(xc + (TQ <= 4 ? 1024 * TQ : 4352 * NT));
+    const float *DX = S + 16 * MP;
+    int ih[NT][4], il[NT][4];
+    float ms[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; nt++) tmp[nt][0] = tmp[nt][1] = tmp[nt][2] = tmp[nt][3] = 0.f;
+    for (int nt = 0; nt < NT; nt++)
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-        // int8 scale sc[8n + 2i + lh] of each row, as (sc, sc) in f16
-        const int idx = 2 * i + lh;
-        const uint32_t swg = (idx < 4 ? r.scg.x : r.scg.y) ^ 0x80808080u;
-        const uint32_t swg8 = (idx < 4 ? r.scg8.x : r.scg8.y) ^ 0x80808080u;
-        const uint32_t sel = 0x4040u | (uint32_t)(idx & 3) | ((uint32_t)(idx & 3) << 8);
-        const uint32_t scg = hsub2u(prmt(swg, 0x64646464u, sel), H2_1152);
-        const uint32_t scg8 = hsub2u(prmt(swg8, 0x64646464u, sel), H2_1152);
-        const int nsb = (i >> 1) * 8;
+        for (int i = 0; i < 4; i++) {
+            ih[nt][i] = il[nt][i] = 0;
+            ms[nt][i] = 0.f;
+        }
+    if constexpr (TQ == 8) {
 #pragma unroll
-        for (int jj = 0; jj < 4; jj++) {
-            const uint32_t nwg = wsel(r.q[i & 1], jj), nwg8 = wsel(r.q[3 + (i & 1)], jj);
-            const uint32_t hwg = wsel(r.q[2], i), hwg8 = wsel(r.q[5], i);
-            const int h0 = 4 * jj - 4, h1 = 4 * jj - 2;
-            const uint32_t a0 = q6_pair(nwg, nsb, hwg, h0, scg);
-            const uint32_t a2 = q6_pair(nwg, nsb + 4, hwg, h1, scg);
-            const uint32_t a1 = q6_pair(nwg8, nsb, hwg8, h0, scg8);
-            const uint32_t a3 = q6_pair(nwg8, nsb + 4, hwg8, h1, scg8);
-            mma_step<NT>(tmp, xsc, 4 * i + jj, lane, a0, a1, a2, a3);
+        for (int s = 0; s < 8; s++) {
+            uint32_t a0, a1, a2, a3;
+            q6k_afrag(r, s, a0, a1, a2, a3);
+            const int sg0 = q6_sc(r.scg, 2 * s), sg1 = q6_sc(r.scg, 2 * s + 1);
+            const int sh0 = q6_sc(r.scg8, 2 * s), sh1 = q6_sc(r.scg8, 2 * s + 1);
+#pragma unroll
+            for (int nt = 0; nt < NT; nt++) {
+                const uint4 b = lds128(xc + ((nt * 8 + s) * 32 + lane) * 16);
+                int d0[4] = {0, 0, 0, 0}, d1[4] = {0, 0, 0, 0}, e0[4] = {0, 0, 0, 0}, e1[4] = {0, 0, 0, 0};
+                imma16816(d0, a0, a1, b.x);   // sub-block 2s, plane h
+                imma16816(d1, a2, a3, b.y);   // sub-block 2s+1
+                imma16816(e0, a0, a1, b.z);   // plane l
+                imma16816(e1, a2, a3, b.w);
+                ih[nt][0] += sg0 * d0[0] + sg1 * d1[0];
+                ih[nt][1] += sg0 * d0[1] + sg1 * d1[1];
+                ih[nt][2] += sh0 * d0[2] + sh1 * d1[2];
+                ih[nt][3] += sh0 * d0[3] + sh1 * d1[3];
+                il[nt][0] += sg0 * e0[0] + sg1 * e1[0];
+                il[nt][1] += sg0 * e0[1] + sg1 * e1[1];
+                il[nt][2] += sh0 * e0[2] + sh1 * e1[2];
+                il[nt][3] += sh0 * e0[3] + sh1 * e1[3];
+            }
+        }
+        // sum_sub sc * S_sub / dx for 16 rows x 8 tokens: one f16 MMA per tile
+        // (int8 scales are exact in f16; A: sub-blocks 2t, 2t+1 and 8+2t, 9+2t)
+        const uint32_t ma0 = pack_h2((float)q6_sc(r.scg, 2 * t), (float)q6_sc(r.scg, 2 * t + 1));
+        const uint32_t ma1 = pack_h2((float)q6_sc(r.scg8, 2 * t), (float)q6_sc(r.scg8, 2 * t + 1));
+        const uint32_t ma2 = pack_h2((float)q6_sc(r.scg, 8 + 2 * t), (float)q6_sc(r.scg, 9 + 2 * t));
+        const uint32_t ma3 = pack_h2((float)q6_sc(r.scg8, 8 + 2 * t), (float)q6_sc(r.scg8, 9 + 2 * t));
+#pragma unroll
+        for (int nt = 0; nt < NT; nt++) {
+            const uint2 b = lds64(xc + 4096 * NT + (nt * 32 + lane) * 8);
+            mma16816(ms[nt], ma0, ma1, ma2, ma3, b.x, b.y);
+        }
+    } else {
+        constexpr int FLS = 8 / TQ;          // sub-blocks per flush
+        constexpr int SPF = FLS / 2;         // 32-weight steps per flush
+        const int ql = (g / TQ) >> 1;        // step of the flush in which this lane's B fragment is nonzero
+#pragma unroll
+        for (int f = 0; f < 2 * TQ; f++) {
+            const uint4 xb = lds128(xc + (f * 32 + lane) * 16);
+            int dh[4] = {0, 0, 0, 0}, dl[4] = {0, 0, 0, 0}, eh[4] = {0, 0, 0, 0}, el[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int q = 0; q < SPF; q++) {
+                uint32_t a0, a1, a2, a3;
+                q6k_afrag(r, f * SPF + q, a0, a1, a2, a3);
+                const uint32_t mk = (SPF == 1 || q == ql) ? 0xFFFFFFFFu : 0u;
+                if (q & 1) {
+                    imma16832(eh, a0, a1, a2, a3, xb.x & mk, xb.y & mk);
+                    imma16832(el, a0, a1, a2, a3, xb.z & mk, xb.w & mk);
+                } else {
+                    imma16832(dh, a0, a1, a2, a3, xb.x & mk, xb.y & mk);
+                    imma16832(dl, a0, a1, a2, a3, xb.z & mk, xb.w & mk);
+                }
+            }
+            if (SPF > 1)
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    dh[i] += eh[i];
+                    dl[i] += el[i];
+                }
+            // accumulator column 2t + c: sub-block f*FLS + (2t+c)/TQ, token (2t+c) % TQ
+            int s0, s1, tok0;
+            if (TQ == 1) {
+                s0 = 8 * f + 2 * t;
+                s1 = s0 + 1;
+                tok0 = 0;
+            } else if (TQ == 2) {
+                s0 = s1 = 4 * f + t;
+                tok0 = 0;
+            } else {
+                s0 = s1 = 2 * f + (t >> 1);
+                tok0 = 2 * (t & 1);
+            }
+            const int sg0 = q6_sc(r.scg, s0), sg1 = q6_sc(r.scg, s1);
+            const int sh0 = q6_sc(r.scg8, s0), sh1 = q6_sc(r.scg8, s1);
+            ih[0][0] += sg0 * dh[0];
+            ih[0][1] += sg1 * dh[1];
+            ih[0][2] += sh0 * dh[2];
+            ih[0][3] += sh1 * dh[3];
+            il[0][0] += sg0 * dl[0];
+            il[0][1] += sg1 * dl[1];
+            il[0][2] += sh0 * dl[2];
+            il[0][3] += sh1 * dl[3];
+            float2 sv;
+            if (TQ == 1) sv = *reinterpret_cast<const float2 *>(S + s0);               // S[s0][0], S[s0+1][0]
+            else sv = *reinterpret_cast<const float2 *>(S + s0 * MP + tok0);          // S[s][tok0], S[s][tok0+1]
+            ms[0][0] = fmaf((float)sg0, sv.x, ms[0][0]);
+            ms[0][1] = fmaf((float)sg1, sv.y, ms[0][1]);
+            ms[0][2] = fmaf((float)sh0, sv.x, ms[0][2]);
+            ms[0][3] = fmaf((float)sh1, sv.y, ms[0][3]);
         }
     }
-    // the superblock d is common to the 4 lane columns of a row: apply in f32
-    const float dg = h2f(r.d & 0xFFFF), dg8 = h2f(r.d >> 16);
+    const float dg = h2f(r.d & 0xFFFF), dh8 = h2f(r.d >> 16);
 #pragma unroll
     for (int nt = 0; nt < NT; nt++) {
-        acc[nt][0] = fmaf(dg, tmp[nt][0], acc[nt][0]);
-        acc[nt][1] = fmaf(dg, tmp[nt][1], acc[nt][1]);
-        acc[nt][2] = fmaf(dg8, tmp[nt][2], acc[nt][2]);
-        acc[nt][3] = fmaf(dg8, tmp[nt][3], acc[nt][3]);
+        float dx0, dx1;
+        if (TQ == 1) {
+            dx0 = dx1 = DX[0];
+        } else {
+            const int tk = TQ == 2 ? 0 : TQ == 4 ? 2 * (t & 1) : nt * 8 + 2 * t;
+            const float2 d2 = *reinterpret_cast<const float2 *>(DX + tk);
+            dx0 = d2.x;
+            dx1 = d2.y;
+        }
+        const float v0 = fmaf((float)il[nt][0], 1.f / 256.f, (float)ih[nt][0]);
+        const float v1 = fmaf((float)il[nt][1], 1.f / 256.f, (float)ih[nt][1]);
+        const float v2 = fmaf((float)il[nt][2], 1.f / 256.f, (float)ih[nt][2]);
+        const float v3 = fmaf((float)il[nt][3], 1.f / 256.f, (float)ih[nt][3]);
+        if (TQ == 8) {   // ms holds sum sc * S / dx
+            acc[nt][0] = fmaf(dg * dx0, fmaf(-32.f, ms[nt][0], v0), acc[nt][0]);
+            acc[nt][1] = fmaf(dg * dx1, fmaf(-32.f, ms[nt][1], v1), acc[nt][1]);
+            acc[nt][2] = fmaf(dh8 * dx0, fmaf(-32.f, ms[nt][2], v2), acc[nt][2]);
+            acc[nt][3] = fmaf(dh8 * dx1, fmaf(-32.f, ms[nt][3], v3), acc[nt][3]);
+        } else {
+            acc[nt][0] = fmaf(dg, fmaf(dx0, v0, -32.f * ms[nt][0]), acc[nt][0]);
+            acc[nt][1] = fmaf(dg, fmaf(dx1, v1, -32.f * ms[nt][1]), acc[nt][1]);
+            acc[nt][2] = fmaf(dh8, fmaf(dx0, v2, -32.f * ms[nt][2]), acc[nt][2]);
+            acc[nt][3] = fmaf(dh8, fmaf(dx1, v3, -32.f * ms[nt][3]), acc[nt][3]);
+        }
     }
 }
 
@@ -587,15 +721,16 @@ __device__ __forceinline__ void stage_f16(const float *__restrict__ x, int M, in
             make_uint2(pack_h2(v.x, v.y), pack_h2(v.z, v.w));
     }
 }
-// Q4_K: per 256-weight chunk and token x = dx * (xh + xl/256), dx =
+// 8-bit types: per 256-weight chunk and token x = dx * (xh + xl/256), dx =
 // max|x|/127, xh = rne(x/dx), xl = rne(256 * (x/dx - xh)), both int8, as the
-// B fragments of the column layout of q4_tq (tokens M..MP-1 are zero); the f32
-// sums of x over each 32-weight sub-block; dx. One warp per (chunk, token);
-// lane l holds weights 8l .. 8l+7.
+// B fragments of the column layout of i8_tq (tokens M..MP-1 are zero); the f32
+// sums of x over each sub-block; dx. One warp per (chunk, token); lane l holds
+// weights 8l .. 8l+7.
+template <int TYPE>
 __device__ __forceinline__ void stage_i8(const float *__restrict__ x, int M, int64_t K, int64_t c, int n,
                                          uint8_t *dst, int xb, int tid, int nthreads) {
     const int lane = tid & 31;
-    const int tq = q4_tq(M), ntl = q4_nt(M), mp = tq * ntl, fl = 8 / tq;
+    const int tq = i8_tq(M), ntl = i8_nt(M), mp = tq * ntl;
     for (int w = tid >> 5; w < n * mp; w += nthreads >> 5) {
         const int cc = w / mp, token = w - cc * mp;
         const int64_t k0 = (c + cc) * 256 + 8 * lane;
@@ -613,8 +748,8 @@ __device__ __forceinline__ void stage_i8(const float *__restrict__ x, int M, int
             sum += v[i];
         }
         for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        const float sum16 = sum + __shfl_xor_sync(0xffffffffu, sum, 1);
+        const float sum32 = sum16 + __shfl_xor_sync(0xffffffffu, sum16, 2);
         const float dx = amax / 127.f, inv = amax > 0.f ? 127.f / amax : 0.f;
         uint32_t wq[2], wl[2];
         for (int h = 0; h < 2; h++) {
@@ -630,26 +765,62 @@ __device__ __forceinline__ void stage_i8(const float *__restrict__ x, int M, int
             wl[h] = wlo;
         }
         uint8_t *base = dst + (int64_t)cc * xb;
-        const int sub = lane >> 2, kk = 8 * (lane & 3);       // k within the sub-block
+        float *S = reinterpret_cast<float *>(base + i8_frag_bytes<TYPE>(M));
         const int nt = token >> 3, tk = token & 7;            // n-tile, token within it
-        const int n_col = (sub % fl) * tq + (tq == 8 ? tk : token);   // B column
-        const int f = sub / fl;                               // fragment index of that lane
-        const int tb = (kk & 15) >> 2, reg = kk >> 4;         // lane t of the B fragment, b0 or b1
-        uint8_t *fr0 = base + ((nt * tq + f) * 32 + 4 * n_col + tb) * 16 + reg * 4;
-        uint8_t *fr1 = fr0 + 16;
-        *reinterpret_cast<uint32_t *>(fr0) = wq[0];
-        *reinterpret_cast<uint32_t *>(fr0 + 8) = wl[0];
-        *reinterpret_cast<uint32_t *>(fr1) = wq[1];
-        *reinterpret_cast<uint32_t *>(fr1 + 8) = wl[1];
-        float *S = reinterpret_cast<float *>(base + 512 * tq * ntl);
-        if ((lane & 3) == 0) S[sub * mp + token] = sum;
-        if (lane == 0) S[8 * mp + token] = dx;
+        if (TYPE == EF_Q4_K) {
+            const int fl = 8 / tq;
+            const int sub = lane >> 2, kk = 8 * (lane & 3);   // 32-weight sub-block, k within it
+            const int n_col = (sub % fl) * tq + (tq == 8 ? tk : token);   // B column
+            const int f = sub / fl;                           // fragment index of that lane
+            const int tb = (kk & 15) >> 2, reg = kk >> 4;     // lane t of the B fragment, b0 or b1
+            uint8_t *fr0 = base + ((nt * tq + f) * 32 + 4 * n_col + tb) * 16 + reg * 4;
+            uint8_t *fr1 = fr0 + 16;
+            *reinterpret_cast<uint32_t *>(fr0) = wq[0];
+            *reinterpret_cast<uint32_t *>(fr0 + 8) = wl[0];
+            *reinterpret_cast<uint32_t *>(fr1) = wq[1];
+            *reinterpret_cast<uint32_t *>(fr1 + 8) = wl[1];
+            if ((lane & 3) == 0) S[sub * mp + token] = sum32;
+            if (lane == 0) S[8 * mp + token] = dx;
+        } else {
+            // Q6_K: 16-weight sub-block sig = lane >> 1 is half sig & 1 (b0 or
+            // b1) of 32-weight step sig >> 1; the lane's 8 weights are the
+            // k-quads of B-fragment lanes t = 2(lane&1), 2(lane&1)+1.
+            const int sig = lane >> 1, half = sig & 1, tb = 2 * (lane & 1);
+            if (tq <= 4) {
+                const int fls = 8 / tq;                       // sub-blocks per flush
+                const int n_col = (sig % fls) * tq + token, f = sig / fls;
+                uint8_t *fr0 = base + (f * 32 + 4 * n_col + tb) * 16;
+                uint8_t *fr1 = fr0 + 16;
+                // the other half of each entry is zero: one sub-block per lane and flush
+                *reinterpret_cast<uint2 *>(fr0) = half ? make_uint2(0u, wq[0]) : make_uint2(wq[0], 0u);
+                *reinterpret_cast<uint2 *>(fr0 + 8) = half ? make_uint2(0u, wl[0]) : make_uint2(wl[0], 0u);
+                *reinterpret_cast<uint2 *>(fr1) = half ? make_uint2(0u, wq[1]) : make_uint2(wq[1], 0u);
+                *reinterpret_cast<uint2 *>(fr1 + 8) = half ? make_uint2(0u, wl[1]) : make_uint2(wl[1], 0u);
+            } else {
+                uint8_t *fr0 = base + ((nt * 8 + (sig >> 1)) * 32 + 4 * tk + tb) * 16 + half * 4;
+                uint8_t *fr1 = fr0 + 16;
+                *reinterpret_cast<uint32_t *>(fr0) = wq[0];
+                *reinterpret_cast<uint32_t *>(fr0 + 8) = wl[0];
+                *reinterpret_cast<uint32_t *>(fr1) = wq[1];
+                *reinterpret_cast<uint32_t *>(fr1 + 8) = wl[1];
+            }
+            if ((lane & 1) == 0) {
+                S[sig * mp + token] = sum16;
+                if (tq == 8) {   // S/dx (|S/dx| <= 16 * 127) as f16, B fragment of the sub-block-sum MMA
+                    const float sd = amax > 0.f ? sum16 * inv : 0.f;
+                    __half *hb = reinterpret_cast<__half *>(base + 4096 * ntl + (nt * 32 + 4 * tk + ((sig & 7) >> 1)) * 8 +
+                                                            (sig >> 3) * 4) + (sig & 1);
+                    *hb = __float2half_rn(sd);
+                }
+            }
+            if (lane == 0) S[16 * mp + token] = dx;
+        }
     }
 }
 template <int TYPE>
 __device__ __forceinline__ void stage_x(const float *x, int M, int64_t K, int64_t c, int n, uint8_t *dst, int xb,
                                         int tid, int nthreads) {
-    if (Tr<TYPE>::I8) stage_i8(x, M, K, c, n, dst, xb, tid, nthreads);
+    if (Tr<TYPE>::I8) stage_i8<TYPE>(x, M, K, c, n, dst, xb, tid, nthreads);
     else stage_f16<TYPE>(x, M, K, c, n, dst, xb, tid, nthreads);
 }
 
@@ -667,7 +838,7 @@ __global__ void gemv_xprep(const float *__restrict__ x, int M, int64_t K, int64_
 
 // ------------------------------------------------------- result columns ----
 // After a segment, the accumulators of the 4 lanes t of a group are reduced
-// over the lanes that hold the same token (q4_tq column layouts); then
+// over the lanes that hold the same token (i8_tq column layouts); then
 // for_owned visits each (row, token) value exactly once, on its owner lane:
 // f(nt, i, row within the rowgroup, token).
 template <int TQ, int NT>
@@ -862,9 +1033,11 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) gemv_kernel(const GemvA
             if (active) {
                 const uint8_t *xc = xbase + (c - (a.whole ? c0 : p0)) * FB;
                 if constexpr (TYPE == EF_Q4_K) compute_q4k<TQ, NT>(r, xc, acc, lane);
+                else if constexpr (TYPE == EF_Q6_K) compute_q6k<TQ, NT>(r, xc, acc, lane);
                 else compute<NT>(r, xc, a.M, acc, lane, grid, sgn);
                 if (SWIGLU) {
                     if constexpr (TYPE == EF_Q4_K) compute_q4k<TQ, NT>(ru, xc, acc2, lane);
+                    else if constexpr (TYPE == EF_Q6_K) compute_q6k<TQ, NT>(ru, xc, acc2, lane);
                     else compute<NT>(ru, xc, a.M, acc2, lane, grid, sgn);
                 }
             }
@@ -1024,7 +1197,7 @@ static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int64_t ctas) {
 constexpr int FUSED_MAX_TOKENS = 2;
 
 template <int TYPE> static int x_bytes_per_chunk(int M) {
-    return Tr<TYPE>::I8 ? i8_xbytes(M) : f16_xbytes<TYPE>(M);
+    return Tr<TYPE>::I8 ? i8_xbytes<TYPE>(M) : f16_xbytes<TYPE>(M);
 }
 
 template <int TYPE, int TQ, int NT, bool SWIGLU>
@@ -1038,7 +1211,7 @@ static int launch_t(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n,
         const size_t xbytes = (size_t)a.nchunks * a.xb;
         if (int rc = ensure_scratch(ctx, 0, xbytes)) return rc;
         a.xf = (const uint8_t *)ctx->scratch[0];
-        const int64_t work = Tr<TYPE>::I8 ? a.nchunks * q4_tq(a.M) * q4_nt(a.M) * 32
+        const int64_t work = Tr<TYPE>::I8 ? a.nchunks * i8_tq(a.M) * i8_nt(a.M) * 32
                                           : a.nchunks * a.M * (Tr<TYPE>::CHUNK / 4);
         int64_t blocks = (work + 255) / 256;
         if (blocks > 2LL * ctx->sm_count) blocks = 2LL * ctx->sm_count;
@@ -1069,8 +1242,8 @@ static int launch_t(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n,
     a.whole = p.whole;
     a.xs_bytes = p.xs_bytes;
     a.xs_half = p.xs_half;
-    // (1-2 tokens run TQ <= 2 for Q4_K and one 8-token tile for the others)
-    if constexpr (NT == 1 && (TYPE != EF_Q4_K || TQ <= 2))
+    // (1-2 tokens run TQ <= 2 for the 8-bit types and one 8-token tile for the others)
+    if constexpr (NT == 1 && (!Tr<TYPE>::I8 || TQ <= 2))
         if (fused) return launch_kernel<TYPE, TQ, NT, SWIGLU, true>(ctx, a, p.ctas);
     return launch_kernel<TYPE, TQ, NT, SWIGLU, false>(ctx, a, p.ctas);
 }
@@ -1078,7 +1251,7 @@ static int launch_t(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n,
 template <int TYPE, bool SWIGLU>
 static int launch_type(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n, const float *x) {
     const int M = a.M;
-    if constexpr (TYPE == EF_Q4_K) {
+    if constexpr (Tr<TYPE>::I8) {
         if (M <= 1) return launch_t<TYPE, 1, 1, SWIGLU>(ctx, a, ws, n, x);
         if (M <= 2) return launch_t<TYPE, 2, 1, SWIGLU>(ctx, a, ws, n, x);
         if (M <= 4) return launch_t<TYPE, 4, 1, SWIGLU>(ctx, a, ws, n, x);
@@ -1140,8 +1313,8 @@ static size_t gemv_xfrag_bytes(int type, int64_t nchunks, int M) {
     size_t fb = 0;
     switch (type) {
     case EF_Q8_0: fb = (size_t)f16_xbytes<EF_Q8_0>(M); break;
-    case EF_Q4_K: fb = (size_t)i8_xbytes(M); break;
-    case EF_Q6_K: fb = (size_t)f16_xbytes<EF_Q6_K>(M); break;
+    case EF_Q4_K: fb = (size_t)i8_xbytes<EF_Q4_K>(M); break;
+    case EF_Q6_K: fb = (size_t)i8_xbytes<EF_Q6_K>(M); break;
     case EF_IQ2_XXS: fb = (size_t)f16_xbytes<EF_IQ2_XXS>(M); break;
     case EF_IQ1_S: fb = (size_t)f16_xbytes<EF_IQ1_S>(M); break;
     default: return 0;
