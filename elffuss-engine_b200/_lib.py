@@ -68,6 +68,14 @@ _SIGS = {
     "ef_gemm": ([_P, _P, _P, _I, _I, _P, ctypes.c_uint32], _I),
     "ef_matmul": ([_P, _P, _P, _I, _P], _I),
     "ef_gemv_noalloc": ([_P, _P, _I, _P, _P], _I),
+    "ef_gather": ([_P, _P, _P, _I, _P], _I),
+    "ef_rmsnorm": ([_P, _P, _P, _I, _I, ctypes.c_float, _P], _I),
+    "ef_norm_add_norm": ([_P, _P, _P, _P, _P, _I, _I, ctypes.c_float, _P], _I),
+    "ef_shortconv": ([_P, _P, _P, _P, _I, _I, _I, _P], _I),
+    "ef_qk_norm_rope_cache": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, ctypes.c_float,
+                               _P, _P], _I),
+    "ef_attn_decode": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
+    "ef_argmax_step": ([_P, _P, _I, _P, _P, _P, _I, _I], _I),
 }
 
 

@@ -311,6 +311,13 @@ int ef_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows, flo
     return launch_dequant(ctx, w, row0, nrows, out);
 }
 
+int ef_gather(ef_ctx *ctx, const ef_weight *w, const int *dev_ids, int tokens, float *out) {
+    if (!ctx || !w || !dev_ids || !out) return EF_ERR_INVALID;
+    if (tokens < 1) return set_err(ctx, EF_ERR_SHAPE, "gather: tokens=%d < 1", tokens);
+    if (int rc = use_device(ctx)) return rc;
+    return launch_gather(ctx, w, dev_ids, tokens, out);
+}
+
 static int check_gemv(ef_ctx *ctx, const ef_weight *w, const float *x, int M, const void *y) {
     if (!w || !x || !y) return set_err(ctx, EF_ERR_INVALID, "gemv: null argument");
     if (M < 1) return set_err(ctx, EF_ERR_SHAPE, "gemv: M=%d < 1", M);

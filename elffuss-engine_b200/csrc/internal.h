@@ -51,6 +51,7 @@ int launch_repack(ef_ctx *ctx, int type, const uint8_t *dev_gguf, int64_t rows, 
                   ef_weight *w);
 int launch_unpack(ef_ctx *ctx, const ef_weight *w, uint8_t *dev_gguf);
 int launch_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows, float *out);
+int launch_gather(ef_ctx *ctx, const ef_weight *w, const int *ids, int tokens, float *out);
 
 // gemv.cu
 struct GemvPlan {

@@ -78,6 +78,34 @@ __global__ void dequant_kernel(int type, const uint8_t *__restrict__ src, int64_
     }
 }
 
+// Thread per GGUF block of `tokens` rows chosen by device-side ids (the
+// reference's quant.gather, js/ops.js:1104-1118 / gatherShader
+// kernels.wgsl.js:1199): out[t][:] = dequant(W)[ids[t]][:]. Ids outside
+// [0, rows) produce a row of zeros.
+__global__ void gather_kernel(int type, const uint8_t *__restrict__ src, const int *__restrict__ ids, int tokens,
+                              int64_t rows, int64_t bpr, int64_t nchunks, int bpc, int bb, int be, int tile_bytes,
+                              int64_t k, float *__restrict__ out) {
+    const int8_t *grid = type == EF_IQ2_XXS ? g_grid_iq2xxs_i8 : g_grid_iq1s_i8;
+    const int64_t total = (int64_t)tokens * bpr;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t t = i / bpr, b = i % bpr;
+        const int64_t row = ids[t];
+        float *o = out + t * k + b * be;
+        if (row < 0 || row >= rows) {
+            for (int j = 0; j < be; j++) o[j] = 0.f;
+            continue;
+        }
+        const int64_t rg = row / RG_ROWS, c = b / bpc;
+        const uint8_t *T = src + (rg * nchunks + c) * tile_bytes;
+        uint8_t blk[256];
+        float v[256];
+        gather_block(type, T, (int)(row % RG_ROWS), (int)(b % bpc), blk);
+        decode_block(type, blk, grid, v);
+        for (int j = 0; j < be; j++) o[j] = v[j];
+    }
+}
+
 static int grid_for(int64_t total) {
     int64_t g = (total + 255) / 256;
     if (g > 148 * 64) g = 148 * 64;
@@ -121,6 +149,18 @@ int launch_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows,
         w->type, w->dev, row0, nrows, bpr, w->nchunks, bpc, geo.block_bytes, geo.block_elems,
         geo.tile_bytes, w->k, out);
     return check_cuda(ctx, cudaGetLastError(), "dequant launch");
+}
+
+int launch_gather(ef_ctx *ctx, const ef_weight *w, const int *ids, int tokens, float *out) {
+    TypeGeo geo;
+    geo_of(w->type, geo);
+    const int bpc = geo.chunk_k / geo.block_elems;
+    const int64_t bpr = w->k / geo.block_elems;
+    ctx->launches++;
+    gather_kernel<<<grid_for((int64_t)tokens * bpr), 128, 0, ctx->stream>>>(
+        w->type, w->dev, ids, tokens, w->rows, bpr, w->nchunks, bpc, geo.block_bytes, geo.block_elems,
+        geo.tile_bytes, w->k, out);
+    return check_cuda(ctx, cudaGetLastError(), "gather launch");
 }
 
 }  // namespace ef

@@ -1,0 +1,243 @@
+"""Synthetic LFM3-shaped decoder driven through the quantized GEMV path.
+
+The reference runs LFM3 (LiquidAI's hybrid of gated short convolutions and
+grouped-query attention) in js/model.js: per layer an RMSNorm, either the
+short-conv block (convBlock, js/model.js:758-794) or the attention block
+(attnBlock, :853-983, with per-head QK-norm, NEOX RoPE, a sigmoid gate per
+head and sliding-window layers), each followed by a post-norm, the residual,
+the FFN norm, a SwiGLU FFN, its post-norm and the residual (feedForward,
+:635-664); the head is the tied embedding on the final norm of the last token
+(:1158-1171) and sampling is greedy (js/sample.js:95-99).
+
+This module builds that network from seeded synthetic weights (N(0, 0.02),
+quantized to Q8_0 with d = max|x|/127 and round-to-nearest-even; norm weights
+1; the depthwise conv weights kept in f32 as GGUF keeps them) and runs one
+token per step entirely on the device: every matrix product is this library's
+GEMV (q/k/v/gate as one sections call, gate/up as one SwiGLU call, the LM head
+over the 65536-row tied embedding), the rest are the library's decoder-step
+kernels. Position and token live in device memory, so a step is captured once
+as a CUDA graph and replayed per token.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import torch
+
+from . import formats
+from ._lib import EfError, check, lib
+
+Q8_0 = formats.type_id("Q8_0")
+
+
+@dataclass
+class LFM3Config:
+    hidden: int = 2048
+    layers: int = 16
+    attn_layers: tuple = (2, 5, 8, 10, 12, 14)   # the attention layers; the others are short-conv
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 64
+    ffn: int = 8192
+    vocab: int = 65536
+    conv_k: int = 3
+    rope_theta: float = 1e6
+    window: int = 4096              # sliding window of every other attention layer (the first, third, ...)
+    eps: float = 1e-5
+    max_pos: int = 4096 + 1024      # KV-cache capacity
+
+    def windows(self) -> dict:
+        """window per attention layer (0 = global): alternating, starting with a sliding one."""
+        return {l: (self.window if j % 2 == 0 else 0) for j, l in enumerate(self.attn_layers)}
+
+    def weight_params(self) -> int:
+        E, H, KV, D, F = self.hidden, self.heads, self.kv_heads, self.head_dim, self.ffn
+        conv = 3 * E * E + E * E
+        attn = H * D * E + 2 * KV * D * E + H * E + E * H * D
+        n_att = len(self.attn_layers)
+        return (self.layers - n_att) * conv + n_att * attn + self.layers * 3 * F * E + self.vocab * E
+
+
+SMALL = dict(hidden=256, layers=4, attn_layers=(1, 3), heads=4, kv_heads=2, head_dim=64, ffn=512, vocab=1024,
+             window=8, max_pos=96)
+
+
+def quantize_q8_0_torch(w: torch.Tensor) -> torch.Tensor:
+    """f32 [rows][k] -> Q8_0 bytes (uint8, same device): d = max|x|/127 stored
+    as f16, q = round-half-even(x / d) in f32 -- the arithmetic of
+    formats.quantize_q8_0."""
+    b = w.reshape(-1, 32).float()
+    amax = b.abs().amax(dim=1)
+    d = amax / 127.0
+    inv = torch.where(d > 0, 1.0 / torch.where(d > 0, d, torch.ones_like(d)), torch.zeros_like(d))
+    q = torch.clamp(torch.round(b * inv[:, None]), -127, 127).to(torch.int8)
+    out = torch.empty(b.shape[0], 34, dtype=torch.uint8, device=w.device)
+    out[:, 0:2] = d.to(torch.float16).view(torch.uint8).reshape(-1, 2)
+    out[:, 2:] = q.view(torch.uint8)
+    return out.reshape(-1)
+
+
+def synth_weights(cfg: LFM3Config, seed: int = 0, device: str = "cpu") -> dict:
+    """Named tensors of the network: Q8_0 bytes (uint8, 1-D) for the matrices,
+    f32 for the conv kernels and the norms. Tensor i draws N(0, 0.02) from a
+    generator seeded with seed * 1000 + i on `device`."""
+    E, H, KV, D, F, V = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab
+    out, idx = {}, [0]
+
+    def normal(*shape):
+        g = torch.Generator(device=device)
+        g.manual_seed(seed * 1000 + idx[0])
+        idx[0] += 1
+        return torch.empty(*shape, device=device).normal_(0.0, 0.02, generator=g)
+
+    def mat(name, rows, k):
+        out[name] = (quantize_q8_0_torch(normal(rows, k)), rows, k)
+
+    ones = lambda n: torch.ones(n, device=device)
+    mat("token_embd", V, E)
+    out["output_norm"] = ones(E)
+    for l in range(cfg.layers):
+        p = f"blk.{l}."
+        out[p + "attn_norm"] = ones(E)
+        out[p + "post_attention_norm"] = ones(E)
+        out[p + "ffn_norm"] = ones(E)
+        out[p + "post_ffw_norm"] = ones(E)
+        if l in cfg.attn_layers:
+            mat(p + "attn_q", H * D, E)
+            mat(p + "attn_k", KV * D, E)
+            mat(p + "attn_v", KV * D, E)
+            mat(p + "attn_gate", H, E)
+            mat(p + "attn_output", E, H * D)
+            out[p + "attn_q_norm"] = ones(D)
+            out[p + "attn_k_norm"] = ones(D)
+        else:
+            mat(p + "shortconv.in_proj", 3 * E, E)
+            out[p + "shortconv.conv"] = normal(E, cfg.conv_k)
+            mat(p + "shortconv.out_proj", E, E)
+        mat(p + "ffn_gate", F, E)
+        mat(p + "ffn_up", F, E)
+        mat(p + "ffn_down", E, F)
+    return out
+
+
+def _p(t: torch.Tensor):
+    return ctypes.c_void_p(t.data_ptr())
+
+
+class LFM3Decoder:
+    """The network on one GPU, a step per token (see the module docstring)."""
+
+    def __init__(self, ops, cfg: LFM3Config, weights: dict):
+        self.ops, self.cfg, self.L = ops, cfg, lib()
+        E, H, KV, D, F = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn
+        dev = torch.device("cuda", ops.ctx.device)
+        self.w, self.f32 = {}, {}
+        for name, val in weights.items():
+            if isinstance(val, tuple):
+                raw, rows, k = val
+                self.w[name] = ops.load_weight("Q8_0", raw.to(dev), rows, k, label=name)
+            else:
+                self.f32[name] = val.to(dev).float().contiguous()
+        z = lambda *s: torch.zeros(*s, device=dev)
+        self.x, self.nrm = z(E), z(E)
+        self.bcx, self.conv_y = z(3 * E), z(E)
+        self.o, self.sw, self.d = z(E), z(F), z(E)
+        self.q, self.k, self.v, self.g, self.att = z(H * D), z(KV * D), z(KV * D), z(H), z(H * D)
+        self.logits = z(cfg.vocab)
+        self.state = {l: z(cfg.conv_k - 1, E) for l in range(cfg.layers) if l not in cfg.attn_layers}
+        self.kc = {l: z(cfg.max_pos, KV, D) for l in cfg.attn_layers}
+        self.vc = {l: z(cfg.max_pos, KV, D) for l in cfg.attn_layers}
+        self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.out_tokens = torch.full((cfg.max_pos,), -1, dtype=torch.int32, device=dev)
+        self.out_base = 0
+        self.windows = cfg.windows()
+        self.graph = None
+
+    def reset(self, out_base: int):
+        for t in list(self.state.values()) + list(self.kc.values()) + list(self.vc.values()):
+            t.zero_()
+        self.pos.zero_()
+        self.out_tokens.fill_(-1)
+        self.out_base = out_base
+        self.graph = None
+
+    # -- one decode step (token self.tok at position self.pos) -----------------
+    def step(self):
+        L, cfg, h = self.L, self.cfg, self.ops.ctx.bind()
+        E, H, KV, D, F = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn
+        W, f = self.w, self.f32
+        eps = ctypes.c_float(cfg.eps)
+        check(L.ef_gather(h, W["token_embd"].h, _p(self.tok), 1, _p(self.x)), h)
+        check(L.ef_rmsnorm(h, _p(self.x), _p(f["blk.0.attn_norm"]), 1, E, eps, _p(self.nrm)), h)
+        for l in range(cfg.layers):
+            p = f"blk.{l}."
+            if l in cfg.attn_layers:
+                ws = (ctypes.c_void_p * 4)(W[p + "attn_q"].h.value, W[p + "attn_k"].h.value, W[p + "attn_v"].h.value,
+                                           W[p + "attn_gate"].h.value)
+                ys = (ctypes.c_void_p * 4)(self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.g.data_ptr())
+                check(L.ef_gemv_sections(h, ctypes.cast(ws, ctypes.POINTER(ctypes.c_void_p)), 4, _p(self.nrm), 1,
+                                         ctypes.cast(ys, ctypes.POINTER(ctypes.c_void_p))), h)
+                check(L.ef_qk_norm_rope_cache(h, _p(self.q), _p(self.k), _p(self.v), _p(f[p + "attn_q_norm"]),
+                                              _p(f[p + "attn_k_norm"]), _p(self.pos), cfg.max_pos, H, KV, D,
+                                              ctypes.c_float(cfg.rope_theta), eps, _p(self.kc[l]), _p(self.vc[l])), h)
+                check(L.ef_attn_decode(h, _p(self.q), _p(self.kc[l]), _p(self.vc[l]), _p(self.g), _p(self.pos),
+                                       cfg.max_pos, self.windows[l], H, KV, D, _p(self.att)), h)
+                check(L.ef_gemv(h, W[p + "attn_output"].h, _p(self.att), 1, _p(self.o)), h)
+            else:
+                check(L.ef_gemv(h, W[p + "shortconv.in_proj"].h, _p(self.nrm), 1, _p(self.bcx)), h)
+                check(L.ef_shortconv(h, _p(self.bcx), _p(f[p + "shortconv.conv"]), _p(self.state[l]), 1, E,
+                                     cfg.conv_k, _p(self.conv_y)), h)
+                check(L.ef_gemv(h, W[p + "shortconv.out_proj"].h, _p(self.conv_y), 1, _p(self.o)), h)
+            check(L.ef_norm_add_norm(h, _p(self.o), _p(f[p + "post_attention_norm"]), _p(self.x),
+                                     _p(f[p + "ffn_norm"]), 1, E, eps, _p(self.nrm)), h)
+            check(L.ef_gemv_swiglu(h, W[p + "ffn_gate"].h, W[p + "ffn_up"].h, _p(self.nrm), 1, _p(self.sw)), h)
+            check(L.ef_gemv(h, W[p + "ffn_down"].h, _p(self.sw), 1, _p(self.d)), h)
+            nxt = f[f"blk.{l + 1}.attn_norm"] if l + 1 < cfg.layers else f["output_norm"]
+            check(L.ef_norm_add_norm(h, _p(self.d), _p(f[p + "post_ffw_norm"]), _p(self.x), _p(nxt), 1, E, eps,
+                                     _p(self.nrm)), h)
+        check(L.ef_gemv(h, W["token_embd"].h, _p(self.nrm), 1, _p(self.logits)), h)
+        check(L.ef_argmax_step(h, _p(self.logits), cfg.vocab, _p(self.tok), _p(self.pos), _p(self.out_tokens),
+                               self.out_base, cfg.max_pos), h)
+
+    def capture(self):
+        """Record one step as a CUDA graph (after one eager step has sized every scratch)."""
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=s):
+            self.step()
+        torch.cuda.synchronize()
+
+    def run_step(self):
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self.step()
+
+    def prefill(self, prompt: torch.Tensor):
+        """Prompt ids one step each (the token each step predicts is replaced by
+        the next prompt id); after the last one, self.tok is the first
+        generated token."""
+        prompt = prompt.to(self.tok.device, torch.int32)
+        for i in range(prompt.numel()):
+            self.tok.copy_(prompt[i:i + 1])
+            self.run_step()
+
+    def generate(self, prompt: torch.Tensor, n: int, use_graph: bool = True) -> list:
+        """Greedy continuation of `prompt` by n tokens."""
+        self.reset(out_base=prompt.numel())
+        # one eager step sizes the scratch and configures every kernel; then
+        # the state is reset and the graph recorded
+        self.tok.copy_(prompt[:1].to(self.tok.device, torch.int32))
+        self.step()
+        torch.cuda.synchronize()
+        self.reset(out_base=prompt.numel())
+        if use_graph:
+            self.capture()
+        self.prefill(prompt)
+        for _ in range(n - 1):
+            self.run_step()
+        torch.cuda.synchronize()
+        return self.out_tokens[:n].cpu().tolist()

@@ -138,6 +138,13 @@ EF_API int ef_weight_unpack(ef_ctx *ctx, const ef_weight *w, void *dev_gguf_out)
  * reference decoders. quant.dequant (js/ops.js:813-823, kernels.wgsl.js:903). */
 EF_API int ef_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows, float *dev_out);
 
+/* Rows of dequant(W) chosen by device-side ids: out[t][:] = dequant(W)[ids[t]]
+ * for t < tokens (f32 [tokens][k]); an id outside [0, rows) gives zeros.
+ * quant.gather (js/ops.js:1104-1118, gatherShader kernels.wgsl.js:1199), the
+ * embedding lookup; the ids are read on the device, so the call can sit in a
+ * captured CUDA graph. */
+EF_API int ef_gather(ef_ctx *ctx, const ef_weight *w, const int *dev_ids, int tokens, float *dev_out);
+
 /* Decode GEMV, 1 <= M <= 16 tokens: y[M][rows] = x[M][k] . dequant(W)^T.
  * quant.gemv.matmul / quant.matmul for few tokens (js/ops.gemv.js:148-165,
  * js/ops.js:834-837). EF_NOT_APPLICABLE for M > 16. */
@@ -189,6 +196,57 @@ EF_API int ef_gemv_noalloc(const ef_weight *w, const float *x, int M, float *y, 
 /* The dispatcher of quant.matmul (js/ops.js:827-1101): GEMV for tokens <= 16,
  * GEMM above, same contract and output. */
 EF_API int ef_matmul(ef_ctx *ctx, const ef_weight *w, const float *x, int tokens, float *y);
+
+/* ---- decoder-step operations ---------------------------------------------
+ * The non-matmul steps of the reference's forward (js/model.js), used by the
+ * synthetic LFM3-shaped decoder that measures the GEMV path end to end. All
+ * pointers are device pointers, f32 unless stated; rows are contiguous.
+ * Positions are int32 in device memory so that a decode step can be captured
+ * as a CUDA graph. */
+
+/* y = x * rsqrt(mean(x^2) + eps) * w per row of n (nn.rmsnorm,
+ * kernels.nn.wgsl.js:46-80). */
+EF_API int ef_rmsnorm(ef_ctx *ctx, const float *x, const float *w, int rows, int n, float eps, float *y);
+
+/* Per row: x += rmsnorm(o) * w_post (x += o when w_post is NULL), then
+ * nrm = rmsnorm(x) * w_next -- post-norm, residual and the next block's norm
+ * in one pass (js/model.js:635-664, fusion F1 js/ops.fusion.js:131-150). */
+EF_API int ef_norm_add_norm(ef_ctx *ctx, const float *o, const float *w_post, float *x, const float *w_next,
+                            int rows, int n, float eps, float *nrm);
+
+/* Gated short convolution (js/model.js:758-794): bcx [tokens][3C] = B | C | x,
+ * y[t][c] = C[t][c] * sum_r win[c][t+r] * w[c][r] over the window of the
+ * kernel-1 previous B*x values (state [kernel-1][C], oldest first, updated in
+ * place) followed by the tokens' B*x; w [C][kernel] in temporal order.
+ * kernel 3 only. */
+EF_API int ef_shortconv(ef_ctx *ctx, const float *bcx, const float *conv_w, float *state, int tokens, int channels,
+                        int kernel, float *y);
+
+/* One decode token: per-head RMSNorm (weights wq, wk [head_dim]) of q [heads]
+ * [head_dim] (in place) and k [kv_heads][head_dim], NEOX RoPE at position
+ * *pos with theta = pos * theta_base^(-2i/head_dim), then k and v written to
+ * the caches [max_pos][kv_heads][head_dim] at *pos (js/model.js:853-945); a
+ * position at or past max_pos is not stored. head_dim 64 only. */
+EF_API int ef_qk_norm_rope_cache(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq,
+                                 const float *wk, const int *pos, int max_pos, int heads, int kv_heads,
+                                 int head_dim, float theta_base, float eps, float *kcache, float *vcache);
+
+/* One decode token of attention over cache positions 0..*pos (a key is
+ * visible when *pos - key < window; window 0 = all), scale 1/sqrt(head_dim),
+ * grouped heads (heads / kv_heads queries per cache head); when head_gate is
+ * not NULL each head's output is multiplied by sigmoid(head_gate[h])
+ * (kernels.nn.wgsl.js:141-200, kernels.model.wgsl.js:89-105). out
+ * [heads][head_dim]; head_dim 64 only; max_pos = the caches' capacity. */
+EF_API int ef_attn_decode(ef_ctx *ctx, const float *q, const float *kcache, const float *vcache,
+                          const float *head_gate, const int *pos, int max_pos, int window, int heads, int kv_heads,
+                          int head_dim, float *out);
+
+/* Greedy sampling (js/sample.js:95-99): *token = argmax of n logits (strict
+ * '>', the lowest index wins ties); *pos += 1; when out_tokens is not NULL the
+ * token is also stored at out_tokens[new *pos - out_base] if that index is in
+ * [0, out_cap). */
+EF_API int ef_argmax_step(ef_ctx *ctx, const float *logits, int n, int *token, int *pos, int *out_tokens,
+                          int out_base, int out_cap);
 
 #ifdef __cplusplus
 }
