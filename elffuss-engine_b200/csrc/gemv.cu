@@ -11,8 +11,8 @@
 //  * Work split: CTA = one rowblock (8 rowgroups of 16 rows) x one k-slice;
 //    the k-slices of a rowblock form one thread-block cluster whose partial
 //    sums are added through distributed shared memory in rank order
-//    (deterministic, no atomics). The smallest k-split that keeps 3/4 of the
-//    SMs busy is used.
+//    (deterministic, no atomics). The widest k-split (up to 8) whose
+//    clusters all fit on the device at once is used.
 //  * Weights: each warp streams the tiles of its rowgroup straight from HBM
 //    into registers (128-bit non-allocating loads of the lane's fragment
 //    parts), one tile ahead of the math. Measured on B200, loads into
@@ -48,6 +48,9 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "common.cuh"
 #include "gen/iq_grids.h"
@@ -1110,18 +1113,12 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) gemv_kernel(const GemvA
 }
 
 // ------------------------------------------------------------------ host ---
-// Work split: CTA = 8 rowgroups (one rowblock) x one k-slice; the smallest
-// k-split that puts at least 3/4 of the SMs to work (at most 8, one cluster).
-// Measured on B200: splitting rowblocks further (stream-K over all SMs) or
-// adding rows per SM loses more to the cross-CTA reduction and the shorter
-// weight streams than it gains from the idle SMs. Activation data: with 1-2
-// tokens the slice's chunks at once when they fit, else phases (two buffers
-// when a prep kernel supplies the data).
-GemvPlan gemv_plan(int sm_count, int64_t rowblocks, int64_t nchunks, int xb, bool fused) {
+// Work split: CTA = 8 rowgroups (one rowblock) x one k-slice, the k-slices of
+// a rowblock in one thread-block cluster. Activation data: with 1-2 tokens
+// the slice's chunks at once when they fit, else phases (two buffers when a
+// prep kernel supplies the data).
+GemvPlan gemv_plan(int64_t rowblocks, int64_t nchunks, int xb, bool fused, int ks) {
     GemvPlan p = {};
-    const int64_t want = (3LL * sm_count + 3) / 4;
-    int ks = 1;
-    while (ks < 8 && ks < nchunks && rowblocks * ks < want) ks++;
     p.kslices = ks;
     p.ctas = rowblocks * ks;
     const int64_t slice = (nchunks + ks - 1) / ks;
@@ -1140,6 +1137,41 @@ GemvPlan gemv_plan(int sm_count, int64_t rowblocks, int64_t nchunks, int xb, boo
     return p;
 }
 
+// How many clusters of `ks` CTAs of this kernel the device holds at once
+// (cudaOccupancyMaxActiveClusters; cached per kernel, device, size and shared
+// memory). On B200 this is not SMs / ks: clusters are placed inside one GPC,
+// and with one 512-thread CTA per SM it measured 148, 74, 45, 33, 26, 22, 15,
+// 15 for ks = 1..8.
+static int max_active_clusters(ef_ctx *ctx, const void *kern, int threads, size_t smem, int ks) {
+    static std::mutex mu;
+    static std::map<std::tuple<const void *, int, int, size_t>, int> cache;
+    const auto key = std::make_tuple(kern, ctx->device, ks, smem);
+    {
+        std::lock_guard<std::mutex> g(mu);
+        auto it = cache.find(key);
+        if (it != cache.end()) return it->second;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)ks, 1, 1);
+    cfg.blockDim = dim3((unsigned)threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = ks;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        n = 0;
+    }
+    std::lock_guard<std::mutex> g(mu);
+    cache[key] = n;
+    return n;
+}
+
 // Programmatic dependent launch between consecutive kernels: off by default
 // (measured on B200 over the mixed-shape benchmark sequence: the early-
 // launched CTAs of the next GEMV hold shared memory and registers that the
@@ -1156,8 +1188,9 @@ template <int TYPE, int TQ, int NT, bool SWIGLU> constexpr int kh_of() {
 }
 
 template <int TYPE, int TQ, int NT, bool SWIGLU, bool FUSED>
-static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int64_t ctas) {
+static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int64_t rowblocks, bool fused) {
     constexpr int KH = kh_of<TYPE, TQ, NT, SWIGLU>();
+    constexpr int threads = GV_WARPS * KH * 32;
     auto kern = gemv_kernel<TYPE, TQ, NT, SWIGLU, FUSED, KH>;
     static unsigned long long configured = 0;   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
@@ -1165,10 +1198,28 @@ static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int64_t ctas) {
         if (e != cudaSuccess) return check_cuda(ctx, e, "gemv smem attribute");
         configured |= 1ull << ctx->device;
     }
+    // The widest k-split (at most 8 slices, a portable cluster) whose clusters
+    // all fit on the device at once. Measured on B200 over 1024-12288 rows x
+    // 2048-8192 columns: the time falls as the split widens until the grid no
+    // longer fits in one wave, then rises by 40-70 %.
+    GemvPlan p = {};
+    size_t smem = 0;
+    for (int ks = (int)std::min<int64_t>(8, a.nchunks); ks >= 1; ks--) {
+        p = gemv_plan(rowblocks, a.nchunks, a.xb, fused, ks);
+        smem = gemv_smem<TYPE, NT, SWIGLU, KH>(p.xs_bytes, ks > 1);
+        if (ks == 1 || (smem <= 227 * 1024 && rowblocks <= max_active_clusters(ctx, (const void *)kern, threads, smem, ks)))
+            break;
+    }
+    a.kslices = p.kslices;
+    a.phase_chunks = p.phase_chunks;
+    a.whole = p.whole;
+    a.xs_bytes = p.xs_bytes;
+    a.xs_half = p.xs_half;
+    const int64_t ctas = p.ctas;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctas, 1, 1);
-    cfg.blockDim = dim3(GV_WARPS * KH * 32, 1, 1);
-    cfg.dynamicSmemBytes = gemv_smem<TYPE, NT, SWIGLU, KH>(a.xs_bytes, a.kslices > 1);
+    cfg.blockDim = dim3(threads, 1, 1);
+    cfg.dynamicSmemBytes = smem;
     if (cfg.dynamicSmemBytes > 227 * 1024)
         return set_err(ctx, EF_ERR_RANGE, "gemv: %zu bytes of shared memory needed", cfg.dynamicSmemBytes);
     cfg.stream = ctx->stream;
@@ -1236,16 +1287,10 @@ static int launch_t(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n,
         rowblocks += (int)((ws[i]->rowgroups + GV_WARPS - 1) / GV_WARPS);
         a.rb_end[i] = rowblocks;
     }
-    const GemvPlan p = gemv_plan(ctx->sm_count, rowblocks, a.nchunks, a.xb, fused);
-    a.kslices = p.kslices;
-    a.phase_chunks = p.phase_chunks;
-    a.whole = p.whole;
-    a.xs_bytes = p.xs_bytes;
-    a.xs_half = p.xs_half;
     // (1-2 tokens run TQ <= 2 for the 8-bit types and one 8-token tile for the others)
     if constexpr (NT == 1 && (!Tr<TYPE>::I8 || TQ <= 2))
-        if (fused) return launch_kernel<TYPE, TQ, NT, SWIGLU, true>(ctx, a, p.ctas);
-    return launch_kernel<TYPE, TQ, NT, SWIGLU, false>(ctx, a, p.ctas);
+        if (fused) return launch_kernel<TYPE, TQ, NT, SWIGLU, true>(ctx, a, rowblocks, fused);
+    return launch_kernel<TYPE, TQ, NT, SWIGLU, false>(ctx, a, rowblocks, fused);
 }
 
 template <int TYPE, bool SWIGLU>

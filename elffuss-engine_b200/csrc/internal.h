@@ -62,7 +62,7 @@ struct GemvPlan {
     int xs_bytes;      // shared memory for activation data
     int xs_half;       // bytes of one phase buffer
 };
-GemvPlan gemv_plan(int sm_count, int64_t rowblocks, int64_t nchunks, int xb, bool fused);
+GemvPlan gemv_plan(int64_t rowblocks, int64_t nchunks, int xb, bool fused, int ks);
 int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight *w_up,
                 const float *x, int M, float *const *ys);
 

@@ -43,39 +43,77 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
     return warp_sum(s);
 }
 
-// one CTA per row
-__global__ void rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w, int n, float eps,
-                               float *__restrict__ y) {
+// One CTA per row of T = min(256, n/4) threads; each thread keeps V float4 of
+// the row in registers (all loads issued before the first reduction),
+// n = 4 * T * V.
+template <int V>
+__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
+                                                      int n, float eps, float *__restrict__ y) {
     __shared__ float red[32];
-    const float *xr = x + (int64_t)blockIdx.x * n;
-    float *yr = y + (int64_t)blockIdx.x * n;
+    const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)blockIdx.x * n);
+    const float4 *wr = reinterpret_cast<const float4 *>(w);
+    float4 *yr = reinterpret_cast<float4 *>(y + (int64_t)blockIdx.x * n);
+    float4 v[V], wv[V];
+#pragma unroll
+    for (int j = 0; j < V; j++) {
+        v[j] = xr[threadIdx.x + blockDim.x * j];
+        wv[j] = wr[threadIdx.x + blockDim.x * j];
+    }
     float ss = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += xr[i] * xr[i];
+#pragma unroll
+    for (int j = 0; j < V; j++) ss += v[j].x * v[j].x + v[j].y * v[j].y + v[j].z * v[j].z + v[j].w * v[j].w;
     const float scale = rsqrtf(block_sum(ss, red) / (float)n + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = xr[i] * scale * w[i];
+#pragma unroll
+    for (int j = 0; j < V; j++)
+        yr[threadIdx.x + blockDim.x * j] = make_float4(v[j].x * scale * wv[j].x, v[j].y * scale * wv[j].y,
+                                                v[j].z * scale * wv[j].z, v[j].w * scale * wv[j].w);
 }
 
-// x += rmsnorm(o) * w_post (or += o without a post-norm); nrm = rmsnorm(x) * w_next
-__global__ void norm_add_norm_kernel(const float *__restrict__ o, const float *__restrict__ w_post,
-                                     float *__restrict__ x, const float *__restrict__ w_next, int n, float eps,
-                                     float *__restrict__ nrm) {
+// x += rmsnorm(o) * w_post (or += o without a post-norm); nrm = rmsnorm(x) * w_next.
+// Same shape rules as rmsnorm_kernel.
+template <int V>
+__global__ void __launch_bounds__(256) norm_add_norm_kernel(const float *__restrict__ o,
+                                                            const float *__restrict__ w_post, float *__restrict__ x,
+                                                            const float *__restrict__ w_next, int n, float eps,
+                                                            float *__restrict__ nrm) {
     __shared__ float red[32];
-    const int64_t base = (int64_t)blockIdx.x * n;
+    const int64_t row = (int64_t)blockIdx.x * (n / 4);
+    const float4 *o4 = reinterpret_cast<const float4 *>(o) + row;
+    float4 *x4 = reinterpret_cast<float4 *>(x) + row;
+    float4 *n4 = reinterpret_cast<float4 *>(nrm) + row;
+    const float4 *wp = reinterpret_cast<const float4 *>(w_post), *wn = reinterpret_cast<const float4 *>(w_next);
+    float4 ov[V], xv[V], wpv[V], wnv[V];
+#pragma unroll
+    for (int j = 0; j < V; j++) {
+        const int i = threadIdx.x + blockDim.x * j;
+        ov[j] = o4[i];
+        xv[j] = x4[i];
+        wpv[j] = w_post ? wp[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+        wnv[j] = wn[i];
+    }
     float s1 = 1.f;
     if (w_post) {
         float ss = 0.f;
-        for (int i = threadIdx.x; i < n; i += blockDim.x) ss += o[base + i] * o[base + i];
+#pragma unroll
+        for (int j = 0; j < V; j++)
+            ss += ov[j].x * ov[j].x + ov[j].y * ov[j].y + ov[j].z * ov[j].z + ov[j].w * ov[j].w;
         s1 = rsqrtf(block_sum(ss, red) / (float)n + eps);
     }
     float ss2 = 0.f;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-        const float add = w_post ? o[base + i] * s1 * w_post[i] : o[base + i];
-        const float r = x[base + i] + add;
-        x[base + i] = r;
-        ss2 += r * r;
+#pragma unroll
+    for (int j = 0; j < V; j++) {
+        xv[j].x += ov[j].x * s1 * wpv[j].x;
+        xv[j].y += ov[j].y * s1 * wpv[j].y;
+        xv[j].z += ov[j].z * s1 * wpv[j].z;
+        xv[j].w += ov[j].w * s1 * wpv[j].w;
+        ss2 += xv[j].x * xv[j].x + xv[j].y * xv[j].y + xv[j].z * xv[j].z + xv[j].w * xv[j].w;
+        x4[threadIdx.x + blockDim.x * j] = xv[j];
     }
     const float s2 = rsqrtf(block_sum(ss2, red) / (float)n + eps);
-    for (int i = threadIdx.x; i < n; i += blockDim.x) nrm[base + i] = x[base + i] * s2 * w_next[i];
+#pragma unroll
+    for (int j = 0; j < V; j++)
+        n4[threadIdx.x + blockDim.x * j] = make_float4(xv[j].x * s2 * wnv[j].x, xv[j].y * s2 * wnv[j].y,
+                                                xv[j].z * s2 * wnv[j].z, xv[j].w * s2 * wnv[j].w);
 }
 
 // One thread per channel; tokens in order. bcx [T][3C] = B | C | x;
@@ -201,13 +239,36 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const float *__r
 // Greedy argmax over n logits (strict '>': lowest index wins ties); writes the
 // token, records it in out_tokens[*pos + 1 - out_base] when that index is in
 // [0, out_cap), and advances *pos.
-__global__ void argmax_step_kernel(const float *__restrict__ logits, int n, int *__restrict__ token,
-                                   int *__restrict__ pos, int *__restrict__ out_tokens, int out_base, int out_cap) {
+__global__ void __launch_bounds__(1024) argmax_step_kernel(const float *__restrict__ logits, int n,
+                                                           int *__restrict__ token, int *__restrict__ pos,
+                                                           int *__restrict__ out_tokens, int out_base, int out_cap) {
     __shared__ float bv[32];
     __shared__ int bi[32];
     float best = -INFINITY;
     int bidx = 0x7fffffff;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    // float4 of each thread in order, 8 loads in flight; then the scalar tail
+    const int n4 = n / 4;
+    const float4 *l4 = reinterpret_cast<const float4 *>(logits);
+    for (int base = 0; base < n4; base += 8 * blockDim.x) {
+        float4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i = base + u * blockDim.x + threadIdx.x;
+            v[u] = i < n4 ? l4[i] : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; u++) {
+            const int i4 = 4 * (base + u * blockDim.x + threadIdx.x);
+            const float e[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                if (e[c] > best || (e[c] == best && i4 + c < bidx)) {
+                    best = e[c];
+                    bidx = i4 + c;
+                }
+        }
+    }
+    for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) {
         const float v = logits[i];
         if (v > best || (v == best && i < bidx)) {
             best = v;
@@ -259,10 +320,28 @@ using namespace ef;
 
 extern "C" {
 
+// Row of n: T = min(256, n/4) threads with V float4 each, n = 4 * T * V,
+// V in {1, 2, 4, 8}; 0 when n has no such split (n a multiple of 128 up to 8192).
+static int norm_v(int n, int &threads) {
+    if (n < 128 || n % 128) return 0;
+    threads = n / 4 < 256 ? n / 4 : 256;
+    if (n % (4 * threads)) return 0;
+    const int v = n / (4 * threads);
+    return v == 1 || v == 2 || v == 4 || v == 8 ? v : 0;
+}
+
 int ef_rmsnorm(ef_ctx *ctx, const float *x, const float *w, int rows, int n, float eps, float *y) {
     if (!ctx || !x || !w || !y || rows < 1 || n < 1) return ctx ? set_err(ctx, EF_ERR_INVALID, "rmsnorm: bad arguments") : EF_ERR_INVALID;
+    int th = 0;
+    const int v = norm_v(n, th);
+    if (!v) return set_err(ctx, EF_ERR_SHAPE, "rmsnorm: n=%d (a multiple of 128 up to 8192, power-of-2 blocks)", n);
     ctx->launches++;
-    rmsnorm_kernel<<<rows, 256, 0, ctx->stream>>>(x, w, n, eps, y);
+    switch (v) {
+    case 1: rmsnorm_kernel<1><<<rows, th, 0, ctx->stream>>>(x, w, n, eps, y); break;
+    case 2: rmsnorm_kernel<2><<<rows, th, 0, ctx->stream>>>(x, w, n, eps, y); break;
+    case 4: rmsnorm_kernel<4><<<rows, th, 0, ctx->stream>>>(x, w, n, eps, y); break;
+    default: rmsnorm_kernel<8><<<rows, th, 0, ctx->stream>>>(x, w, n, eps, y); break;
+    }
     return check_cuda(ctx, cudaGetLastError(), "rmsnorm launch");
 }
 
@@ -270,8 +349,16 @@ int ef_norm_add_norm(ef_ctx *ctx, const float *o, const float *w_post, float *x,
                      float eps, float *nrm) {
     if (!ctx || !o || !x || !w_next || !nrm || rows < 1 || n < 1)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "norm_add_norm: bad arguments") : EF_ERR_INVALID;
+    int th = 0;
+    const int v = norm_v(n, th);
+    if (!v) return set_err(ctx, EF_ERR_SHAPE, "norm_add_norm: n=%d (a multiple of 128 up to 8192, power-of-2 blocks)", n);
     ctx->launches++;
-    norm_add_norm_kernel<<<rows, 256, 0, ctx->stream>>>(o, w_post, x, w_next, n, eps, nrm);
+    switch (v) {
+    case 1: norm_add_norm_kernel<1><<<rows, th, 0, ctx->stream>>>(o, w_post, x, w_next, n, eps, nrm); break;
+    case 2: norm_add_norm_kernel<2><<<rows, th, 0, ctx->stream>>>(o, w_post, x, w_next, n, eps, nrm); break;
+    case 4: norm_add_norm_kernel<4><<<rows, th, 0, ctx->stream>>>(o, w_post, x, w_next, n, eps, nrm); break;
+    default: norm_add_norm_kernel<8><<<rows, th, 0, ctx->stream>>>(o, w_post, x, w_next, n, eps, nrm); break;
+    }
     return check_cuda(ctx, cudaGetLastError(), "norm_add_norm launch");
 }
 

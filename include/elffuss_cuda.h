@@ -205,12 +205,15 @@ EF_API int ef_matmul(ef_ctx *ctx, const ef_weight *w, const float *x, int tokens
  * as a CUDA graph. */
 
 /* y = x * rsqrt(mean(x^2) + eps) * w per row of n (nn.rmsnorm,
- * kernels.nn.wgsl.js:46-80). */
+ * kernels.nn.wgsl.js:46-80); n = 128 * 2^j up to 8192 (other multiples of
+ * 512 up to 8192 where n / min(256, n/4) / 4 is 1, 2, 4 or 8), rows 16-byte
+ * aligned. */
 EF_API int ef_rmsnorm(ef_ctx *ctx, const float *x, const float *w, int rows, int n, float eps, float *y);
 
 /* Per row: x += rmsnorm(o) * w_post (x += o when w_post is NULL), then
  * nrm = rmsnorm(x) * w_next -- post-norm, residual and the next block's norm
- * in one pass (js/model.js:635-664, fusion F1 js/ops.fusion.js:131-150). */
+ * in one pass (js/model.js:635-664, fusion F1 js/ops.fusion.js:131-150).
+ * Same n and alignment rules as ef_rmsnorm. */
 EF_API int ef_norm_add_norm(ef_ctx *ctx, const float *o, const float *w_post, float *x, const float *w_next,
                             int rows, int n, float eps, float *nrm);
 
