@@ -229,6 +229,68 @@ def bench_gemm(ops, L, args, capture, timed_replays, rank):
                          "frac": round(ach / peak, 4), "peak_source": src, "kernel": "gemm_q8_0_kernel"}}
 
 
+DECODE_PROMPT, DECODE_TOKENS = 512, 128
+
+
+def bench_decode(ops, args, world, rank, barrier, max_over_ranks):
+    """Config 3: the synthetic LFM3-shaped decoder (lfm3.py), tensor-parallel
+    over the ranks when world > 1: a 512-id prompt (one captured step per id),
+    then 128 greedy tokens, each one replay of the captured step."""
+    import torch
+
+    from elffuss_engine_b200.lfm3 import LFM3Config, LFM3Decoder, shard_weights, synth_weights
+    cfg = LFM3Config()
+    w = synth_weights(cfg, seed=0, device="cuda")
+    if world > 1:
+        w = shard_weights(cfg, w, rank, world)
+    dec = LFM3Decoder(ops, cfg, w, rank, world)
+    del w
+    torch.cuda.empty_cache()
+    prompt = torch.randint(0, cfg.vocab, (DECODE_PROMPT,), generator=torch.Generator().manual_seed(0),
+                           dtype=torch.int32).pin_memory()
+    total = DECODE_PROMPT + DECODE_TOKENS
+    # warm-up: eager step, capture, a short greedy run
+    dec.generate(prompt[:8], 4, use_graph=True)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    tokens_h = torch.empty(DECODE_TOKENS + 1, dtype=torch.int32).pin_memory()
+    dec.reset(out_base=DECODE_PROMPT)
+    dec.capture()                                         # the step with this run's token offset
+    barrier()
+    ev[0].record()
+    dec.tok.copy_(prompt[:1], non_blocking=True)          # prompt ids host -> device
+    prompt_d = prompt.to(dec.tok.device, non_blocking=True)
+    for i in range(DECODE_PROMPT):
+        dec.tok.copy_(prompt_d[i:i + 1])
+        dec.run_step()
+    ev[1].record()
+    for _ in range(DECODE_TOKENS):
+        dec.run_step()
+    ev[2].record()
+    tokens_h.copy_(dec.out_tokens[:DECODE_TOKENS + 1], non_blocking=True)   # tokens device -> host
+    ev[3].record()
+    barrier()
+    prefill_ms = max_over_ranks(ev[0].elapsed_time(ev[1]))
+    decode_ms = max_over_ranks(ev[1].elapsed_time(ev[2]))
+    e2e_ms = max_over_ranks(ev[0].elapsed_time(ev[3]))
+    toks = tokens_h.tolist()
+    weight_bytes = cfg.weight_params() * 34 // 32
+    dec.graph = None
+    del dec
+    torch.cuda.empty_cache()
+    return {"workload": f"config3 synthetic LFM3-shaped decoder (Q8_0, hidden 2048, 16 layers: 10 short-conv + "
+                        f"6 GQA at {list(cfg.attn_layers)}), {DECODE_PROMPT}-id prompt then {DECODE_TOKENS} "
+                        f"greedy steps, each step one CUDA-graph replay",
+            "parallelism": f"tp{world}" if world > 1 else "single GPU",
+            "tok_s": round(DECODE_TOKENS / (decode_ms * 1e-3), 1),
+            "ms_per_token": round(decode_ms / DECODE_TOKENS, 4),
+            "weight_GBps_per_gpu": round(weight_bytes / world / (decode_ms / DECODE_TOKENS * 1e-3) / 1e9, 1),
+            "prefill_ms": round(prefill_ms, 2),
+            "e2e": {"tok_s": round(DECODE_TOKENS / (e2e_ms * 1e-3), 1), "ms": round(e2e_ms, 2),
+                    "what": "prompt ids host->device, prompt steps, greedy steps, tokens device->host",
+                    "h2d_bytes": 4 * DECODE_PROMPT, "d2h_bytes": 4 * (DECODE_TOKENS + 1)},
+            "first_tokens": toks[:8]}
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -382,6 +444,12 @@ def run_ours(args):
 
     # ---- config 2: Q8_0 prefill GEMM on tcgen05 (tensor roofline) ----
     gemm = None if args.no_gemm else bench_gemm(ops, L, args, capture, timed_replays, rank)
+    for wk in work:
+        wk[4].free()                  # the sweep's weights (486 MB) are no longer needed
+    torch.cuda.empty_cache()
+
+    # ---- config 3: LFM3-shaped decode, tensor-parallel over the ranks ----
+    decode = None if args.no_decode else bench_decode(ops, args, world, rank, barrier, max_over_ranks)
 
     # ---- roofline of the dominant kernel (the GEMV) ----
     peak, peak_kind = peaks()
@@ -419,6 +487,7 @@ def run_ours(args):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "gemm": gemm,
+            "decode": decode,
             "per_call": per_call,
         }
         print(json.dumps(line), flush=True)
@@ -436,6 +505,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-2 GEMM measurement")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-3 LFM3 decode measurement")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ncu-step", action="store_true",
                     help="profiling mode for ncu: eager warm-up steps plus one eager step, no timing")

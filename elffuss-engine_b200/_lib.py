@@ -76,6 +76,8 @@ _SIGS = {
                                _P, _P], _I),
     "ef_attn_decode": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "ef_argmax_step": ([_P, _P, _I, _P, _P, _P, _I, _I], _I),
+    "ef_argmax_partial": ([_P, _P, _I, _I, _P], _I),
+    "ef_argmax_select": ([_P, _P, _I, _P, _P, _P, _I, _I], _I),
 }
 
 

@@ -236,12 +236,26 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const float *__r
     }
 }
 
-// Greedy argmax over n logits (strict '>': lowest index wins ties); writes the
-// token, records it in out_tokens[*pos + 1 - out_base] when that index is in
-// [0, out_cap), and advances *pos.
-__global__ void __launch_bounds__(1024) argmax_step_kernel(const float *__restrict__ logits, int n,
-                                                           int *__restrict__ token, int *__restrict__ pos,
-                                                           int *__restrict__ out_tokens, int out_base, int out_cap) {
+// The step's token: writes it, records it in out_tokens[*pos + 1 - out_base]
+// when that index is in [0, out_cap), and advances *pos.
+__device__ __forceinline__ void finish_step(int tok, int *token, int *pos, int *out_tokens, int out_base,
+                                            int out_cap) {
+    *token = tok;
+    const int np = *pos + 1;
+    const int slot = np - out_base;
+    if (out_tokens && slot >= 0 && slot < out_cap) out_tokens[slot] = tok;
+    *pos = np;
+}
+
+// Greedy argmax over n logits (strict '>': lowest index wins ties). PAIR =
+// false: finish_step with the winner. PAIR = true (one vocabulary shard of a
+// tensor-parallel head): pair[0] = the best value's bits, pair[1] = its index
+// + offset, for argmax_select over the shards.
+template <bool PAIR>
+__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ logits, int n,
+                                                      int *__restrict__ token, int *__restrict__ pos,
+                                                      int *__restrict__ out_tokens, int out_base, int out_cap,
+                                                      int offset, int *__restrict__ pair) {
     __shared__ float bv[32];
     __shared__ int bi[32];
     float best = -INFINITY;
@@ -303,13 +317,41 @@ __global__ void __launch_bounds__(1024) argmax_step_kernel(const float *__restri
             }
         }
         if (lane == 0) {
-            *token = bidx;
-            const int np = *pos + 1;
-            const int slot = np - out_base;
-            if (out_tokens && slot >= 0 && slot < out_cap) out_tokens[slot] = bidx;
-            *pos = np;
+            if (PAIR) {
+                pair[0] = __float_as_int(best);
+                pair[1] = bidx + offset;
+            } else {
+                finish_step(bidx, token, pos, out_tokens, out_base, out_cap);
+            }
         }
     }
+}
+
+// The winner over the shards' (value, index) pairs, in the same order as one
+// argmax over the whole vocabulary: larger value, then lower index.
+__global__ void argmax_select_kernel(const int *__restrict__ pairs, int npairs, int *__restrict__ token,
+                                     int *__restrict__ pos, int *__restrict__ out_tokens, int out_base,
+                                     int out_cap) {
+    float best = -INFINITY;
+    int bidx = 0x7fffffff;
+    for (int i = threadIdx.x; i < npairs; i += 32) {
+        const float v = __int_as_float(pairs[2 * i]);
+        const int ix = pairs[2 * i + 1];
+        if (v > best || (v == best && ix < bidx)) {
+            best = v;
+            bidx = ix;
+        }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+        if (ov > best || (ov == best && oi < bidx)) {
+            best = ov;
+            bidx = oi;
+        }
+    }
+    if (threadIdx.x == 0) finish_step(bidx, token, pos, out_tokens, out_base, out_cap);
 }
 
 static int grid1d(int64_t n, int b) { return (int)((n + b - 1) / b); }
@@ -411,8 +453,26 @@ int ef_argmax_step(ef_ctx *ctx, const float *logits, int n, int *token, int *pos
     if (!ctx || !logits || !token || !pos || n < 1)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "argmax_step: bad arguments") : EF_ERR_INVALID;
     ctx->launches++;
-    argmax_step_kernel<<<1, 1024, 0, ctx->stream>>>(logits, n, token, pos, out_tokens, out_base, out_cap);
+    argmax_kernel<false><<<1, 1024, 0, ctx->stream>>>(logits, n, token, pos, out_tokens, out_base, out_cap, 0,
+                                                       nullptr);
     return check_cuda(ctx, cudaGetLastError(), "argmax_step launch");
+}
+
+int ef_argmax_partial(ef_ctx *ctx, const float *logits, int n, int offset, int *pair) {
+    if (!ctx || !logits || !pair || n < 1 || offset < 0)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "argmax_partial: bad arguments") : EF_ERR_INVALID;
+    ctx->launches++;
+    argmax_kernel<true><<<1, 1024, 0, ctx->stream>>>(logits, n, nullptr, nullptr, nullptr, 0, 0, offset, pair);
+    return check_cuda(ctx, cudaGetLastError(), "argmax_partial launch");
+}
+
+int ef_argmax_select(ef_ctx *ctx, const int *pairs, int npairs, int *token, int *pos, int *out_tokens,
+                     int out_base, int out_cap) {
+    if (!ctx || !pairs || !token || !pos || npairs < 1)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "argmax_select: bad arguments") : EF_ERR_INVALID;
+    ctx->launches++;
+    argmax_select_kernel<<<1, 32, 0, ctx->stream>>>(pairs, npairs, token, pos, out_tokens, out_base, out_cap);
+    return check_cuda(ctx, cudaGetLastError(), "argmax_select launch");
 }
 
 }  // extern "C"

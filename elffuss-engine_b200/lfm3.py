@@ -17,6 +17,17 @@ GEMV (q/k/v/gate as one sections call, gate/up as one SwiGLU call, the LM head
 over the 65536-row tied embedding), the rest are the library's decoder-step
 kernels. Position and token live in device memory, so a step is captured once
 as a CUDA graph and replayed per token.
+
+Tensor parallel (one process per GPU, Megatron-style; the reference runs on
+one device): shard_weights gives rank r of g its slices -- q/k/v/gate by
+heads, shortconv.in_proj by channel (the B, C and x rows of the same
+channels, so the depthwise conv stays local), ffn_gate/up by inner rows, the
+LM head by vocabulary rows (column-parallel, no exchange); attn_output,
+shortconv.out_proj and ffn_down by input columns (row-parallel), each
+followed by an all-reduce of the hidden vector (NCCL through
+torch.distributed, captured in the step's graph). The head ends with a local
+argmax per rank and an all-gather of the (value, index) pairs, so the token is
+the one a single argmax over the whole vocabulary picks.
 """
 from __future__ import annotations
 
@@ -121,16 +132,81 @@ def synth_weights(cfg: LFM3Config, seed: int = 0, device: str = "cpu") -> dict:
     return out
 
 
+def _q8_rows(raw: torch.Tensor, rows: int, k: int, ranges) -> torch.Tensor:
+    """Q8_0 bytes of the rows [a, b) of each range, concatenated in order."""
+    m = raw.reshape(rows, (k // 32) * 34)
+    return torch.cat([m[a:b] for a, b in ranges]).reshape(-1).contiguous()
+
+
+def _q8_cols(raw: torch.Tensor, rows: int, k: int, c0: int, c1: int) -> torch.Tensor:
+    """Q8_0 bytes of the columns [c0, c1) (multiples of 32) of every row."""
+    m = raw.reshape(rows, k // 32, 34)
+    return m[:, c0 // 32:c1 // 32].reshape(-1).contiguous()
+
+
+def shard_weights(cfg: LFM3Config, weights: dict, rank: int, world: int) -> dict:
+    """Rank `rank` of `world`: the slices of synth_weights' tensors this rank
+    holds (see the module docstring). token_embd stays whole (the embedding
+    gather reads one row of it); "output" is this rank's vocabulary rows of it."""
+    E, H, KV, D, F, V = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn, cfg.vocab
+    g, r = world, rank
+    for what, n in (("heads", H), ("kv_heads", KV), ("hidden", E), ("ffn", F), ("vocab", V)):
+        if n % g:
+            raise ValueError(f"tensor parallel over {g} ranks: {what}={n} does not split")
+    Hl, KVl, Ec, Fl, Vl = H // g, KV // g, E // g, F // g, V // g
+    for what, n in (("heads*head_dim", Hl * D), ("hidden", Ec), ("ffn", Fl)):
+        if n % 32:
+            raise ValueError(f"tensor parallel over {g} ranks: the {what} slice {n} is not a multiple of 32")
+    out = {}
+    for name, val in weights.items():
+        short = name.split(".", 2)[-1] if name.startswith("blk.") else name
+        if not isinstance(val, tuple):
+            if short == "shortconv.conv":
+                out[name] = val[r * Ec:(r + 1) * Ec].contiguous()
+            else:
+                out[name] = val
+            continue
+        raw, rows, k = val
+        if short == "token_embd":
+            out[name] = val
+            out["output"] = (_q8_rows(raw, rows, k, [(r * Vl, (r + 1) * Vl)]), Vl, k)
+        elif short == "attn_q":
+            out[name] = (_q8_rows(raw, rows, k, [(r * Hl * D, (r + 1) * Hl * D)]), Hl * D, k)
+        elif short in ("attn_k", "attn_v"):
+            out[name] = (_q8_rows(raw, rows, k, [(r * KVl * D, (r + 1) * KVl * D)]), KVl * D, k)
+        elif short == "attn_gate":
+            out[name] = (_q8_rows(raw, rows, k, [(r * Hl, (r + 1) * Hl)]), Hl, k)
+        elif short == "attn_output":
+            out[name] = (_q8_cols(raw, rows, k, r * Hl * D, (r + 1) * Hl * D), rows, Hl * D)
+        elif short == "shortconv.in_proj":
+            rr = [(j * E + r * Ec, j * E + (r + 1) * Ec) for j in range(3)]
+            out[name] = (_q8_rows(raw, rows, k, rr), 3 * Ec, k)
+        elif short == "shortconv.out_proj":
+            out[name] = (_q8_cols(raw, rows, k, r * Ec, (r + 1) * Ec), rows, Ec)
+        elif short in ("ffn_gate", "ffn_up"):
+            out[name] = (_q8_rows(raw, rows, k, [(r * Fl, (r + 1) * Fl)]), Fl, k)
+        elif short == "ffn_down":
+            out[name] = (_q8_cols(raw, rows, k, r * Fl, (r + 1) * Fl), rows, Fl)
+        else:
+            raise ValueError(f"no shard rule for {name}")
+    return out
+
+
 def _p(t: torch.Tensor):
     return ctypes.c_void_p(t.data_ptr())
 
 
 class LFM3Decoder:
-    """The network on one GPU, a step per token (see the module docstring)."""
+    """The network, a step per token (see the module docstring). With
+    world > 1, `weights` are this rank's shard_weights and the collectives go
+    through torch.distributed's default (NCCL) process group."""
 
-    def __init__(self, ops, cfg: LFM3Config, weights: dict):
+    def __init__(self, ops, cfg: LFM3Config, weights: dict, rank: int = 0, world: int = 1):
         self.ops, self.cfg, self.L = ops, cfg, lib()
-        E, H, KV, D, F = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn
+        self.rank, self.world = rank, world
+        E, D = cfg.hidden, cfg.head_dim
+        H, KV, F = cfg.heads // world, cfg.kv_heads // world, cfg.ffn // world
+        self.Hl, self.KVl, self.Ec, self.Fl, self.Vl = H, KV, E // world, F, cfg.vocab // world
         dev = torch.device("cuda", ops.ctx.device)
         self.w, self.f32 = {}, {}
         for name, val in weights.items():
@@ -139,13 +215,17 @@ class LFM3Decoder:
                 self.w[name] = ops.load_weight("Q8_0", raw.to(dev), rows, k, label=name)
             else:
                 self.f32[name] = val.to(dev).float().contiguous()
+        if world == 1:
+            self.w["output"] = self.w["token_embd"]
         z = lambda *s: torch.zeros(*s, device=dev)
         self.x, self.nrm = z(E), z(E)
-        self.bcx, self.conv_y = z(3 * E), z(E)
+        self.bcx, self.conv_y = z(3 * self.Ec), z(self.Ec)
         self.o, self.sw, self.d = z(E), z(F), z(E)
         self.q, self.k, self.v, self.g, self.att = z(H * D), z(KV * D), z(KV * D), z(H), z(H * D)
-        self.logits = z(cfg.vocab)
-        self.state = {l: z(cfg.conv_k - 1, E) for l in range(cfg.layers) if l not in cfg.attn_layers}
+        self.logits = z(self.Vl)
+        self.pair = torch.zeros(2, dtype=torch.int32, device=dev)
+        self.pairs = torch.zeros(2 * world, dtype=torch.int32, device=dev)
+        self.state = {l: z(cfg.conv_k - 1, self.Ec) for l in range(cfg.layers) if l not in cfg.attn_layers}
         self.kc = {l: z(cfg.max_pos, KV, D) for l in cfg.attn_layers}
         self.vc = {l: z(cfg.max_pos, KV, D) for l in cfg.attn_layers}
         self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -164,9 +244,16 @@ class LFM3Decoder:
         self.graph = None
 
     # -- one decode step (token self.tok at position self.pos) -----------------
+    def _reduce(self, t: torch.Tensor):
+        """Sum of the ranks' partial row-parallel outputs (in place)."""
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(t)
+
     def step(self):
         L, cfg, h = self.L, self.cfg, self.ops.ctx.bind()
-        E, H, KV, D, F = cfg.hidden, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.ffn
+        E, D = cfg.hidden, cfg.head_dim
+        H, KV = self.Hl, self.KVl
         W, f = self.w, self.f32
         eps = ctypes.c_float(cfg.eps)
         check(L.ef_gather(h, W["token_embd"].h, _p(self.tok), 1, _p(self.x)), h)
@@ -187,26 +274,37 @@ class LFM3Decoder:
                 check(L.ef_gemv(h, W[p + "attn_output"].h, _p(self.att), 1, _p(self.o)), h)
             else:
                 check(L.ef_gemv(h, W[p + "shortconv.in_proj"].h, _p(self.nrm), 1, _p(self.bcx)), h)
-                check(L.ef_shortconv(h, _p(self.bcx), _p(f[p + "shortconv.conv"]), _p(self.state[l]), 1, E,
+                check(L.ef_shortconv(h, _p(self.bcx), _p(f[p + "shortconv.conv"]), _p(self.state[l]), 1, self.Ec,
                                      cfg.conv_k, _p(self.conv_y)), h)
                 check(L.ef_gemv(h, W[p + "shortconv.out_proj"].h, _p(self.conv_y), 1, _p(self.o)), h)
+            self._reduce(self.o)
             check(L.ef_norm_add_norm(h, _p(self.o), _p(f[p + "post_attention_norm"]), _p(self.x),
                                      _p(f[p + "ffn_norm"]), 1, E, eps, _p(self.nrm)), h)
             check(L.ef_gemv_swiglu(h, W[p + "ffn_gate"].h, W[p + "ffn_up"].h, _p(self.nrm), 1, _p(self.sw)), h)
             check(L.ef_gemv(h, W[p + "ffn_down"].h, _p(self.sw), 1, _p(self.d)), h)
+            self._reduce(self.d)
             nxt = f[f"blk.{l + 1}.attn_norm"] if l + 1 < cfg.layers else f["output_norm"]
             check(L.ef_norm_add_norm(h, _p(self.d), _p(f[p + "post_ffw_norm"]), _p(self.x), _p(nxt), 1, E, eps,
                                      _p(self.nrm)), h)
-        check(L.ef_gemv(h, W["token_embd"].h, _p(self.nrm), 1, _p(self.logits)), h)
-        check(L.ef_argmax_step(h, _p(self.logits), cfg.vocab, _p(self.tok), _p(self.pos), _p(self.out_tokens),
-                               self.out_base, cfg.max_pos), h)
+        check(L.ef_gemv(h, W["output"].h, _p(self.nrm), 1, _p(self.logits)), h)
+        if self.world == 1:
+            check(L.ef_argmax_step(h, _p(self.logits), cfg.vocab, _p(self.tok), _p(self.pos), _p(self.out_tokens),
+                                   self.out_base, cfg.max_pos), h)
+        else:
+            import torch.distributed as dist
+            check(L.ef_argmax_partial(h, _p(self.logits), self.Vl, self.rank * self.Vl, _p(self.pair)), h)
+            dist.all_gather_into_tensor(self.pairs, self.pair)
+            h = self.ops.ctx.bind()
+            check(L.ef_argmax_select(h, _p(self.pairs), self.world, _p(self.tok), _p(self.pos), _p(self.out_tokens),
+                                     self.out_base, cfg.max_pos), h)
 
     def capture(self):
         """Record one step as a CUDA graph (after one eager step has sized every scratch)."""
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph, stream=s):
+        # thread_local: the process group's watchdog thread may query events meanwhile
+        with torch.cuda.graph(self.graph, stream=s, capture_error_mode="thread_local"):
             self.step()
         torch.cuda.synchronize()
 

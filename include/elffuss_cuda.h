@@ -251,6 +251,19 @@ EF_API int ef_attn_decode(ef_ctx *ctx, const float *q, const float *kcache, cons
 EF_API int ef_argmax_step(ef_ctx *ctx, const float *logits, int n, int *token, int *pos, int *out_tokens,
                           int out_base, int out_cap);
 
+/* Tensor-parallel greedy head (the LM head split by vocabulary rows over the
+ * ranks; the reference has one device and no counterpart, its single-device
+ * argmax is js/sample.js:95-99). ef_argmax_partial: the argmax of this
+ * rank's n logits as pair[0] = the value's f32 bits, pair[1] = its index +
+ * offset (the shard's first vocabulary id). ef_argmax_select: given the
+ * ranks' pairs gathered in rank order (2 * npairs ints), the winner in the
+ * order of one argmax over the whole vocabulary (larger value, then lower
+ * index), then the same token / position / out_tokens update as
+ * ef_argmax_step. */
+EF_API int ef_argmax_partial(ef_ctx *ctx, const float *logits, int n, int offset, int *pair);
+EF_API int ef_argmax_select(ef_ctx *ctx, const int *pairs, int npairs, int *token, int *pos, int *out_tokens,
+                            int out_base, int out_cap);
+
 #ifdef __cplusplus
 }
 #endif

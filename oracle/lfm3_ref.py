@@ -24,6 +24,12 @@ the GPU is f32 accumulation order, and greedy tokens can be compared exactly.
 Parity of this file with the reference's own code is unpinned: the reference
 ships no model tests and its CPU path (Node + WebAssembly) cannot run here; it
 is a restatement of the cited code.
+
+Tensor parallel (no counterpart in the reference, which runs on one device):
+given one rank's shard of the weights (lfm3.shard_weights) and callbacks that
+sum a vector over the ranks and gather one (value, index) pair per rank, the
+same forward runs on the local heads / channels / rows, so that the sharding
+rules can be checked on the CPU against the unsharded forward.
 """
 from __future__ import annotations
 
@@ -61,8 +67,11 @@ class LFM3Oracle:
     """cfg: an object with the LFM3Config fields; weights: name -> (Q8_0 bytes,
     rows, k) or an f32 array (numpy)."""
 
-    def __init__(self, cfg, weights: dict):
+    def __init__(self, cfg, weights: dict, rank: int = 0, world: int = 1, allreduce=None, allgather=None):
         self.cfg = cfg
+        self.rank, self.world = rank, world
+        self.allreduce = allreduce or (lambda v: v)
+        self.allgather = allgather
         self.w16, self.f = {}, {}
         for name, val in weights.items():
             if isinstance(val, tuple):
@@ -78,7 +87,8 @@ class LFM3Oracle:
 
     def reset(self):
         c = self.cfg
-        self.state = {l: np.zeros((c.conv_k - 1, c.hidden)) for l in range(c.layers) if l not in c.attn_layers}
+        ec = c.hidden // self.world
+        self.state = {l: np.zeros((c.conv_k - 1, ec)) for l in range(c.layers) if l not in c.attn_layers}
         self.kc = {l: [] for l in c.attn_layers}
         self.vc = {l: [] for l in c.attn_layers}
         self.pos = 0
@@ -88,7 +98,8 @@ class LFM3Oracle:
 
     def step(self, tok: int) -> int:
         c, f = self.cfg, self.f
-        E, H, KV, D = c.hidden, c.heads, c.kv_heads, c.head_dim
+        E, D = c.hidden, c.head_dim
+        H, KV, Ec = c.heads // self.world, c.kv_heads // self.world, c.hidden // self.world
         x = self.embd[tok].copy()
         nrm = rmsnorm(x, f["blk.0.attn_norm"], c.eps)
         for l in range(c.layers):
@@ -119,7 +130,7 @@ class LFM3Oracle:
                 o = self.mm(p + "attn_output", att.reshape(-1))
             else:
                 bcx = self.mm(p + "shortconv.in_proj", nrm)
-                B, C, xs = bcx[:E], bcx[E:2 * E], bcx[2 * E:]
+                B, C, xs = bcx[:Ec], bcx[Ec:2 * Ec], bcx[2 * Ec:]
                 bx = B * xs
                 st = self.state[l]
                 w = f[p + "shortconv.conv"]                   # [E][K], r = 0 oldest
@@ -128,18 +139,25 @@ class LFM3Oracle:
                 y = C * conv
                 self.state[l] = win[1:]
                 o = self.mm(p + "shortconv.out_proj", y)
+            o = self.allreduce(o)
             x = x + rmsnorm(o, f[p + "post_attention_norm"], c.eps)
             nrm = rmsnorm(x, f[p + "ffn_norm"], c.eps)
             gate = self.mm(p + "ffn_gate", nrm)
             up = self.mm(p + "ffn_up", nrm)
             sw = gate / (1.0 + np.exp(-gate)) * up
-            dn = self.mm(p + "ffn_down", sw)
+            dn = self.allreduce(self.mm(p + "ffn_down", sw))
             x = x + rmsnorm(dn, f[p + "post_ffw_norm"], c.eps)
             nxt = f[f"blk.{l + 1}.attn_norm"] if l + 1 < c.layers else f["output_norm"]
             nrm = rmsnorm(x, nxt, c.eps)
-        logits = self.mm("token_embd", nrm)
         self.pos += 1
-        return int(np.argmax(logits))     # first maximum = lowest index wins ties
+        if self.world == 1:
+            logits = self.mm("token_embd", nrm)
+            return int(np.argmax(logits))     # first maximum = lowest index wins ties
+        logits = self.mm("output", nrm)       # this rank's vocabulary rows
+        i = int(np.argmax(logits))
+        pairs = self.allgather((float(logits[i]), i + self.rank * logits.size))
+        best = max(v for v, _ in pairs)
+        return min(ix for v, ix in pairs if v == best)
 
     def generate(self, prompt, n: int) -> list:
         self.reset()
