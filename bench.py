@@ -291,6 +291,67 @@ def bench_decode(ops, args, world, rank, barrier, max_over_ranks):
             "first_tokens": toks[:8]}
 
 
+LLAMA_CONTEXT, LLAMA_STEPS = 4096, 32
+
+
+def bench_llama(ops, args, world, rank, barrier, max_over_ranks):
+    """Config 4: the synthetic Llama-architecture 8B-shaped decoder (llama.py,
+    Q4_K with Q6_K for attn_v, even-layer ffn_down and the head),
+    tensor-parallel over the ranks when world > 1: a 4096-id context (its
+    first 4095 ids through the GEMM path once), then greedy decode steps at
+    batch 1 and at batch 16 (16 sequences sharing the first 4095 ids, each
+    with its own last id), each step one CUDA-graph replay."""
+    import torch
+
+    from elffuss_engine_b200.llama import LlamaConfig, LlamaDecoder, shard_weights, synth_weights
+    cfg = LlamaConfig()
+    w = synth_weights(cfg, seed=0, device="cuda")
+    if world > 1:
+        w = shard_weights(cfg, w, rank, world)
+    ids = torch.randint(0, cfg.vocab, (LLAMA_CONTEXT + 15,), generator=torch.Generator().manual_seed(4),
+                        dtype=torch.int32)
+    prompt = ids[:LLAMA_CONTEXT]
+    out = {"workload": f"config4 synthetic Llama-architecture 8B shape (32 layers, hidden 4096, 32/8 heads x 128, "
+                       f"FFN 14336, vocab 128256; Q4_K, Q6_K for attn_v / even ffn_down / output), "
+                       f"{LLAMA_CONTEXT}-id context, {LLAMA_STEPS} greedy steps per batch size",
+           "parallelism": f"tp{world}" if world > 1 else "single GPU",
+           "weight_bytes_per_step_per_gpu": cfg.step_weight_bytes() // world}
+    for B in (1, 16):
+        dec = LlamaDecoder(ops, cfg, w, batch=B, rank=rank, world=world)
+        lasts = [int(prompt[-1])] + [int(t) for t in ids[LLAMA_CONTEXT:LLAMA_CONTEXT + B - 1]]
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        barrier()
+        ev[0].record()
+        dec.start(prompt, lasts)
+        ev[1].record()
+        barrier()
+        prefill_ms = max_over_ranks(ev[0].elapsed_time(ev[1]))
+        dec.step()                                           # eager: sizes scratch, configures kernels
+        torch.cuda.synchronize()
+        dec.rewind(LLAMA_CONTEXT, lasts)
+        dec.capture()
+        for _ in range(2):                                   # warm-up replays (positions advance)
+            dec.run_step()
+        barrier()
+        ev[1].record()
+        for _ in range(LLAMA_STEPS):
+            dec.run_step()
+        ev[2].record()
+        barrier()
+        ms = max_over_ranks(ev[1].elapsed_time(ev[2])) / LLAMA_STEPS
+        toks = dec.out_tokens[:, :4].cpu().tolist()
+        out[f"batch{B}"] = {"tok_s": round(B * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+                            "weight_GBps_per_gpu": round(cfg.step_weight_bytes() / world / (ms * 1e-3) / 1e9, 1),
+                            "prefill_4095_ms": round(prefill_ms, 1), "first_tokens": toks[0][:4],
+                            "distinct_first_tokens": len({t[0] for t in toks})}
+        dec.graph = None
+        del dec
+        torch.cuda.empty_cache()
+    del w
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -450,6 +511,7 @@ def run_ours(args):
 
     # ---- config 3: LFM3-shaped decode, tensor-parallel over the ranks ----
     decode = None if args.no_decode else bench_decode(ops, args, world, rank, barrier, max_over_ranks)
+    decode8b = None if args.no_decode else bench_llama(ops, args, world, rank, barrier, max_over_ranks)
 
     # ---- roofline of the dominant kernel (the GEMV) ----
     peak, peak_kind = peaks()
@@ -488,6 +550,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "gemm": gemm,
             "decode": decode,
+            "decode_8b": decode8b,
             "per_call": per_call,
         }
         print(json.dumps(line), flush=True)

@@ -76,8 +76,14 @@ _SIGS = {
                                _P, _P], _I),
     "ef_attn_decode": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "ef_argmax_step": ([_P, _P, _I, _P, _P, _P, _I, _I], _I),
-    "ef_argmax_partial": ([_P, _P, _I, _I, _P], _I),
-    "ef_argmax_select": ([_P, _P, _I, _P, _P, _P, _I, _I], _I),
+    "ef_ctx_set_pdl": ([_P, _I], _I),
+    "ef_argmax_rows": ([_P, _P, _I, _I, _P, _P, _P, _I, _I], _I),
+    "ef_argmax_partial": ([_P, _P, _I, _I, _I, _P], _I),
+    "ef_argmax_select": ([_P, _P, _I, _I, _P, _P, _P, _I, _I], _I),
+    "ef_rope_cache": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, ctypes.c_float,
+                       _P, _P], _I),
+    "ef_attention": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
+    "ef_swiglu": ([_P, _P, _P, ctypes.c_int64, _P], _I),
 }
 
 

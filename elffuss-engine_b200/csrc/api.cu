@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -81,6 +82,8 @@ int ef_ctx_create(int device, ef_ctx **out) {
     }
     c->stream = c->own;
     cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
+    const char *pdl = getenv("EF_PDL");
+    c->pdl = pdl && pdl[0] == '1';
     *out = c;
     return EF_OK;
 }
@@ -93,7 +96,7 @@ int ef_ctx_destroy(ef_ctx *ctx) {
         cudaFree(b->ptr);
         delete b;
     }
-    for (int i = 0; i < 2; i++)
+    for (int i = 0; i < ef_ctx::kScratchSlots; i++)
         if (ctx->scratch[i]) cudaFree(ctx->scratch[i]);
     if (ctx->own) cudaStreamDestroy(ctx->own);
     delete ctx;
@@ -103,6 +106,12 @@ int ef_ctx_destroy(ef_ctx *ctx) {
 int ef_ctx_set_stream(ef_ctx *ctx, void *stream) {
     if (!ctx) return EF_ERR_INVALID;
     ctx->stream = (cudaStream_t)stream;   // NULL = the CUDA default (legacy) stream
+    return EF_OK;
+}
+
+int ef_ctx_set_pdl(ef_ctx *ctx, int on) {
+    if (!ctx) return EF_ERR_INVALID;
+    ctx->pdl = on != 0;
     return EF_OK;
 }
 

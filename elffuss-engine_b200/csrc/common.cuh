@@ -30,6 +30,24 @@
 
 namespace ef {
 
+// Programmatic dependent launch. pdl_trigger: kernels queued after this one
+// may be scheduled now; pdl_wait: block until the kernels this one depends on
+// have finished and their writes are visible (a no-op without the launch
+// attribute). Every kernel of a PDL chain executes pdl_wait in every CTA
+// before its first read of an earlier kernel's output and before it exits, so
+// completion stays transitive along the chain.
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// 16-byte asynchronous global -> shared copy (L2 only), its group commit and wait.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+
 // ---------------------------------------------------------------- geometry --
 struct TypeGeo {
     int block_elems;   // weights per GGUF block

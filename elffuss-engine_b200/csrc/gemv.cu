@@ -186,12 +186,6 @@ __device__ __forceinline__ uint32_t ldh32(const uint8_t *p) {
 
 // Asynchronous 16-byte global -> shared copies (LDGSTS, L2 only), for the
 // activation phases.
-__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
-    const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N> __device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // x data of one chunk for the f16 types: B fragments [step][token][lane t]
 // (8 B each), tokens 0..M-1 only; lanes whose token is >= M feed zeros.
@@ -1172,15 +1166,6 @@ static int max_active_clusters(ef_ctx *ctx, const void *kern, int threads, size_
     return n;
 }
 
-// Programmatic dependent launch between consecutive kernels: off by default
-// (measured on B200 over the mixed-shape benchmark sequence: the early-
-// launched CTAs of the next GEMV hold shared memory and registers that the
-// current one still needs, a net loss); EF_GEMV_PDL=1 turns it on.
-static bool gemv_pdl() {
-    const char *v = getenv("EF_GEMV_PDL");
-    return v && v[0] == '1';
-}
-
 // Warps per rowgroup: two (16-warp CTAs) where the kernel fits 128 registers
 // per thread, else one.
 template <int TYPE, int TQ, int NT, bool SWIGLU> constexpr int kh_of() {
@@ -1225,7 +1210,7 @@ static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int64_t rowblocks, bool fused
     cfg.stream = ctx->stream;
     cudaLaunchAttribute attr[2];
     int na = 0;
-    if (gemv_pdl()) {
+    if (ctx->pdl) {
         attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[na].val.programmaticStreamSerializationAllowed = 1;
         na++;
@@ -1274,7 +1259,7 @@ static int launch_t(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n,
         attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
         attr[0].val.programmaticStreamSerializationAllowed = 1;
         cfg.attrs = attr;
-        cfg.numAttrs = gemv_pdl() ? 1 : 0;
+        cfg.numAttrs = ctx->pdl ? 1 : 0;
         ctx->launches++;
         if (int rc = check_cuda(ctx, cudaLaunchKernelEx(&cfg, gemv_xprep<TYPE>, x, a.M, a.K, a.nchunks, a.xb,
                                                         (uint8_t *)ctx->scratch[0]), "gemv xprep launch"))

@@ -4,6 +4,7 @@
 #include <stdint.h>
 
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "../../include/elffuss_cuda.h"
@@ -33,17 +34,42 @@ struct ef_ctx {
     uint64_t seq = 0;
     // Persistent device scratch owned by the context (grown on demand):
     // slot 0 holds the GEMV's activation data, slot 1 the GEMM's converted
-    // activations. A first call of a new, larger shape grows them
-    // (cudaMalloc), so that call must come before any stream capture.
-    void *scratch[2] = {nullptr, nullptr};
-    size_t scratch_bytes[2] = {0, 0};
+    // activations, slot 2 the decode attention's per-split partial results.
+    // A first call of a new, larger shape grows them (cudaMalloc), so that
+    // call must come before any stream capture.
+    static constexpr int kScratchSlots = 3;
+    void *scratch[kScratchSlots] = {nullptr, nullptr, nullptr};
+    size_t scratch_bytes[kScratchSlots] = {0, 0, 0};
     uint64_t launches = 0;            // kernels this context has launched (diagnostic counter)
+    // Programmatic dependent launch: each kernel may be scheduled while the
+    // previous one on the stream finishes; it waits for that kernel's results
+    // (griddepcontrol.wait) before reading them.
+    bool pdl = false;
 };
 
 namespace ef {
 
 int set_err(ef_ctx *ctx, int code, const char *fmt, ...);
 int check_cuda(ef_ctx *ctx, cudaError_t e, const char *what);
+
+// Launch `kern` on the context's stream (with the programmatic-dependent-
+// launch attribute when ctx->pdl), counting it.
+template <typename... KArgs, typename... Args>
+int launch_on(ef_ctx *ctx, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, const char *what,
+              Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = ctx->stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = ctx->pdl ? 1 : 0;
+    ctx->launches++;
+    return check_cuda(ctx, cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...), what);
+}
 int ensure_scratch(ef_ctx *ctx, int slot, size_t bytes, bool zero = false);
 
 // weights.cu

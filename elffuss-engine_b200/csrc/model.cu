@@ -49,6 +49,8 @@ __device__ __forceinline__ float block_sum(float v, float *red) {
 template <int V>
 __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
                                                       int n, float eps, float *__restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[32];
     const float4 *xr = reinterpret_cast<const float4 *>(x + (int64_t)blockIdx.x * n);
     const float4 *wr = reinterpret_cast<const float4 *>(w);
@@ -76,6 +78,8 @@ __global__ void __launch_bounds__(256) norm_add_norm_kernel(const float *__restr
                                                             const float *__restrict__ w_post, float *__restrict__ x,
                                                             const float *__restrict__ w_next, int n, float eps,
                                                             float *__restrict__ nrm) {
+    pdl_trigger();
+    pdl_wait();
     __shared__ float red[32];
     const int64_t row = (int64_t)blockIdx.x * (n / 4);
     const float4 *o4 = reinterpret_cast<const float4 *>(o) + row;
@@ -121,6 +125,8 @@ __global__ void __launch_bounds__(256) norm_add_norm_kernel(const float *__restr
 template <int K>
 __global__ void shortconv_kernel(const float *__restrict__ bcx, const float *__restrict__ w, float *__restrict__ state,
                                  int tokens, int C, float *__restrict__ y) {
+    pdl_trigger();
+    pdl_wait();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= C) return;
     float win[K - 1], wc[K];
@@ -144,59 +150,108 @@ __global__ void shortconv_kernel(const float *__restrict__ bcx, const float *__r
     for (int r = 0; r < K - 1; r++) state[(int64_t)r * C + c] = win[r];
 }
 
-// One warp per head (q heads first, then k heads); head_dim 64 = 2 per lane.
-// NEOX pairs (i, i + D/2); theta = pos * base^(-2i/D).
-__global__ void qk_norm_rope_cache_kernel(float *__restrict__ q, const float *__restrict__ k,
-                                          const float *__restrict__ v, const float *__restrict__ wq,
-                                          const float *__restrict__ wk, const int *__restrict__ pos, int max_pos,
-                                          int H, int KVH, float theta_scale, float eps,
-                                          float *__restrict__ kcache, float *__restrict__ vcache) {
-    constexpr int D = 64;
-    const int head = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
-    if (head >= H + KVH) return;
-    const int p = *pos;
+// One warp per (token row, head), q heads first, then k heads. Rows are
+// seqs x tokens (row r = sequence r / tokens, token t = r % tokens at position
+// pos[seq] + t); q [rows][H][D] is rotated in place, k and v [rows][KVH][D]
+// go to the caches [seqs][max_pos][KVH][D]. Lane pairs p = lane + 32 j
+// (j < D/64): NEOX pairs elements (p, p + D/2), NORM pairs (2p, 2p + 1);
+// theta = position * base^(-2p/D) (kernels.nn.wgsl.js:87-139). With wq / wk,
+// the per-head RMSNorm comes first (model.js:877-917).
+template <int D, bool NEOX>
+__global__ void rope_cache_kernel(float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+                                  const float *__restrict__ wq, const float *__restrict__ wk,
+                                  const int *__restrict__ pos, int seqs, int tokens, int max_pos, int H, int KVH,
+                                  float theta_scale, float eps, float *__restrict__ kcache,
+                                  float *__restrict__ vcache) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int J = D / 64;
+    const int64_t wid = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31, per = H + KVH;
+    if (wid >= (int64_t)seqs * tokens * per) return;
+    const int r = (int)(wid / per), head = (int)(wid - (int64_t)r * per);
+    const int sq = r / tokens, t = r - sq * tokens;
+    const int p = pos[sq] + t;
     const bool isq = head < H;
     const int hh = isq ? head : head - H;
-    const float *src = isq ? q + hh * D : k + hh * D;
+    float *qrow = q + ((int64_t)r * H + hh) * D;
+    const float *src = isq ? qrow : k + ((int64_t)r * KVH + hh) * D;
     const float *wn = isq ? wq : wk;
-    const float x0 = src[lane], x1 = src[lane + 32];
-    const float scale = rsqrtf(warp_sum(x0 * x0 + x1 * x1) / (float)D + eps);
-    const float n0 = x0 * scale * wn[lane], n1 = x1 * scale * wn[lane + 32];
-    const float theta = (float)p * powf(theta_scale, (float)lane);
-    float sn, cs;
-    sincosf(theta, &sn, &cs);
-    const float r0 = n0 * cs - n1 * sn, r1 = n0 * sn + n1 * cs;
-    if (isq) {
-        q[hh * D + lane] = r0;
-        q[hh * D + lane + 32] = r1;
-    } else if (p >= 0 && p < max_pos) {   // (a position past the caches is not stored)
-        float *kc = kcache + ((int64_t)p * KVH + hh) * D;
-        kc[lane] = r0;
-        kc[lane + 32] = r1;
-        float *vc = vcache + ((int64_t)p * KVH + hh) * D;
-        vc[lane] = v[hh * D + lane];
-        vc[lane + 32] = v[hh * D + lane + 32];
+    float a[J], b[J];
+    int i0[J], i1[J];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+        const int pp = lane + 32 * j;
+        i0[j] = NEOX ? pp : 2 * pp;
+        i1[j] = NEOX ? pp + D / 2 : 2 * pp + 1;
+        a[j] = src[i0[j]];
+        b[j] = src[i1[j]];
+        ss += a[j] * a[j] + b[j] * b[j];
+    }
+    if (wn) {
+        const float scale = rsqrtf(warp_sum(ss) / (float)D + eps);
+#pragma unroll
+        for (int j = 0; j < J; j++) {
+            a[j] = a[j] * scale * wn[i0[j]];
+            b[j] = b[j] * scale * wn[i1[j]];
+        }
+    }
+    const bool store = !isq && p >= 0 && p < max_pos;   // (a position past the caches is not stored)
+    float *kc = kcache + (((int64_t)sq * max_pos + p) * KVH + hh) * D;
+#pragma unroll
+    for (int j = 0; j < J; j++) {
+        const float theta = (float)p * powf(theta_scale, (float)(lane + 32 * j));
+        float sn, cs;
+        sincosf(theta, &sn, &cs);
+        const float r0 = a[j] * cs - b[j] * sn, r1 = a[j] * sn + b[j] * cs;
+        if (isq) {
+            qrow[i0[j]] = r0;
+            qrow[i1[j]] = r1;
+        } else if (store) {
+            kc[i0[j]] = r0;
+            kc[i1[j]] = r1;
+        }
+    }
+    if (store) {
+        const float *vr = v + ((int64_t)r * KVH + hh) * D;
+        float *vc = vcache + (((int64_t)sq * max_pos + p) * KVH + hh) * D;
+#pragma unroll
+        for (int j = 0; j < D / 32; j++) vc[lane + 32 * j] = vr[lane + 32 * j];
     }
 }
 
-// One CTA per query head; keys 0..pos, visible when pos - key < window
-// (window 0 = all). Scores into shared memory, then out[d] = sum p * v.
-__global__ void attn_decode_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
-                                   const float *__restrict__ vcache, const float *__restrict__ gate,
-                                   const int *__restrict__ pos, int max_pos, int window, int H, int KVH,
-                                   float *__restrict__ out) {
-    constexpr int D = 64;
+// CTA per (head h = blockIdx.x, query row r = blockIdx.y); rows as in
+// rope_cache_kernel. The query at position qp sees keys 0..qp of its
+// sequence's caches, those with qp - key < window (window 0 = all); scale
+// 1/sqrt(D); grouped heads (H / KVH queries per cache head); times
+// sigmoid(gate[r][h]) when gate is given (kernels.nn.wgsl.js:141-200,
+// kernels.model.wgsl.js:89-105). Scores in shared memory; the weighted sum of
+// v rows is split over blockDim / D groups of keys, then added in group order.
+template <int D>
+__global__ void __launch_bounds__(256) attention_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
+                                                        const float *__restrict__ vcache,
+                                                        const float *__restrict__ gate, const int *__restrict__ pos,
+                                                        int tokens, int max_pos, int window, int H, int KVH,
+                                                        float *__restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     extern __shared__ float sc[];
     __shared__ float red[32];
     __shared__ float qs[D];
-    const int h = blockIdx.x, kvh = h / (H / KVH);
-    const int nkv = min(*pos + 1, max_pos), qpos = nkv - 1;   // never past the caches
+    __shared__ float part[256];
+    const int h = blockIdx.x, r = blockIdx.y, kvh = h / (H / KVH);
+    const int sq = r / tokens, t = r - sq * tokens;
+    const int nkv = min(pos[sq] + t + 1, max_pos), qpos = nkv - 1;   // never past the caches
     const int k0 = window > 0 && qpos - window + 1 > 0 ? qpos - window + 1 : 0;
-    if (threadIdx.x < D) qs[threadIdx.x] = q[h * D + threadIdx.x] * rsqrtf((float)D);
+    const float *kb = kcache + (int64_t)sq * max_pos * KVH * D;
+    const float *vb = vcache + (int64_t)sq * max_pos * KVH * D;
+    const float *qr = q + ((int64_t)r * H + h) * D;
+    for (int i = threadIdx.x; i < D; i += blockDim.x) qs[i] = qr[i] * rsqrtf((float)D);
     __syncthreads();
     float mx = -1e30f;
     for (int kk = k0 + threadIdx.x; kk < nkv; kk += blockDim.x) {
-        const float4 *kr = reinterpret_cast<const float4 *>(kcache + ((int64_t)kk * KVH + kvh) * D);
+        const float4 *kr = reinterpret_cast<const float4 *>(kb + ((int64_t)kk * KVH + kvh) * D);
         float s = 0.f;
 #pragma unroll
         for (int i = 0; i < D / 4; i++) {
@@ -206,7 +261,6 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const float *__r
         sc[kk - k0] = s;
         mx = fmaxf(mx, s);
     }
-    // block max
     {
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
 #pragma unroll
@@ -226,13 +280,213 @@ __global__ void attn_decode_kernel(const float *__restrict__ q, const float *__r
     }
     sum = block_sum(sum, red);   // (its barriers also order the exp writes before the reads below)
     const float inv = 1.f / sum;
+    constexpr int G = 256 / D;   // key groups
+    const int d = threadIdx.x % D, g = threadIdx.x / D;
+    float acc = 0.f;
+    for (int kk = k0 + g; kk < nkv; kk += G) acc += sc[kk - k0] * vb[((int64_t)kk * KVH + kvh) * D + d];
+    part[threadIdx.x] = acc;
+    __syncthreads();
     if (threadIdx.x < D) {
-        const int d = threadIdx.x;
-        float acc = 0.f;
-        for (int kk = k0; kk < nkv; kk++) acc += sc[kk - k0] * vcache[((int64_t)kk * KVH + kvh) * D + d];
-        float o = acc * inv;
-        if (gate) o = o / (1.0f + expf(-gate[h]));
-        out[h * D + d] = o;
+        float o = 0.f;
+#pragma unroll
+        for (int gg = 0; gg < G; gg++) o += part[gg * D + d];
+        o *= inv;
+        if (gate) o = o / (1.0f + expf(-gate[(int64_t)r * H + h]));
+        out[((int64_t)r * H + h) * D + d] = o;
+    }
+}
+
+// Decode attention split over the keys (one new token per row): CTA =
+// (key range `split` of AK keys, cache head kvh, row r) for all G = H / KVH
+// query heads that share the cache head. The range's k and v rows are copied
+// into shared memory at once (asynchronous 16-byte copies, all in flight
+// together; small CTAs so that several load while others compute), then: a
+// warp per key with the lanes across the head dimension for the G scores;
+// per head the range's max m and sum l of exp(s - m); a thread per dimension
+// for the unnormalised sums of exp(s - m) * v. attn_combine_kernel merges the
+// ranges. Same masking and scale as attention_kernel.
+constexpr int AK = 32;         // keys per range
+constexpr int AT = 128;        // threads per CTA
+static_assert(AK == 32, "the softmax step holds one key per lane");
+
+template <int D, int G>
+__global__ void __launch_bounds__(AT) attn_part_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
+                                                       const float *__restrict__ vcache, const int *__restrict__ pos,
+                                                       int tokens, int max_pos, int window, int H, int KVH,
+                                                       float *__restrict__ part) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ __align__(16) float kv_s[];   // k rows [AK][D], then v rows [AK][D]
+    __shared__ float sc[G][AK];
+    __shared__ float ml[G][2];
+    const int split = blockIdx.x, kvh = blockIdx.y, r = blockIdx.z, nsplit = gridDim.x;
+    const int sq = r / tokens, t = r - sq * tokens;
+    const int nkv = min(pos[sq] + t + 1, max_pos), qpos = nkv - 1;
+    const int k0 = window > 0 && qpos - window + 1 > 0 ? qpos - window + 1 : 0;
+    const int a = k0 + split * AK, b = min(nkv, a + AK);
+    float *pr = part + (((int64_t)r * H + kvh * G) * nsplit + split) * (D + 2);   // head g at + g * nsplit * (D+2)
+    if (a >= b) {                    // an empty range: weight 0 in the merge
+        for (int i = threadIdx.x; i < G * (D + 2); i += AT) {
+            const int g = i / (D + 2), c = i - g * (D + 2);
+            pr[(int64_t)g * nsplit * (D + 2) + c] = c == D ? -1e30f : 0.f;
+        }
+        return;
+    }
+    const int n = b - a;
+    float *ks = kv_s, *vs = kv_s + AK * D;
+    {
+        const float *kb = kcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
+        const float *vb = vcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
+        constexpr int C = D / 4;     // 16-byte pieces per row
+        for (int i = threadIdx.x; i < n * C; i += AT) {
+            const int j = i / C, c = i - j * C;
+            cp_async16(ks + j * D + 4 * c, kb + (int64_t)j * KVH * D + 4 * c);
+            cp_async16(vs + j * D + 4 * c, vb + (int64_t)j * KVH * D + 4 * c);
+        }
+        cp_commit();
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+    constexpr int E = D / 32;        // head-dimension elements per lane
+    float qv[G][E];
+    const float qscale = rsqrtf((float)D);
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < E; e++) qv[g][e] = q[((int64_t)r * H + kvh * G + g) * D + lane * E + e] * qscale;
+    cp_wait<0>();
+    __syncthreads();
+    for (int j = warp; j < n; j += AT / 32) {
+        float kr[E];
+        if constexpr (E == 4) {
+            const float4 v4 = *reinterpret_cast<const float4 *>(ks + j * D + lane * 4);
+            kr[0] = v4.x; kr[1] = v4.y; kr[2] = v4.z; kr[3] = v4.w;
+        } else {
+            const float2 v2 = *reinterpret_cast<const float2 *>(ks + j * D + lane * 2);
+            kr[0] = v2.x; kr[1] = v2.y;
+        }
+        float s[G];
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            s[g] = 0.f;
+#pragma unroll
+            for (int e = 0; e < E; e++) s[g] += qv[g][e] * kr[e];
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1)
+#pragma unroll
+            for (int g = 0; g < G; g++) s[g] += __shfl_xor_sync(0xffffffffu, s[g], o);
+        if (lane == 0)
+#pragma unroll
+            for (int g = 0; g < G; g++) sc[g][j] = s[g];
+    }
+    __syncthreads();
+    for (int g = warp; g < G; g += AT / 32) {
+        const float v = lane < n ? sc[g][lane] : -1e30f;      // AK == 32: a key per lane
+        float m = v;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        const float e = lane < n ? expf(v - m) : 0.f;
+        if (lane < n) sc[g][lane] = e;
+        float l = e;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+        if (lane == 0) {
+            ml[g][0] = m;
+            ml[g][1] = l;
+        }
+    }
+    __syncthreads();
+    constexpr int GS = AT / D;       // head groups side by side (1 for D = 128, 2 for D = 64)
+    constexpr int GJ = (G + GS - 1) / GS;
+    const int d = threadIdx.x % D, g0 = threadIdx.x / D;
+    float acc[GJ];
+#pragma unroll
+    for (int jj = 0; jj < GJ; jj++) acc[jj] = 0.f;
+#pragma unroll 4
+    for (int j = 0; j < n; j++) {
+        const float v = vs[j * D + d];
+#pragma unroll
+        for (int jj = 0; jj < GJ; jj++)
+            if (g0 + jj * GS < G) acc[jj] += sc[g0 + jj * GS][j] * v;
+    }
+#pragma unroll
+    for (int jj = 0; jj < GJ; jj++) {
+        const int g = g0 + jj * GS;
+        if (g < G) {
+            float *o = pr + (int64_t)g * nsplit * (D + 2);
+            o[d] = acc[jj];
+            if (d == 0) {
+                o[D] = ml[g][0];
+                o[D + 1] = ml[g][1];
+            }
+        }
+    }
+}
+
+// out[r][h] = sum over ranges of exp(m_s - M) acc_s / sum of exp(m_s - M) l_s
+// (M = the largest m_s); times sigmoid(gate[r][h]) when given. CTA (head,
+// row) of CT threads = CT / D groups of ranges x D dimensions: the ranges'
+// weights first, then each thread its dimension over its group's ranges
+// (many loads in flight), then the groups added in order.
+constexpr int CT = 512;
+
+template <int D>
+__global__ void __launch_bounds__(CT) attn_combine_kernel(const float *__restrict__ part,
+                                                          const float *__restrict__ gate, int H, int nsplit,
+                                                          float *__restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ float wgt[];   // [nsplit]
+    __shared__ float red[CT / 32];
+    __shared__ float sums[CT / D][D + 1];
+    constexpr int SG = CT / D;
+    const int h = blockIdx.x, r = blockIdx.y;
+    const float *pr = part + ((int64_t)r * H + h) * nsplit * (D + 2);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    float M = -1e30f;
+    for (int s = threadIdx.x; s < nsplit; s += CT) M = fmaxf(M, pr[(int64_t)s * (D + 2) + D]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (lane == 0) red[warp] = M;
+    __syncthreads();
+    M = red[0];
+#pragma unroll
+    for (int w = 1; w < CT / 32; w++) M = fmaxf(M, red[w]);
+    for (int s = threadIdx.x; s < nsplit; s += CT) wgt[s] = expf(pr[(int64_t)s * (D + 2) + D] - M);
+    __syncthreads();
+    const int d = threadIdx.x % D, sg = threadIdx.x / D;
+    float acc = 0.f, L = 0.f;
+#pragma unroll 8
+    for (int s = sg; s < nsplit; s += SG) {
+        const float w = wgt[s];
+        acc += w * pr[(int64_t)s * (D + 2) + d];
+        L += w * pr[(int64_t)s * (D + 2) + D + 1];
+    }
+    sums[sg][d] = acc;
+    if (d == 0) sums[sg][D] = L;
+    __syncthreads();
+    if (sg == 0) {
+        float o = 0.f, ll = 0.f;
+#pragma unroll
+        for (int g = 0; g < SG; g++) {
+            o += sums[g][d];
+            ll += sums[g][D];
+        }
+        o /= ll;
+        if (gate) o = o / (1.0f + expf(-gate[(int64_t)r * H + h]));
+        out[((int64_t)r * H + h) * D + d] = o;
+    }
+}
+
+// out = g * sigmoid(g) * u, elementwise (kernels.nn.wgsl.js swiglu; the same
+// expression as the fused SwiGLU GEMV's epilogue).
+__global__ void swiglu_kernel(const float *__restrict__ g, const float *__restrict__ u, int64_t n,
+                              float *__restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const float a = g[i];
+        out[i] = a / (1.0f + expf(-a)) * u[i];
     }
 }
 
@@ -247,15 +501,26 @@ __device__ __forceinline__ void finish_step(int tok, int *token, int *pos, int *
     *pos = np;
 }
 
-// Greedy argmax over n logits (strict '>': lowest index wins ties). PAIR =
-// false: finish_step with the winner. PAIR = true (one vocabulary shard of a
-// tensor-parallel head): pair[0] = the best value's bits, pair[1] = its index
-// + offset, for argmax_select over the shards.
+// Greedy argmax over the n logits of row blockIdx.x (strict '>': lowest index
+// wins ties). PAIR = false: finish_step with the winner (token, pos and
+// out_tokens of that row). PAIR = true (one vocabulary shard of a
+// tensor-parallel head): the row's pair[0] = the best value's bits, pair[1] =
+// its index + offset, for argmax_select over the shards.
 template <bool PAIR>
 __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ logits, int n,
                                                       int *__restrict__ token, int *__restrict__ pos,
                                                       int *__restrict__ out_tokens, int out_base, int out_cap,
                                                       int offset, int *__restrict__ pair) {
+    pdl_trigger();
+    pdl_wait();
+    logits += (int64_t)blockIdx.x * n;
+    if (PAIR) {
+        pair += 2 * blockIdx.x;
+    } else {
+        token += blockIdx.x;
+        pos += blockIdx.x;
+        if (out_tokens) out_tokens += (int64_t)blockIdx.x * out_cap;
+    }
     __shared__ float bv[32];
     __shared__ int bi[32];
     float best = -INFINITY;
@@ -327,16 +592,23 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
     }
 }
 
-// The winner over the shards' (value, index) pairs, in the same order as one
-// argmax over the whole vocabulary: larger value, then lower index.
+// Row blockIdx.x: the winner over the shards' (value, index) pairs (pairs
+// [nranks][rows][2]), in the same order as one argmax over the whole
+// vocabulary: larger value, then lower index.
 __global__ void argmax_select_kernel(const int *__restrict__ pairs, int npairs, int *__restrict__ token,
                                      int *__restrict__ pos, int *__restrict__ out_tokens, int out_base,
                                      int out_cap) {
+    pdl_trigger();
+    pdl_wait();
+    const int row = blockIdx.x, rows = gridDim.x;
+    token += row;
+    pos += row;
+    if (out_tokens) out_tokens += (int64_t)row * out_cap;
     float best = -INFINITY;
     int bidx = 0x7fffffff;
     for (int i = threadIdx.x; i < npairs; i += 32) {
-        const float v = __int_as_float(pairs[2 * i]);
-        const int ix = pairs[2 * i + 1];
+        const float v = __int_as_float(pairs[2 * (i * rows + row)]);
+        const int ix = pairs[2 * (i * rows + row) + 1];
         if (v > best || (v == best && ix < bidx)) {
             best = v;
             bidx = ix;
@@ -355,6 +627,22 @@ __global__ void argmax_select_kernel(const int *__restrict__ pairs, int npairs, 
 }
 
 static int grid1d(int64_t n, int b) { return (int)((n + b - 1) / b); }
+
+template <int D, int G>
+static int part_launch(ef_ctx *ctx, dim3 grid, const float *q, const float *kcache, const float *vcache, const int *pos,
+                       int tokens, int max_pos, int window, int heads, int kv_heads, float *part) {
+    constexpr size_t smem = 2 * AK * D * sizeof(float);
+    static unsigned long long configured = 0;   // per instantiation, one bit per device
+    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(attn_part_kernel<D, G>,
+                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                                "attention smem attribute"))
+            return rc;
+        configured |= 1ull << ctx->device;
+    }
+    return launch_on(ctx, attn_part_kernel<D, G>, grid, AT, smem, "attention launch", q, kcache, vcache, pos, tokens,
+                     max_pos, window, heads, kv_heads, part);
+}
 
 }  // namespace ef
 
@@ -377,14 +665,14 @@ int ef_rmsnorm(ef_ctx *ctx, const float *x, const float *w, int rows, int n, flo
     int th = 0;
     const int v = norm_v(n, th);
     if (!v) return set_err(ctx, EF_ERR_SHAPE, "rmsnorm: n=%d (a multiple of 128 up to 8192, power-of-2 blocks)", n);
-    ctx->launches++;
+    int rc = EF_OK;
     switch (v) {
-    case 1: rmsnorm_kernel<1><<<rows, th, 0, ctx->stream>>>(x, w, n, eps, y); break;
-    case 2: rmsnorm_kernel<2><<<rows, th, 0, ctx->stream>>>(x, w, n, eps, y); break;
-    case 4: rmsnorm_kernel<4><<<rows, th, 0, ctx->stream>>>(x, w, n, eps, y); break;
-    default: rmsnorm_kernel<8><<<rows, th, 0, ctx->stream>>>(x, w, n, eps, y); break;
+    case 1: rc = launch_on(ctx, rmsnorm_kernel<1>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
+    case 2: rc = launch_on(ctx, rmsnorm_kernel<2>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
+    case 4: rc = launch_on(ctx, rmsnorm_kernel<4>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
+    default: rc = launch_on(ctx, rmsnorm_kernel<8>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
     }
-    return check_cuda(ctx, cudaGetLastError(), "rmsnorm launch");
+    return rc;
 }
 
 int ef_norm_add_norm(ef_ctx *ctx, const float *o, const float *w_post, float *x, const float *w_next, int rows, int n,
@@ -394,14 +682,14 @@ int ef_norm_add_norm(ef_ctx *ctx, const float *o, const float *w_post, float *x,
     int th = 0;
     const int v = norm_v(n, th);
     if (!v) return set_err(ctx, EF_ERR_SHAPE, "norm_add_norm: n=%d (a multiple of 128 up to 8192, power-of-2 blocks)", n);
-    ctx->launches++;
+    int rc = EF_OK;
     switch (v) {
-    case 1: norm_add_norm_kernel<1><<<rows, th, 0, ctx->stream>>>(o, w_post, x, w_next, n, eps, nrm); break;
-    case 2: norm_add_norm_kernel<2><<<rows, th, 0, ctx->stream>>>(o, w_post, x, w_next, n, eps, nrm); break;
-    case 4: norm_add_norm_kernel<4><<<rows, th, 0, ctx->stream>>>(o, w_post, x, w_next, n, eps, nrm); break;
-    default: norm_add_norm_kernel<8><<<rows, th, 0, ctx->stream>>>(o, w_post, x, w_next, n, eps, nrm); break;
+    case 1: rc = launch_on(ctx, norm_add_norm_kernel<1>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
+    case 2: rc = launch_on(ctx, norm_add_norm_kernel<2>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
+    case 4: rc = launch_on(ctx, norm_add_norm_kernel<4>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
+    default: rc = launch_on(ctx, norm_add_norm_kernel<8>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
     }
-    return check_cuda(ctx, cudaGetLastError(), "norm_add_norm launch");
+    return rc;
 }
 
 int ef_shortconv(ef_ctx *ctx, const float *bcx, const float *conv_w, float *state, int tokens, int channels, int kernel,
@@ -409,9 +697,26 @@ int ef_shortconv(ef_ctx *ctx, const float *bcx, const float *conv_w, float *stat
     if (!ctx || !bcx || !conv_w || !state || !y || tokens < 1 || channels < 1)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "shortconv: bad arguments") : EF_ERR_INVALID;
     if (kernel != 3) return set_err(ctx, EF_ERR_SHAPE, "shortconv: kernel %d (3 supported)", kernel);
-    ctx->launches++;
-    shortconv_kernel<3><<<grid1d(channels, 256), 256, 0, ctx->stream>>>(bcx, conv_w, state, tokens, channels, y);
-    return check_cuda(ctx, cudaGetLastError(), "shortconv launch");
+    return launch_on(ctx, shortconv_kernel<3>, grid1d(channels, 256), 256, 0, "shortconv launch", bcx, conv_w,
+                     state, tokens, channels, y);
+}
+
+static int rope_launch(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
+                       const int *pos, int seqs, int tokens, int max_pos, int heads, int kv_heads, int head_dim,
+                       int neox, float theta_base, float eps, float *kcache, float *vcache) {
+    const float theta_scale = powf(theta_base, -2.0f / (float)head_dim);
+    const int64_t warps = (int64_t)seqs * tokens * (heads + kv_heads);
+    const int grid = (int)((warps + 7) / 8);
+#define EF_ROPE(DD, NX)                                                                                     \
+    return launch_on(ctx, rope_cache_kernel<DD, NX>, grid, 256, 0, "rope_cache launch", q, k, v, wq, wk, pos, \
+                     seqs, tokens, max_pos, heads, kv_heads, theta_scale, eps, kcache, vcache)
+    if (head_dim == 64) {
+        if (neox) EF_ROPE(64, true);
+        EF_ROPE(64, false);
+    }
+    if (neox) EF_ROPE(128, true);
+    EF_ROPE(128, false);
+#undef EF_ROPE
 }
 
 int ef_qk_norm_rope_cache(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
@@ -420,11 +725,85 @@ int ef_qk_norm_rope_cache(ef_ctx *ctx, float *q, const float *k, const float *v,
     if (!ctx || !q || !k || !v || !wq || !wk || !pos || !kcache || !vcache || heads < 1 || kv_heads < 1)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "qk_norm_rope_cache: bad arguments") : EF_ERR_INVALID;
     if (head_dim != 64) return set_err(ctx, EF_ERR_SHAPE, "qk_norm_rope_cache: head_dim %d (64 supported)", head_dim);
-    const float theta_scale = powf(theta_base, -2.0f / (float)head_dim);
-    ctx->launches++;
-    qk_norm_rope_cache_kernel<<<grid1d(heads + kv_heads, 8), 256, 0, ctx->stream>>>(
-        q, k, v, wq, wk, pos, max_pos, heads, kv_heads, theta_scale, eps, kcache, vcache);
-    return check_cuda(ctx, cudaGetLastError(), "qk_norm_rope_cache launch");
+    return rope_launch(ctx, q, k, v, wq, wk, pos, 1, 1, max_pos, heads, kv_heads, 64, 1, theta_base, eps, kcache,
+                       vcache);
+}
+
+int ef_rope_cache(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
+                  const int *pos, int seqs, int tokens, int max_pos, int heads, int kv_heads, int head_dim,
+                  int rope_mode, float theta_base, float eps, float *kcache, float *vcache) {
+    if (!ctx || !q || !k || !v || !pos || !kcache || !vcache || heads < 1 || kv_heads < 1 || seqs < 1 ||
+        tokens < 1 || max_pos < 1 || (!wq) != (!wk))
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "rope_cache: bad arguments") : EF_ERR_INVALID;
+    if (head_dim != 64 && head_dim != 128)
+        return set_err(ctx, EF_ERR_SHAPE, "rope_cache: head_dim %d (64 or 128 supported)", head_dim);
+    if (rope_mode != EF_ROPE_NORM && rope_mode != EF_ROPE_NEOX)
+        return set_err(ctx, EF_ERR_INVALID, "rope_cache: unknown RoPE mode %d", rope_mode);
+    if ((int64_t)seqs * tokens > 65535) return set_err(ctx, EF_ERR_RANGE, "rope_cache: more than 65535 rows");
+    return rope_launch(ctx, q, k, v, wq, wk, pos, seqs, tokens, max_pos, heads, kv_heads, head_dim,
+                       rope_mode == EF_ROPE_NEOX, theta_base, eps, kcache, vcache);
+}
+
+static int attention_launch(ef_ctx *ctx, const float *q, const float *kcache, const float *vcache,
+                            const float *head_gate, const int *pos, int seqs, int tokens, int max_pos, int window,
+                            int heads, int kv_heads, int head_dim, float *out) {
+    const int span = window > 0 && window < max_pos ? window : max_pos;
+    const size_t smem = (size_t)span * 4;
+    if (smem > 200 * 1024) return set_err(ctx, EF_ERR_RANGE, "attention: %d keys exceed shared memory", span);
+    static unsigned long long configured[2] = {0, 0};
+    const int di = head_dim == 64 ? 0 : 1;
+    if (ctx->device < 64 && !(configured[di] & (1ull << ctx->device))) {
+        cudaError_t e = di == 0 ? cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       200 * 1024)
+                                : cudaFuncSetAttribute(attention_kernel<128>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (int rc = check_cuda(ctx, e, "attention smem attribute")) return rc;
+        configured[di] |= 1ull << ctx->device;
+    }
+    const int G = heads / kv_heads;
+    if (tokens == 1 && (G == 1 || G == 2 || G == 4 || G == 8)) {
+        // one new token per sequence: the keys split over CTAs, then merged
+        const int nsplit = (span + AK - 1) / AK;
+        const int64_t rows = seqs;
+        const size_t bytes = (size_t)rows * heads * nsplit * (head_dim + 2) * sizeof(float);
+        if (int rc = ensure_scratch(ctx, 2, bytes)) return rc;
+        float *part = (float *)ctx->scratch[2];
+        const dim3 pg(nsplit, kv_heads, (unsigned)rows);
+#define EF_PART(DD, GG)                                                                                          \
+    rc = part_launch<DD, GG>(ctx, pg, q, kcache, vcache, pos, tokens, max_pos, window, heads, kv_heads, part)
+        int rc;
+        if (head_dim == 64) {
+            switch (G) {
+            case 1: EF_PART(64, 1); break;
+            case 2: EF_PART(64, 2); break;
+            case 4: EF_PART(64, 4); break;
+            default: EF_PART(64, 8); break;
+            }
+        } else {
+            switch (G) {
+            case 1: EF_PART(128, 1); break;
+            case 2: EF_PART(128, 2); break;
+            case 4: EF_PART(128, 4); break;
+            default: EF_PART(128, 8); break;
+            }
+        }
+#undef EF_PART
+        if (rc) return rc;
+        const dim3 cg(heads, (unsigned)rows);
+        const size_t cs = (size_t)nsplit * sizeof(float);
+        if (cs > 48 * 1024) return set_err(ctx, EF_ERR_RANGE, "attention: %d key ranges", nsplit);
+        if (head_dim == 64)
+            return launch_on(ctx, attn_combine_kernel<64>, cg, CT, cs, "attention combine launch",
+                             (const float *)part, head_gate, heads, nsplit, out);
+        return launch_on(ctx, attn_combine_kernel<128>, cg, CT, cs, "attention combine launch", (const float *)part,
+                         head_gate, heads, nsplit, out);
+    }
+    const dim3 grid(heads, seqs * tokens);
+    if (di == 0)
+        return launch_on(ctx, attention_kernel<64>, grid, 256, smem, "attention launch", q, kcache, vcache,
+                         head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+    return launch_on(ctx, attention_kernel<128>, grid, 256, smem, "attention launch", q, kcache, vcache, head_gate,
+                     pos, tokens, max_pos, window, heads, kv_heads, out);
 }
 
 int ef_attn_decode(ef_ctx *ctx, const float *q, const float *kcache, const float *vcache, const float *head_gate,
@@ -432,47 +811,56 @@ int ef_attn_decode(ef_ctx *ctx, const float *q, const float *kcache, const float
     if (!ctx || !q || !kcache || !vcache || !pos || !out || heads < 1 || kv_heads < 1 || heads % kv_heads)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "attn_decode: bad arguments") : EF_ERR_INVALID;
     if (head_dim != 64) return set_err(ctx, EF_ERR_SHAPE, "attn_decode: head_dim %d (64 supported)", head_dim);
-    const int span = window > 0 && window < max_pos ? window : max_pos;
-    const size_t smem = (size_t)span * 4;
-    if (smem > 200 * 1024) return set_err(ctx, EF_ERR_RANGE, "attn_decode: %d keys exceed shared memory", span);
-    static unsigned long long configured = 0;
-    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
-        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(attn_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                          200 * 1024), "attn smem attribute"))
-            return rc;
-        configured |= 1ull << ctx->device;
-    }
-    ctx->launches++;
-    attn_decode_kernel<<<heads, 256, smem, ctx->stream>>>(q, kcache, vcache, head_gate, pos, max_pos, window, heads,
-                                                          kv_heads, out);
-    return check_cuda(ctx, cudaGetLastError(), "attn_decode launch");
+    return attention_launch(ctx, q, kcache, vcache, head_gate, pos, 1, 1, max_pos, window, heads, kv_heads, 64, out);
+}
+
+int ef_attention(ef_ctx *ctx, const float *q, const float *kcache, const float *vcache, const float *head_gate,
+                 const int *pos, int seqs, int tokens, int max_pos, int window, int heads, int kv_heads, int head_dim,
+                 float *out) {
+    if (!ctx || !q || !kcache || !vcache || !pos || !out || heads < 1 || kv_heads < 1 || heads % kv_heads ||
+        seqs < 1 || tokens < 1 || max_pos < 1 || window < 0)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "attention: bad arguments") : EF_ERR_INVALID;
+    if (head_dim != 64 && head_dim != 128)
+        return set_err(ctx, EF_ERR_SHAPE, "attention: head_dim %d (64 or 128 supported)", head_dim);
+    if ((int64_t)seqs * tokens > 65535) return set_err(ctx, EF_ERR_RANGE, "attention: more than 65535 rows");
+    return attention_launch(ctx, q, kcache, vcache, head_gate, pos, seqs, tokens, max_pos, window, heads, kv_heads,
+                            head_dim, out);
+}
+
+int ef_swiglu(ef_ctx *ctx, const float *gate, const float *up, int64_t n, float *out) {
+    if (!ctx || !gate || !up || !out || n < 1)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "swiglu: bad arguments") : EF_ERR_INVALID;
+    int64_t blocks = (n + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    return launch_on(ctx, swiglu_kernel, (int)blocks, 256, 0, "swiglu launch", gate, up, n, out);
 }
 
 int ef_argmax_step(ef_ctx *ctx, const float *logits, int n, int *token, int *pos, int *out_tokens, int out_base,
                    int out_cap) {
-    if (!ctx || !logits || !token || !pos || n < 1)
-        return ctx ? set_err(ctx, EF_ERR_INVALID, "argmax_step: bad arguments") : EF_ERR_INVALID;
-    ctx->launches++;
-    argmax_kernel<false><<<1, 1024, 0, ctx->stream>>>(logits, n, token, pos, out_tokens, out_base, out_cap, 0,
-                                                       nullptr);
-    return check_cuda(ctx, cudaGetLastError(), "argmax_step launch");
+    return ef_argmax_rows(ctx, logits, 1, n, token, pos, out_tokens, out_base, out_cap);
 }
 
-int ef_argmax_partial(ef_ctx *ctx, const float *logits, int n, int offset, int *pair) {
-    if (!ctx || !logits || !pair || n < 1 || offset < 0)
+int ef_argmax_rows(ef_ctx *ctx, const float *logits, int rows, int n, int *tokens, int *pos, int *out_tokens,
+                   int out_base, int out_cap) {
+    if (!ctx || !logits || !tokens || !pos || n < 1 || rows < 1 || rows > 65535)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "argmax: bad arguments") : EF_ERR_INVALID;
+    return launch_on(ctx, argmax_kernel<false>, rows, 1024, 0, "argmax launch", logits, n, tokens, pos, out_tokens,
+                     out_base, out_cap, 0, (int *)nullptr);
+}
+
+int ef_argmax_partial(ef_ctx *ctx, const float *logits, int rows, int n, int offset, int *pairs) {
+    if (!ctx || !logits || !pairs || n < 1 || offset < 0 || rows < 1 || rows > 65535)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "argmax_partial: bad arguments") : EF_ERR_INVALID;
-    ctx->launches++;
-    argmax_kernel<true><<<1, 1024, 0, ctx->stream>>>(logits, n, nullptr, nullptr, nullptr, 0, 0, offset, pair);
-    return check_cuda(ctx, cudaGetLastError(), "argmax_partial launch");
+    return launch_on(ctx, argmax_kernel<true>, rows, 1024, 0, "argmax_partial launch", logits, n, (int *)nullptr,
+                     (int *)nullptr, (int *)nullptr, 0, 0, offset, pairs);
 }
 
-int ef_argmax_select(ef_ctx *ctx, const int *pairs, int npairs, int *token, int *pos, int *out_tokens,
+int ef_argmax_select(ef_ctx *ctx, const int *pairs, int nranks, int rows, int *tokens, int *pos, int *out_tokens,
                      int out_base, int out_cap) {
-    if (!ctx || !pairs || !token || !pos || npairs < 1)
+    if (!ctx || !pairs || !tokens || !pos || nranks < 1 || rows < 1 || rows > 65535)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "argmax_select: bad arguments") : EF_ERR_INVALID;
-    ctx->launches++;
-    argmax_select_kernel<<<1, 32, 0, ctx->stream>>>(pairs, npairs, token, pos, out_tokens, out_base, out_cap);
-    return check_cuda(ctx, cudaGetLastError(), "argmax_select launch");
+    return launch_on(ctx, argmax_select_kernel, rows, 32, 0, "argmax_select launch", pairs, nranks, tokens, pos,
+                     out_tokens, out_base, out_cap);
 }
 
 }  // extern "C"

@@ -85,6 +85,8 @@ __global__ void dequant_kernel(int type, const uint8_t *__restrict__ src, int64_
 __global__ void gather_kernel(int type, const uint8_t *__restrict__ src, const int *__restrict__ ids, int tokens,
                               int64_t rows, int64_t bpr, int64_t nchunks, int bpc, int bb, int be, int tile_bytes,
                               int64_t k, float *__restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
     const int8_t *grid = type == EF_IQ2_XXS ? g_grid_iq2xxs_i8 : g_grid_iq1s_i8;
     const int64_t total = (int64_t)tokens * bpr;
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
@@ -156,11 +158,9 @@ int launch_gather(ef_ctx *ctx, const ef_weight *w, const int *ids, int tokens, f
     geo_of(w->type, geo);
     const int bpc = geo.chunk_k / geo.block_elems;
     const int64_t bpr = w->k / geo.block_elems;
-    ctx->launches++;
-    gather_kernel<<<grid_for((int64_t)tokens * bpr), 128, 0, ctx->stream>>>(
-        w->type, w->dev, ids, tokens, w->rows, bpr, w->nchunks, bpc, geo.block_bytes, geo.block_elems,
-        geo.tile_bytes, w->k, out);
-    return check_cuda(ctx, cudaGetLastError(), "gather launch");
+    return launch_on(ctx, gather_kernel, grid_for((int64_t)tokens * bpr), 128, 0, "gather launch", w->type,
+                     (const uint8_t *)w->dev, ids, tokens, w->rows, bpr, w->nchunks, bpc, geo.block_bytes,
+                     geo.block_elems, geo.tile_bytes, w->k, out);
 }
 
 }  // namespace ef

@@ -201,9 +201,9 @@ class LFM3Decoder:
     world > 1, `weights` are this rank's shard_weights and the collectives go
     through torch.distributed's default (NCCL) process group."""
 
-    def __init__(self, ops, cfg: LFM3Config, weights: dict, rank: int = 0, world: int = 1):
+    def __init__(self, ops, cfg: LFM3Config, weights: dict, rank: int = 0, world: int = 1, pdl: bool = True):
         self.ops, self.cfg, self.L = ops, cfg, lib()
-        self.rank, self.world = rank, world
+        self.rank, self.world, self.pdl = rank, world, pdl
         E, D = cfg.hidden, cfg.head_dim
         H, KV, F = cfg.heads // world, cfg.kv_heads // world, cfg.ffn // world
         self.Hl, self.KVl, self.Ec, self.Fl, self.Vl = H, KV, E // world, F, cfg.vocab // world
@@ -251,6 +251,16 @@ class LFM3Decoder:
             dist.all_reduce(t)
 
     def step(self):
+        """Queue one step; with pdl, its kernels are launched as a programmatic-
+        dependent-launch chain (each scheduled while the previous one ends)."""
+        L, h = self.L, self.ops.ctx.bind()
+        check(L.ef_ctx_set_pdl(h, 1 if self.pdl else 0), h)
+        try:
+            self._step()
+        finally:
+            L.ef_ctx_set_pdl(h, 0)
+
+    def _step(self):
         L, cfg, h = self.L, self.cfg, self.ops.ctx.bind()
         E, D = cfg.hidden, cfg.head_dim
         H, KV = self.Hl, self.KVl
@@ -292,11 +302,10 @@ class LFM3Decoder:
                                    self.out_base, cfg.max_pos), h)
         else:
             import torch.distributed as dist
-            check(L.ef_argmax_partial(h, _p(self.logits), self.Vl, self.rank * self.Vl, _p(self.pair)), h)
+            check(L.ef_argmax_partial(h, _p(self.logits), 1, self.Vl, self.rank * self.Vl, _p(self.pair)), h)
             dist.all_gather_into_tensor(self.pairs, self.pair)
-            h = self.ops.ctx.bind()
-            check(L.ef_argmax_select(h, _p(self.pairs), self.world, _p(self.tok), _p(self.pos), _p(self.out_tokens),
-                                     self.out_base, cfg.max_pos), h)
+            check(L.ef_argmax_select(h, _p(self.pairs), self.world, 1, _p(self.tok), _p(self.pos),
+                                     _p(self.out_tokens), self.out_base, cfg.max_pos), h)
 
     def capture(self):
         """Record one step as a CUDA graph (after one eager step has sized every scratch)."""

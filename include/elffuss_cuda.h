@@ -82,6 +82,14 @@ EF_API int ef_ctx_destroy(ef_ctx *ctx);
  * stream); NULL selects the CUDA default stream. Until the first call the
  * context uses a stream of its own. */
 EF_API int ef_ctx_set_stream(ef_ctx *ctx, void *cuda_stream);
+
+/* Programmatic dependent launch for this context's kernels (on != 0): each
+ * kernel may be scheduled while the one before it on the stream finishes,
+ * fetching what does not depend on it (the weights) early, and waits for
+ * that kernel's results before reading them. Off by default (and when the
+ * environment variable EF_PDL is not "1"): it pays where short kernels
+ * follow one another, as in a decode step. No counterpart in the reference. */
+EF_API int ef_ctx_set_pdl(ef_ctx *ctx, int on);
 EF_API void *ef_ctx_stream(const ef_ctx *ctx);
 
 /* Wait for all work queued on the context's stream (the readback sync point,
@@ -251,18 +259,56 @@ EF_API int ef_attn_decode(ef_ctx *ctx, const float *q, const float *kcache, cons
 EF_API int ef_argmax_step(ef_ctx *ctx, const float *logits, int n, int *token, int *pos, int *out_tokens,
                           int out_base, int out_cap);
 
+/* Several rows at once (one per sequence of a batch): row r's argmax updates
+ * tokens[r], pos[r] and out_tokens[r * out_cap + new pos[r] - out_base]
+ * (when in [0, out_cap)); logits [rows][n]. */
+EF_API int ef_argmax_rows(ef_ctx *ctx, const float *logits, int rows, int n, int *tokens, int *pos,
+                          int *out_tokens, int out_base, int out_cap);
+
 /* Tensor-parallel greedy head (the LM head split by vocabulary rows over the
  * ranks; the reference has one device and no counterpart, its single-device
- * argmax is js/sample.js:95-99). ef_argmax_partial: the argmax of this
- * rank's n logits as pair[0] = the value's f32 bits, pair[1] = its index +
- * offset (the shard's first vocabulary id). ef_argmax_select: given the
- * ranks' pairs gathered in rank order (2 * npairs ints), the winner in the
- * order of one argmax over the whole vocabulary (larger value, then lower
- * index), then the same token / position / out_tokens update as
- * ef_argmax_step. */
-EF_API int ef_argmax_partial(ef_ctx *ctx, const float *logits, int n, int offset, int *pair);
-EF_API int ef_argmax_select(ef_ctx *ctx, const int *pairs, int npairs, int *token, int *pos, int *out_tokens,
-                            int out_base, int out_cap);
+ * argmax is js/sample.js:95-99). ef_argmax_partial: for each of `rows` rows of
+ * this rank's n logits, pairs[2r] = the best value's f32 bits, pairs[2r+1] =
+ * its index + offset (the shard's first vocabulary id). ef_argmax_select:
+ * given the ranks' pairs gathered in rank order ([nranks][rows][2] ints), each
+ * row's winner in the order of one argmax over the whole vocabulary (larger
+ * value, then lower index), then the same update as ef_argmax_rows. */
+EF_API int ef_argmax_partial(ef_ctx *ctx, const float *logits, int rows, int n, int offset, int *pairs);
+EF_API int ef_argmax_select(ef_ctx *ctx, const int *pairs, int nranks, int rows, int *tokens, int *pos,
+                            int *out_tokens, int out_base, int out_cap);
+
+/* RoPE pairing (js/kernels.nn.wgsl.js:27, js/state.js:345-349): NORM rotates
+ * adjacent elements (2i, 2i+1) -- llama --, NEOX elements (i, i + D/2) --
+ * lfm3, qwen35. */
+#define EF_ROPE_NORM 0
+#define EF_ROPE_NEOX 2
+
+/* Attention input for `seqs` sequences of `tokens` new tokens each (rows r =
+ * seq * tokens + t, token t of sequence s at position pos[s] + t): optional
+ * per-head RMSNorm (wq, wk [head_dim], both NULL for none: llama has no
+ * QK-norm, js/model.js:905-917), RoPE in `rope_mode` with theta = position *
+ * theta_base^(-2i/head_dim) on q [rows][heads][head_dim] (in place) and k
+ * [rows][kv_heads][head_dim], then k and v into the caches
+ * [seqs][max_pos][kv_heads][head_dim] (js/model.js:895-945); positions at or
+ * past max_pos are not stored. head_dim 64 or 128; rows <= 65535. */
+EF_API int ef_rope_cache(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
+                         const int *pos, int seqs, int tokens, int max_pos, int heads, int kv_heads, int head_dim,
+                         int rope_mode, float theta_base, float eps, float *kcache, float *vcache);
+
+/* Causal attention for the rows of ef_rope_cache: the query at position p of
+ * sequence s attends to that sequence's cache positions 0..p (those with
+ * p - key < window; window 0 = all), scale 1/sqrt(head_dim), heads / kv_heads
+ * queries per cache head, times sigmoid(head_gate[r][h]) when head_gate is not
+ * NULL (js/model.js:946-983, kernels.nn.wgsl.js:141-200). out
+ * [rows][heads][head_dim]; head_dim 64 or 128. A prompt of T tokens is one
+ * call with tokens = T after ef_rope_cache has stored all T. */
+EF_API int ef_attention(ef_ctx *ctx, const float *q, const float *kcache, const float *vcache,
+                        const float *head_gate, const int *pos, int seqs, int tokens, int max_pos, int window,
+                        int heads, int kv_heads, int head_dim, float *out);
+
+/* out[i] = gate[i] * sigmoid(gate[i]) * up[i] for the n elements (the
+ * prompt-side SwiGLU after two separate GEMMs; js/model.js:651-655). */
+EF_API int ef_swiglu(ef_ctx *ctx, const float *gate, const float *up, int64_t n, float *out);
 
 #ifdef __cplusplus
 }
