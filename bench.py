@@ -230,6 +230,18 @@ def bench_gemm(ops, L, args, capture, timed_replays, rank):
 
 
 DECODE_PROMPT, DECODE_TOKENS = 512, 128
+_COMM = {}
+
+
+def tp_comm(ops, args, world, rank):
+    """The decoders' collectives for world > 1: the library's peer-memory
+    kernels (tp.TPComm, default) or NCCL (--tp-comm nccl)."""
+    if world == 1 or args.tp_comm != "peer":
+        return None
+    if "c" not in _COMM:
+        from elffuss_engine_b200.tp import TPComm
+        _COMM["c"] = TPComm(ops, rank, world, max_bytes=1 << 20)
+    return _COMM["c"]
 
 
 def bench_decode(ops, args, world, rank, barrier, max_over_ranks):
@@ -243,7 +255,7 @@ def bench_decode(ops, args, world, rank, barrier, max_over_ranks):
     w = synth_weights(cfg, seed=0, device="cuda")
     if world > 1:
         w = shard_weights(cfg, w, rank, world)
-    dec = LFM3Decoder(ops, cfg, w, rank, world)
+    dec = LFM3Decoder(ops, cfg, w, rank, world, comm=tp_comm(ops, args, world, rank))
     del w
     torch.cuda.empty_cache()
     prompt = torch.randint(0, cfg.vocab, (DECODE_PROMPT,), generator=torch.Generator().manual_seed(0),
@@ -280,7 +292,7 @@ def bench_decode(ops, args, world, rank, barrier, max_over_ranks):
     return {"workload": f"config3 synthetic LFM3-shaped decoder (Q8_0, hidden 2048, 16 layers: 10 short-conv + "
                         f"6 GQA at {list(cfg.attn_layers)}), {DECODE_PROMPT}-id prompt then {DECODE_TOKENS} "
                         f"greedy steps, each step one CUDA-graph replay",
-            "parallelism": f"tp{world}" if world > 1 else "single GPU",
+            "parallelism": f"tp{world} ({args.tp_comm} collectives)" if world > 1 else "single GPU",
             "tok_s": round(DECODE_TOKENS / (decode_ms * 1e-3), 1),
             "ms_per_token": round(decode_ms / DECODE_TOKENS, 4),
             "weight_GBps_per_gpu": round(weight_bytes / world / (decode_ms / DECODE_TOKENS * 1e-3) / 1e9, 1),
@@ -314,10 +326,10 @@ def bench_llama(ops, args, world, rank, barrier, max_over_ranks):
     out = {"workload": f"config4 synthetic Llama-architecture 8B shape (32 layers, hidden 4096, 32/8 heads x 128, "
                        f"FFN 14336, vocab 128256; Q4_K, Q6_K for attn_v / even ffn_down / output), "
                        f"{LLAMA_CONTEXT}-id context, {LLAMA_STEPS} greedy steps per batch size",
-           "parallelism": f"tp{world}" if world > 1 else "single GPU",
+           "parallelism": f"tp{world} ({args.tp_comm} collectives)" if world > 1 else "single GPU",
            "weight_bytes_per_step_per_gpu": cfg.step_weight_bytes() // world}
     for B in (1, 16):
-        dec = LlamaDecoder(ops, cfg, w, batch=B, rank=rank, world=world)
+        dec = LlamaDecoder(ops, cfg, w, batch=B, rank=rank, world=world, comm=tp_comm(ops, args, world, rank))
         lasts = [int(prompt[-1])] + [int(t) for t in ids[LLAMA_CONTEXT:LLAMA_CONTEXT + B - 1]]
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         barrier()
@@ -350,6 +362,48 @@ def bench_llama(ops, args, world, rank, barrier, max_over_ranks):
     del w
     torch.cuda.empty_cache()
     return out
+
+
+def run_profile(args):
+    """Profiling drivers for ncu (no timing): --ncu-gemm runs config 2's first
+    GEMM shape (M=512, K=2048, N=8192) on 4 weight copies, eagerly, 3 times;
+    --ncu-decode builds the config-3 LFM3 decoder and runs 8 eager decode
+    steps, the last inside an NVTX range named "step"."""
+    import torch
+
+    import __graft_entry__
+    __graft_entry__.package()
+    from elffuss_engine_b200 import formats
+    from elffuss_engine_b200._lib import check, lib
+    from elffuss_engine_b200.ops import QuantOps, _ptr
+    ops, L = QuantOps(0), lib()
+    if args.ncu_gemm:
+        m, k, n = GEMM_SHAPES[0]
+        raw = formats.synth("Q8_0", n, k, seed=500)
+        ws = [ops.load_weight("Q8_0", raw, n, k) for _ in range(4)]
+        x = torch.randn(m, k, device="cuda", generator=torch.Generator("cuda").manual_seed(0)).half()
+        y = torch.empty(m, n, device="cuda")
+        for _ in range(3):
+            h = ops.ctx.bind()
+            for w in ws:
+                check(L.ef_gemm(h, w.h, _ptr(x), 1, m, _ptr(y), 0), h)
+        torch.cuda.synchronize()
+        print(json.dumps({"ncu_gemm": True, "launches": 12}), flush=True)
+        return 0
+    from elffuss_engine_b200.lfm3 import LFM3Config, LFM3Decoder, synth_weights
+    cfg = LFM3Config()
+    dec = LFM3Decoder(ops, cfg, synth_weights(cfg, seed=0, device="cuda"))
+    dec.reset(out_base=0)
+    for i in range(8):
+        dec.tok.fill_(i)
+        if i == 7:
+            torch.cuda.nvtx.range_push("step")
+        dec.step()
+        if i == 7:
+            torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    print(json.dumps({"ncu_decode": True}), flush=True)
+    return 0
 
 
 def run_ours(args):
@@ -405,14 +459,6 @@ def run_ours(args):
         h = ops.ctx.bind()
         for (t, n, k, m, w, x, y, xh, yh, b) in work:
             check(L.ef_gemv(h, w.h, _ptr(x), m, _ptr(y)), h)
-
-    def step_device_evs(evs):
-        h = ops.ctx.bind()
-        s = torch.cuda.current_stream()
-        for j, (t, n, k, m, w, x, y, xh, yh, b) in enumerate(work):
-            evs[j][0].record(s)
-            check(L.ef_gemv(h, w.h, _ptr(x), m, _ptr(y)), h)
-            evs[j][1].record(s)
 
     def step_e2e():
         x_all.copy_(xh_all, non_blocking=True)                      # the step's inputs, host -> device
@@ -481,17 +527,34 @@ def run_ours(args):
     ms_step = t_ms / args.steps
     value = world * step_bytes / (ms_step * 1e-3) / 1e9
 
-    # ---- per-kernel durations: events between the kernels of the step ----
-    evs = [(torch.cuda.Event(enable_timing=True, external=True),
-            torch.cuda.Event(enable_timing=True, external=True)) for _ in work]
-    g_ker = capture(step_device_evs, evs)
+    # ---- per-kernel durations: each call's GEMV launched back to back on 8
+    # distinct copies of its weight (more than L2 between reuses), CUDA events
+    # around the replays of that captured sequence ----
+    COPIES = 8
     reps = max(3, min(args.steps, 20))
-    kern_ms = [0.0] * len(work)
-    for _ in range(reps):
-        g_ker.replay()
+    kern_ms = []
+    for i, (t, n, k, m, w, x, y, xh, yh, b) in enumerate(work):
+        raw = formats.synth(t, n, k, seed=1000 * rank + i)
+        ws = [w] + [ops.load_weight(t, raw, n, k) for _ in range(COPIES - 1)]
+        del raw
+
+        def seq(ws=ws, x=x, y=y, m=m):
+            h = ops.ctx.bind()
+            for wc in ws:
+                check(L.ef_gemv(h, wc.h, _ptr(x), m, _ptr(y)), h)
+        g_k = capture(seq)
+        g_k.replay()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize()
-        for j in range(len(work)):
-            kern_ms[j] += evs[j][0].elapsed_time(evs[j][1]) / reps
+        ev0.record()
+        for _ in range(reps):
+            g_k.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+        kern_ms.append(ev0.elapsed_time(ev1) / (reps * COPIES))
+        del g_k
+        for wc in ws[1:]:
+            wc.free()
 
     # ---- end to end through the public operator, pinned host buffers ----
     g_e2e = capture(step_e2e)
@@ -501,7 +564,7 @@ def run_ours(args):
     e2e_val = world * step_bytes / (e2e_ms * 1e-3) / 1e9
     h2d = 4 * x_elems
     d2h = 4 * y_elems
-    del g_dev, g_ker, g_e2e
+    del g_dev, g_e2e
 
     # ---- config 2: Q8_0 prefill GEMM on tcgen05 (tensor roofline) ----
     gemm = None if args.no_gemm else bench_gemm(ops, L, args, capture, timed_replays, rank)
@@ -541,7 +604,9 @@ def run_ours(args):
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": profile_traffic(), "algorithmic_bytes": step_bytes,
-                         "per": "one step = the 12 gemv_kernel launches (sum of bytes / sum of launch times)",
+                         "per": "the 12 calls of a step: sum of their algorithmic bytes / sum of their average "
+                                "launch durations (each call launched back to back on 8 weight copies; for M > 2 "
+                                "the duration includes the call's activation-prep kernel)",
                          "kernel": "gemv_kernel"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
@@ -556,6 +621,9 @@ def run_ours(args):
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
+        if "c" in _COMM:
+            torch.cuda.synchronize()
+            _COMM.pop("c").close()
         dist.destroy_process_group()
     return 0
 
@@ -568,10 +636,15 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-2 GEMM measurement")
-    ap.add_argument("--no-decode", action="store_true", help="skip the config-3 LFM3 decode measurement")
+    ap.add_argument("--no-decode", action="store_true", help="skip the config-3/4 decode measurements")
+    ap.add_argument("--tp-comm", default="peer", choices=["peer", "nccl"],
+                    help="tensor-parallel decode collectives: the library's peer-memory kernels or NCCL")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ncu-step", action="store_true",
                     help="profiling mode for ncu: eager warm-up steps plus one eager step, no timing")
+    ap.add_argument("--ncu-gemm", action="store_true", help="profiling mode for ncu: config-2 GEMM calls only")
+    ap.add_argument("--ncu-decode", action="store_true",
+                    help="profiling mode for ncu: config-3 decode steps, the last in an NVTX range 'step'")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -579,6 +652,8 @@ def main():
     __graft_entry__.package()
     if args.impl == "reference":
         return run_reference(args)
+    if args.ncu_gemm or args.ncu_decode:
+        return run_profile(args)
     return run_ours(args)
 
 

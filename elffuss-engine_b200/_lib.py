@@ -15,7 +15,7 @@ HEADER = os.path.join(HERE, "..", "include", "elffuss_cuda.h")
 
 EF_OK, EF_NOT_APPLICABLE = 0, 1
 ERRORS = {-1: "EF_ERR_INVALID", -2: "EF_ERR_TYPE", -3: "EF_ERR_SHAPE", -4: "EF_ERR_CUDA",
-          -5: "EF_ERR_OOM", -6: "EF_ERR_MISMATCH", -7: "EF_ERR_RANGE"}
+          -5: "EF_ERR_OOM", -6: "EF_ERR_MISMATCH", -7: "EF_ERR_RANGE", -8: "EF_ERR_TIMEOUT"}
 F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, IQ2_XXS, IQ1_S = 0, 1, 2, 8, 12, 14, 16, 19
 TYPE_IDS = {"F32": F32, "F16": F16, "Q4_0": Q4_0, "Q8_0": Q8_0, "Q4_K": Q4_K, "Q6_K": Q6_K,
             "IQ2_XXS": IQ2_XXS, "IQ1_S": IQ1_S}
@@ -84,6 +84,13 @@ _SIGS = {
                        _P, _P], _I),
     "ef_attention": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
     "ef_swiglu": ([_P, _P, _P, ctypes.c_int64, _P], _I),
+    "ef_tp_create": ([_P, _I, _I, ctypes.c_size_t, ctypes.c_double, _P], _I),
+    "ef_tp_handle": ([_P, _P, _P], _I),
+    "ef_tp_connect": ([_P, _P, _P], _I),
+    "ef_allreduce_sum": ([_P, _P, _P, ctypes.c_int64], _I),
+    "ef_allgather": ([_P, _P, _P, ctypes.c_int64, _P], _I),
+    "ef_tp_status": ([_P, _P], _I),
+    "ef_tp_destroy": ([_P, _P], _I),
 }
 
 

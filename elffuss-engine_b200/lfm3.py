@@ -24,8 +24,9 @@ heads, shortconv.in_proj by channel (the B, C and x rows of the same
 channels, so the depthwise conv stays local), ffn_gate/up by inner rows, the
 LM head by vocabulary rows (column-parallel, no exchange); attn_output,
 shortconv.out_proj and ffn_down by input columns (row-parallel), each
-followed by an all-reduce of the hidden vector (NCCL through
-torch.distributed, captured in the step's graph). The head ends with a local
+followed by an all-reduce of the hidden vector (the library's peer-memory
+collectives of tp.TPComm, or NCCL through torch.distributed; either is
+captured in the step's graph). The head ends with a local
 argmax per rank and an all-gather of the (value, index) pairs, so the token is
 the one a single argmax over the whole vocabulary picks.
 """
@@ -201,9 +202,10 @@ class LFM3Decoder:
     world > 1, `weights` are this rank's shard_weights and the collectives go
     through torch.distributed's default (NCCL) process group."""
 
-    def __init__(self, ops, cfg: LFM3Config, weights: dict, rank: int = 0, world: int = 1, pdl: bool = True):
+    def __init__(self, ops, cfg: LFM3Config, weights: dict, rank: int = 0, world: int = 1, pdl: bool = True,
+                 comm=None):
         self.ops, self.cfg, self.L = ops, cfg, lib()
-        self.rank, self.world, self.pdl = rank, world, pdl
+        self.rank, self.world, self.pdl, self.comm = rank, world, pdl, comm
         E, D = cfg.hidden, cfg.head_dim
         H, KV, F = cfg.heads // world, cfg.kv_heads // world, cfg.ffn // world
         self.Hl, self.KVl, self.Ec, self.Fl, self.Vl = H, KV, E // world, F, cfg.vocab // world
@@ -245,10 +247,14 @@ class LFM3Decoder:
 
     # -- one decode step (token self.tok at position self.pos) -----------------
     def _reduce(self, t: torch.Tensor):
-        """Sum of the ranks' partial row-parallel outputs (in place)."""
+        """Sum of the ranks' partial row-parallel outputs (in place): through
+        the peer-memory collectives (tp.TPComm) when given, else NCCL."""
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(t)
+            if self.comm is not None:
+                self.comm.all_reduce(t)
+            else:
+                import torch.distributed as dist
+                dist.all_reduce(t)
 
     def step(self):
         """Queue one step; with pdl, its kernels are launched as a programmatic-
@@ -303,7 +309,10 @@ class LFM3Decoder:
         else:
             import torch.distributed as dist
             check(L.ef_argmax_partial(h, _p(self.logits), 1, self.Vl, self.rank * self.Vl, _p(self.pair)), h)
-            dist.all_gather_into_tensor(self.pairs, self.pair)
+            if self.comm is not None:
+                self.comm.all_gather(self.pairs, self.pair)
+            else:
+                dist.all_gather_into_tensor(self.pairs, self.pair)
             check(L.ef_argmax_select(h, _p(self.pairs), self.world, 1, _p(self.tok), _p(self.pos),
                                      _p(self.out_tokens), self.out_base, cfg.max_pos), h)
 

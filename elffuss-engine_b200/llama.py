@@ -166,11 +166,12 @@ class LlamaDecoder:
     through torch.distributed's default (NCCL) process group."""
 
     def __init__(self, ops, cfg: LlamaConfig, weights: dict, batch: int = 1, rank: int = 0, world: int = 1,
-                 pdl: bool = True, out_cap: int = 512):
+                 pdl: bool = True, out_cap: int = 512, comm=None):
         if not 1 <= batch <= 16:
             raise ValueError("batch must be 1..16 (the GEMV path)")
         self.ops, self.cfg, self.L = ops, cfg, lib()
         self.B, self.rank, self.world, self.pdl, self.out_cap = batch, rank, world, pdl, out_cap
+        self.comm = comm
         E, D = cfg.hidden, cfg.head_dim
         self.Hl, self.KVl, self.Fl, self.Vl = cfg.heads // world, cfg.kv_heads // world, cfg.ffn // world, \
             cfg.vocab // world
@@ -200,9 +201,14 @@ class LlamaDecoder:
 
     # -- helpers ---------------------------------------------------------------
     def _reduce(self, t):
+        """In-place sum over the ranks: the peer-memory collectives (tp.TPComm)
+        when given and the data fits them, else NCCL."""
         if self.world > 1:
-            import torch.distributed as dist
-            dist.all_reduce(t)
+            if self.comm is not None:
+                self.comm.all_reduce(t)
+            else:
+                import torch.distributed as dist
+                dist.all_reduce(t)
 
     def _head(self, h, rows):
         """logits of `rows` rows of self.nrm -> tokens / positions / out_tokens."""
@@ -214,7 +220,10 @@ class LlamaDecoder:
         else:
             import torch.distributed as dist
             check(L.ef_argmax_partial(h, _p(self.logits), rows, self.Vl, self.rank * self.Vl, _p(self.pairs1)), h)
-            dist.all_gather_into_tensor(self.pairs, self.pairs1.view(-1))
+            if self.comm is not None:
+                self.comm.all_gather(self.pairs, self.pairs1.view(-1))
+            else:
+                dist.all_gather_into_tensor(self.pairs, self.pairs1.view(-1))
             check(L.ef_argmax_select(h, _p(self.pairs), self.world, rows, _p(self.tok), _p(self.pos),
                                      _p(self.out_tokens), self.out_base, self.out_cap), h)
 

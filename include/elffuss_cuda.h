@@ -51,7 +51,8 @@ enum {
     EF_ERR_CUDA = -4,        /* CUDA runtime failure; message in ef_last_error */
     EF_ERR_OOM = -5,         /* device allocation failed */
     EF_ERR_MISMATCH = -6,    /* weight handle does not match the call (js/repack.js:268-286) */
-    EF_ERR_RANGE = -7        /* offset/size outside a buffer, or a slice outside a tensor */
+    EF_ERR_RANGE = -7,       /* offset/size outside a buffer, or a slice outside a tensor */
+    EF_ERR_TIMEOUT = -8      /* a tensor-parallel peer did not arrive within the wait limit */
 };
 
 /* GGUF tensor types (ggml ids, js/gguf.js:48-64). */
@@ -63,6 +64,7 @@ enum {
 typedef struct ef_ctx ef_ctx;        /* device + stream + buffer pool (js/ops.js:134 createContext) */
 typedef struct ef_buf ef_buf;        /* device allocation (a GPUBuffer of the reference) */
 typedef struct ef_weight ef_weight;  /* a weight tensor repacked on the device (creaBufferR) */
+typedef struct ef_tp ef_tp;          /* tensor-parallel exchange buffers of one rank (no reference counterpart) */
 
 /* ---- library / context ---------------------------------------------------- */
 
@@ -309,6 +311,33 @@ EF_API int ef_attention(ef_ctx *ctx, const float *q, const float *kcache, const 
 /* out[i] = gate[i] * sigmoid(gate[i]) * up[i] for the n elements (the
  * prompt-side SwiGLU after two separate GEMMs; js/model.js:651-655). */
 EF_API int ef_swiglu(ef_ctx *ctx, const float *gate, const float *up, int64_t n, float *out);
+
+/* ---- Tensor-parallel decode collectives (one process per GPU, one node).
+ * The reference runs on one device and has none; these replace the
+ * all-reduce after each row-parallel projection and the gather of the
+ * sharded head's argmax pairs (the TP entry points the drop-in boundary
+ * lists: ef_tp_init / ef_allreduce_sum / ef_allgather). Each rank creates
+ * its exchange buffers, publishes their CUDA IPC handle (EF_TP_HANDLE_BYTES
+ * bytes), and connects to the others' handles (nranks * EF_TP_HANDLE_BYTES
+ * bytes in rank order; its own entry is ignored). A call is one kernel per
+ * rank that stores its data into every rank's buffer over NVLink and waits
+ * for the others' (release / acquire flags): every rank must make the same
+ * calls in the same order. A wait longer than timeout_s records the error
+ * and turns every later call into a no-op; ef_tp_status reports it
+ * (EF_ERR_TIMEOUT). Calls are stream-ordered and may be captured in a CUDA
+ * graph. max_bytes bounds one call's data per rank. */
+#define EF_TP_MAX_RANKS 8
+#define EF_TP_HANDLE_BYTES 64
+EF_API int ef_tp_create(ef_ctx *ctx, int rank, int nranks, size_t max_bytes, double timeout_s, ef_tp **out);
+EF_API int ef_tp_handle(ef_ctx *ctx, const ef_tp *tp, void *handle_out);
+EF_API int ef_tp_connect(ef_ctx *ctx, ef_tp *tp, const void *handles);
+/* buf[i] = sum over ranks r = 0, 1, ... (in that order) of rank r's buf[i];
+ * the same bits on every rank. */
+EF_API int ef_allreduce_sum(ef_ctx *ctx, ef_tp *tp, float *buf, int64_t n);
+/* dst[r * bytes ...] = rank r's src (bytes a multiple of 4). */
+EF_API int ef_allgather(ef_ctx *ctx, ef_tp *tp, const void *src, int64_t bytes, void *dst);
+EF_API int ef_tp_status(ef_ctx *ctx, const ef_tp *tp);
+EF_API int ef_tp_destroy(ef_ctx *ctx, ef_tp *tp);
 
 #ifdef __cplusplus
 }

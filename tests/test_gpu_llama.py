@@ -8,7 +8,6 @@ tensor-parallel on 2 (skipped with fewer)."""
 import ctypes
 import datetime
 import os
-import socket
 import sys
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -20,12 +19,13 @@ import numpy as np  # noqa: E402
 import pytest  # noqa: E402
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
-import torch.multiprocessing as mp  # noqa: E402
 
 from elffuss_engine_b200._lib import check, lib  # noqa: E402
 from elffuss_engine_b200.llama import SMALL, LlamaConfig, LlamaDecoder, shard_weights, synth_weights  # noqa: E402
 from oracle.lfm3_ref import rmsnorm, rope_neox  # noqa: E402
 from oracle.llama_ref import LlamaOracle, rope_norm  # noqa: E402
+
+from _spawn import run_ranks  # noqa: E402
 
 pytestmark = pytest.mark.gpu
 MED = dict(hidden=512, layers=2, heads=8, kv_heads=4, head_dim=128, ffn=1024, vocab=1024, max_pos=64)
@@ -137,8 +137,8 @@ def test_swiglu_and_argmax_rows(ops):
     assert outt[0, 2].item() == want[0] and outt[2, 0].item() == want[2] and outt[1].tolist() == [-1] * 4
 
 
-def _run_small(ops, cfg, w, prefix, lasts, n, rank=0, world=1):
-    dec = LlamaDecoder(ops, cfg, w, batch=len(lasts), rank=rank, world=world)
+def _run_small(ops, cfg, w, prefix, lasts, n, rank=0, world=1, comm=None):
+    dec = LlamaDecoder(ops, cfg, w, batch=len(lasts), rank=rank, world=world, comm=comm)
     prompt = torch.tensor(list(prefix) + [int(lasts[0])], dtype=torch.int32)
     got_graph = dec.generate(prompt, lasts, n, use_graph=True)
     got_eager = dec.generate(prompt, lasts, n, use_graph=False)
@@ -158,46 +158,31 @@ def test_small_llama_three_sequences_match_oracle(ops):
     assert got_graph == want
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _rank_main(rank, world, port, prefix, lasts, n, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+def _rank_main(rank, world, init, q, prefix, lasts, n, use_comm):
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
-                            device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", init_method=init, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     try:
         from elffuss_engine_b200.ops import QuantOps
+        from elffuss_engine_b200.tp import TPComm
         cfg = LlamaConfig(**MED)
         w = shard_weights(cfg, synth_weights(cfg, seed=2), rank, world)
-        q.put((rank,) + _run_small(QuantOps(rank), cfg, w, prefix, lasts, n, rank, world))
+        ops = QuantOps(rank)
+        comm = TPComm(ops, rank, world) if use_comm else None
+        q.put((rank,) + _run_small(ops, cfg, w, prefix, lasts, n, rank, world, comm))
     finally:
         torch.cuda.synchronize()
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_tensor_parallel_llama_matches_oracle():
+@pytest.mark.parametrize("use_comm", [False, True], ids=["nccl", "peer"])
+def test_two_gpu_tensor_parallel_llama_matches_oracle(use_comm):
     cfg = LlamaConfig(**MED)
     ids = np.random.default_rng(8).integers(0, cfg.vocab, 14)
     prefix, lasts, n = ids[:12], [int(t) for t in ids[12:]], 12
     orc = LlamaOracle(cfg, _np(synth_weights(cfg, seed=2)))
     want = [orc.generate(prefix, last, n) for last in lasts]
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, prefix, lasts, n, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    got = {}
-    for _ in procs:
-        r, gg, ee = q.get(timeout=300)
-        got[r] = (gg, ee)
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
+    got = run_ranks(_rank_main, 2, prefix, lasts, n, use_comm)
     for r in range(2):
         assert got[r][0] == got[r][1] == want

@@ -1,0 +1,106 @@
+"""The peer-memory collectives (ef_tp_*, tp.TPComm) on 2 GPUs (skipped with
+fewer): the all-reduce is the rank-order sum bit for bit on every rank, the
+all-gather concatenates in rank order, both replay correctly from a CUDA
+graph; a rank that never arrives makes the other's wait run out, which is
+reported as EF_ERR_TIMEOUT with the context still usable."""
+import datetime
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+import __graft_entry__  # noqa: E402  (spawned ranks import this module before conftest runs)
+
+__graft_entry__.package()
+
+import pytest  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+from _spawn import run_ranks  # noqa: E402
+
+pytestmark = [pytest.mark.gpu,
+              pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                                 reason="needs 2 GPUs")]
+
+
+def _rank_main(rank, world, init, q, mode):
+    os.environ.update(NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        from elffuss_engine_b200.ops import QuantOps
+        from elffuss_engine_b200.tp import TPComm
+        ops = QuantOps(rank)
+        if mode == "timeout":
+            comm = TPComm(ops, rank, world, max_bytes=4096, timeout_s=0.2)
+            if rank == 0:                      # rank 1 never makes this call
+                x = torch.ones(16, device="cuda")
+                comm.all_reduce(x)
+                torch.cuda.synchronize()
+                st = comm.status()
+                y = (torch.arange(4, device="cuda") * 2).tolist()      # the context still works
+                q.put((rank, st, y))
+            else:
+                q.put((rank, 0, None))
+            dist.barrier()
+            comm.close()
+            return
+        comm = TPComm(ops, rank, world, max_bytes=1 << 16)
+        g = torch.Generator("cuda").manual_seed(100 + rank)
+        xs = [torch.randn(n, device="cuda", generator=g) for n in (2048, 7, 4096)]
+        inputs = [x.clone() for x in xs]
+        for x in xs:
+            comm.all_reduce(x)
+        pair = torch.tensor([rank * 10 + 1, rank * 10 + 2], dtype=torch.int32, device="cuda")
+        gathered = torch.zeros(2 * world, dtype=torch.int32, device="cuda")
+        comm.all_gather(gathered, pair)
+        # the same calls replayed from a graph
+        gx = torch.zeros(2048, device="cuda")
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=s, capture_error_mode="thread_local"):
+            comm.all_reduce(gx)
+            comm.all_reduce(gx)
+        torch.cuda.synchronize()
+        replays = []
+        for k in range(3):
+            gx.fill_(float(rank + 1 + k))
+            graph.replay()
+            torch.cuda.synchronize()
+            replays.append(gx[:4].tolist())
+        del graph
+        torch.cuda.synchronize()
+        q.put((rank, comm.status(), [i.cpu() for i in inputs], [x.cpu() for x in xs], gathered.cpu().tolist(),
+               replays))
+        dist.barrier()
+        comm.close()
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(mode):
+    return run_ranks(_rank_main, 2, mode, timeout=180)
+
+
+def test_allreduce_allgather_exact_and_graph_replay():
+    got = _run("exact")
+    for r in range(2):
+        st, inputs, outs, gathered, replays = got[r]
+        assert st == 0
+        for j in range(3):
+            want = got[0][1][j] + got[1][1][j]            # rank order: rank 0 + rank 1
+            assert torch.equal(outs[j], want)
+        assert gathered == [1, 2, 11, 12]
+        for k in range(3):
+            # two all-reduces of (1 + k) and (2 + k): (3 + 2k) * 2
+            assert replays[k] == [float((3 + 2 * k) * 2)] * 4
+    assert torch.equal(got[0][2][0], got[1][2][0])
+
+
+def test_missing_rank_times_out_with_status():
+    got = _run("timeout")
+    st, y = got[0]
+    assert st == -8                      # EF_ERR_TIMEOUT
+    assert y == [0, 2, 4, 6]

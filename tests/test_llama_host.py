@@ -3,7 +3,6 @@ quantizers against the CPU dequant, the config's byte counts, the shard rules
 against slices of the whole tensors and a 2-rank gloo run of the CPU forward
 on the shards against the unsharded forward."""
 import os
-import socket
 import sys
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -15,12 +14,13 @@ import numpy as np  # noqa: E402
 import pytest  # noqa: E402
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
-import torch.multiprocessing as mp  # noqa: E402
 
 import oracle  # noqa: E402
 from elffuss_engine_b200.llama import LlamaConfig, shard_weights, synth_weights  # noqa: E402
 from elffuss_engine_b200.quantize import quantize  # noqa: E402
 from oracle.llama_ref import LlamaOracle, rope_norm  # noqa: E402
+
+from _spawn import run_ranks  # noqa: E402
 
 MED = dict(hidden=512, layers=2, heads=8, kv_heads=4, head_dim=128, ffn=1024, vocab=1024, max_pos=64)
 
@@ -94,15 +94,8 @@ def _np(w):
     return {k: ((v[0].numpy(), v[1], v[2], v[3]) if isinstance(v, tuple) else v.numpy()) for k, v in w.items()}
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _rank_main(rank, world, port, prefix, last, n, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+def _rank_main(rank, world, init, q, prefix, last, n):
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
     try:
         cfg = LlamaConfig(**MED)
         w = shard_weights(cfg, synth_weights(cfg, seed=2), rank, world)
@@ -127,14 +120,5 @@ def test_two_rank_forward_matches_unsharded():
     ids = np.random.default_rng(7).integers(0, cfg.vocab, 10)
     prefix, last, n = ids[:-1], int(ids[-1]), 6
     want = LlamaOracle(cfg, _np(synth_weights(cfg, seed=2))).generate(prefix, last, n)
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, prefix, last, n, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    got = dict(q.get(timeout=120) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
+    got = {r: v[0] for r, v in run_ranks(_rank_main, 2, prefix, last, n).items()}
     assert got[0] == want and got[1] == want

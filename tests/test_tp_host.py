@@ -2,7 +2,6 @@
 (lfm3.shard_weights) against slices of the whole tensors, and a 2-rank gloo
 run of the CPU forward on the shards against the unsharded forward."""
 import os
-import socket
 import sys
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
@@ -14,10 +13,11 @@ import numpy as np  # noqa: E402
 import pytest  # noqa: E402
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
-import torch.multiprocessing as mp  # noqa: E402
 
 from elffuss_engine_b200.lfm3 import SMALL, LFM3Config, shard_weights, synth_weights  # noqa: E402
 from oracle.lfm3_ref import LFM3Oracle, dequant_q8_0  # noqa: E402
+
+from _spawn import run_ranks  # noqa: E402
 
 MEDIUM = dict(hidden=512, layers=3, attn_layers=(1,), heads=8, kv_heads=8, head_dim=64, ffn=1024, vocab=2048,
               window=8, max_pos=64)
@@ -69,15 +69,8 @@ def test_shard_rejects_a_split_that_does_not_divide():
         shard_weights(cfg, synth_weights(cfg, seed=1), 0, 4)
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _rank_main(rank, world, port, prompt, n, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+def _rank_main(rank, world, init, q, prompt, n):
+    dist.init_process_group("gloo", init_method=init, rank=rank, world_size=world)
     try:
         cfg = LFM3Config(**SMALL)
         w = shard_weights(cfg, synth_weights(cfg, seed=1), rank, world)
@@ -103,14 +96,5 @@ def test_two_rank_forward_matches_unsharded():
     prompt = np.random.default_rng(5).integers(0, cfg.vocab, 12)
     n = 10
     want = LFM3Oracle(cfg, _np(synth_weights(cfg, seed=1))).generate(prompt, n)
-    ctx = mp.get_context("spawn")
-    q = ctx.Queue()
-    port = _free_port()
-    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, prompt, n, q)) for r in range(2)]
-    for p in procs:
-        p.start()
-    got = dict(q.get(timeout=120) for _ in procs)
-    for p in procs:
-        p.join(timeout=60)
-        assert p.exitcode == 0
+    got = {r: v[0] for r, v in run_ranks(_rank_main, 2, prompt, n).items()}
     assert got[0] == want and got[1] == want
