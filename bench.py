@@ -236,7 +236,7 @@ _COMM = {}
 def tp_comm(ops, args, world, rank):
     """The decoders' collectives for world > 1: the library's peer-memory
     kernels (tp.TPComm, default) or NCCL (--tp-comm nccl)."""
-    if world == 1 or args.tp_comm != "peer":
+    if world == 1 or args.tp_comm == "nccl":
         return None
     if "c" not in _COMM:
         from elffuss_engine_b200.tp import TPComm
@@ -255,7 +255,8 @@ def bench_decode(ops, args, world, rank, barrier, max_over_ranks):
     w = synth_weights(cfg, seed=0, device="cuda")
     if world > 1:
         w = shard_weights(cfg, w, rank, world)
-    dec = LFM3Decoder(ops, cfg, w, rank, world, comm=tp_comm(ops, args, world, rank))
+    dec = LFM3Decoder(ops, cfg, w, rank, world, comm=tp_comm(ops, args, world, rank),
+                      fused=world > 1 and args.tp_comm == "peer")
     del w
     torch.cuda.empty_cache()
     prompt = torch.randint(0, cfg.vocab, (DECODE_PROMPT,), generator=torch.Generator().manual_seed(0),
@@ -329,7 +330,8 @@ def bench_llama(ops, args, world, rank, barrier, max_over_ranks):
            "parallelism": f"tp{world} ({args.tp_comm} collectives)" if world > 1 else "single GPU",
            "weight_bytes_per_step_per_gpu": cfg.step_weight_bytes() // world}
     for B in (1, 16):
-        dec = LlamaDecoder(ops, cfg, w, batch=B, rank=rank, world=world, comm=tp_comm(ops, args, world, rank))
+        dec = LlamaDecoder(ops, cfg, w, batch=B, rank=rank, world=world, comm=tp_comm(ops, args, world, rank),
+                           fused=world > 1 and args.tp_comm == "peer")
         lasts = [int(prompt[-1])] + [int(t) for t in ids[LLAMA_CONTEXT:LLAMA_CONTEXT + B - 1]]
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         barrier()
@@ -637,8 +639,9 @@ def main():
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-2 GEMM measurement")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3/4 decode measurements")
-    ap.add_argument("--tp-comm", default="peer", choices=["peer", "nccl"],
-                    help="tensor-parallel decode collectives: the library's peer-memory kernels or NCCL")
+    ap.add_argument("--tp-comm", default="peer", choices=["peer", "peer-separate", "nccl"],
+                    help="tensor-parallel decode collectives: the library's peer-memory kernels with the "
+                         "row-parallel GEMV and its all-reduce fused (peer) or as separate kernels, or NCCL")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ncu-step", action="store_true",
                     help="profiling mode for ncu: eager warm-up steps plus one eager step, no timing")

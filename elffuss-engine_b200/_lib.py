@@ -90,6 +90,7 @@ _SIGS = {
     "ef_allreduce_sum": ([_P, _P, _P, ctypes.c_int64], _I),
     "ef_allgather": ([_P, _P, _P, ctypes.c_int64, _P], _I),
     "ef_tp_status": ([_P, _P], _I),
+    "ef_gemv_allreduce_norm": ([_P, _P, _P, _P, _I, _P, _P, _P, ctypes.c_float, _P], _I),
     "ef_tp_destroy": ([_P, _P], _I),
 }
 

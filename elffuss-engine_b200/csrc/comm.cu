@@ -20,6 +20,16 @@
 // same CTA on any other rank, so it never overwrites words still being read.
 // A wait that runs out sets the buffer's error word, skips the read and
 // returns; every later call returns at once, and the host reads the status.
+//
+// Fused form (ef_gemv_allreduce_norm): the row-parallel GEMV itself stores its
+// output rows into slot [parity][rank] of a second data region of every rank
+// and each of its CTAs adds 1 to counter [parity][rank] of every rank
+// (gemv.cu, GemvPush); tp_norm_kernel waits until every rank's counter has
+// reached the GEMV's CTA count, sums the slots in rank order and applies the
+// post-norm + residual + next norm of the decoder. Its last CTA clears the
+// parity's counters and advances the call counter that gives the parity. A
+// rank can be at most one call ahead of another here too, so it only ever
+// writes the other parity's slots and counters.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
@@ -34,7 +44,9 @@ struct ef_tp {
     int rank = 0, nranks = 1, device = 0;
     size_t slot_bytes = 0;           // per rank per parity
     size_t data_bytes = 0;           // 2 * nranks * slot_bytes
-    // [2][nranks][slot_bytes] data | flags u32 [TP_CTAS][nranks] | epoch u32 [TP_CTAS] | error u32
+    // [2][nranks][slot_bytes] data (collectives) | [2][nranks][slot_bytes] data (fused GEMV) | control:
+    // flags u32 [TP_CTAS][nranks] | epoch u32 [TP_CTAS] | error u32 | counters u32 [2][nranks] |
+    // fused call counter u32 | CTAs done u32
     uint8_t *buf = nullptr;
     uint8_t *peer[EF_TP_MAX_RANKS] = {};
     bool opened[EF_TP_MAX_RANKS] = {};
@@ -46,8 +58,23 @@ namespace ef {
 struct TpArgs {
     uint8_t *peer[EF_TP_MAX_RANKS];
     int rank, nranks;
-    int64_t slot_bytes, data_bytes, timeout_ns;
+    int64_t slot_bytes, data_bytes, timeout_ns;   // the control block is at 2 * data_bytes
 };
+
+// control block words of a rank's buffer
+struct TpCtl {
+    uint32_t *flags, *epoch, *error, *ctr, *fepoch, *fdone;
+};
+__host__ __device__ inline TpCtl tp_ctl(uint8_t *buf, int64_t data_bytes, int nranks) {
+    TpCtl c;
+    c.flags = reinterpret_cast<uint32_t *>(buf + 2 * data_bytes);
+    c.epoch = c.flags + TP_CTAS * nranks;
+    c.error = c.epoch + TP_CTAS;
+    c.ctr = c.error + 1;
+    c.fepoch = c.ctr + 2 * nranks;
+    c.fdone = c.fepoch + 1;
+    return c;
+}
 
 __device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -73,8 +100,8 @@ __global__ void __launch_bounds__(256) tp_kernel(const TpArgs a, const uint32_t 
     __shared__ uint32_t ep, bad;
     const int cb = blockIdx.x;
     uint8_t *mine = a.peer[a.rank];
-    uint32_t *flags = reinterpret_cast<uint32_t *>(mine + a.data_bytes);          // [TP_CTAS][nranks]
-    uint32_t *epoch = flags + TP_CTAS * a.nranks, *error = epoch + TP_CTAS;
+    const TpCtl ctl = tp_ctl(mine, a.data_bytes, a.nranks);
+    uint32_t *flags = ctl.flags, *epoch = ctl.epoch, *error = ctl.error;
     if (threadIdx.x == 0) {
         bad = *(volatile uint32_t *)error;
         ep = *(volatile uint32_t *)(epoch + cb) + 1;
@@ -102,7 +129,7 @@ __global__ void __launch_bounds__(256) tp_kernel(const TpArgs a, const uint32_t 
     // and a release is cumulative over what happens before it
     __syncthreads();
     if (threadIdx.x < a.nranks) {
-        uint32_t *f = reinterpret_cast<uint32_t *>(a.peer[threadIdx.x] + a.data_bytes) + cb * a.nranks + a.rank;
+        uint32_t *f = tp_ctl(a.peer[threadIdx.x], a.data_bytes, a.nranks).flags + cb * a.nranks + a.rank;
         st_release_sys(f, ep);
     }
     // wait for every rank's part of this call (bounded)
@@ -135,6 +162,111 @@ __global__ void __launch_bounds__(256) tp_kernel(const TpArgs a, const uint32_t 
     }
     __syncthreads();
     if (threadIdx.x == 0) *(volatile uint32_t *)(epoch + cb) = ep;
+}
+
+// Consumer of the fused row-parallel GEMV: row blockIdx.x of o = sum over
+// ranks (in order) of the slots; then x += rmsnorm(o) * w_post (or += o without
+// w_post) and nrm = rmsnorm(x) * w_next, as norm_add_norm_kernel.
+template <int V>
+__global__ void __launch_bounds__(256) tp_norm_kernel(const TpArgs a, uint32_t expected,
+                                                      const float *__restrict__ w_post, float *__restrict__ x,
+                                                      const float *__restrict__ w_next, int n, float eps,
+                                                      float *__restrict__ nrm) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ float red[32];
+    __shared__ uint32_t par, ep, bad;
+    uint8_t *mine = a.peer[a.rank];
+    const TpCtl ctl = tp_ctl(mine, a.data_bytes, a.nranks);
+    if (threadIdx.x == 0) {
+        bad = *(volatile uint32_t *)ctl.error;
+        ep = *(volatile uint32_t *)ctl.fepoch;
+        par = ep & 1;
+    }
+    __syncthreads();
+    if (bad) return;
+    if (threadIdx.x < a.nranks) {
+        const uint32_t *c = ctl.ctr + par * a.nranks + threadIdx.x;
+        const uint64_t t0 = global_ns();
+        while (ld_acquire_sys(c) < expected) {
+            if ((int64_t)(global_ns() - t0) > a.timeout_ns) {
+                atomicExch(ctl.error, 1u + threadIdx.x);
+                bad = 1;
+                break;
+            }
+            __nanosleep(20);
+        }
+    }
+    __syncthreads();
+    if (bad) return;
+    const int64_t row = (int64_t)blockIdx.x * (n / 4);
+    const uint8_t *slots = mine + a.data_bytes + (int64_t)par * a.nranks * a.slot_bytes;
+    float4 *x4 = reinterpret_cast<float4 *>(x) + row;
+    float4 *n4 = reinterpret_cast<float4 *>(nrm) + row;
+    const float4 *wp = reinterpret_cast<const float4 *>(w_post), *wn = reinterpret_cast<const float4 *>(w_next);
+    float4 ov[V], xv[V];
+#pragma unroll
+    for (int j = 0; j < V; j++) {
+        const int i = threadIdx.x + blockDim.x * j;
+        float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int r = 0; r < a.nranks; r++) {
+            const float4 v = reinterpret_cast<const float4 *>(slots + r * a.slot_bytes)[row + i];
+            s.x += v.x;
+            s.y += v.y;
+            s.z += v.z;
+            s.w += v.w;
+        }
+        ov[j] = s;
+        xv[j] = x4[i];
+    }
+    float s1 = 1.f;
+    if (w_post) {
+        float ss = 0.f;
+#pragma unroll
+        for (int j = 0; j < V; j++) ss += ov[j].x * ov[j].x + ov[j].y * ov[j].y + ov[j].z * ov[j].z + ov[j].w * ov[j].w;
+        s1 = rsqrtf(block_sum(ss, red) / (float)n + eps);
+    }
+    float ss2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < V; j++) {
+        const int i = threadIdx.x + blockDim.x * j;
+        const float4 w4 = w_post ? wp[i] : make_float4(1.f, 1.f, 1.f, 1.f);
+        xv[j].x += ov[j].x * s1 * w4.x;
+        xv[j].y += ov[j].y * s1 * w4.y;
+        xv[j].z += ov[j].z * s1 * w4.z;
+        xv[j].w += ov[j].w * s1 * w4.w;
+        ss2 += xv[j].x * xv[j].x + xv[j].y * xv[j].y + xv[j].z * xv[j].z + xv[j].w * xv[j].w;
+        x4[i] = xv[j];
+    }
+    const float s2 = rsqrtf(block_sum(ss2, red) / (float)n + eps);
+#pragma unroll
+    for (int j = 0; j < V; j++) {
+        const int i = threadIdx.x + blockDim.x * j;
+        const float4 w4 = wn[i];
+        n4[i] = make_float4(xv[j].x * s2 * w4.x, xv[j].y * s2 * w4.y, xv[j].z * s2 * w4.z, xv[j].w * s2 * w4.w);
+    }
+    // the last CTA clears this parity's counters and advances the call counter
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(ctl.fdone, 1u) == gridDim.x - 1) {
+            for (int r = 0; r < a.nranks; r++) ctl.ctr[par * a.nranks + r] = 0;
+            *ctl.fdone = 0;
+            __threadfence();
+            *(volatile uint32_t *)ctl.fepoch = ep + 1;
+        }
+    }
+}
+
+static TpArgs tp_args(ef_tp *tp) {
+    TpArgs a = {};
+    for (int r = 0; r < tp->nranks; r++) a.peer[r] = tp->peer[r];
+    a.rank = tp->rank;
+    a.nranks = tp->nranks;
+    a.slot_bytes = (int64_t)tp->slot_bytes;
+    a.data_bytes = (int64_t)tp->data_bytes;
+    a.timeout_ns = tp->timeout_ns;
+    return a;
 }
 
 static int tp_launch(ef_ctx *ctx, ef_tp *tp, bool sum, const void *src, int64_t words, void *dst) {
@@ -173,7 +305,7 @@ int ef_tp_create(ef_ctx *ctx, int rank, int nranks, size_t max_bytes, double tim
     tp->slot_bytes = (max_bytes + 255) / 256 * 256;
     tp->data_bytes = 2 * (size_t)nranks * tp->slot_bytes;
     tp->timeout_ns = (int64_t)(timeout_s * 1e9);
-    const size_t total = tp->data_bytes + TP_CTRL_BYTES;
+    const size_t total = 2 * tp->data_bytes + TP_CTRL_BYTES;
     int rc = check_cuda(ctx, cudaMalloc(&tp->buf, total), "tp buffer alloc");
     if (!rc) rc = check_cuda(ctx, cudaMemset(tp->buf, 0, total), "tp buffer clear");
     if (rc) {
@@ -228,11 +360,51 @@ int ef_allgather(ef_ctx *ctx, ef_tp *tp, const void *src, int64_t bytes, void *d
     return tp_launch(ctx, tp, false, src, bytes / 4, dst);
 }
 
+int ef_gemv_allreduce_norm(ef_ctx *ctx, ef_tp *tp, const ef_weight *w, const float *x, int M, const float *w_post,
+                           float *x_resid, const float *w_next, float eps, float *nrm) {
+    if (!ctx || !tp || !w || !x || !x_resid || !w_next || !nrm || M < 1 || M > 16)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "gemv_allreduce_norm: bad arguments") : EF_ERR_INVALID;
+    for (int r = 0; r < tp->nranks; r++)
+        if (!tp->peer[r]) return set_err(ctx, EF_ERR_INVALID, "tp: rank %d is not connected", r);
+    if ((size_t)M * w->rows * 4 > tp->slot_bytes)
+        return set_err(ctx, EF_ERR_RANGE, "gemv_allreduce_norm: %d x %lld floats exceed the %zu-byte slot", M,
+                       (long long)w->rows, tp->slot_bytes);
+    int th = 0;
+    const int v = norm_v((int)w->rows, th);
+    if (!v || w->rows > 8192)
+        return set_err(ctx, EF_ERR_SHAPE, "gemv_allreduce_norm: %lld rows (a multiple of 128 up to 8192)",
+                       (long long)w->rows);
+    const TpArgs a = tp_args(tp);
+    GemvPush push;
+    push.n = tp->nranks;
+    push.rank = tp->rank;
+    push.slot_bytes = (int64_t)tp->slot_bytes;
+    for (int r = 0; r < tp->nranks; r++) {
+        push.data[r] = tp->peer[r] + tp->data_bytes;
+        push.ctr[r] = tp_ctl(tp->peer[r], (int64_t)tp->data_bytes, tp->nranks).ctr;
+    }
+    push.epoch = tp_ctl(tp->buf, (int64_t)tp->data_bytes, tp->nranks).fepoch;
+    int64_t ctas = 0;
+    float *ys[1] = {nrm};    // (not written: the output goes to the ranks' slots)
+    if (int rc = launch_gemv(ctx, &w, 1, nullptr, x, M, ys, &push, &ctas)) return rc;
+    const uint32_t expected = (uint32_t)ctas;
+    switch (v) {
+    case 1: return launch_on(ctx, tp_norm_kernel<1>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
+                             (int)w->rows, eps, nrm);
+    case 2: return launch_on(ctx, tp_norm_kernel<2>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
+                             (int)w->rows, eps, nrm);
+    case 4: return launch_on(ctx, tp_norm_kernel<4>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
+                             (int)w->rows, eps, nrm);
+    default: return launch_on(ctx, tp_norm_kernel<8>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid,
+                              w_next, (int)w->rows, eps, nrm);
+    }
+}
+
 int ef_tp_status(ef_ctx *ctx, const ef_tp *tp) {
     if (!ctx || !tp) return ctx ? set_err(ctx, EF_ERR_INVALID, "tp_status: bad arguments") : EF_ERR_INVALID;
     uint32_t err = 0;
-    const size_t at = tp->data_bytes + 4 * ((size_t)TP_CTAS * tp->nranks + TP_CTAS);
-    if (int rc = check_cuda(ctx, cudaMemcpy(&err, tp->buf + at, 4, cudaMemcpyDeviceToHost), "tp status read"))
+    const TpCtl c = tp_ctl(tp->buf, (int64_t)tp->data_bytes, tp->nranks);
+    if (int rc = check_cuda(ctx, cudaMemcpy(&err, c.error, 4, cudaMemcpyDeviceToHost), "tp status read"))
         return rc;
     if (err) return set_err(ctx, EF_ERR_TIMEOUT, "tp: rank %d did not arrive in time", (int)err - 1);
     return EF_OK;

@@ -39,6 +39,22 @@ namespace ef {
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+// sum over the CTA (blockDim.x a multiple of 32, <= 1024); `red` >= 32 floats
+__device__ __forceinline__ float block_sum(float v, float *red) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[warp] = v;
+    __syncthreads();
+    float s = lane < nw ? red[lane] : 0.f;
+    return warp_sum(s);
+}
+
 // 16-byte asynchronous global -> shared copy (L2 only), its group commit and wait.
 __device__ __forceinline__ void cp_async16(void *dst, const void *src) {
     const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);

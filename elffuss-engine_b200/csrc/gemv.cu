@@ -87,6 +87,8 @@ struct GemvArgs {
     const uint8_t *xf;        // activation data from gemv_xprep (3..16 tokens)
     const float *x;           // f32 activations [M][K] (1..2 tokens: staged by each CTA)
     int64_t K;
+    GemvPush push;            // tensor-parallel row-parallel output (push.n = 0: write y)
+    int64_t ctas;             // (host) CTAs of the launch
 };
 
 // ---------------------------------------------------------------- traits ---
@@ -1068,6 +1070,18 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) gemv_kernel(const GemvA
     const int M = a.M;
     const int64_t rows = a.rows[m];
     float *y = a.y[m];
+    // output element [tok][r]: y, or every rank's exchange slot (tensor parallel)
+    const int npush = a.push.n;
+    const int64_t slot_off = npush ? ((int64_t)((*(volatile const uint32_t *)a.push.epoch) & 1) * npush +
+                                      a.push.rank) * a.push.slot_bytes : 0;
+    auto put = [&](int tok, int64_t r, float v) {
+        const int64_t idx = (int64_t)tok * rows + r;
+        if (!npush) {
+            y[idx] = v;
+        } else {
+            for (int p = 0; p < npush; p++) reinterpret_cast<float *>(a.push.data[p] + slot_off)[idx] = v;
+        }
+    };
     if (kh == 0 && active) {
         reduce_cols<TQ, NT>(acc);
         if (SWIGLU) reduce_cols<TQ, NT>(acc2);
@@ -1076,34 +1090,44 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) gemv_kernel(const GemvA
         if (kh == 0 && active)
             for_owned<TQ, NT>(lane, [&](int nt, int i, int row, int tok) {
                 const int64_t r = rg * 16 + row;
-                if (tok < M && r < rows) y[(int64_t)tok * rows + r] = out_value<SWIGLU>(acc[nt][i], acc2[nt][i]);
+                if (tok < M && r < rows) put(tok, r, out_value<SWIGLU>(acc[nt][i], acc2[nt][i]));
             });
-        return;
+    } else {
+        // ---- k-slices of this rowblock: one cluster, added in rank order ----
+        float *mine = red + wr * NMAT * 16 * 16;
+        if (kh == 0 && active)
+            for_owned<TQ, NT>(lane, [&](int nt, int i, int row, int tok) {
+                if (tok < M) {
+                    mine[tok * 16 + row] = acc[nt][i];
+                    if (SWIGLU) mine[256 + tok * 16 + row] = acc2[nt][i];
+                }
+            });
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        if (kh == 0 && active && wr % ks == ksi) {   // rowgroup wr is finished by rank wr % ks
+            for (int i = lane; i < 16 * M; i += 32) {
+                float s1 = 0.f, s2 = 0.f;
+                for (int rk = 0; rk < ks; rk++) {
+                    const float *src = cluster.map_shared_rank(mine, rk);
+                    s1 += src[i];
+                    if (SWIGLU) s2 += src[256 + i];
+                }
+                const int64_t r = rg * 16 + (i & 15);
+                if (r < rows) put(i >> 4, r, out_value<SWIGLU>(s1, s2));
+            }
+        }
+        cluster.sync();              // keep this CTA's shared memory alive until all ranks have read it
     }
-    // ---- k-slices of this rowblock: one cluster, added in rank order ----
-    float *mine = red + wr * NMAT * 16 * 16;
-    if (kh == 0 && active)
-        for_owned<TQ, NT>(lane, [&](int nt, int i, int row, int tok) {
-            if (tok < M) {
-                mine[tok * 16 + row] = acc[nt][i];
-                if (SWIGLU) mine[256 + tok * 16 + row] = acc2[nt][i];
-            }
-        });
-    cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    if (kh == 0 && active && wr % ks == ksi) {   // rowgroup wr is finished by rank wr % ks
-        for (int i = lane; i < 16 * M; i += 32) {
-            float s1 = 0.f, s2 = 0.f;
-            for (int rk = 0; rk < ks; rk++) {
-                const float *src = cluster.map_shared_rank(mine, rk);
-                s1 += src[i];
-                if (SWIGLU) s2 += src[256 + i];
-            }
-            const int64_t r = rg * 16 + (i & 15);
-            if (r < rows) y[(int64_t)(i >> 4) * rows + r] = out_value<SWIGLU>(s1, s2);
+    if (npush) {
+        // this CTA's stores, then one count per rank (the barrier orders every
+        // thread's stores before the release, which is cumulative)
+        __syncthreads();
+        if (threadIdx.x < npush) {
+            const int parity = (int)((*(volatile const uint32_t *)a.push.epoch) & 1);
+            uint32_t *c = a.push.ctr[threadIdx.x] + parity * npush + a.push.rank;
+            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(c) : "memory");
         }
     }
-    cluster.sync();                  // keep this CTA's shared memory alive until all ranks have read it
 }
 
 // ------------------------------------------------------------------ host ---
@@ -1201,6 +1225,7 @@ static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int64_t rowblocks, bool fused
     a.xs_bytes = p.xs_bytes;
     a.xs_half = p.xs_half;
     const int64_t ctas = p.ctas;
+    a.ctas = ctas;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((unsigned)ctas, 1, 1);
     cfg.blockDim = dim3(threads, 1, 1);
@@ -1296,8 +1321,9 @@ static int launch_sw(ef_ctx *ctx, GemvArgs &a, bool sw, const ef_weight *const *
 }
 
 int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight *w_up, const float *x, int M,
-                float *const *ys) {
+                float *const *ys, const GemvPush *push, int64_t *ctas_out) {
     GemvArgs a = {};
+    if (push) a.push = *push;
     const ef_weight *w0 = ws[0];
     a.nmat = n;
     for (int i = 0; i < n; i++) {
@@ -1310,14 +1336,17 @@ int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight 
     a.M = M;
     a.nchunks = w0->nchunks;
     const bool sw = w_up != nullptr;
+    int rc;
     switch (w0->type) {
-    case EF_Q8_0: return launch_sw<EF_Q8_0>(ctx, a, sw, ws, n, x);
-    case EF_Q4_K: return launch_sw<EF_Q4_K>(ctx, a, sw, ws, n, x);
-    case EF_Q6_K: return launch_sw<EF_Q6_K>(ctx, a, sw, ws, n, x);
-    case EF_IQ2_XXS: return launch_sw<EF_IQ2_XXS>(ctx, a, sw, ws, n, x);
-    case EF_IQ1_S: return launch_sw<EF_IQ1_S>(ctx, a, sw, ws, n, x);
+    case EF_Q8_0: rc = launch_sw<EF_Q8_0>(ctx, a, sw, ws, n, x); break;
+    case EF_Q4_K: rc = launch_sw<EF_Q4_K>(ctx, a, sw, ws, n, x); break;
+    case EF_Q6_K: rc = launch_sw<EF_Q6_K>(ctx, a, sw, ws, n, x); break;
+    case EF_IQ2_XXS: rc = launch_sw<EF_IQ2_XXS>(ctx, a, sw, ws, n, x); break;
+    case EF_IQ1_S: rc = launch_sw<EF_IQ1_S>(ctx, a, sw, ws, n, x); break;
     default: return set_err(ctx, EF_ERR_TYPE, "gemv: unsupported type %d", w0->type);
     }
+    if (ctas_out) *ctas_out = a.ctas;
+    return rc;
 }
 
 

@@ -79,7 +79,29 @@ int launch_unpack(ef_ctx *ctx, const ef_weight *w, uint8_t *dev_gguf);
 int launch_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows, float *out);
 int launch_gather(ef_ctx *ctx, const ef_weight *w, const int *ids, int tokens, float *out);
 
+// model.cu / comm.cu: a row of n floats per CTA of T = min(256, n/4) threads
+// with V float4 each, n = 4 * T * V, V in {1, 2, 4, 8}; 0 when n has no such
+// split (n a multiple of 128 up to 8192).
+inline int norm_v(int n, int &threads) {
+    if (n < 128 || n % 128) return 0;
+    threads = n / 4 < 256 ? n / 4 : 256;
+    if (n % (4 * threads)) return 0;
+    const int v = n / (4 * threads);
+    return v == 1 || v == 2 || v == 4 || v == 8 ? v : 0;
+}
+
 // gemv.cu
+// Row-parallel output of a tensor-parallel GEMV (comm.cu): instead of y, the
+// kernel stores its rows into slot [parity][rank] of every rank's exchange
+// data region (parity = *epoch & 1) and each CTA then adds 1 (release, system
+// scope) to counter [parity][rank] of every rank.
+struct GemvPush {
+    int n = 0, rank = 0;                      // ranks (0 = off), this rank
+    int64_t slot_bytes = 0;
+    uint8_t *data[EF_TP_MAX_RANKS] = {};      // each rank's data region [2][n][slot_bytes]
+    uint32_t *ctr[EF_TP_MAX_RANKS] = {};      // each rank's counters [2][n]
+    const uint32_t *epoch = nullptr;          // this rank's call counter
+};
 struct GemvPlan {
     int64_t ctas;      // rowblocks x kslices
     int kslices;       // CTAs (one cluster) per rowblock, each a contiguous k-slice
@@ -90,7 +112,8 @@ struct GemvPlan {
 };
 GemvPlan gemv_plan(int64_t rowblocks, int64_t nchunks, int xb, bool fused, int ks);
 int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight *w_up,
-                const float *x, int M, float *const *ys);
+                const float *x, int M, float *const *ys, const GemvPush *push = nullptr,
+                int64_t *ctas_out = nullptr);
 
 // gemm.cu
 int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y);

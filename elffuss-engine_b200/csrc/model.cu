@@ -27,21 +27,6 @@
 
 namespace ef {
 
-__device__ __forceinline__ float warp_sum(float v) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    return v;
-}
-// sum over the CTA (blockDim.x a multiple of 32, <= 1024); `red` >= 32 floats
-__device__ __forceinline__ float block_sum(float v, float *red) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    v = warp_sum(v);
-    __syncthreads();
-    if (lane == 0) red[warp] = v;
-    __syncthreads();
-    float s = lane < nw ? red[lane] : 0.f;
-    return warp_sum(s);
-}
 
 // One CTA per row of T = min(256, n/4) threads; each thread keeps V float4 of
 // the row in registers (all loads issued before the first reduction),
@@ -650,15 +635,6 @@ using namespace ef;
 
 extern "C" {
 
-// Row of n: T = min(256, n/4) threads with V float4 each, n = 4 * T * V,
-// V in {1, 2, 4, 8}; 0 when n has no such split (n a multiple of 128 up to 8192).
-static int norm_v(int n, int &threads) {
-    if (n < 128 || n % 128) return 0;
-    threads = n / 4 < 256 ? n / 4 : 256;
-    if (n % (4 * threads)) return 0;
-    const int v = n / (4 * threads);
-    return v == 1 || v == 2 || v == 4 || v == 8 ? v : 0;
-}
 
 int ef_rmsnorm(ef_ctx *ctx, const float *x, const float *w, int rows, int n, float eps, float *y) {
     if (!ctx || !x || !w || !y || rows < 1 || n < 1) return ctx ? set_err(ctx, EF_ERR_INVALID, "rmsnorm: bad arguments") : EF_ERR_INVALID;

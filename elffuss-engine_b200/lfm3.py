@@ -203,9 +203,9 @@ class LFM3Decoder:
     through torch.distributed's default (NCCL) process group."""
 
     def __init__(self, ops, cfg: LFM3Config, weights: dict, rank: int = 0, world: int = 1, pdl: bool = True,
-                 comm=None):
+                 comm=None, fused: bool = True):
         self.ops, self.cfg, self.L = ops, cfg, lib()
-        self.rank, self.world, self.pdl, self.comm = rank, world, pdl, comm
+        self.rank, self.world, self.pdl, self.comm, self.fused = rank, world, pdl, comm, fused
         E, D = cfg.hidden, cfg.head_dim
         H, KV, F = cfg.heads // world, cfg.kv_heads // world, cfg.ffn // world
         self.Hl, self.KVl, self.Ec, self.Fl, self.Vl = H, KV, E // world, F, cfg.vocab // world
@@ -256,6 +256,20 @@ class LFM3Decoder:
                 import torch.distributed as dist
                 dist.all_reduce(t)
 
+    def _rowpar(self, h, w, xin, out, w_post, w_next):
+        """out = w xin (this rank's columns), summed over the ranks; then x +=
+        rmsnorm(out) * w_post and nrm = rmsnorm(x) * w_next. With the
+        peer-memory collectives, one fused call (ef_gemv_allreduce_norm)."""
+        L, eps = self.L, ctypes.c_float(self.cfg.eps)
+        if self.world > 1 and self.comm is not None and self.fused:
+            check(L.ef_gemv_allreduce_norm(h, self.comm.tp, w.h, _p(xin), 1, _p(w_post), _p(self.x), _p(w_next),
+                                           eps, _p(self.nrm)), h)
+            return
+        check(L.ef_gemv(h, w.h, _p(xin), 1, _p(out)), h)
+        self._reduce(out)
+        check(L.ef_norm_add_norm(h, _p(out), _p(w_post), _p(self.x), _p(w_next), 1, self.cfg.hidden, eps,
+                                 _p(self.nrm)), h)
+
     def step(self):
         """Queue one step; with pdl, its kernels are launched as a programmatic-
         dependent-launch chain (each scheduled while the previous one ends)."""
@@ -287,21 +301,16 @@ class LFM3Decoder:
                                               ctypes.c_float(cfg.rope_theta), eps, _p(self.kc[l]), _p(self.vc[l])), h)
                 check(L.ef_attn_decode(h, _p(self.q), _p(self.kc[l]), _p(self.vc[l]), _p(self.g), _p(self.pos),
                                        cfg.max_pos, self.windows[l], H, KV, D, _p(self.att)), h)
-                check(L.ef_gemv(h, W[p + "attn_output"].h, _p(self.att), 1, _p(self.o)), h)
+                out_w, out_x = W[p + "attn_output"], self.att
             else:
                 check(L.ef_gemv(h, W[p + "shortconv.in_proj"].h, _p(self.nrm), 1, _p(self.bcx)), h)
                 check(L.ef_shortconv(h, _p(self.bcx), _p(f[p + "shortconv.conv"]), _p(self.state[l]), 1, self.Ec,
                                      cfg.conv_k, _p(self.conv_y)), h)
-                check(L.ef_gemv(h, W[p + "shortconv.out_proj"].h, _p(self.conv_y), 1, _p(self.o)), h)
-            self._reduce(self.o)
-            check(L.ef_norm_add_norm(h, _p(self.o), _p(f[p + "post_attention_norm"]), _p(self.x),
-                                     _p(f[p + "ffn_norm"]), 1, E, eps, _p(self.nrm)), h)
+                out_w, out_x = W[p + "shortconv.out_proj"], self.conv_y
+            self._rowpar(h, out_w, out_x, self.o, f[p + "post_attention_norm"], f[p + "ffn_norm"])
             check(L.ef_gemv_swiglu(h, W[p + "ffn_gate"].h, W[p + "ffn_up"].h, _p(self.nrm), 1, _p(self.sw)), h)
-            check(L.ef_gemv(h, W[p + "ffn_down"].h, _p(self.sw), 1, _p(self.d)), h)
-            self._reduce(self.d)
             nxt = f[f"blk.{l + 1}.attn_norm"] if l + 1 < cfg.layers else f["output_norm"]
-            check(L.ef_norm_add_norm(h, _p(self.d), _p(f[p + "post_ffw_norm"]), _p(self.x), _p(nxt), 1, E, eps,
-                                     _p(self.nrm)), h)
+            self._rowpar(h, W[p + "ffn_down"], self.sw, self.d, f[p + "post_ffw_norm"], nxt)
         check(L.ef_gemv(h, W["output"].h, _p(self.nrm), 1, _p(self.logits)), h)
         if self.world == 1:
             check(L.ef_argmax_step(h, _p(self.logits), cfg.vocab, _p(self.tok), _p(self.pos), _p(self.out_tokens),

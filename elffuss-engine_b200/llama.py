@@ -166,12 +166,12 @@ class LlamaDecoder:
     through torch.distributed's default (NCCL) process group."""
 
     def __init__(self, ops, cfg: LlamaConfig, weights: dict, batch: int = 1, rank: int = 0, world: int = 1,
-                 pdl: bool = True, out_cap: int = 512, comm=None):
+                 pdl: bool = True, out_cap: int = 512, comm=None, fused: bool = True):
         if not 1 <= batch <= 16:
             raise ValueError("batch must be 1..16 (the GEMV path)")
         self.ops, self.cfg, self.L = ops, cfg, lib()
         self.B, self.rank, self.world, self.pdl, self.out_cap = batch, rank, world, pdl, out_cap
-        self.comm = comm
+        self.comm, self.fused = comm, fused
         E, D = cfg.hidden, cfg.head_dim
         self.Hl, self.KVl, self.Fl, self.Vl = cfg.heads // world, cfg.kv_heads // world, cfg.ffn // world, \
             cfg.vocab // world
@@ -209,6 +209,20 @@ class LlamaDecoder:
             else:
                 import torch.distributed as dist
                 dist.all_reduce(t)
+
+    def _rowpar(self, h, w, xin, out, w_next):
+        """out = w xin for the B rows (this rank's columns), summed over the
+        ranks; then x += out and nrm = rmsnorm(x) * w_next. With the
+        peer-memory collectives, one fused call (ef_gemv_allreduce_norm)."""
+        L, eps = self.L, ctypes.c_float(self.cfg.eps)
+        if self.world > 1 and self.comm is not None and self.fused:
+            check(L.ef_gemv_allreduce_norm(h, self.comm.tp, w.h, _p(xin), self.B, None, _p(self.x), _p(w_next),
+                                           eps, _p(self.nrm)), h)
+            return
+        check(L.ef_gemv(h, w.h, _p(xin), self.B, _p(out)), h)
+        self._reduce(out)
+        check(L.ef_norm_add_norm(h, _p(out), None, _p(self.x), _p(w_next), self.B, self.cfg.hidden, eps,
+                                 _p(self.nrm)), h)
 
     def _head(self, h, rows):
         """logits of `rows` rows of self.nrm -> tokens / positions / out_tokens."""
@@ -252,15 +266,10 @@ class LlamaDecoder:
                                   _p(self.kc[l]), _p(self.vc[l])), h)
             check(L.ef_attention(h, _p(self.q), _p(self.kc[l]), _p(self.vc[l]), None, _p(self.pos), B, 1,
                                  cfg.max_pos, 0, self.Hl, self.KVl, D, _p(self.att)), h)
-            check(L.ef_gemv(h, W[p + "attn_output"].h, _p(self.att), B, _p(self.o)), h)
-            self._reduce(self.o)
-            check(L.ef_norm_add_norm(h, _p(self.o), None, _p(self.x), _p(f[p + "ffn_norm"]), B, E, eps,
-                                     _p(self.nrm)), h)
+            self._rowpar(h, W[p + "attn_output"], self.att, self.o, f[p + "ffn_norm"])
             check(L.ef_gemv_swiglu(h, W[p + "ffn_gate"].h, W[p + "ffn_up"].h, _p(self.nrm), B, _p(self.sw)), h)
-            check(L.ef_gemv(h, W[p + "ffn_down"].h, _p(self.sw), B, _p(self.d)), h)
-            self._reduce(self.d)
             nxt = f[f"blk.{l + 1}.attn_norm"] if l + 1 < cfg.layers else f["output_norm"]
-            check(L.ef_norm_add_norm(h, _p(self.d), None, _p(self.x), _p(nxt), B, E, eps, _p(self.nrm)), h)
+            self._rowpar(h, W[p + "ffn_down"], self.sw, self.d, nxt)
         self._head(h, B)
 
     def capture(self):

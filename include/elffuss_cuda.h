@@ -336,6 +336,17 @@ EF_API int ef_tp_connect(ef_ctx *ctx, ef_tp *tp, const void *handles);
 EF_API int ef_allreduce_sum(ef_ctx *ctx, ef_tp *tp, float *buf, int64_t n);
 /* dst[r * bytes ...] = rank r's src (bytes a multiple of 4). */
 EF_API int ef_allgather(ef_ctx *ctx, ef_tp *tp, const void *src, int64_t bytes, void *dst);
+/* The row-parallel GEMV of a decoder layer with its all-reduce and the norms
+ * after it, fused: y = W x (this rank's columns; M tokens, W's rows = the
+ * hidden size n) is stored by the GEMV kernel straight into every rank's
+ * exchange buffer over NVLink; then o = the sum over ranks (in rank order)
+ * and, per token row, x_resid += rmsnorm(o) * w_post (or += o when w_post is
+ * NULL) and nrm = rmsnorm(x_resid) * w_next -- the same as ef_gemv followed by
+ * ef_allreduce_sum and ef_norm_add_norm, with one launch and one exchange
+ * fewer (js/model.js:635-664 for the norms). n a multiple of 128 up to 8192,
+ * M <= 16, M * n * 4 bytes within max_bytes. */
+EF_API int ef_gemv_allreduce_norm(ef_ctx *ctx, ef_tp *tp, const ef_weight *w, const float *x, int M,
+                                  const float *w_post, float *x_resid, const float *w_next, float eps, float *nrm);
 EF_API int ef_tp_status(ef_ctx *ctx, const ef_tp *tp);
 EF_API int ef_tp_destroy(ef_ctx *ctx, ef_tp *tp);
 

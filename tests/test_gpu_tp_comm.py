@@ -47,6 +47,45 @@ def _rank_main(rank, world, init, q, mode):
             comm.close()
             return
         comm = TPComm(ops, rank, world, max_bytes=1 << 16)
+        if mode == "fused":
+            import ctypes
+            import numpy as np
+            from elffuss_engine_b200 import formats
+            from elffuss_engine_b200._lib import check, lib
+            L, h = lib(), ops.ctx.bind()
+            P = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+            n, k, M = 256, 512, 3                          # this rank's k columns of a 256-row weight
+            raw = formats.quantize_q8_0(np.random.default_rng(10 + rank).standard_normal((n, k)).astype(np.float32)
+                                        * 0.05)
+            w = ops.load_weight("Q8_0", raw, n, k)
+            g = torch.Generator("cuda").manual_seed(7 + rank)
+            x = torch.randn(M, k, device="cuda", generator=g)
+            gen = torch.Generator("cuda").manual_seed(99)     # the same residual and norms on every rank
+            resid0 = torch.randn(M, n, device="cuda", generator=gen)
+            wp = torch.rand(n, device="cuda", generator=gen) + 0.5
+            wn = torch.rand(n, device="cuda", generator=gen) + 0.5
+            out = {}
+            for fused in (True, False):
+                for w_post in (wp, None):
+                    xr = resid0.clone()
+                    nrm = torch.empty(M, n, device="cuda")
+                    if fused:
+                        for _ in range(3):                     # repeated calls: parities and counters cycle
+                            xr.copy_(resid0)
+                            check(L.ef_gemv_allreduce_norm(h, comm.tp, w.h, P(x), M, P(w_post), P(xr), P(wn),
+                                                           ctypes.c_float(1e-5), P(nrm)), h)
+                    else:
+                        o = torch.empty(M, n, device="cuda")
+                        check(L.ef_gemv(h, w.h, P(x), M, P(o)), h)
+                        comm.all_reduce(o)
+                        check(L.ef_norm_add_norm(h, P(o), P(w_post), P(xr), P(wn), M, n, ctypes.c_float(1e-5),
+                                                 P(nrm)), h)
+                    torch.cuda.synchronize()
+                    out[(fused, w_post is not None)] = (xr.cpu(), nrm.cpu())
+            q.put((rank, comm.status(), out))
+            dist.barrier()
+            comm.close()
+            return
         g = torch.Generator("cuda").manual_seed(100 + rank)
         xs = [torch.randn(n, device="cuda", generator=g) for n in (2048, 7, 4096)]
         inputs = [x.clone() for x in xs]
@@ -97,6 +136,18 @@ def test_allreduce_allgather_exact_and_graph_replay():
             # two all-reduces of (1 + k) and (2 + k): (3 + 2k) * 2
             assert replays[k] == [float((3 + 2 * k) * 2)] * 4
     assert torch.equal(got[0][2][0], got[1][2][0])
+
+
+def test_fused_gemv_allreduce_norm_equals_the_separate_calls():
+    got = _run("fused")
+    for r in range(2):
+        st, out = got[r]
+        assert st == 0
+        for post in (True, False):
+            xf, nf = out[(True, post)]
+            xs, ns = out[(False, post)]
+            assert torch.equal(xf, xs) and torch.equal(nf, ns)
+            assert torch.equal(xf, got[0][1][(True, post)][0])      # the same bits on both ranks
 
 
 def test_missing_rank_times_out_with_status():
