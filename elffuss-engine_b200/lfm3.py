@@ -311,7 +311,12 @@ class LFM3Decoder:
             check(L.ef_gemv_swiglu(h, W[p + "ffn_gate"].h, W[p + "ffn_up"].h, _p(self.nrm), 1, _p(self.sw)), h)
             nxt = f[f"blk.{l + 1}.attn_norm"] if l + 1 < cfg.layers else f["output_norm"]
             self._rowpar(h, W[p + "ffn_down"], self.sw, self.d, f[p + "post_ffw_norm"], nxt)
-        check(L.ef_gemv(h, W["output"].h, _p(self.nrm), 1, _p(self.logits)), h)
+        self._head(h, self.nrm)
+
+    def _head(self, h, nrm_row: torch.Tensor):
+        """Logits of the normalised row -> greedy token, position + 1, out_tokens."""
+        L, cfg, W = self.L, self.cfg, self.w
+        check(L.ef_gemv(h, W["output"].h, _p(nrm_row), 1, _p(self.logits)), h)
         if self.world == 1:
             check(L.ef_argmax_step(h, _p(self.logits), cfg.vocab, _p(self.tok), _p(self.pos), _p(self.out_tokens),
                                    self.out_base, cfg.max_pos), h)
@@ -341,7 +346,7 @@ class LFM3Decoder:
         else:
             self.step()
 
-    def prefill(self, prompt: torch.Tensor):
+    def prefill_steps(self, prompt: torch.Tensor):
         """Prompt ids one step each (the token each step predicts is replaced by
         the next prompt id); after the last one, self.tok is the first
         generated token."""
@@ -350,8 +355,70 @@ class LFM3Decoder:
             self.tok.copy_(prompt[i:i + 1])
             self.run_step()
 
-    def generate(self, prompt: torch.Tensor, n: int, use_graph: bool = True) -> list:
-        """Greedy continuation of `prompt` by n tokens."""
+    def prefill(self, prompt: torch.Tensor):
+        """All prompt ids at once, at positions pos .. pos + T - 1: every matrix
+        product through the GEMM path (Q8_0 on tcgen05, f16 activations, the
+        numerics of the GEMV), RoPE / cache / causal attention and the short
+        convolution over the T tokens; then the head on the last row, so
+        self.tok is the first generated token and pos has advanced by T (the
+        reference's prompt forward, js/model.js:1135-1171)."""
+        L, cfg, W, f = self.L, self.cfg, self.w, self.f32
+        E, D, H, KV, Ec, Fl = cfg.hidden, cfg.head_dim, self.Hl, self.KVl, self.Ec, self.Fl
+        T = int(prompt.numel())
+        h = self.ops.ctx.bind()
+        eps = ctypes.c_float(cfg.eps)
+        dev = self.x.device
+        z = lambda *s: torch.empty(*s, device=dev)
+        x, nrm, o = z(T, E), z(T, E), z(T, E)
+        q, k, v, g, att = z(T, H * D), z(T, KV * D), z(T, KV * D), z(T, H), z(T, H * D)
+        bcx, cy, gt, up = z(T, 3 * Ec), z(T, Ec), z(T, Fl), z(T, Fl)
+        ids = prompt.to(dev, torch.int32)
+        gemm = lambda name, xin, out: check(L.ef_gemm(h, W[name].h, _p(xin), 0, T, _p(out), 0), h)
+
+        def reduce(t):
+            if self.world > 1:
+                import torch.distributed as dist
+                if self.comm is not None and self.comm.fits(t):
+                    self.comm.all_reduce(t)
+                else:
+                    dist.all_reduce(t)
+
+        check(L.ef_gather(h, W["token_embd"].h, _p(ids), T, _p(x)), h)
+        check(L.ef_rmsnorm(h, _p(x), _p(f["blk.0.attn_norm"]), T, E, eps, _p(nrm)), h)
+        for l in range(cfg.layers):
+            p = f"blk.{l}."
+            if l in cfg.attn_layers:
+                gemm(p + "attn_q", nrm, q)
+                gemm(p + "attn_k", nrm, k)
+                gemm(p + "attn_v", nrm, v)
+                gemm(p + "attn_gate", nrm, g)
+                check(L.ef_rope_cache(h, _p(q), _p(k), _p(v), _p(f[p + "attn_q_norm"]), _p(f[p + "attn_k_norm"]),
+                                      _p(self.pos), 1, T, cfg.max_pos, H, KV, D, 2, ctypes.c_float(cfg.rope_theta),
+                                      eps, _p(self.kc[l]), _p(self.vc[l])), h)
+                check(L.ef_attention(h, _p(q), _p(self.kc[l]), _p(self.vc[l]), _p(g), _p(self.pos), 1, T,
+                                     cfg.max_pos, self.windows[l], H, KV, D, _p(att)), h)
+                gemm(p + "attn_output", att, o)
+            else:
+                gemm(p + "shortconv.in_proj", nrm, bcx)
+                check(L.ef_shortconv(h, _p(bcx), _p(f[p + "shortconv.conv"]), _p(self.state[l]), T, Ec, cfg.conv_k,
+                                     _p(cy)), h)
+                gemm(p + "shortconv.out_proj", cy, o)
+            reduce(o)
+            check(L.ef_norm_add_norm(h, _p(o), _p(f[p + "post_attention_norm"]), _p(x), _p(f[p + "ffn_norm"]), T, E,
+                                     eps, _p(nrm)), h)
+            gemm(p + "ffn_gate", nrm, gt)
+            gemm(p + "ffn_up", nrm, up)
+            check(L.ef_swiglu(h, _p(gt), _p(up), T * Fl, _p(gt)), h)
+            gemm(p + "ffn_down", gt, o)
+            reduce(o)
+            nxt = f[f"blk.{l + 1}.attn_norm"] if l + 1 < cfg.layers else f["output_norm"]
+            check(L.ef_norm_add_norm(h, _p(o), _p(f[p + "post_ffw_norm"]), _p(x), _p(nxt), T, E, eps, _p(nrm)), h)
+        self.pos.add_(T - 1)                       # the head's step advances it to pos + T
+        self._head(h, nrm[T - 1])
+
+    def generate(self, prompt: torch.Tensor, n: int, use_graph: bool = True, batched_prompt: bool = True) -> list:
+        """Greedy continuation of `prompt` by n tokens (the prompt all at once,
+        or one step per id)."""
         self.reset(out_base=prompt.numel())
         # one eager step sizes the scratch and configures every kernel; then
         # the state is reset and the graph recorded
@@ -359,9 +426,14 @@ class LFM3Decoder:
         self.step()
         torch.cuda.synchronize()
         self.reset(out_base=prompt.numel())
-        if use_graph:
-            self.capture()
-        self.prefill(prompt)
+        if batched_prompt:
+            self.prefill(prompt)
+            if use_graph:
+                self.capture()
+        else:
+            if use_graph:
+                self.capture()
+            self.prefill_steps(prompt)
         for _ in range(n - 1):
             self.run_step()
         torch.cuda.synchronize()

@@ -133,5 +133,7 @@ def test_small_decoder_greedy_tokens_match_oracle(ops):
     dec = LFM3Decoder(ops, cfg, w)
     got_graph = dec.generate(prompt, 32, use_graph=True)
     got_eager = dec.generate(prompt, 32, use_graph=False)
+    got_steps = dec.generate(prompt, 32, use_graph=True, batched_prompt=False)
     assert got_graph == got_eager
     assert got_graph == want
+    assert got_steps == want
