@@ -83,7 +83,7 @@ int ef_ctx_create(int device, ef_ctx **out) {
     c->stream = c->own;
     cudaDeviceGetAttribute(&c->sm_count, cudaDevAttrMultiProcessorCount, device);
     const char *pdl = getenv("EF_PDL");
-    c->pdl = pdl && pdl[0] == '1';
+    c->pdl = !(pdl && pdl[0] == '0');
     *out = c;
     return EF_OK;
 }
@@ -241,6 +241,14 @@ int ef_weight_load_device(ef_ctx *ctx, int type, const void *dev_gguf, int64_t r
     ef_weight *w = nullptr;
     if (int rc = new_weight(ctx, type, rows, k, g, &w)) return rc;
     if (int rc = launch_repack(ctx, type, (const uint8_t *)dev_gguf, rows, k, w)) {
+        cudaFree(w->dev);
+        delete w;
+        return rc;
+    }
+    // Kernels launched with programmatic dependent launch read weights before
+    // they wait for the kernel ahead of them: the repacked tiles must be in
+    // memory before any later launch.
+    if (int rc = check_cuda(ctx, cudaStreamSynchronize(ctx->stream), "weight repack")) {
         cudaFree(w->dev);
         delete w;
         return rc;

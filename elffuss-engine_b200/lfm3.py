@@ -278,7 +278,7 @@ class LFM3Decoder:
         try:
             self._step()
         finally:
-            L.ef_ctx_set_pdl(h, 0)
+            L.ef_ctx_set_pdl(h, 1)   # the context default
 
     def _step(self):
         L, cfg, h = self.L, self.cfg, self.ops.ctx.bind()

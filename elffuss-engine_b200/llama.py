@@ -248,7 +248,7 @@ class LlamaDecoder:
         try:
             self._step(h)
         finally:
-            L.ef_ctx_set_pdl(h, 0)
+            L.ef_ctx_set_pdl(h, 1)   # the context default
 
     def _step(self, h):
         L, cfg, W, f = self.L, self.cfg, self.w, self.f32

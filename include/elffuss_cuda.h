@@ -88,9 +88,10 @@ EF_API int ef_ctx_set_stream(ef_ctx *ctx, void *cuda_stream);
 /* Programmatic dependent launch for this context's kernels (on != 0): each
  * kernel may be scheduled while the one before it on the stream finishes,
  * fetching what does not depend on it (the weights) early, and waits for
- * that kernel's results before reading them. Off by default (and when the
- * environment variable EF_PDL is not "1"): it pays where short kernels
- * follow one another, as in a decode step. No counterpart in the reference. */
+ * that kernel's results before reading them. On by default (the environment
+ * variable EF_PDL=0 turns the default off). Weight loads synchronize the
+ * stream, so weights are complete before any later kernel starts. No
+ * counterpart in the reference. */
 EF_API int ef_ctx_set_pdl(ef_ctx *ctx, int on);
 EF_API void *ef_ctx_stream(const ef_ctx *ctx);
 
