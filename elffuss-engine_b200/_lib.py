@@ -90,6 +90,15 @@ _SIGS = {
     "ef_allreduce_sum": ([_P, _P, _P, ctypes.c_int64], _I),
     "ef_allgather": ([_P, _P, _P, ctypes.c_int64, _P], _I),
     "ef_tp_status": ([_P, _P], _I),
+    "ef_gguf_open": ([ctypes.c_char_p, _P, ctypes.c_char_p, ctypes.c_size_t], _I),
+    "ef_gguf_close": ([_P], _I),
+    "ef_gguf_header": ([_P, _P, _P, _P, _P, _P], _I),
+    "ef_gguf_tensor": ([_P, ctypes.c_int64, _P, _P, _P, _P, _P, _P], _I),
+    "ef_gguf_find_tensor": ([_P, ctypes.c_char_p], ctypes.c_int64),
+    "ef_gguf_tensor_data": ([_P, ctypes.c_int64], _P),
+    "ef_gguf_find_key": ([_P, ctypes.c_char_p], ctypes.c_int64),
+    "ef_gguf_meta": ([_P, ctypes.c_int64, _P, _P, _P, _P, _P], _I),
+    "ef_gguf_load_weight": ([_P, _P, ctypes.c_char_p, _P], _I),
     "ef_gemv_allreduce_norm": ([_P, _P, _P, _P, _I, _P, _P, _P, ctypes.c_float, _P], _I),
     "ef_tp_destroy": ([_P, _P], _I),
 }

@@ -65,6 +65,7 @@ typedef struct ef_ctx ef_ctx;        /* device + stream + buffer pool (js/ops.js
 typedef struct ef_buf ef_buf;        /* device allocation (a GPUBuffer of the reference) */
 typedef struct ef_weight ef_weight;  /* a weight tensor repacked on the device (creaBufferR) */
 typedef struct ef_tp ef_tp;          /* tensor-parallel exchange buffers of one rank (no reference counterpart) */
+typedef struct ef_gguf ef_gguf;      /* an opened GGUF file (js/gguf.js parseGGUF) */
 
 /* ---- library / context ---------------------------------------------------- */
 
@@ -312,6 +313,33 @@ EF_API int ef_attention(ef_ctx *ctx, const float *q, const float *kcache, const 
 /* out[i] = gate[i] * sigmoid(gate[i]) * up[i] for the n elements (the
  * prompt-side SwiGLU after two separate GEMMs; js/model.js:651-655). */
 EF_API int ef_swiglu(ef_ctx *ctx, const float *gate, const float *up, int64_t n, float *out);
+
+/* ---- GGUF files (js/gguf.js parseGGUF :324-438 and the type table :48-76).
+ * ef_gguf_open maps the file and checks its structure as the reference does
+ * (magic, version 2-3, no big-endian files, unique non-empty keys, value
+ * types, general.alignment a uint32 power of two, unique tensor names, <= 4
+ * dimensions, a known non-retired type, ne0 a multiple of the block, each
+ * tensor's offset the padded running sum, data inside the file); on failure
+ * it returns a negative status and, when err is given, a message. Tensors:
+ * index, name, ggml type, dimensions (ne0 = k first; missing ones = 1), file
+ * offset and bytes; ef_gguf_tensor_data points into the mapping. Metadata:
+ * key, value type (GGUF codes 0..12: u8 i8 u16 i16 u32 i32 f32 bool string
+ * array u64 i64 f64), for arrays the element type and count, and a pointer
+ * to the little-endian value (strings: the bytes, count = length; arrays of
+ * strings: not decoded). ef_gguf_load_weight loads a tensor as a weight
+ * (k = ne0, rows = ne1 * ne2 * ne3) through ef_weight_load. */
+EF_API int ef_gguf_open(const char *path, ef_gguf **out, char *err, size_t errlen);
+EF_API int ef_gguf_close(ef_gguf *g);
+EF_API int ef_gguf_header(const ef_gguf *g, uint32_t *version, uint32_t *alignment, uint64_t *data_start,
+                          int64_t *n_tensors, int64_t *n_meta);
+EF_API int ef_gguf_tensor(const ef_gguf *g, int64_t i, const char **name, int *type, int *n_dims, int64_t *dims,
+                          uint64_t *file_offset, uint64_t *bytes);
+EF_API int64_t ef_gguf_find_tensor(const ef_gguf *g, const char *name);
+EF_API const void *ef_gguf_tensor_data(const ef_gguf *g, int64_t i);
+EF_API int64_t ef_gguf_find_key(const ef_gguf *g, const char *key);
+EF_API int ef_gguf_meta(const ef_gguf *g, int64_t i, const char **key, int *type, int *elem_type, uint64_t *count,
+                        const void **value);
+EF_API int ef_gguf_load_weight(ef_ctx *ctx, const ef_gguf *g, const char *name, ef_weight **out);
 
 /* ---- Tensor-parallel decode collectives (one process per GPU, one node).
  * The reference runs on one device and has none; these replace the
