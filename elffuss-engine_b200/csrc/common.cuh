@@ -75,6 +75,7 @@ struct TypeGeo {
 __host__ __device__ inline bool geo_of(int type, TypeGeo &g) {
     switch (type) {
     case EF_Q8_0: g = {32, 34, 128, 2176}; return true;
+    case EF_Q4_0: g = {32, 18, 128, 1152}; return true;
     case EF_Q4_K: g = {256, 144, 256, 2304}; return true;
     case EF_Q6_K: g = {256, 210, 256, 3360}; return true;
     case EF_IQ2_XXS: g = {256, 66, 256, 1056}; return true;
@@ -104,6 +105,9 @@ __host__ __device__ inline int q6_hi2(const uint8_t *blk, int p) {
     const int n = p >> 7, i = (p >> 5) & 3, l = p & 31;
     return (blk[128 + 32 * n + l] >> (2 * i)) & 3;
 }
+
+// Q4_0: bit position, inside a 32-bit tile word, of the word's weight m (0..7).
+__host__ __device__ inline int q40_slot(int m) { return 16 * (m & 1) + 4 * (m >> 1); }
 
 // --------------------------------------------- scatter (GGUF -> tile) -------
 // Write GGUF block `blk` (row r of the rowgroup, block `bic` within the chunk)
@@ -189,6 +193,25 @@ __host__ __device__ inline void scatter_block(int type, const uint8_t *blk, int 
         T[768 + 4 * g + 2 * hs] = blk[0];
         T[768 + 4 * g + 2 * hs + 1] = blk[1];
     } break;
+    case EF_Q4_0: {
+        // lane (g, t=bic) owns block bic of rows g and g+8: part hs holds its 32
+        // nibbles, word j the weights 8j..8j+7 at nibble slots (bits) 0, 16,
+        // 4, 20, 8, 24, 12, 28 -- so (w >> 8u) & 0x000F000F gives weights
+        // 8j+4u, 8j+4u+1 and (w >> 8u+4) & 0x000F000F the next two, each in the
+        // low bits of a 16-bit half; the f16 d goes to 1024 + 4*lane + 2*hs.
+        const int lane = 4 * g + bic;
+        for (int j = 0; j < 4; j++) {
+            uint32_t wd = 0;
+            for (int m = 0; m < 8; m++) {
+                const int i = 8 * j + m;
+                const uint32_t q = i < 16 ? (blk[2 + i] & 15) : (blk[2 + i - 16] >> 4);
+                wd |= q << q40_slot(m);
+            }
+            for (int b = 0; b < 4; b++) T[hs * 512 + lane * 16 + 4 * j + b] = (uint8_t)(wd >> (8 * b));
+        }
+        T[1024 + lane * 4 + hs * 2] = blk[0];
+        T[1024 + lane * 4 + hs * 2 + 1] = blk[1];
+    } break;
     default:
         break;
     }
@@ -249,6 +272,18 @@ __host__ __device__ inline void gather_block(int type, const uint8_t *T, int r, 
         blk[0] = T[768 + 4 * g + 2 * hs];
         blk[1] = T[768 + 4 * g + 2 * hs + 1];
     } break;
+    case EF_Q4_0: {
+        const int lane = 4 * g + bic;
+        uint32_t wds[4];
+        for (int j = 0; j < 4; j++) wds[j] = rd32(T + hs * 512 + lane * 16 + 4 * j);
+        for (int i = 0; i < 16; i++) {
+            const uint32_t lo = (wds[i >> 3] >> q40_slot(i & 7)) & 15;
+            const uint32_t hi = (wds[(i + 16) >> 3] >> q40_slot((i + 16) & 7)) & 15;
+            blk[2 + i] = (uint8_t)(lo | (hi << 4));
+        }
+        blk[0] = T[1024 + lane * 4 + hs * 2];
+        blk[1] = T[1024 + lane * 4 + hs * 2 + 1];
+    } break;
     default:
         break;
     }
@@ -273,6 +308,14 @@ __device__ inline void decode_block(int type, const uint8_t *blk, const int8_t *
     case EF_Q8_0: {
         const float d = h2f(blk[0] | (blk[1] << 8));
         for (int i = 0; i < 32; i++) out[i] = __fmul_rn((float)(int8_t)blk[2 + i], d);
+    } break;
+    case EF_Q4_0: {
+        // kernels.wgsl.js:171-190: low nibble -> weight i, high -> i + 16; (q - 8) * d
+        const float d = h2f(blk[0] | (blk[1] << 8));
+        for (int i = 0; i < 16; i++) {
+            out[i] = __fmul_rn((float)((int)(blk[2 + i] & 15) - 8), d);
+            out[i + 16] = __fmul_rn((float)((int)(blk[2 + i] >> 4) - 8), d);
+        }
     } break;
     case EF_Q4_K: {
         const float d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));

@@ -64,6 +64,7 @@ __device__ const __align__(16) uint16_t g_grid_iq2xxs_f16[EF_GRID_IQ2XXS_ENTRIES
 __device__ const __align__(16) uint16_t g_grid_iq1s_f16[EF_GRID_IQ1S_ENTRIES * 8] = {EF_GRID_IQ1S_F16_INIT};
 
 constexpr uint32_t H2_1152 = 0x64806480u;   // half2(1152, 1152)
+constexpr uint32_t H2_1032 = 0x64086408u;   // half2(1032, 1032)
 constexpr int GV_WARPS = 8;                 // rowgroups (warps) per CTA = one rowblock
 constexpr int MAX_XS_BYTES = 64 * 1024;     // shared memory for activation data
 
@@ -97,6 +98,10 @@ struct GemvArgs {
 template <int TYPE> struct Tr;
 template <> struct Tr<EF_Q8_0> {
     static constexpr int CHUNK = 128, STEPS = 8, TILE = 2176, I8 = 0;
+    __device__ static void inv(int kq, int &t, int &s) { t = kq >> 3; s = kq & 7; }
+};
+template <> struct Tr<EF_Q4_0> {   // the Q8_0 chunk and activation layout
+    static constexpr int CHUNK = 128, STEPS = 8, TILE = 1152, I8 = 0;
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 3; s = kq & 7; }
 };
 template <> struct Tr<EF_Q4_K> {
@@ -241,6 +246,34 @@ __device__ __forceinline__ void compute(const RawQ8 &r, const uint8_t *xc, int M
         const uint32_t a2 = hmul2u(hsub2u(prmt(wg, 0x64646464u, 0x7362), H2_1152), dg);
         const uint32_t a1 = hmul2u(hsub2u(prmt(wg8, 0x64646464u, 0x5140), H2_1152), dg8);
         const uint32_t a3 = hmul2u(hsub2u(prmt(wg8, 0x64646464u, 0x7362), H2_1152), dg8);
+        mma_step<NT>(acc, xsc, s, lane, a0, a1, a2, a3);
+    }
+}
+
+// ------------------------------------------------------------------ Q4_0 ---
+// lane (g,t): part 0 / 1 = the 32 nibbles of block t of row g / g+8 (word j:
+// weights 8j..8j+7 at the nibble slots of common.cuh q40_slot), the two rows'
+// f16 d at 1024 + 4*lane.
+struct RawQ40 { uint4 q[2]; uint32_t sc; };
+__device__ __forceinline__ void load_raw(RawQ40 &r, const uint8_t *T, int lane) {
+    r.q[0] = ldq128(T + lane * 16);
+    r.q[1] = ldq128(T + 512 + lane * 16);
+    r.sc = ldq32(T + 1024 + lane * 4);
+}
+template <int NT>
+__device__ __forceinline__ void compute(const RawQ40 &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
+                                        const uint4 *, const uint4 *) {
+    const XF xsc = make_xf<NT>(xc, M, lane);
+    const uint32_t dg = prmt(r.sc, 0, 0x1010), dg8 = prmt(r.sc, 0, 0x3232);
+#pragma unroll
+    for (int s = 0; s < 8; s++) {
+        const int sh = 8 * (s & 1);
+        const uint32_t wg = wsel(r.q[0], s >> 1), wg8 = wsel(r.q[1], s >> 1);
+        // (1024 + q) - 1032 = q - 8 exactly; then one rounding of d*(q-8)
+        const uint32_t a0 = hmul2u(hsub2u(((wg >> sh) & 0x000F000Fu) | 0x64006400u, H2_1032), dg);
+        const uint32_t a2 = hmul2u(hsub2u(((wg >> (sh + 4)) & 0x000F000Fu) | 0x64006400u, H2_1032), dg);
+        const uint32_t a1 = hmul2u(hsub2u(((wg8 >> sh) & 0x000F000Fu) | 0x64006400u, H2_1032), dg8);
+        const uint32_t a3 = hmul2u(hsub2u(((wg8 >> (sh + 4)) & 0x000F000Fu) | 0x64006400u, H2_1032), dg8);
         mma_step<NT>(acc, xsc, s, lane, a0, a1, a2, a3);
     }
 }
@@ -685,6 +718,7 @@ __device__ __forceinline__ void compute(const RawIQ1 &r, const uint8_t *xc, int 
 
 template <int TYPE> struct RawOf;
 template <> struct RawOf<EF_Q8_0> { using T = RawQ8; };
+template <> struct RawOf<EF_Q4_0> { using T = RawQ40; };
 template <> struct RawOf<EF_Q4_K> { using T = RawQ4K; };
 template <> struct RawOf<EF_Q6_K> { using T = RawQ6K; };
 template <> struct RawOf<EF_IQ2_XXS> { using T = RawIQ2; };
@@ -1193,7 +1227,7 @@ static int max_active_clusters(ef_ctx *ctx, const void *kern, int threads, size_
 // Warps per rowgroup: two (16-warp CTAs) where the kernel fits 128 registers
 // per thread, else one.
 template <int TYPE, int TQ, int NT, bool SWIGLU> constexpr int kh_of() {
-    return !SWIGLU && (NT == 1 || TYPE == EF_Q8_0) ? 2 : 1;
+    return !SWIGLU && (NT == 1 || TYPE == EF_Q8_0 || TYPE == EF_Q4_0) ? 2 : 1;
 }
 
 template <int TYPE, int TQ, int NT, bool SWIGLU, bool FUSED>
@@ -1339,6 +1373,7 @@ int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight 
     int rc;
     switch (w0->type) {
     case EF_Q8_0: rc = launch_sw<EF_Q8_0>(ctx, a, sw, ws, n, x); break;
+    case EF_Q4_0: rc = launch_sw<EF_Q4_0>(ctx, a, sw, ws, n, x); break;
     case EF_Q4_K: rc = launch_sw<EF_Q4_K>(ctx, a, sw, ws, n, x); break;
     case EF_Q6_K: rc = launch_sw<EF_Q6_K>(ctx, a, sw, ws, n, x); break;
     case EF_IQ2_XXS: rc = launch_sw<EF_IQ2_XXS>(ctx, a, sw, ws, n, x); break;
@@ -1372,6 +1407,7 @@ static size_t gemv_xfrag_bytes(int type, int64_t nchunks, int M) {
     size_t fb = 0;
     switch (type) {
     case EF_Q8_0: fb = (size_t)f16_xbytes<EF_Q8_0>(M); break;
+    case EF_Q4_0: fb = (size_t)f16_xbytes<EF_Q4_0>(M); break;
     case EF_Q4_K: fb = (size_t)i8_xbytes<EF_Q4_K>(M); break;
     case EF_Q6_K: fb = (size_t)i8_xbytes<EF_Q6_K>(M); break;
     case EF_IQ2_XXS: fb = (size_t)f16_xbytes<EF_IQ2_XXS>(M); break;

@@ -22,7 +22,7 @@ from ._lib import TYPE_IDS, TYPE_NAMES
 
 BLOCKS = {"Q4_0": (32, 18), "Q8_0": (32, 34), "Q4_K": (256, 144), "Q6_K": (256, 210),
           "IQ2_XXS": (256, 66), "IQ1_S": (256, 50)}
-HOT_TYPES = ("Q8_0", "Q4_K", "Q6_K", "IQ2_XXS", "IQ1_S")
+HOT_TYPES = ("Q8_0", "Q4_0", "Q4_K", "Q6_K", "IQ2_XXS", "IQ1_S")
 
 
 def type_name(t) -> str:

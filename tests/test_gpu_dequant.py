@@ -10,6 +10,7 @@ pytestmark = pytest.mark.gpu
 
 SHAPES = {  # rows x k, including ragged rows (not a multiple of 16) and partial chunks
     "Q8_0": [(16, 128), (37, 96), (8192 // 64, 2048), (5, 32 * 7)],
+    "Q4_0": [(16, 128), (29, 96), (64, 2048), (3, 32 * 5)],
     "Q4_K": [(16, 256), (33, 768), (64, 4096)],
     "Q6_K": [(16, 256), (19, 512), (48, 4096)],
     "IQ2_XXS": [(16, 256), (21, 512)],
@@ -36,7 +37,7 @@ def test_repack_round_trip(ops, t, rows, k):
     np.testing.assert_array_equal(back, raw)
 
 
-@pytest.mark.parametrize("t", ["Q8_0", "Q4_K", "Q6_K", "IQ2_XXS", "IQ1_S"])
+@pytest.mark.parametrize("t", ["Q8_0", "Q4_0", "Q4_K", "Q6_K", "IQ2_XXS", "IQ1_S"])
 def test_golden_blocks_on_gpu(ops, golden, t):
     """The fixture's seeded + edge blocks (negative, subnormal, max scales) as a
     one-row-per-block tensor, decoded on the GPU vs gguf-py's bits."""

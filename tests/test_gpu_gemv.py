@@ -21,7 +21,8 @@ def _check(oracle_mod, t, raw, rows, k, x, y):
     return (err / tol).max()
 
 
-SHAPES = [("Q8_0", 128, 2048), ("Q8_0", 40, 96), ("Q4_K", 256, 1024), ("Q4_K", 36, 4096),
+SHAPES = [("Q8_0", 128, 2048), ("Q8_0", 40, 96), ("Q4_0", 128, 2048), ("Q4_0", 24, 160),
+          ("Q4_K", 256, 1024), ("Q4_K", 36, 4096),
           ("Q6_K", 128, 1024), ("Q6_K", 20, 2304), ("IQ2_XXS", 64, 1024), ("IQ1_S", 64, 1024)]
 
 
