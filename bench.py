@@ -556,6 +556,32 @@ def run_ours(args):
         for wc in ws[1:]:
             wc.free()
 
+    # ---- config 0: Q8_0 GEMV 8192 x 2048, 1 token (the same back-to-back method) ----
+    raw0 = formats.synth("Q8_0", 8192, 2048, seed=77 + rank)
+    ws0 = [ops.load_weight("Q8_0", raw0, 8192, 2048) for _ in range(COPIES)]
+    del raw0
+    x0 = torch.randn(1, 2048, device="cuda", generator=torch.Generator("cuda").manual_seed(77))
+    y0 = torch.empty(1, 8192, device="cuda")
+
+    def seq0():
+        h = ops.ctx.bind()
+        for wc in ws0:
+            check(L.ef_gemv(h, wc.h, _ptr(x0), 1, _ptr(y0)), h)
+    g0 = capture(seq0)
+    g0.replay()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record()
+    for _ in range(reps):
+        g0.replay()
+    ev1.record()
+    torch.cuda.synchronize()
+    us0 = ev0.elapsed_time(ev1) * 1e3 / (reps * COPIES)
+    b0 = formats.tensor_bytes("Q8_0", 8192, 2048) + 4 * 2048 + 4 * 8192
+    del g0
+    for wc in ws0:
+        wc.free()
+
     # ---- end to end through the public operator, pinned host buffers ----
     g_e2e = capture(step_e2e)
     for _ in range(args.warmup):
@@ -614,6 +640,9 @@ def run_ours(args):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "gemm": gemm,
+            "config0": {"workload": "config0 Q8_0 GEMV 8192x2048, 1 token (8 weight copies back to back)",
+                        "us": round(us0, 2), "GBps": round(b0 / (us0 * 1e-6) / 1e9, 1),
+                        "frac": round(b0 / (us0 * 1e-6) / 1e9 / peak, 4), "algorithmic_bytes": b0},
             "decode": decode,
             "decode_8b": decode8b,
             "per_call": per_call,

@@ -21,6 +21,9 @@ Arithmetic: f64 throughout, except that every matrix product takes its
 operands at the precision of the f16 tensor-core GEMV it checks -- weights as
 f16(d*q), activations rounded to f16 -- so that the remaining difference to
 the GPU is f32 accumulation order, and greedy tokens can be compared exactly.
+With matmul="f32" (for the full-size model, whose f64 weights would not fit
+a test's memory) the products of those same f16 operands are summed in f32
+by the host BLAS; everything else stays f64.
 Parity of this file with the reference's own code is unpinned: the reference
 ships no model tests and its CPU path (Node + WebAssembly) cannot run here; it
 is a restatement of the cited code.
@@ -67,8 +70,10 @@ class LFM3Oracle:
     """cfg: an object with the LFM3Config fields; weights: name -> (Q8_0 bytes,
     rows, k) or an f32 array (numpy)."""
 
-    def __init__(self, cfg, weights: dict, rank: int = 0, world: int = 1, allreduce=None, allgather=None):
+    def __init__(self, cfg, weights: dict, rank: int = 0, world: int = 1, allreduce=None, allgather=None,
+                 matmul: str = "f64"):
         self.cfg = cfg
+        self.f32 = matmul == "f32"
         self.rank, self.world = rank, world
         self.allreduce = allreduce or (lambda v: v)
         self.allgather = allgather
@@ -77,9 +82,9 @@ class LFM3Oracle:
             if isinstance(val, tuple):
                 raw, rows, k = val
                 w = dequant_q8_0(raw, rows, k)
-                self.w16[name] = w.astype(np.float16).astype(np.float64)
+                self.w16[name] = w.astype(np.float16).astype(np.float32 if self.f32 else np.float64)
                 if name == "token_embd":
-                    self.embd = w.astype(np.float64)
+                    self.embd = w if self.f32 else w.astype(np.float64)
             else:
                 self.f[name] = np.asarray(val, np.float64)
         self.windows = cfg.windows()
@@ -94,13 +99,15 @@ class LFM3Oracle:
         self.pos = 0
 
     def mm(self, name: str, x: np.ndarray) -> np.ndarray:
+        if self.f32:
+            return (self.w16[name] @ f16(x).astype(np.float32)).astype(np.float64)
         return self.w16[name] @ f16(x)
 
     def step(self, tok: int) -> int:
         c, f = self.cfg, self.f
         E, D = c.hidden, c.head_dim
         H, KV, Ec = c.heads // self.world, c.kv_heads // self.world, c.hidden // self.world
-        x = self.embd[tok].copy()
+        x = self.embd[tok].astype(np.float64)
         nrm = rmsnorm(x, f["blk.0.attn_norm"], c.eps)
         for l in range(c.layers):
             p = f"blk.{l}."
