@@ -84,6 +84,7 @@ _SIGS = {
                        _P, _P], _I),
     "ef_attention": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
     "ef_swiglu": ([_P, _P, _P, ctypes.c_int64, _P], _I),
+    "ef_topk": ([_P, _P, _I, _I, _I, _P, _P, _P], _I),
     "ef_tp_create": ([_P, _I, _I, ctypes.c_size_t, ctypes.c_double, _P], _I),
     "ef_tp_handle": ([_P, _P, _P], _I),
     "ef_tp_connect": ([_P, _P, _P], _I),

@@ -34,12 +34,13 @@ struct ef_ctx {
     uint64_t seq = 0;
     // Persistent device scratch owned by the context (grown on demand):
     // slot 0 holds the GEMV's activation data, slot 1 the GEMM's converted
-    // activations, slot 2 the decode attention's per-split partial results.
-    // A first call of a new, larger shape grows them (cudaMalloc), so that
-    // call must come before any stream capture.
-    static constexpr int kScratchSlots = 3;
-    void *scratch[kScratchSlots] = {nullptr, nullptr, nullptr};
-    size_t scratch_bytes[kScratchSlots] = {0, 0, 0};
+    // activations, slot 2 the decode attention's per-split partial results,
+    // slot 3 the top-k kernel's per-chunk candidates. A first call of a new,
+    // larger shape grows them (cudaMalloc), so that call must come before any
+    // stream capture.
+    static constexpr int kScratchSlots = 4;
+    void *scratch[kScratchSlots] = {nullptr, nullptr, nullptr, nullptr};
+    size_t scratch_bytes[kScratchSlots] = {0, 0, 0, 0};
     uint64_t launches = 0;            // kernels this context has launched (diagnostic counter)
     // Programmatic dependent launch: each kernel may be scheduled while the
     // previous one on the stream finishes; it waits for that kernel's results

@@ -463,6 +463,94 @@ __global__ void __launch_bounds__(CT) attn_combine_kernel(const float *__restric
     }
 }
 
+// ---------------------------------------------------------------- top-k ---
+// The m first logits of a row in the sampler's order -- larger value first,
+// the lower index first among equal values (kernels.topk.wgsl.js:3-36,
+// topk.js) -- exactly, as 64-bit keys (value key << 32 | ~index) sorted in
+// shared memory: each CTA sorts one chunk of TK_CHUNK logits and keeps its m
+// first (every element of the row's top m is in its chunk's top m), one CTA
+// per row sorts the union. The value key orders f32 bits as numbers with -0
+// equal to +0; NaN logits set flag 2 for the row (their order cannot be
+// reproduced, kernels.topk.wgsl.js:18-36).
+constexpr int TK_CHUNK = 4096;
+
+__device__ __forceinline__ uint32_t order_key(uint32_t bits) {
+    const uint32_t b = bits == 0x80000000u ? 0u : bits;
+    return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+// descending bitonic sort of n (a power of two) keys in shared memory
+__device__ void bitonic_desc(unsigned long long *a, int n) {
+    for (int k = 2; k <= n; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            __syncthreads();
+            for (int i = threadIdx.x; i < n; i += blockDim.x) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const unsigned long long x = a[i], y = a[l];
+                    const bool desc = (i & k) == 0;
+                    if (desc ? x < y : x > y) {
+                        a[i] = y;
+                        a[l] = x;
+                    }
+                }
+            }
+        }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(512) topk_chunk_kernel(const float *__restrict__ logits, int n, int m,
+                                                         unsigned long long *__restrict__ cand,
+                                                         int *__restrict__ flags) {
+    pdl_trigger();
+    pdl_wait();
+    __shared__ unsigned long long a[TK_CHUNK];
+    __shared__ int nan_seen;
+    const int chunk = blockIdx.x, row = blockIdx.y, nch = gridDim.x;
+    const uint32_t *lr = reinterpret_cast<const uint32_t *>(logits + (int64_t)row * n);
+    if (threadIdx.x == 0) nan_seen = 0;
+    __syncthreads();
+    bool nan = false;
+    for (int i = threadIdx.x; i < TK_CHUNK; i += blockDim.x) {
+        const int idx = chunk * TK_CHUNK + i;
+        unsigned long long v = 0;                     // padding: below every logit
+        if (idx < n) {
+            const uint32_t bits = lr[idx];
+            nan |= (bits & 0x7fffffffu) > 0x7f800000u;
+            v = ((unsigned long long)order_key(bits) << 32) | (uint32_t)~(uint32_t)idx;
+        }
+        a[i] = v;
+    }
+    if (nan) atomicOr(&nan_seen, 1);
+    bitonic_desc(a, TK_CHUNK);
+    unsigned long long *out = cand + ((int64_t)row * nch + chunk) * m;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) out[i] = a[i];
+    if (threadIdx.x == 0 && nan_seen) atomicOr(flags + row, 2);
+}
+
+__global__ void __launch_bounds__(1024) topk_final_kernel(const float *__restrict__ logits, int n, int m, int nch,
+                                                          int sort_n, const unsigned long long *__restrict__ cand,
+                                                          int *__restrict__ ids, float *__restrict__ vals) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ unsigned long long u[];
+    const int row = blockIdx.x;
+    const unsigned long long *c = cand + (int64_t)row * nch * m;
+    for (int i = threadIdx.x; i < sort_n; i += blockDim.x) u[i] = i < nch * m ? c[i] : 0ull;
+    bitonic_desc(u, sort_n);
+    const int cnt = m < n ? m : n;
+    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+        int id = -1;
+        float v = 0.f;
+        if (i < cnt) {
+            id = (int)~(uint32_t)(u[i] & 0xffffffffull);
+            v = logits[(int64_t)row * n + id];          // the logit's own bits
+        }
+        ids[(int64_t)row * m + i] = id;
+        vals[(int64_t)row * m + i] = v;
+    }
+}
+
 // out = g * sigmoid(g) * u, elementwise (kernels.nn.wgsl.js swiglu; the same
 // expression as the fused SwiGLU GEMV's epilogue).
 __global__ void swiglu_kernel(const float *__restrict__ g, const float *__restrict__ u, int64_t n,
@@ -801,6 +889,32 @@ int ef_attention(ef_ctx *ctx, const float *q, const float *kcache, const float *
     if ((int64_t)seqs * tokens > 65535) return set_err(ctx, EF_ERR_RANGE, "attention: more than 65535 rows");
     return attention_launch(ctx, q, kcache, vcache, head_gate, pos, seqs, tokens, max_pos, window, heads, kv_heads,
                             head_dim, out);
+}
+
+int ef_topk(ef_ctx *ctx, const float *logits, int rows, int n, int m, int *ids, float *vals, int *flags) {
+    if (!ctx || !logits || !ids || !vals || !flags || rows < 1 || rows > 65535 || n < 1 || m < 1)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "topk: bad arguments") : EF_ERR_INVALID;
+    if (m > EF_TOPK_MAX_M || n > EF_TOPK_MAX_N)
+        return set_err(ctx, EF_ERR_RANGE, "topk: m=%d n=%d (at most %d and %d)", m, n, EF_TOPK_MAX_M, EF_TOPK_MAX_N);
+    const int nch = (n + TK_CHUNK - 1) / TK_CHUNK;
+    int sort_n = 1;
+    while (sort_n < nch * m) sort_n <<= 1;
+    const size_t smem = (size_t)sort_n * 8;
+    if (int rc = ensure_scratch(ctx, 3, (size_t)rows * nch * m * 8)) return rc;
+    static unsigned long long configured = 0;
+    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(topk_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                          227 * 1024), "topk smem attribute"))
+            return rc;
+        configured |= 1ull << ctx->device;
+    }
+    if (int rc = check_cuda(ctx, cudaMemsetAsync(flags, 0, (size_t)rows * sizeof(int), ctx->stream), "topk flags"))
+        return rc;
+    unsigned long long *cand = (unsigned long long *)ctx->scratch[3];
+    if (int rc = launch_on(ctx, topk_chunk_kernel, dim3(nch, rows), 512, 0, "topk launch", logits, n, m, cand, flags))
+        return rc;
+    return launch_on(ctx, topk_final_kernel, rows, 1024, smem, "topk launch", logits, n, m, nch, sort_n,
+                     (const unsigned long long *)cand, ids, vals);
 }
 
 int ef_swiglu(ef_ctx *ctx, const float *gate, const float *up, int64_t n, float *out) {

@@ -310,6 +310,17 @@ EF_API int ef_attention(ef_ctx *ctx, const float *q, const float *kcache, const 
                         const float *head_gate, const int *pos, int seqs, int tokens, int max_pos, int window,
                         int heads, int kv_heads, int head_dim, float *out);
 
+/* Sampling candidates on the device (kernels.topk.wgsl.js, topk.js): for each
+ * of `rows` rows of n logits, the m first in the sampler's order -- larger
+ * value first, the lower index first among equal values, -0 equal to +0 --
+ * exactly: ids[r][i] and vals[r][i] (the logit's own f32 bits) for i < m in
+ * that order (ids -1 past n). flags[r] = 2 when the row holds a NaN (the
+ * order is then not the sampler's; read the row instead). m <=
+ * EF_TOPK_MAX_M, n <= EF_TOPK_MAX_N. */
+#define EF_TOPK_MAX_M 256
+#define EF_TOPK_MAX_N 262144
+EF_API int ef_topk(ef_ctx *ctx, const float *logits, int rows, int n, int m, int *ids, float *vals, int *flags);
+
 /* out[i] = gate[i] * sigmoid(gate[i]) * up[i] for the n elements (the
  * prompt-side SwiGLU after two separate GEMMs; js/model.js:651-655). */
 EF_API int ef_swiglu(ef_ctx *ctx, const float *gate, const float *up, int64_t n, float *out);
