@@ -16,9 +16,9 @@ HEADER = os.path.join(HERE, "..", "include", "elffuss_cuda.h")
 EF_OK, EF_NOT_APPLICABLE = 0, 1
 ERRORS = {-1: "EF_ERR_INVALID", -2: "EF_ERR_TYPE", -3: "EF_ERR_SHAPE", -4: "EF_ERR_CUDA",
           -5: "EF_ERR_OOM", -6: "EF_ERR_MISMATCH", -7: "EF_ERR_RANGE", -8: "EF_ERR_TIMEOUT"}
-F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, IQ2_XXS, IQ1_S = 0, 1, 2, 8, 12, 14, 16, 19
-TYPE_IDS = {"F32": F32, "F16": F16, "Q4_0": Q4_0, "Q8_0": Q8_0, "Q4_K": Q4_K, "Q6_K": Q6_K,
-            "IQ2_XXS": IQ2_XXS, "IQ1_S": IQ1_S}
+F32, F16, Q4_0, Q8_0, Q2_K, Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ1_S = 0, 1, 2, 8, 10, 12, 13, 14, 16, 19
+TYPE_IDS = {"F32": F32, "F16": F16, "Q4_0": Q4_0, "Q8_0": Q8_0, "Q2_K": Q2_K, "Q4_K": Q4_K, "Q5_K": Q5_K,
+            "Q6_K": Q6_K, "IQ2_XXS": IQ2_XXS, "IQ1_S": IQ1_S}
 TYPE_NAMES = {v: k for k, v in TYPE_IDS.items()}
 
 

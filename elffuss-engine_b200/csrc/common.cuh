@@ -77,6 +77,8 @@ __host__ __device__ inline bool geo_of(int type, TypeGeo &g) {
     case EF_Q8_0: g = {32, 34, 128, 2176}; return true;
     case EF_Q4_0: g = {32, 18, 128, 1152}; return true;
     case EF_Q4_K: g = {256, 144, 256, 2304}; return true;
+    case EF_Q5_K: g = {256, 176, 256, 2816}; return true;
+    case EF_Q2_K: g = {256, 84, 256, 1344}; return true;
     case EF_Q6_K: g = {256, 210, 256, 3360}; return true;
     case EF_IQ2_XXS: g = {256, 66, 256, 1056}; return true;
     case EF_IQ1_S: g = {256, 50, 256, 800}; return true;
@@ -212,6 +214,49 @@ __host__ __device__ inline void scatter_block(int type, const uint8_t *blk, int 
         T[1024 + lane * 4 + hs * 2] = blk[0];
         T[1024 + lane * 4 + hs * 2 + 1] = blk[1];
     } break;
+    case EF_Q5_K: {
+        // lane (g,t) owns the 64-weight group t (sub-blocks 2t: low nibbles,
+        // 2t+1: high nibbles) of rows g and g+8. Parts 2hs, 2hs+1: its 32 qs
+        // bytes; part 4 at 8*hs: two words of fifth bits, bit l = qh[l] bit 2t
+        // (low) / 2t+1 (high); the row's d, dmin, scales verbatim at 2560 + 16 r.
+        // bic = 0: a whole superblock per chunk.
+        for (int t = 0; t < 4; t++) {
+            const int lane = 4 * g + t;
+            for (int b = 0; b < 32; b++) T[(2 * hs + (b >> 4)) * 512 + lane * 16 + (b & 15)] = blk[48 + 32 * t + b];
+            uint32_t lo = 0, hi = 0;
+            for (int l = 0; l < 32; l++) {
+                lo |= (uint32_t)((blk[16 + l] >> (2 * t)) & 1) << l;
+                hi |= (uint32_t)((blk[16 + l] >> (2 * t + 1)) & 1) << l;
+            }
+            for (int b = 0; b < 4; b++) {
+                T[4 * 512 + lane * 16 + 8 * hs + b] = (uint8_t)(lo >> (8 * b));
+                T[4 * 512 + lane * 16 + 8 * hs + 4 + b] = (uint8_t)(hi >> (8 * b));
+            }
+        }
+        for (int b = 0; b < 16; b++) T[2560 + 16 * r + b] = blk[b];
+    } break;
+    case EF_Q2_K: {
+        // lane (g,t) owns weights 64t..64t+63 (sub-blocks 4t..4t+3 of 16) of
+        // rows g and g+8. Part hs word w, byte c: bits 2s'..2s'+1 = the 2-bit q
+        // of weight 64t + 4(4w + s') + c (kernels.wgsl.js:192-217: byte
+        // qs[32n + r] >> 2j for weight 128n + 32j + r); the four scale bytes
+        // of its sub-blocks at 1024 + 8*lane + 4*hs; d, dmin at 1280 + 4 r.
+        for (int t = 0; t < 4; t++) {
+            const int lane = 4 * g + t;
+            for (int w = 0; w < 4; w++)
+                for (int c = 0; c < 4; c++) {
+                    uint32_t byte = 0;
+                    for (int sp = 0; sp < 4; sp++) {
+                        const int i = 64 * t + 4 * (4 * w + sp) + c;
+                        const int n = i >> 7, jj = (i >> 5) & 3, rr = i & 31;
+                        byte |= (uint32_t)((blk[16 + 32 * n + rr] >> (2 * jj)) & 3) << (2 * sp);
+                    }
+                    T[hs * 512 + lane * 16 + 4 * w + c] = (uint8_t)byte;
+                }
+            for (int k = 0; k < 4; k++) T[1024 + 8 * lane + 4 * hs + k] = blk[4 * t + k];
+        }
+        for (int b = 0; b < 4; b++) T[1280 + 4 * r + b] = blk[80 + b];
+    } break;
     default:
         break;
     }
@@ -284,6 +329,34 @@ __host__ __device__ inline void gather_block(int type, const uint8_t *T, int r, 
         blk[0] = T[1024 + lane * 4 + hs * 2];
         blk[1] = T[1024 + lane * 4 + hs * 2 + 1];
     } break;
+    case EF_Q5_K: {
+        for (int b = 0; b < 16; b++) blk[b] = T[2560 + 16 * r + b];
+        for (int l = 0; l < 32; l++) blk[16 + l] = 0;
+        for (int t = 0; t < 4; t++) {
+            const int lane = 4 * g + t;
+            for (int b = 0; b < 32; b++) blk[48 + 32 * t + b] = T[(2 * hs + (b >> 4)) * 512 + lane * 16 + (b & 15)];
+            const uint32_t lo = rd32(T + 4 * 512 + lane * 16 + 8 * hs), hi = rd32(T + 4 * 512 + lane * 16 + 8 * hs + 4);
+            for (int l = 0; l < 32; l++)
+                blk[16 + l] |= (uint8_t)((((lo >> l) & 1) << (2 * t)) | (((hi >> l) & 1) << (2 * t + 1)));
+        }
+    } break;
+    case EF_Q2_K: {
+        for (int b = 0; b < 64; b++) blk[16 + b] = 0;
+        for (int t = 0; t < 4; t++) {
+            const int lane = 4 * g + t;
+            for (int w = 0; w < 4; w++)
+                for (int c = 0; c < 4; c++) {
+                    const uint32_t byte = T[hs * 512 + lane * 16 + 4 * w + c];
+                    for (int sp = 0; sp < 4; sp++) {
+                        const int i = 64 * t + 4 * (4 * w + sp) + c;
+                        const int n = i >> 7, jj = (i >> 5) & 3, rr = i & 31;
+                        blk[16 + 32 * n + rr] |= (uint8_t)(((byte >> (2 * sp)) & 3) << (2 * jj));
+                    }
+                }
+            for (int k = 0; k < 4; k++) blk[4 * t + k] = T[1024 + 8 * lane + 4 * hs + k];
+        }
+        for (int b = 0; b < 4; b++) blk[80 + b] = T[1280 + 4 * r + b];
+    } break;
     default:
         break;
     }
@@ -316,6 +389,39 @@ __device__ inline void decode_block(int type, const uint8_t *blk, const int8_t *
             out[i] = __fmul_rn((float)((int)(blk[2 + i] & 15) - 8), d);
             out[i + 16] = __fmul_rn((float)((int)(blk[2 + i] >> 4) - 8), d);
         }
+    } break;
+    case EF_Q5_K: {
+        // kernels.wgsl.js:333-362
+        const float d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));
+        for (int j = 0; j < 4; j++) {
+            int s1, m1i, s2, m2i;
+            scale_min_k4(blk + 4, 2 * j, s1, m1i);
+            scale_min_k4(blk + 4, 2 * j + 1, s2, m2i);
+            const float d1 = __fmul_rn(d, (float)s1), m1 = __fmul_rn(dmin, (float)m1i);
+            const float d2 = __fmul_rn(d, (float)s2), m2 = __fmul_rn(dmin, (float)m2i);
+            for (int l = 0; l < 32; l++) {
+                const int q = blk[48 + 32 * j + l], h = blk[16 + l];
+                const int a = (q & 15) + (((h >> (2 * j)) & 1) ? 16 : 0);
+                const int b = (q >> 4) + (((h >> (2 * j + 1)) & 1) ? 16 : 0);
+                out[64 * j + l] = __fsub_rn(__fmul_rn(d1, (float)a), m1);
+                out[64 * j + 32 + l] = __fsub_rn(__fmul_rn(d2, (float)b), m2);
+            }
+        }
+    } break;
+    case EF_Q2_K: {
+        // kernels.wgsl.js:192-217
+        const float d = h2f(blk[80] | (blk[81] << 8)), dmin = h2f(blk[82] | (blk[83] << 8));
+        for (int n = 0; n < 2; n++)
+            for (int j = 0; j < 4; j++) {
+                const int sa = blk[8 * n + 2 * j], sb = blk[8 * n + 2 * j + 1];
+                const float dl1 = __fmul_rn(d, (float)(sa & 15)), ml1 = __fmul_rn(dmin, (float)(sa >> 4));
+                const float dl2 = __fmul_rn(d, (float)(sb & 15)), ml2 = __fmul_rn(dmin, (float)(sb >> 4));
+                for (int l = 0; l < 16; l++) {
+                    const int qa = (blk[16 + 32 * n + l] >> (2 * j)) & 3, qb = (blk[16 + 32 * n + 16 + l] >> (2 * j)) & 3;
+                    out[128 * n + 32 * j + l] = __fsub_rn(__fmul_rn(dl1, (float)qa), ml1);
+                    out[128 * n + 32 * j + 16 + l] = __fsub_rn(__fmul_rn(dl2, (float)qb), ml2);
+                }
+            }
     } break;
     case EF_Q4_K: {
         const float d = h2f(blk[0] | (blk[1] << 8)), dmin = h2f(blk[2] | (blk[3] << 8));

@@ -65,6 +65,7 @@ __device__ const __align__(16) uint16_t g_grid_iq1s_f16[EF_GRID_IQ1S_ENTRIES * 8
 
 constexpr uint32_t H2_1152 = 0x64806480u;   // half2(1152, 1152)
 constexpr uint32_t H2_1032 = 0x64086408u;   // half2(1032, 1032)
+constexpr uint32_t H2_1024 = 0x64006400u;   // half2(1024, 1024)
 constexpr int GV_WARPS = 8;                 // rowgroups (warps) per CTA = one rowblock
 constexpr int MAX_XS_BYTES = 64 * 1024;     // shared memory for activation data
 
@@ -103,6 +104,14 @@ template <> struct Tr<EF_Q8_0> {
 template <> struct Tr<EF_Q4_0> {   // the Q8_0 chunk and activation layout
     static constexpr int CHUNK = 128, STEPS = 8, TILE = 1152, I8 = 0;
     __device__ static void inv(int kq, int &t, int &s) { t = kq >> 3; s = kq & 7; }
+};
+template <> struct Tr<EF_Q5_K> {   // lane t: weights 64t..64t+63, step s: 64t + 4s..+3
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 2816, I8 = 0;
+    __device__ static void inv(int kq, int &t, int &s) { t = kq >> 4; s = kq & 15; }
+};
+template <> struct Tr<EF_Q2_K> {   // the same lane ownership as Q5_K
+    static constexpr int CHUNK = 256, STEPS = 16, TILE = 1344, I8 = 0;
+    __device__ static void inv(int kq, int &t, int &s) { t = kq >> 4; s = kq & 15; }
 };
 template <> struct Tr<EF_Q4_K> {
     static constexpr int CHUNK = 256, STEPS = 16, TILE = 2304, I8 = 1;
@@ -275,6 +284,116 @@ __device__ __forceinline__ void compute(const RawQ40 &r, const uint8_t *xc, int 
         const uint32_t a1 = hmul2u(hsub2u(((wg8 >> sh) & 0x000F000Fu) | 0x64006400u, H2_1032), dg8);
         const uint32_t a3 = hmul2u(hsub2u(((wg8 >> (sh + 4)) & 0x000F000Fu) | 0x64006400u, H2_1032), dg8);
         mma_step<NT>(acc, xsc, s, lane, a0, a1, a2, a3);
+    }
+}
+
+// --------------------------------------------------------- Q5_K / Q2_K ---
+// f16 operands: q as (1024 + q) - 1024 exactly, then one f16 fma with the
+// sub-block's f16(d * sc) and -f16(dmin * m).
+__device__ __forceinline__ uint32_t f16_pair_dm(uint32_t qbytes, uint32_t sel, uint32_t d2, uint32_t negm2) {
+    uint32_t r;
+    const uint32_t q = hsub2u(prmt(qbytes, 0x64646464u, sel), H2_1024);
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(q), "r"(d2), "r"(negm2));
+    return r;
+}
+// two f32 -> f16x2 (d, d) and (-m, -m)
+__device__ __forceinline__ uint32_t f16x2_bcast(float v) {
+    const uint32_t h = __half_as_ushort(__float2half_rn(v));
+    return h | (h << 16);
+}
+// bit c of x (c < 4) to bit 8c
+__device__ __forceinline__ uint32_t spread4(uint32_t x) { return (x * 0x00204081u) & 0x01010101u; }
+
+// Q5_K, lane (g,t): parts 0,1 / 2,3 = qs bytes 32t.. of rows g / g+8, part 4 =
+// fifth-bit words (low, high sub-block) of both rows, the rows' verbatim
+// 16-byte headers (d, dmin, scale_min_k4 bytes) at 2560 + 16 * row.
+struct RawQ5K { uint4 q[5]; uint4 hg, hg8; };
+__device__ __forceinline__ void load_raw(RawQ5K &r, const uint8_t *T, int lane) {
+#pragma unroll
+    for (int p = 0; p < 5; p++) r.q[p] = ldq128(T + p * 512 + lane * 16);
+    const int g = lane >> 2;
+    r.hg = ldh128(T + 2560 + g * 16);
+    r.hg8 = ldh128(T + 2560 + (g + 8) * 16);
+}
+// f16 (d * sc, -dmin * m) of sub-block j of a Q5_K / Q4_K header (scale_min_k4)
+__device__ __forceinline__ void q5_dm(const uint4 &h, int j, uint32_t &d2, uint32_t &negm2) {
+    const uint32_t w[4] = {h.x, h.y, h.z, h.w};
+    auto byte = [&](int i) { return (int)((w[i >> 2] >> (8 * (i & 3))) & 0xFF); };
+    int sc, mn;
+    if (j < 4) {
+        sc = byte(4 + j) & 63;
+        mn = byte(8 + j) & 63;
+    } else {
+        sc = (byte(8 + j) & 0xF) | ((byte(j) >> 6) << 4);
+        mn = (byte(8 + j) >> 4) | ((byte(4 + j) >> 6) << 4);
+    }
+    const float d = __half2float(__ushort_as_half((unsigned short)(h.x & 0xFFFF)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    d2 = f16x2_bcast(d * (float)sc);
+    negm2 = f16x2_bcast(-(dmin * (float)mn));
+}
+template <int NT>
+__device__ __forceinline__ void compute(const RawQ5K &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
+                                        const uint4 *, const uint4 *) {
+    const XF xsc = make_xf<NT>(xc, M, lane);
+    const int t = lane & 3;
+    uint32_t dg[2], mg[2], dg8[2], mg8[2];
+#pragma unroll
+    for (int u = 0; u < 2; u++) {
+        q5_dm(r.hg, 2 * t + u, dg[u], mg[u]);
+        q5_dm(r.hg8, 2 * t + u, dg8[u], mg8[u]);
+    }
+    const uint32_t hb[4] = {r.q[4].x, r.q[4].y, r.q[4].z, r.q[4].w};   // row g: lo, hi; row g+8: lo, hi
+#pragma unroll
+    for (int s = 0; s < 16; s++) {
+        const int u = s >> 3, ls = s & 7;                                  // sub-block 2t+u, bytes 4ls..
+        const uint32_t wg = wsel(r.q[ls >> 2], ls & 3), wg8 = wsel(r.q[2 + (ls >> 2)], ls & 3);
+        const uint32_t ng = u ? (wg >> 4) & 0x0F0F0F0Fu : wg & 0x0F0F0F0Fu;
+        const uint32_t ng8 = u ? (wg8 >> 4) & 0x0F0F0F0Fu : wg8 & 0x0F0F0F0Fu;
+        const uint32_t q5 = ng | (spread4((hb[u] >> (4 * ls)) & 0xF) << 4);
+        const uint32_t q58 = ng8 | (spread4((hb[2 + u] >> (4 * ls)) & 0xF) << 4);
+        const uint32_t a0 = f16_pair_dm(q5, 0x5140, dg[u], mg[u]);
+        const uint32_t a2 = f16_pair_dm(q5, 0x7362, dg[u], mg[u]);
+        const uint32_t a1 = f16_pair_dm(q58, 0x5140, dg8[u], mg8[u]);
+        const uint32_t a3 = f16_pair_dm(q58, 0x7362, dg8[u], mg8[u]);
+        mma_step<NT>(acc, xsc, s, lane, a0, a1, a2, a3);
+    }
+}
+
+// Q2_K, lane (g,t): part 0 / 1 = the 2-bit q of weights 64t.. of row g / g+8
+// (word w, byte c, bits 2s'.. = weight 4(4w + s') + c), the four scale bytes
+// of its sub-blocks per row at 1024 + 8 * lane, d and dmin per row at 1280.
+struct RawQ2K { uint4 q[2]; uint2 sc; uint32_t dm, dm8; };
+__device__ __forceinline__ void load_raw(RawQ2K &r, const uint8_t *T, int lane) {
+    r.q[0] = ldq128(T + lane * 16);
+    r.q[1] = ldq128(T + 512 + lane * 16);
+    r.sc = ldq64(T + 1024 + lane * 8);
+    const int g = lane >> 2;
+    r.dm = ldh32(T + 1280 + 4 * g);
+    r.dm8 = ldh32(T + 1280 + 4 * (g + 8));
+}
+template <int NT>
+__device__ __forceinline__ void compute(const RawQ2K &r, const uint8_t *xc, int M, float (&acc)[NT][4], int lane,
+                                        const uint4 *, const uint4 *) {
+    const XF xsc = make_xf<NT>(xc, M, lane);
+    const float d = __half2float(__ushort_as_half((unsigned short)(r.dm & 0xFFFF)));
+    const float dmin = __half2float(__ushort_as_half((unsigned short)(r.dm >> 16)));
+    const float d8 = __half2float(__ushort_as_half((unsigned short)(r.dm8 & 0xFFFF)));
+    const float dmin8 = __half2float(__ushort_as_half((unsigned short)(r.dm8 >> 16)));
+#pragma unroll
+    for (int k = 0; k < 4; k++) {                                          // sub-block 4t + k: steps 4k..4k+3
+        const int sc = (int)((r.sc.x >> (8 * k)) & 0xFF), sc8 = (int)((r.sc.y >> (8 * k)) & 0xFF);
+        const uint32_t dd = f16x2_bcast(d * (float)(sc & 15)), mm = f16x2_bcast(-(dmin * (float)(sc >> 4)));
+        const uint32_t dd8 = f16x2_bcast(d8 * (float)(sc8 & 15)), mm8 = f16x2_bcast(-(dmin8 * (float)(sc8 >> 4)));
+#pragma unroll
+        for (int sp = 0; sp < 4; sp++) {
+            const int s = 4 * k + sp;
+            const uint32_t qg = (wsel(r.q[0], k) >> (2 * sp)) & 0x03030303u;
+            const uint32_t qg8 = (wsel(r.q[1], k) >> (2 * sp)) & 0x03030303u;
+            const uint32_t a0 = f16_pair_dm(qg, 0x5140, dd, mm), a2 = f16_pair_dm(qg, 0x7362, dd, mm);
+            const uint32_t a1 = f16_pair_dm(qg8, 0x5140, dd8, mm8), a3 = f16_pair_dm(qg8, 0x7362, dd8, mm8);
+            mma_step<NT>(acc, xsc, s, lane, a0, a1, a2, a3);
+        }
     }
 }
 
@@ -719,6 +838,8 @@ __device__ __forceinline__ void compute(const RawIQ1 &r, const uint8_t *xc, int 
 template <int TYPE> struct RawOf;
 template <> struct RawOf<EF_Q8_0> { using T = RawQ8; };
 template <> struct RawOf<EF_Q4_0> { using T = RawQ40; };
+template <> struct RawOf<EF_Q5_K> { using T = RawQ5K; };
+template <> struct RawOf<EF_Q2_K> { using T = RawQ2K; };
 template <> struct RawOf<EF_Q4_K> { using T = RawQ4K; };
 template <> struct RawOf<EF_Q6_K> { using T = RawQ6K; };
 template <> struct RawOf<EF_IQ2_XXS> { using T = RawIQ2; };
@@ -1374,6 +1495,8 @@ int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight 
     switch (w0->type) {
     case EF_Q8_0: rc = launch_sw<EF_Q8_0>(ctx, a, sw, ws, n, x); break;
     case EF_Q4_0: rc = launch_sw<EF_Q4_0>(ctx, a, sw, ws, n, x); break;
+    case EF_Q5_K: rc = launch_sw<EF_Q5_K>(ctx, a, sw, ws, n, x); break;
+    case EF_Q2_K: rc = launch_sw<EF_Q2_K>(ctx, a, sw, ws, n, x); break;
     case EF_Q4_K: rc = launch_sw<EF_Q4_K>(ctx, a, sw, ws, n, x); break;
     case EF_Q6_K: rc = launch_sw<EF_Q6_K>(ctx, a, sw, ws, n, x); break;
     case EF_IQ2_XXS: rc = launch_sw<EF_IQ2_XXS>(ctx, a, sw, ws, n, x); break;
@@ -1408,6 +1531,8 @@ static size_t gemv_xfrag_bytes(int type, int64_t nchunks, int M) {
     switch (type) {
     case EF_Q8_0: fb = (size_t)f16_xbytes<EF_Q8_0>(M); break;
     case EF_Q4_0: fb = (size_t)f16_xbytes<EF_Q4_0>(M); break;
+    case EF_Q5_K: fb = (size_t)f16_xbytes<EF_Q5_K>(M); break;
+    case EF_Q2_K: fb = (size_t)f16_xbytes<EF_Q2_K>(M); break;
     case EF_Q4_K: fb = (size_t)i8_xbytes<EF_Q4_K>(M); break;
     case EF_Q6_K: fb = (size_t)i8_xbytes<EF_Q6_K>(M); break;
     case EF_IQ2_XXS: fb = (size_t)f16_xbytes<EF_IQ2_XXS>(M); break;

@@ -20,9 +20,9 @@ import numpy as np
 
 from ._lib import TYPE_IDS, TYPE_NAMES
 
-BLOCKS = {"Q4_0": (32, 18), "Q8_0": (32, 34), "Q4_K": (256, 144), "Q6_K": (256, 210),
-          "IQ2_XXS": (256, 66), "IQ1_S": (256, 50)}
-HOT_TYPES = ("Q8_0", "Q4_0", "Q4_K", "Q6_K", "IQ2_XXS", "IQ1_S")
+BLOCKS = {"Q4_0": (32, 18), "Q8_0": (32, 34), "Q2_K": (256, 84), "Q4_K": (256, 144), "Q5_K": (256, 176),
+          "Q6_K": (256, 210), "IQ2_XXS": (256, 66), "IQ1_S": (256, 50)}
+HOT_TYPES = ("Q8_0", "Q4_0", "Q2_K", "Q4_K", "Q5_K", "Q6_K", "IQ2_XXS", "IQ1_S")
 
 
 def type_name(t) -> str:
@@ -63,9 +63,12 @@ def synth(t, rows: int, k: int, seed: int = 0) -> np.ndarray:
         raw[:, 2:] = rng.integers(-127, 128, size=(n, 32), dtype=np.int8).view(np.uint8)
     elif name == "Q4_0":
         raw[:, 0:2] = _f16(rng, 1e-3, 4e-3, n)
-    elif name == "Q4_K":
+    elif name in ("Q4_K", "Q5_K"):
         raw[:, 0:2] = _f16(rng, 1e-4, 5e-4, n)
         raw[:, 2:4] = _f16(rng, 1e-4, 5e-4, n)
+    elif name == "Q2_K":                  # d, dmin at the end of the block
+        raw[:, 80:82] = _f16(rng, 1e-4, 5e-4, n)
+        raw[:, 82:84] = _f16(rng, 1e-4, 5e-4, n)
     elif name == "Q6_K":
         raw[:, 192:208] = rng.integers(-64, 64, size=(n, 16), dtype=np.int8).view(np.uint8)
         raw[:, 208:210] = _f16(rng, 1e-4, 5e-4, n)

@@ -57,7 +57,7 @@ enum {
 
 /* GGUF tensor types (ggml ids, js/gguf.js:48-64). */
 enum {
-    EF_F32 = 0, EF_F16 = 1, EF_Q4_0 = 2, EF_Q8_0 = 8, EF_Q4_K = 12, EF_Q6_K = 14,
+    EF_F32 = 0, EF_F16 = 1, EF_Q4_0 = 2, EF_Q8_0 = 8, EF_Q2_K = 10, EF_Q4_K = 12, EF_Q5_K = 13, EF_Q6_K = 14,
     EF_IQ2_XXS = 16, EF_IQ1_S = 19
 };
 

@@ -22,11 +22,11 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "liboracle.so")
 
 # ggml type ids (reference js/gguf.js:48-64)
-F32, F16, Q4_0, Q8_0, Q4_K, Q6_K, IQ2_XXS, IQ1_S = 0, 1, 2, 8, 12, 14, 16, 19
-TYPE_IDS = {"F32": F32, "F16": F16, "Q4_0": Q4_0, "Q8_0": Q8_0, "Q4_K": Q4_K,
+F32, F16, Q4_0, Q8_0, Q2_K, Q4_K, Q5_K, Q6_K, IQ2_XXS, IQ1_S = 0, 1, 2, 8, 10, 12, 13, 14, 16, 19
+TYPE_IDS = {"F32": F32, "F16": F16, "Q4_0": Q4_0, "Q8_0": Q8_0, "Q2_K": Q2_K, "Q4_K": Q4_K, "Q5_K": Q5_K,
             "Q6_K": Q6_K, "IQ2_XXS": IQ2_XXS, "IQ1_S": IQ1_S}
-BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q4_K: (256, 144), Q6_K: (256, 210),
-         IQ2_XXS: (256, 66), IQ1_S: (256, 50)}
+BLOCK = {Q4_0: (32, 18), Q8_0: (32, 34), Q2_K: (256, 84), Q4_K: (256, 144), Q5_K: (256, 176),
+         Q6_K: (256, 210), IQ2_XXS: (256, 66), IQ1_S: (256, 50)}
 
 _lib = None
 

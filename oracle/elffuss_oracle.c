@@ -17,6 +17,8 @@
  *   IQ2_XXS(16) 256 w,  66 B: f16 d | 8 x (u32 a0, u32 a1)            kernels.wgsl.js:368-396
  *   IQ1_S  (19) 256 w,  50 B: f16 d | qs[32] | u16 qh[8]              kernels.wgsl.js:805-822
  *   Q4_0    (2)  32 w,  18 B: f16 d | nibbles[16]                     kernels.wgsl.js:176-190
+ *   Q5_K   (13) 256 w, 176 B: f16 d | f16 dmin | u8 sc[12] | qh[32] | qs[128]  kernels.wgsl.js:333-362
+ *   Q2_K   (10) 256 w,  84 B: sc[16] | qs[64] | f16 d | f16 dmin          kernels.wgsl.js:192-217
  *
  * Each dequantised weight is an exact f32 product (f16 scale x small integer),
  * except Q4_K's single rounding in d1*q - m1; the restatement keeps the
@@ -27,8 +29,8 @@
 #include <string.h>
 #include <pthread.h>
 
-enum { OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q8_0 = 8, OR_Q4_K = 12, OR_Q6_K = 14,
-       OR_IQ2_XXS = 16, OR_IQ1_S = 19 };
+enum { OR_F32 = 0, OR_F16 = 1, OR_Q4_0 = 2, OR_Q8_0 = 8, OR_Q2_K = 10, OR_Q4_K = 12, OR_Q5_K = 13,
+       OR_Q6_K = 14, OR_IQ2_XXS = 16, OR_IQ1_S = 19 };
 
 /* f16 -> f32, exact. Restates js/cpu.js:39-44 (deF16) and WGSL unpack2x16float
  * used by load_scale (kernels.wgsl.js:91-93). */
@@ -87,6 +89,8 @@ int or_block_info(int type, int *elems, int *bytes) {
     case OR_Q8_0: *elems = 32; *bytes = 34; return 0;
     case OR_Q4_0: *elems = 32; *bytes = 18; return 0;
     case OR_Q4_K: *elems = 256; *bytes = 144; return 0;
+    case OR_Q5_K: *elems = 256; *bytes = 176; return 0;
+    case OR_Q2_K: *elems = 256; *bytes = 84; return 0;
     case OR_Q6_K: *elems = 256; *bytes = 210; return 0;
     case OR_IQ2_XXS: *elems = 256; *bytes = 66; return 0;
     case OR_IQ1_S: *elems = 256; *bytes = 50; return 0;
@@ -136,6 +140,40 @@ static void dequant_block(int type, const uint8_t *blk, const int8_t *grid, floa
                 /* d1*q is exact, so the only rounding is the subtraction. */
                 out[64 * j + l] = d1 * (float)(q & 0xF) - m1;
                 out[64 * j + 32 + l] = d2 * (float)(q >> 4) - m2;
+            }
+        }
+    } break;
+    case OR_Q5_K: { /* kernels.wgsl.js:333-362: Q4_K plus the fifth bit, qh[l] bit 2j / 2j+1 */
+        float d = or_f16_to_f32(rd16(blk)), dmin = or_f16_to_f32(rd16(blk + 2));
+        const uint8_t *sb = blk + 4, *qh = blk + 16, *qs = blk + 48;
+        for (int j = 0; j < 4; j++) {
+            int sc1, m1i, sc2, m2i;
+            scale_min_k4(sb, 2 * j, &sc1, &m1i);
+            scale_min_k4(sb, 2 * j + 1, &sc2, &m2i);
+            float d1 = d * (float)sc1, m1 = dmin * (float)m1i;
+            float d2 = d * (float)sc2, m2 = dmin * (float)m2i;
+            for (int l = 0; l < 32; l++) {
+                uint8_t q = qs[32 * j + l];
+                int a = (q & 0xF) + ((qh[l] >> (2 * j)) & 1 ? 16 : 0);
+                int b = (q >> 4) + ((qh[l] >> (2 * j + 1)) & 1 ? 16 : 0);
+                out[64 * j + l] = d1 * (float)a - m1;
+                out[64 * j + 32 + l] = d2 * (float)b - m2;
+            }
+        }
+    } break;
+    case OR_Q2_K: { /* kernels.wgsl.js:192-217: 2-bit q, 4+4-bit (scale, min) per 16 weights */
+        float d = or_f16_to_f32(rd16(blk + 80)), dmin = or_f16_to_f32(rd16(blk + 82));
+        for (int n = 0; n < 2; n++) {
+            const uint8_t *qs = blk + 16 + 32 * n;
+            for (int j = 0; j < 4; j++) {
+                uint8_t sca = blk[8 * n + 2 * j], scb = blk[8 * n + 2 * j + 1];
+                float dl1 = d * (float)(sca & 0xF), ml1 = dmin * (float)(sca >> 4);
+                float dl2 = d * (float)(scb & 0xF), ml2 = dmin * (float)(scb >> 4);
+                float *o = out + 128 * n + 32 * j;
+                for (int l = 0; l < 16; l++) {
+                    o[l] = dl1 * (float)((qs[l] >> (2 * j)) & 3) - ml1;
+                    o[16 + l] = dl2 * (float)((qs[16 + l] >> (2 * j)) & 3) - ml2;
+                }
             }
         }
     } break;

@@ -29,7 +29,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 
 TYPES = {"Q8_0": (8, 32, 34), "Q4_K": (12, 256, 144), "Q6_K": (14, 256, 210),
-         "IQ2_XXS": (16, 256, 66), "IQ1_S": (19, 256, 50), "Q4_0": (2, 32, 18)}
+         "IQ2_XXS": (16, 256, 66), "IQ1_S": (19, 256, 50), "Q4_0": (2, 32, 18),
+         "Q5_K": (13, 256, 176), "Q2_K": (10, 256, 84)}      # (appended: earlier draws unchanged)
 
 
 def ref_grid(path: str, name: str) -> np.ndarray:
@@ -61,6 +62,12 @@ def blocks(name: str, nb: int, rng) -> np.ndarray:
     elif name == "Q4_K":        # d, dmin U[1e-4, 5e-4]; sc/m and nibbles uniform (config 1)
         raw[:, 0:2] = f16_bytes(rng.uniform(1e-4, 5e-4, nb))
         raw[:, 2:4] = f16_bytes(rng.uniform(1e-4, 5e-4, nb))
+    elif name == "Q5_K":        # as Q4_K
+        raw[:, 0:2] = f16_bytes(rng.uniform(1e-4, 5e-4, nb))
+        raw[:, 2:4] = f16_bytes(rng.uniform(1e-4, 5e-4, nb))
+    elif name == "Q2_K":        # d, dmin (at the end of the block) U[1e-4, 5e-4]
+        raw[:, 80:82] = f16_bytes(rng.uniform(1e-4, 5e-4, nb))
+        raw[:, 82:84] = f16_bytes(rng.uniform(1e-4, 5e-4, nb))
     elif name == "Q6_K":        # sc int8 U[-64, 63], d U[1e-4, 5e-4] (config 1)
         raw[:, 192:208] = rng.integers(-64, 64, size=(nb, 16)).astype(np.int8).view(np.uint8)
         raw[:, 208:210] = f16_bytes(rng.uniform(1e-4, 5e-4, nb))
@@ -81,11 +88,15 @@ def edge_blocks(name: str) -> np.ndarray:
             b[:192] = (np.arange(192) * 37 + i) & 0xFF
             b[192:208] = np.array([-64, 63, -1, 0, 1, 127, -128, 5] * 2, np.int8).view(np.uint8)
             b[208:210] = np.frombuffer(d.tobytes(), np.uint8)
-        elif name == "Q4_K":
+        elif name == "Q2_K":
+            b[:80] = (np.arange(80) * 41 + 3 * i) & 0xFF
+            b[80:82] = np.frombuffer(d.tobytes(), np.uint8)
+            b[82:84] = np.frombuffer(np.float16(-d if i % 2 else d).tobytes(), np.uint8)
+        elif name in ("Q4_K", "Q5_K"):
             b[0:2] = np.frombuffer(d.tobytes(), np.uint8)
             b[2:4] = np.frombuffer(np.float16(-d if i % 2 else d).tobytes(), np.uint8)
             b[4:16] = [0xFF, 0xC0, 0x3F, 0x80, 0x7F, 0xC1, 0x00, 0xFF, 0xA5, 0x5A, 0xF0, 0x0F]
-            b[16:] = (np.arange(128) * 29 + i) & 0xFF
+            b[16:] = (np.arange(bb - 16) * 29 + i) & 0xFF
         elif name == "Q8_0":
             b[0:2] = np.frombuffer(d.tobytes(), np.uint8)
             b[2:] = np.array([-128, 127, -127, 0, 1, -1] * 6, np.int8)[:32].view(np.uint8)

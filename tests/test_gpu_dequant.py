@@ -12,6 +12,8 @@ SHAPES = {  # rows x k, including ragged rows (not a multiple of 16) and partial
     "Q8_0": [(16, 128), (37, 96), (8192 // 64, 2048), (5, 32 * 7)],
     "Q4_0": [(16, 128), (29, 96), (64, 2048), (3, 32 * 5)],
     "Q4_K": [(16, 256), (33, 768), (64, 4096)],
+    "Q5_K": [(16, 256), (27, 768), (32, 4096)],
+    "Q2_K": [(16, 256), (31, 512), (32, 4096)],
     "Q6_K": [(16, 256), (19, 512), (48, 4096)],
     "IQ2_XXS": [(16, 256), (21, 512)],
     "IQ1_S": [(16, 256), (23, 768)],
@@ -37,7 +39,7 @@ def test_repack_round_trip(ops, t, rows, k):
     np.testing.assert_array_equal(back, raw)
 
 
-@pytest.mark.parametrize("t", ["Q8_0", "Q4_0", "Q4_K", "Q6_K", "IQ2_XXS", "IQ1_S"])
+@pytest.mark.parametrize("t", ["Q8_0", "Q4_0", "Q4_K", "Q5_K", "Q2_K", "Q6_K", "IQ2_XXS", "IQ1_S"])
 def test_golden_blocks_on_gpu(ops, golden, t):
     """The fixture's seeded + edge blocks (negative, subnormal, max scales) as a
     one-row-per-block tensor, decoded on the GPU vs gguf-py's bits."""

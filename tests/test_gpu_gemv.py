@@ -22,7 +22,8 @@ def _check(oracle_mod, t, raw, rows, k, x, y):
 
 
 SHAPES = [("Q8_0", 128, 2048), ("Q8_0", 40, 96), ("Q4_0", 128, 2048), ("Q4_0", 24, 160),
-          ("Q4_K", 256, 1024), ("Q4_K", 36, 4096),
+          ("Q4_K", 256, 1024), ("Q4_K", 36, 4096), ("Q5_K", 128, 1024), ("Q5_K", 21, 2304),
+          ("Q2_K", 128, 1024), ("Q2_K", 19, 2304),
           ("Q6_K", 128, 1024), ("Q6_K", 20, 2304), ("IQ2_XXS", 64, 1024), ("IQ1_S", 64, 1024)]
 
 

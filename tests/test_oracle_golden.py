@@ -10,7 +10,7 @@ import hashlib
 import numpy as np
 import pytest
 
-TYPES = ["Q8_0", "Q4_K", "Q6_K", "IQ2_XXS", "IQ1_S", "Q4_0"]
+TYPES = ["Q8_0", "Q4_K", "Q6_K", "IQ2_XXS", "IQ1_S", "Q4_0", "Q5_K", "Q2_K"]
 
 
 @pytest.mark.parametrize("t", TYPES)
