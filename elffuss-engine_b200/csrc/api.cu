@@ -34,9 +34,9 @@ int check_cuda(ef_ctx *ctx, cudaError_t e, const char *what) {
 int ensure_scratch(ef_ctx *ctx, int slot, size_t bytes, bool zero) {
     if (ctx->scratch_bytes[slot] >= bytes) return EF_OK;
     if (ctx->scratch[slot]) {
-        // the old scratch may still be read by queued work
-        cudaStreamSynchronize(ctx->stream);
-        cudaFree(ctx->scratch[slot]);
+        // Queued work or a CUDA graph captured earlier may still use the old
+        // buffer: it is kept until the context is destroyed.
+        ctx->retired.push_back(ctx->scratch[slot]);
         ctx->scratch[slot] = nullptr;
         ctx->scratch_bytes[slot] = 0;
     }
@@ -98,6 +98,7 @@ int ef_ctx_destroy(ef_ctx *ctx) {
     }
     for (int i = 0; i < ef_ctx::kScratchSlots; i++)
         if (ctx->scratch[i]) cudaFree(ctx->scratch[i]);
+    for (void *p : ctx->retired) cudaFree(p);
     if (ctx->own) cudaStreamDestroy(ctx->own);
     delete ctx;
     return EF_OK;

@@ -41,6 +41,7 @@ struct ef_ctx {
     static constexpr int kScratchSlots = 4;
     void *scratch[kScratchSlots] = {nullptr, nullptr, nullptr, nullptr};
     size_t scratch_bytes[kScratchSlots] = {0, 0, 0, 0};
+    std::vector<void *> retired;      // outgrown scratch buffers, freed with the context
     uint64_t launches = 0;            // kernels this context has launched (diagnostic counter)
     // Programmatic dependent launch: each kernel may be scheduled while the
     // previous one on the stream finishes; it waits for that kernel's results
