@@ -38,7 +38,8 @@ def _write(path, tensors, meta=True, alignment=None):
 
 def _tensors():
     out = []
-    for i, (t, rows, k) in enumerate([("Q8_0", 48, 256), ("Q4_K", 40, 512), ("Q6_K", 16, 256), ("IQ2_XXS", 8, 256)]):
+    for i, (t, rows, k) in enumerate([("Q8_0", 48, 256), ("Q4_K", 40, 512), ("Q6_K", 16, 256), ("IQ2_XXS", 8, 256),
+                                      ("Q4_0", 24, 128), ("Q5_K", 17, 512), ("Q2_K", 9, 256), ("IQ1_S", 5, 256)]):
         out.append((f"blk.{i}.w", t, formats.synth(t, rows, k, seed=i), rows, k))
     return out
 
