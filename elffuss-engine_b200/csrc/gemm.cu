@@ -110,10 +110,16 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
 constexpr uint32_t GM_TMEM_COLS = 512;
 constexpr uint32_t GM_TMEM_A = 256;
 
-__global__ void __launch_bounds__(GM_THREADS, 1)
-    gemm_q8_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
-                     int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
-    constexpr int WRAW = 8 * 2176;                       // 8 rowgroup tiles
+// Weight tile of a rowgroup (16 rows x 128 k) and where its f16 scales start.
+template <int TYPE> struct GmTile;
+template <> struct GmTile<EF_Q8_0> { static constexpr int BYTES = 2176, SC = 2048; };
+template <> struct GmTile<EF_Q4_0> { static constexpr int BYTES = 1152, SC = 1024; };
+
+template <int TYPE>
+__device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+                                          int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
+    constexpr int TB = GmTile<TYPE>::BYTES, SCO = GmTile<TYPE>::SC;
+    constexpr int WRAW = 8 * TB;                         // 8 rowgroup tiles
     constexpr int XBYTES = GM_BN * 128;                  // one 64-k box of 256 rows x 128 B
     constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(GM_BN >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -170,9 +176,9 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 const int sw = kk % GM_SW;
                 if (kk >= GM_SW) ok = mbar_wait(&wempty[sw], ((kk / GM_SW) - 1) & 1);
                 if (!ok) return;
-                mbar_expect_tx(&wfull[sw], (uint32_t)(nrg * 2176));
+                mbar_expect_tx(&wfull[sw], (uint32_t)(nrg * TB));
                 for (int i = 0; i < nrg; i++)
-                    bulk_g2s(ws + sw * WRAW + i * 2176, W + ((rb * 8 + i) * nchunks + kk) * 2176, 2176, &wfull[sw]);
+                    bulk_g2s(ws + sw * WRAW + i * TB, W + ((rb * 8 + i) * nchunks + kk) * TB, TB, &wfull[sw]);
                 wi++;
             };
             for (int kk = 0; kk < GM_SW && kk < nk && ok; kk++) issue_w(kk);
@@ -237,16 +243,23 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
             if (ok && kk >= 2) ok = mbar_wait(&aempty[b], ((kk >> 1) - 1) & 1);
             if (!ok) break;
             tc_fence_after();
-            const uint8_t *T = ws + sw * WRAW + rg_in * 2176;
+            const uint8_t *T = ws + sw * WRAW + rg_in * TB;
+            // Q8_0: block t = parts 2hs, 2hs+1 of lane 4g+t; Q4_0: part hs of
+            // lane 4g+t (word j = weights 8j..8j+7 at nibble slots 0,16,4,20,...)
             uint4 q0[4], q1[4];
             uint32_t sc[4];
 #pragma unroll
             for (int i = 0; i < 4; i++) {
                 const int t = (i + (lane >> 1)) & 3;
                 if (have) {
-                    q0[i] = *reinterpret_cast<const uint4 *>(T + (2 * hs) * 512 + (4 * g + t) * 16);
-                    q1[i] = *reinterpret_cast<const uint4 *>(T + (2 * hs + 1) * 512 + (4 * g + t) * 16);
-                    sc[i] = *reinterpret_cast<const uint32_t *>(T + 2048 + (4 * g + t) * 4);
+                    if (TYPE == EF_Q8_0) {
+                        q0[i] = *reinterpret_cast<const uint4 *>(T + (2 * hs) * 512 + (4 * g + t) * 16);
+                        q1[i] = *reinterpret_cast<const uint4 *>(T + (2 * hs + 1) * 512 + (4 * g + t) * 16);
+                    } else {
+                        q0[i] = *reinterpret_cast<const uint4 *>(T + hs * 512 + (4 * g + t) * 16);
+                        q1[i] = q0[i];
+                    }
+                    sc[i] = *reinterpret_cast<const uint32_t *>(T + SCO + (4 * g + t) * 4);
                 } else {
                     q0[i] = q1[i] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);
                     sc[i] = 0;
@@ -266,12 +279,22 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
                 if (stg == 2) { a0 = q0[(t + 2) & 3]; a1 = q1[(t + 2) & 3]; sct = sc[(t + 2) & 3]; }
                 if (stg == 3) { a0 = q0[(t + 1) & 3]; a1 = q1[(t + 1) & 3]; sct = sc[(t + 1) & 3]; }
                 const uint32_t dd = prmt(sct, 0, hs ? 0x3232 : 0x1010);   // (d, d)
-                const uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
                 uint32_t h[16];
+                if (TYPE == EF_Q8_0) {
+                    const uint32_t w[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
 #pragma unroll
-                for (int j = 0; j < 8; j++) {   // 4 quants (biased by 128) -> 2 x half2 f16(d*q)
-                    h[2 * j] = hmul2u(hsub2u(prmt(w[j], 0x64646464u, 0x5140), 0x64806480u), dd);
-                    h[2 * j + 1] = hmul2u(hsub2u(prmt(w[j], 0x64646464u, 0x7362), 0x64806480u), dd);
+                    for (int j = 0; j < 8; j++) {   // 4 quants (biased by 128) -> 2 x half2 f16(d*q)
+                        h[2 * j] = hmul2u(hsub2u(prmt(w[j], 0x64646464u, 0x5140), 0x64806480u), dd);
+                        h[2 * j + 1] = hmul2u(hsub2u(prmt(w[j], 0x64646464u, 0x7362), 0x64806480u), dd);
+                    }
+                } else {
+                    const uint32_t w[4] = {a0.x, a0.y, a0.z, a0.w};
+#pragma unroll
+                    for (int j = 0; j < 4; j++)     // 8 nibbles -> 4 x half2 f16(d*(q-8)), k order
+#pragma unroll
+                        for (int u = 0; u < 4; u++)
+                            h[4 * j + u] = hmul2u(hsub2u(((w[j] >> (4 * u)) & 0x000F000Fu) | 0x64006400u, 0x64086408u),
+                                                  dd);
                 }
                 tmem_st16(abuf + 16 * t, h);   // k = 32t .. 32t+31 as 16 f16 pairs
             }
@@ -317,6 +340,17 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
 }
 
 // f32 -> f16 activations (round to nearest even), for x given in f32.
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_q8_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+                     int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
+    gemm_body<EF_Q8_0>(xmap, W, rowgroups, nchunks, rows, M, y);
+}
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_q4_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+                     int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
+    gemm_body<EF_Q4_0>(xmap, W, rowgroups, nchunks, rows, M, y);
+}
+
 __global__ void f32_to_f16_kernel(const float *__restrict__ src, __half *__restrict__ dst, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         dst[i] = __float2half_rn(src[i]);
@@ -343,11 +377,12 @@ static EncodeTiledFn encode_fn() {
     return fn;
 }
 
-static size_t gemm_smem() {
-    return 1024 + (size_t)GM_SX * (GM_BN * 128) + (size_t)GM_SW * 8 * 2176 + 256;
+template <int TYPE> static size_t gemm_smem() {
+    return 1024 + (size_t)GM_SX * (GM_BN * 128) + (size_t)GM_SW * 8 * GmTile<TYPE>::BYTES + 256;
 }
 
-static int launch_q8_0(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, float *y) {
+template <int TYPE>
+static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, float *y) {
     EncodeTiledFn enc = encode_fn();
     if (!enc) return set_err(ctx, EF_ERR_CUDA, "gemm: cuTensorMapEncodeTiled unavailable");
     CUtensorMap map;
@@ -359,8 +394,8 @@ static int launch_q8_0(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M,
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return set_err(ctx, EF_ERR_CUDA, "gemm: tensor map encode failed (%d)", (int)cr);
-    auto kern = gemm_q8_0_kernel;
-    const size_t smem = gemm_smem();
+    auto kern = TYPE == EF_Q8_0 ? gemm_q8_0_kernel : gemm_q4_0_kernel;
+    const size_t smem = gemm_smem<TYPE>();
     static unsigned long long configured = 0;
     if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
         if (int rc = check_cuda(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
@@ -375,7 +410,7 @@ static int launch_q8_0(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M,
 }
 
 int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y) {
-    if (w->type == EF_Q8_0 && w->k % 8 == 0) {
+    if ((w->type == EF_Q8_0 || w->type == EF_Q4_0) && w->k % 8 == 0) {
         // tcgen05 path: activations as f16 [M][K] (converted from f32 if needed)
         const __half *xh = (const __half *)x;
         if (x_type == EF_F32) {
@@ -388,7 +423,7 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
             if (int rc = check_cuda(ctx, cudaGetLastError(), "gemm f32->f16")) return rc;
             xh = (const __half *)ctx->scratch[1];
         }
-        return launch_q8_0(ctx, w, xh, M, y);
+        return w->type == EF_Q8_0 ? launch_tc<EF_Q8_0>(ctx, w, xh, M, y) : launch_tc<EF_Q4_0>(ctx, w, xh, M, y);
     }
     // Other types: the token dimension in groups of 16 through the GEMV
     // kernel (same numerics contract: f16 activations, f32 accumulation).
