@@ -1,22 +1,29 @@
 // model.cu -- the non-matmul operations of a decoder step (sm_100a), for the
-// synthetic LFM3-shaped decoder that drives the GEMV hot path end to end.
+// synthetic LFM3- and Llama-shaped decoders that drive the GEMV / GEMM hot
+// path end to end.
 //
 // Each restates one operation of the reference's forward (js/model.js,
-// js/kernels.nn.wgsl.js, js/kernels.model.wgsl.js, js/kernels.ssm.wgsl.js):
+// js/kernels.nn.wgsl.js, js/kernels.model.wgsl.js, js/kernels.ssm.wgsl.js,
+// js/kernels.topk.wgsl.js):
 //   rmsnorm            y = x * rsqrt(mean(x^2) + eps) * w     (kernels.nn.wgsl.js:46-80)
-//   norm_add_norm      x += rmsnorm(o) * w_post; n = rmsnorm(x) * w_next
+//   norm_add_norm      x += rmsnorm(o) * w_post (or += o); n = rmsnorm(x) * w_next
 //                      (post-norm + residual + next norm, model.js:635-664)
 //   shortconv          B|C|x split, B*x, causal depthwise conv with state,
 //                      C*y (model.js:758-794, kernels.model.wgsl.js:45-86,
 //                      kernels.ssm.wgsl.js:64-92)
-//   qk_norm_rope_cache per-head RMSNorm of q and k, NEOX RoPE, k and v into
-//                      the cache at the current position (model.js:853-945,
-//                      kernels.nn.wgsl.js:87-139)
-//   attn_decode        softmax(q.k / sqrt(D)) with causal + window mask, times
+//   rope_cache         optional per-head RMSNorm of q and k, NEOX or NORM RoPE,
+//                      k and v into the caches at each row's position
+//                      (model.js:853-945, kernels.nn.wgsl.js:87-139)
+//   attention          softmax(q.k / sqrt(D)) with causal + window mask, times
 //                      v, times sigmoid(per-head gate) (kernels.nn.wgsl.js:
-//                      141-200, kernels.model.wgsl.js:89-105)
-//   argmax_step        greedy token, strict '>' so the lowest index wins ties
-//                      (sample.js:95-99); advances the device-side position
+//                      141-200, kernels.model.wgsl.js:89-105): split over the
+//                      keys for one new token per sequence, one CTA per query
+//                      row for a prompt
+//   argmax             greedy token, strict '>' so the lowest index wins ties
+//                      (sample.js:95-99); advances the device-side position;
+//                      per-shard pairs and their selection for a sharded head
+//   topk               the sampler's candidates, exactly (kernels.topk.wgsl.js)
+//   swiglu             g * sigmoid(g) * u for the prompt's FFN
 // Positions and tokens live in device memory, so one decode step can be
 // captured as a CUDA graph and replayed with no host round trip.
 #include <cuda_runtime.h>
