@@ -14,7 +14,7 @@ are therefore:
   BASELINE.json distributions plus hand-made edge blocks;
 * small matrix products computed in numpy f64 from those gguf-py decodes.
 
-Usage:  python tests/golden/make_golden.py [--reference PATH]
+Usage:  python tests/golden/make_golden.py --reference PATH
 Writes: tests/golden/golden.npz
 """
 from __future__ import annotations
@@ -109,7 +109,7 @@ def edge_blocks(name: str) -> np.ndarray:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="the reference checkout (for js/quant-tables.js)")
     args = ap.parse_args()
     import gguf.quants as gq
     from gguf.constants import GGMLQuantizationType as GT
