@@ -77,6 +77,7 @@ _SIGS = {
     "ef_attn_decode": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "ef_argmax_step": ([_P, _P, _I, _P, _P, _P, _I, _I], _I),
     "ef_ctx_set_pdl": ([_P, _I], _I),
+    "ef_gather_rmsnorm": ([_P, _P, _P, _I, _P, ctypes.c_float, _P, _P], _I),
     "ef_argmax_rows": ([_P, _P, _I, _I, _P, _P, _P, _I, _I], _I),
     "ef_argmax_partial": ([_P, _P, _I, _I, _I, _P], _I),
     "ef_argmax_select": ([_P, _P, _I, _I, _P, _P, _P, _I, _I], _I),

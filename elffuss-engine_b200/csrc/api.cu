@@ -336,6 +336,14 @@ int ef_gather(ef_ctx *ctx, const ef_weight *w, const int *dev_ids, int tokens, f
     return launch_gather(ctx, w, dev_ids, tokens, out);
 }
 
+int ef_gather_rmsnorm(ef_ctx *ctx, const ef_weight *w, const int *dev_ids, int tokens, const float *w_norm, float eps,
+                      float *x, float *nrm) {
+    if (!ctx || !w || !dev_ids || !w_norm || !x || !nrm) return EF_ERR_INVALID;
+    if (tokens < 1 || tokens > 65535) return set_err(ctx, EF_ERR_SHAPE, "gather_rmsnorm: tokens=%d", tokens);
+    if (int rc = use_device(ctx)) return rc;
+    return launch_gather_norm(ctx, w, dev_ids, tokens, w_norm, eps, x, nrm);
+}
+
 static int check_gemv(ef_ctx *ctx, const ef_weight *w, const float *x, int M, const void *y) {
     if (!w || !x || !y) return set_err(ctx, EF_ERR_INVALID, "gemv: null argument");
     if (M < 1) return set_err(ctx, EF_ERR_SHAPE, "gemv: M=%d < 1", M);

@@ -80,6 +80,8 @@ int launch_repack(ef_ctx *ctx, int type, const uint8_t *dev_gguf, int64_t rows, 
 int launch_unpack(ef_ctx *ctx, const ef_weight *w, uint8_t *dev_gguf);
 int launch_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows, float *out);
 int launch_gather(ef_ctx *ctx, const ef_weight *w, const int *ids, int tokens, float *out);
+int launch_gather_norm(ef_ctx *ctx, const ef_weight *w, const int *ids, int tokens, const float *wn, float eps,
+                       float *x, float *nrm);
 
 // model.cu / comm.cu: a row of n floats per CTA of T = min(256, n/4) threads
 // with V float4 each, n = 4 * T * V, V in {1, 2, 4, 8}; 0 when n has no such

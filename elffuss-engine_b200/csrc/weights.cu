@@ -108,6 +108,45 @@ __global__ void gather_kernel(int type, const uint8_t *__restrict__ src, const i
     }
 }
 
+// F2 (js/ops.fusion.js:152-165, kernels.fusion.wgsl.js:143-200): CTA per
+// token: the embedding row as gather_kernel decodes it (same blocks, same
+// bits) into shared memory and x, then nrm = x * rsqrt(mean(x^2) + eps) * w.
+__global__ void gather_norm_kernel(int type, const uint8_t *__restrict__ src, const int *__restrict__ ids,
+                                   int64_t rows, int64_t bpr, int64_t nchunks, int bpc, int be, int tile_bytes,
+                                   int64_t k, const float *__restrict__ wn, float eps, float *__restrict__ x,
+                                   float *__restrict__ nrm) {
+    pdl_trigger();
+    pdl_wait();
+    extern __shared__ float rowbuf[];
+    __shared__ float red[32];
+    const int8_t *grid = type == EF_IQ2_XXS ? g_grid_iq2xxs_i8 : g_grid_iq1s_i8;
+    const int t = blockIdx.x;
+    const int64_t row = ids[t];
+    const bool valid = row >= 0 && row < rows;
+    for (int64_t b = threadIdx.x; b < bpr; b += blockDim.x) {
+        float *o = rowbuf + b * be;
+        if (!valid) {
+            for (int j = 0; j < be; j++) o[j] = 0.f;
+            continue;
+        }
+        const int64_t rg = row / RG_ROWS, c = b / bpc;
+        const uint8_t *T = src + (rg * nchunks + c) * tile_bytes;
+        uint8_t blk[256];
+        float v[256];
+        gather_block(type, T, (int)(row % RG_ROWS), (int)(b % bpc), blk);
+        decode_block(type, blk, grid, v);
+        for (int j = 0; j < be; j++) o[j] = v[j];
+    }
+    __syncthreads();
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) ss += rowbuf[i] * rowbuf[i];
+    const float scale = rsqrtf(block_sum(ss, red) / (float)k + eps);
+    for (int64_t i = threadIdx.x; i < k; i += blockDim.x) {
+        x[(int64_t)t * k + i] = rowbuf[i];
+        nrm[(int64_t)t * k + i] = rowbuf[i] * scale * wn[i];
+    }
+}
+
 static int grid_for(int64_t total) {
     int64_t g = (total + 255) / 256;
     if (g > 148 * 64) g = 148 * 64;
@@ -151,6 +190,27 @@ int launch_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows,
         w->type, w->dev, row0, nrows, bpr, w->nchunks, bpc, geo.block_bytes, geo.block_elems,
         geo.tile_bytes, w->k, out);
     return check_cuda(ctx, cudaGetLastError(), "dequant launch");
+}
+
+int launch_gather_norm(ef_ctx *ctx, const ef_weight *w, const int *ids, int tokens, const float *wn, float eps,
+                       float *x, float *nrm) {
+    TypeGeo geo;
+    if (!geo_of(w->type, geo)) return set_err(ctx, EF_ERR_TYPE, "gather_rmsnorm: unsupported type %d", w->type);
+    const size_t smem = (size_t)w->k * sizeof(float);
+    if (smem > 200 * 1024) return set_err(ctx, EF_ERR_RANGE, "gather_rmsnorm: row of %lld exceeds shared memory",
+                                          (long long)w->k);
+    static unsigned long long configured = 0;
+    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(gather_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                          200 * 1024), "gather_rmsnorm smem attribute"))
+            return rc;
+        configured |= 1ull << ctx->device;
+    }
+    const int bpc = geo.chunk_k / geo.block_elems;
+    const int64_t bpr = w->k / geo.block_elems;
+    return launch_on(ctx, gather_norm_kernel, tokens, 256, smem, "gather_rmsnorm launch", w->type,
+                     (const uint8_t *)w->dev, ids, w->rows, bpr, w->nchunks, bpc, geo.block_elems, geo.tile_bytes, w->k,
+                     wn, eps, x, nrm);
 }
 
 int launch_gather(ef_ctx *ctx, const ef_weight *w, const int *ids, int tokens, float *out) {

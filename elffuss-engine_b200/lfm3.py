@@ -286,8 +286,8 @@ class LFM3Decoder:
         H, KV = self.Hl, self.KVl
         W, f = self.w, self.f32
         eps = ctypes.c_float(cfg.eps)
-        check(L.ef_gather(h, W["token_embd"].h, _p(self.tok), 1, _p(self.x)), h)
-        check(L.ef_rmsnorm(h, _p(self.x), _p(f["blk.0.attn_norm"]), 1, E, eps, _p(self.nrm)), h)
+        check(L.ef_gather_rmsnorm(h, W["token_embd"].h, _p(self.tok), 1, _p(f["blk.0.attn_norm"]), eps, _p(self.x),
+                                  _p(self.nrm)), h)
         for l in range(cfg.layers):
             p = f"blk.{l}."
             if l in cfg.attn_layers:
@@ -383,8 +383,7 @@ class LFM3Decoder:
                 else:
                     dist.all_reduce(t)
 
-        check(L.ef_gather(h, W["token_embd"].h, _p(ids), T, _p(x)), h)
-        check(L.ef_rmsnorm(h, _p(x), _p(f["blk.0.attn_norm"]), T, E, eps, _p(nrm)), h)
+        check(L.ef_gather_rmsnorm(h, W["token_embd"].h, _p(ids), T, _p(f["blk.0.attn_norm"]), eps, _p(x), _p(nrm)), h)
         for l in range(cfg.layers):
             p = f"blk.{l}."
             if l in cfg.attn_layers:

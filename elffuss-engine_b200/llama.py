@@ -254,8 +254,8 @@ class LlamaDecoder:
         L, cfg, W, f = self.L, self.cfg, self.w, self.f32
         B, E, D = self.B, cfg.hidden, cfg.head_dim
         eps = ctypes.c_float(cfg.eps)
-        check(L.ef_gather(h, W["token_embd"].h, _p(self.tok), B, _p(self.x)), h)
-        check(L.ef_rmsnorm(h, _p(self.x), _p(f["blk.0.attn_norm"]), B, E, eps, _p(self.nrm)), h)
+        check(L.ef_gather_rmsnorm(h, W["token_embd"].h, _p(self.tok), B, _p(f["blk.0.attn_norm"]), eps, _p(self.x),
+                                  _p(self.nrm)), h)
         for l in range(cfg.layers):
             p = f"blk.{l}."
             check(L.ef_gemv_sections(h, _pp([W[p + "attn_q"].h.value, W[p + "attn_k"].h.value]), 2, _p(self.nrm),
@@ -305,8 +305,8 @@ class LlamaDecoder:
         ids_d = ids.to(self.dev, torch.int32)
         pos0 = torch.zeros(1, dtype=torch.int32, device=self.dev)
         gemm = lambda name, xin, out: check(L.ef_gemm(h, W[name].h, _p(xin), EF_F32, T, _p(out), 0), h)
-        check(L.ef_gather(h, W["token_embd"].h, _p(ids_d), T, _p(x)), h)
-        check(L.ef_rmsnorm(h, _p(x), _p(f["blk.0.attn_norm"]), T, E, eps, _p(nrm)), h)
+        check(L.ef_gather_rmsnorm(h, W["token_embd"].h, _p(ids_d), T, _p(f["blk.0.attn_norm"]), eps, _p(x),
+                                  _p(nrm)), h)
         for l in range(cfg.layers):
             p = f"blk.{l}."
             gemm(p + "attn_q", nrm, q)

@@ -157,6 +157,13 @@ EF_API int ef_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nro
  * captured CUDA graph. */
 EF_API int ef_gather(ef_ctx *ctx, const ef_weight *w, const int *dev_ids, int tokens, float *dev_out);
 
+/* ef_gather fused with the first layer's input norm (the reference's fusion
+ * F2, js/ops.fusion.js:152-165): x[t] = the dequantized row ids[t] (the same
+ * bits as ef_gather; zeros outside the rows) and nrm[t] = x[t] *
+ * rsqrt(mean(x[t]^2) + eps) * w_norm. Rows of k <= 51200 floats. */
+EF_API int ef_gather_rmsnorm(ef_ctx *ctx, const ef_weight *w, const int *dev_ids, int tokens, const float *w_norm,
+                             float eps, float *x, float *nrm);
+
 /* Decode GEMV, 1 <= M <= 16 tokens: y[M][rows] = x[M][k] . dequant(W)^T.
  * quant.gemv.matmul / quant.matmul for few tokens (js/ops.gemv.js:148-165,
  * js/ops.js:834-837). EF_NOT_APPLICABLE for M > 16. */

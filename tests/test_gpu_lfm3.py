@@ -125,6 +125,24 @@ def test_gather_rows_are_exact_dequant(ops):
     assert np.all(got[4] == 0)                                   # id outside the rows
 
 
+@pytest.mark.parametrize("t", ["Q8_0", "Q4_K", "Q6_K"])
+def test_gather_rmsnorm_equals_gather_then_norm(ops, t):
+    L, h = lib(), ops.ctx.bind()
+    rows, k = 50, 1024
+    raw = formats.synth(t, rows, k, seed=3)
+    w = ops.load_weight(t, raw, rows, k)
+    ids = torch.tensor([4, 49, 0, 60], dtype=torch.int32, device="cuda")
+    wn = torch.rand(k, device="cuda") + 0.5
+    x, nrm = torch.empty(4, k, device="cuda"), torch.empty(4, k, device="cuda")
+    check(L.ef_gather_rmsnorm(h, w.h, P(ids), 4, P(wn), ctypes.c_float(1e-5), P(x), P(nrm)), h)
+    xg = torch.empty(4, k, device="cuda")
+    check(L.ef_gather(h, w.h, P(ids), 4, P(xg)), h)
+    assert torch.equal(x, xg)                                   # the same bits as the gather
+    ref = rmsnorm(xg.double().cpu().numpy(), wn.double().cpu().numpy(), 1e-5)
+    assert np.allclose(nrm.cpu().numpy()[:3], ref[:3], rtol=2e-5, atol=2e-6)
+    assert torch.all(nrm[3] == 0)
+
+
 def test_small_decoder_greedy_tokens_match_oracle(ops):
     cfg = LFM3Config(**SMALL)
     w = synth_weights(cfg, seed=1)
