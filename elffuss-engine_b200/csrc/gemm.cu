@@ -38,7 +38,6 @@ namespace ef {
 
 constexpr int GM_BM = 128;     // weight rows per CTA tile (MMA M)
 constexpr int GM_BN = 256;     // tokens per CTA tile (MMA N)
-constexpr int GM_BKW = 128;    // k per weight stage (one Q8_0 rowgroup tile)
 constexpr int GM_BKX = 64;     // k per activation stage (one 128-byte swizzle atom)
 constexpr int GM_SW = 4;       // weight stages
 constexpr int GM_SX = 4;       // activation stages
@@ -114,11 +113,15 @@ constexpr uint32_t GM_TMEM_A = 256;
 template <int TYPE> struct GmTile;
 template <> struct GmTile<EF_Q8_0> { static constexpr int BYTES = 2176, SC = 2048; };
 template <> struct GmTile<EF_Q4_0> { static constexpr int BYTES = 1152, SC = 1024; };
+template <> struct GmTile<EF_Q4_K> { static constexpr int BYTES = 2304, SC = 2048; };   // SC: row headers
+// k per weight tile (one chunk), activation boxes per tile, tensor-memory columns per A buffer
+template <int TYPE> constexpr int gm_kw() { return TYPE == EF_Q4_K ? 256 : 128; }
 
 template <int TYPE>
 __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                                           int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
     constexpr int TB = GmTile<TYPE>::BYTES, SCO = GmTile<TYPE>::SC;
+    constexpr int KW = gm_kw<TYPE>(), NBOX = KW / GM_BKX, ACOLS = KW / 2;
     constexpr int WRAW = 8 * TB;                         // 8 rowgroup tiles
     constexpr int XBYTES = GM_BN * 128;                  // one 64-k box of 256 rows x 128 B
     constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(GM_BN >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
@@ -183,12 +186,12 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             };
             for (int kk = 0; kk < GM_SW && kk < nk && ok; kk++) issue_w(kk);
             for (int kk = 0; kk < nk && ok; kk++) {
-                for (int h = 0; h < 2 && ok; h++) {
-                    const int xsi = 2 * kk + h, sx = xsi % GM_SX;
+                for (int h = 0; h < NBOX && ok; h++) {
+                    const int xsi = NBOX * kk + h, sx = xsi % GM_SX;
                     if (xsi >= GM_SX) ok = mbar_wait(&xempty[sx], ((xsi / GM_SX) - 1) & 1);
                     if (!ok) break;
                     mbar_expect_tx(&xfull[sx], XBYTES);
-                    tma_2d(xs + sx * XBYTES, &xmap, kk * GM_BKW + h * GM_BKX, n0, &xfull[sx]);
+                    tma_2d(xs + sx * XBYTES, &xmap, kk * KW + h * GM_BKX, n0, &xfull[sx]);
                     xi++;
                 }
                 if (ok && kk + GM_SW < nk) issue_w(kk + GM_SW);
@@ -207,9 +210,9 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                 ok = mbar_wait(&afull[b], (kk >> 1) & 1);
                 if (!ok) break;
                 tc_fence_after();
-                const uint32_t abuf = tmem + GM_TMEM_A + 64 * b;
-                for (int h = 0; h < 2 && ok; h++) {
-                    const int xsi = 2 * kk + h, sx = xsi % GM_SX;
+                const uint32_t abuf = tmem + GM_TMEM_A + ACOLS * b;
+                for (int h = 0; h < NBOX && ok; h++) {
+                    const int xsi = NBOX * kk + h, sx = xsi % GM_SX;
                     ok = mbar_wait(&xfull[sx], (xsi / GM_SX) & 1);
                     if (!ok) break;
                     tc_fence_after();
@@ -244,6 +247,67 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             if (!ok) break;
             tc_fence_after();
             const uint8_t *T = ws + sw * WRAW + rg_in * TB;
+            if constexpr (TYPE == EF_Q4_K) {
+                // Row r: header (d, dmin, scale_min_k4 bytes) at 2048 + 16 rl; the
+                // qs bytes [4t, 4t+4) and [16+4t, 16+4t+4) of group j in lane
+                // 4g+t's part 2hs + (j>>1) at offset 8(j&1). Low nibbles of group
+                // j are k = 64j + l (sub-block 2j), high nibbles k = 64j + 32 + l.
+                uint4 hdr = make_uint4(0, 0, 0, 0);
+                uint2 pc[4][4];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+#pragma unroll
+                    for (int tt = 0; tt < 4; tt++)
+                        pc[j][tt] = have ? *reinterpret_cast<const uint2 *>(T + (2 * hs + (j >> 1)) * 512 +
+                                                                           (4 * g + tt) * 16 + 8 * (j & 1))
+                                         : make_uint2(0, 0);
+                if (have) hdr = *reinterpret_cast<const uint4 *>(T + SCO + 16 * rl);
+                mbar_arrive(&wempty[sw]);          // raw tile consumed (in registers)
+                const uint32_t abuf = tmem + tlane + GM_TMEM_A + ACOLS * b;
+                const uint32_t hw[4] = {hdr.x, hdr.y, hdr.z, hdr.w};
+                auto hbyte = [&](int i) { return (int)((hw[i >> 2] >> (8 * (i & 3))) & 0xFF); };
+                const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
+                const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {           // u = 0: sub-block 2j (low nibbles), 1: 2j+1
+                        const int sb = 2 * j + u;
+                        int sc, mn;
+                        if (sb < 4) {
+                            sc = hbyte(4 + sb) & 63;
+                            mn = hbyte(8 + sb) & 63;
+                        } else {
+                            sc = (hbyte(8 + sb) & 0xF) | ((hbyte(sb) >> 6) << 4);
+                            mn = (hbyte(8 + sb) >> 4) | ((hbyte(4 + sb) >> 6) << 4);
+                        }
+                        const __half dh = __float2half_rn(d * (float)sc), mh = __float2half_rn(-(dmin * (float)mn));
+                        const uint32_t d2 = (uint32_t)__half_as_ushort(dh) * 0x10001u;
+                        const uint32_t m2 = (uint32_t)__half_as_ushort(mh) * 0x10001u;
+                        uint32_t h[16];
+#pragma unroll
+                        for (int tt = 0; tt < 4; tt++) {
+#pragma unroll
+                            for (int v = 0; v < 2; v++) {   // v = 0: bytes 4tt.., 1: 16+4tt..
+                                const uint32_t w = pc[j][tt].x * (v == 0) + pc[j][tt].y * (v == 1);
+                                const uint32_t q = u ? (w >> 4) & 0x0F0F0F0Fu : w & 0x0F0F0F0Fu;
+                                const int c = 8 * v + 2 * tt;          // column of k = 64j + 32u + 16v + 4tt
+                                uint32_t r0, r1;
+                                const uint32_t q0 = hsub2u(prmt(q, 0x64646464u, 0x5140), 0x64006400u);
+                                const uint32_t q1 = hsub2u(prmt(q, 0x64646464u, 0x7362), 0x64006400u);
+                                asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r0) : "r"(q0), "r"(d2), "r"(m2));
+                                asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r1) : "r"(q1), "r"(d2), "r"(m2));
+                                h[c] = r0;
+                                h[c + 1] = r1;
+                            }
+                        }
+                        tmem_st16(abuf + 32 * j + 16 * u, h);   // k = 64j + 32u .. +31 as 16 f16 pairs
+                    }
+                }
+                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+                tc_fence_before();
+                mbar_arrive(&afull[b]);
+            } else {
             // Q8_0: block t = parts 2hs, 2hs+1 of lane 4g+t; Q4_0: part hs of
             // lane 4g+t (word j = weights 8j..8j+7 at nibble slots 0,16,4,20,...)
             uint4 q0[4], q1[4];
@@ -266,7 +330,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                 }
             }
             mbar_arrive(&wempty[sw]);          // raw tile consumed (in registers)
-            const uint32_t abuf = tmem + tlane + GM_TMEM_A + 64 * b;
+            const uint32_t abuf = tmem + tlane + GM_TMEM_A + ACOLS * b;
             // tcgen05.st takes one column address for the whole warp: block t
             // is stored by all lanes at once, each picking it from the slot
             // its staggered load order put it in (i = (t - stagger) mod 4).
@@ -301,6 +365,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             mbar_arrive(&afull[b]);
+            }
         }
         // ------------------------------------------------------------ epilogue
         if (ok) ok = mbar_wait(tfull, 0);
@@ -344,6 +409,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_q8_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
     gemm_body<EF_Q8_0>(xmap, W, rowgroups, nchunks, rows, M, y);
+}
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_q4_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+                     int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
+    gemm_body<EF_Q4_K>(xmap, W, rowgroups, nchunks, rows, M, y);
 }
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_q4_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
@@ -394,7 +464,7 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return set_err(ctx, EF_ERR_CUDA, "gemm: tensor map encode failed (%d)", (int)cr);
-    auto kern = TYPE == EF_Q8_0 ? gemm_q8_0_kernel : gemm_q4_0_kernel;
+    auto kern = TYPE == EF_Q8_0 ? gemm_q8_0_kernel : TYPE == EF_Q4_0 ? gemm_q4_0_kernel : gemm_q4_k_kernel;
     const size_t smem = gemm_smem<TYPE>();
     static unsigned long long configured = 0;
     if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
@@ -410,7 +480,7 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
 }
 
 int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y) {
-    if ((w->type == EF_Q8_0 || w->type == EF_Q4_0) && w->k % 8 == 0) {
+    if ((w->type == EF_Q8_0 || w->type == EF_Q4_0 || w->type == EF_Q4_K) && w->k % 8 == 0) {
         // tcgen05 path: activations as f16 [M][K] (converted from f32 if needed)
         const __half *xh = (const __half *)x;
         if (x_type == EF_F32) {
@@ -423,7 +493,9 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
             if (int rc = check_cuda(ctx, cudaGetLastError(), "gemm f32->f16")) return rc;
             xh = (const __half *)ctx->scratch[1];
         }
-        return w->type == EF_Q8_0 ? launch_tc<EF_Q8_0>(ctx, w, xh, M, y) : launch_tc<EF_Q4_0>(ctx, w, xh, M, y);
+        if (w->type == EF_Q8_0) return launch_tc<EF_Q8_0>(ctx, w, xh, M, y);
+        if (w->type == EF_Q4_0) return launch_tc<EF_Q4_0>(ctx, w, xh, M, y);
+        return launch_tc<EF_Q4_K>(ctx, w, xh, M, y);
     }
     // Other types: the token dimension in groups of 16 through the GEMV
     // kernel (same numerics contract: f16 activations, f32 accumulation).

@@ -12,7 +12,8 @@ REL = 1e-3
 
 
 @pytest.mark.parametrize("t,rows,k", [("Q8_0", 256, 512), ("Q8_0", 48, 2048), ("Q4_0", 256, 512),
-                                      ("Q4_0", 40, 2048), ("Q4_K", 128, 1024), ("Q6_K", 64, 512)])
+                                      ("Q4_0", 40, 2048), ("Q4_K", 128, 1024), ("Q4_K", 37, 2304),
+                                      ("Q6_K", 64, 512)])
 @pytest.mark.parametrize("M", [17, 64, 130])
 def test_gemm_f16x_vs_oracle(ops, oracle_mod, t, rows, k, M):
     raw = formats.synth(t, rows, k, seed=M + rows)
@@ -27,11 +28,11 @@ def test_gemm_f16x_vs_oracle(ops, oracle_mod, t, rows, k, M):
 
 
 @pytest.mark.parametrize("t,M,k,rows", [("Q8_0", 512, 2048, 8192), ("Q8_0", 2048, 8192, 2048),
-                                        ("Q4_0", 512, 2048, 8192)])
+                                        ("Q4_0", 512, 2048, 8192), ("Q4_K", 512, 4096, 4096)])
 def test_gemm_config2_vs_torch(ops, t, M, k, rows):
     raw = formats.synth(t, rows, k, seed=2)
     w = ops.load_weight(t, raw, rows, k)
-    wd = ops.dequant(t, w, rows * k // 32).reshape(rows, k)
+    wd = ops.dequant(t, w, rows * k // formats.block_info(t)[0]).reshape(rows, k)
     x = torch.randn(M, k, device="cuda").half()
     y = ops.gemm2.matmul(t, w, x, rows, k, M, x_f16=True)
     ref = x.float() @ wd.half().float().T
