@@ -7,16 +7,18 @@
 // activations, accumulating in f32. Here the same contract runs as a tcgen05
 // pipeline. CTA tile: 128 weight rows (MMA M) x 256 tokens (MMA N).
 //
-//   producer (1 thread):  cp.async.bulk of the repacked weight tiles (8
-//                         rowgroup tiles of 2176 B = 128 rows x 128 k, 4
-//                         stages) and TMA loads (128B swizzle, into this CTA only)
-//                         of the f16 activations, 64 k x 256 tokens per stage
-//                         (4 stages);
+//   producer (1 thread):  per stage of 256 k, one cp.async.bulk per rowgroup
+//                         of its repacked chunk tiles (2 x 2176 B for Q8_0,
+//                         2 x 1152 B for Q4_0, 1 x 2304 B for Q4_K: a
+//                         rowgroup's chunks are contiguous), 2-4 stages as
+//                         shared memory allows; and TMA loads (128B swizzle,
+//                         into this CTA only) of the f16 activations, 64 k x
+//                         256 tokens per box (4 boxes in flight);
 //   dequant (2 x 4 warps): thread = weight row = tensor-memory lane; the two
-//                         groups take alternate weight tiles, expand the 128
-//                         quants of their row to f16(d*q) and store them into
-//                         tensor memory (tcgen05.st), where the MMA reads the
-//                         A operand (one buffer per group);
+//                         groups take alternate stages, expand the 256
+//                         quants of their row to f16 weights and store them
+//                         into tensor memory (tcgen05.st), where the MMA
+//                         reads the A operand (one buffer per group);
 //   MMA (1 thread):       tcgen05.mma.kind::f16, A from tensor memory, B from
 //                         shared memory, M=128 x N=256 x K=16, accumulator in
 //                         tensor memory (256 columns);
@@ -39,7 +41,6 @@ namespace ef {
 constexpr int GM_BM = 128;     // weight rows per CTA tile (MMA M)
 constexpr int GM_BN = 256;     // tokens per CTA tile (MMA N)
 constexpr int GM_BKX = 64;     // k per activation stage (one 128-byte swizzle atom)
-constexpr int GM_SW = 4;       // weight stages
 constexpr int GM_SX = 4;       // activation stages
 constexpr int GM_THREADS = 320;   // producer, MMA, 2 x 4 dequant/epilogue warps
 constexpr uint32_t GM_WAIT_LIMIT = 1u << 24;   // try_wait polls before giving up (about a second)
@@ -104,49 +105,68 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&v)[16
         : "memory");
 }
 
-// Tensor memory: accumulator in columns [0, 256), A buffers in [256, 320) and
-// [320, 384) (128 k of f16 pairs each); 512 columns allocated.
+// Tensor memory: accumulator in columns [0, 256), A buffers in [256, 384) and
+// [384, 512) (256 k of f16 pairs each); 512 columns allocated.
 constexpr uint32_t GM_TMEM_COLS = 512;
 constexpr uint32_t GM_TMEM_A = 256;
+constexpr int GM_KW = 256;              // k per pipeline stage (one A buffer)
+constexpr int GM_SMEM_MAX = 232448;     // dynamic shared memory a CTA may opt into
 
-// Weight tile of a rowgroup (16 rows x 128 k) and where its f16 scales start.
+// Weight tile of a rowgroup (16 rows x CK k, one repacked chunk) and where its
+// scales / row headers start.
 template <int TYPE> struct GmTile;
-template <> struct GmTile<EF_Q8_0> { static constexpr int BYTES = 2176, SC = 2048; };
-template <> struct GmTile<EF_Q4_0> { static constexpr int BYTES = 1152, SC = 1024; };
-template <> struct GmTile<EF_Q4_K> { static constexpr int BYTES = 2304, SC = 2048; };   // SC: row headers
-// k per weight tile (one chunk), activation boxes per tile, tensor-memory columns per A buffer
-template <int TYPE> constexpr int gm_kw() { return TYPE == EF_Q4_K ? 256 : 128; }
+template <> struct GmTile<EF_Q8_0> { static constexpr int BYTES = 2176, SC = 2048, CK = 128; };
+template <> struct GmTile<EF_Q4_0> { static constexpr int BYTES = 1152, SC = 1024, CK = 128; };
+template <> struct GmTile<EF_Q4_K> { static constexpr int BYTES = 2304, SC = 2048, CK = 256; };
+// weight stages (each 8 rowgroups x GM_KW) that fit beside the activation ring, at most 4
+template <int TYPE> __host__ __device__ constexpr int gm_sw() {
+    constexpr int per = 8 * (GM_KW / GmTile<TYPE>::CK) * GmTile<TYPE>::BYTES;
+    constexpr int n = (GM_SMEM_MAX - 1024 - GM_SX * GM_BN * 128 - 256) / per;
+    return n > 4 ? 4 : n;
+}
 
 template <int TYPE>
 __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
-                                          int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
-    constexpr int TB = GmTile<TYPE>::BYTES, SCO = GmTile<TYPE>::SC;
-    constexpr int KW = gm_kw<TYPE>(), NBOX = KW / GM_BKX, ACOLS = KW / 2;
-    constexpr int WRAW = 8 * TB;                         // 8 rowgroup tiles
+                                          int64_t nchunks, int64_t rows, int64_t kdim, int M, float *__restrict__ y) {
+    constexpr int TB = GmTile<TYPE>::BYTES, SCO = GmTile<TYPE>::SC, CK = GmTile<TYPE>::CK;
+    constexpr int CPS = GM_KW / CK;                      // chunks per stage (contiguous per rowgroup)
+    constexpr int SW = gm_sw<TYPE>();
+    constexpr int NBOX = GM_KW / GM_BKX, ACOLS = GM_KW / 2;
+    constexpr int WRAW = 8 * CPS * TB;                   // 8 rowgroups x CPS chunk tiles
     constexpr int XBYTES = GM_BN * 128;                  // one 64-k box of 256 rows x 128 B
     constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(GM_BN >> 3) << 17) | ((uint32_t)(GM_BM >> 4) << 24);
+    static_assert(SW >= 2, "two weight stages at least (one per dequant group)");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled activation tiles
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
     uint8_t *xs = smem;                                  // GM_SX x XBYTES
-    uint8_t *ws = xs + GM_SX * XBYTES;                   // GM_SW x WRAW
-    uint64_t *bars = reinterpret_cast<uint64_t *>(ws + GM_SW * WRAW);
+    uint8_t *ws = xs + GM_SX * XBYTES;                   // SW x WRAW
+    uint64_t *bars = reinterpret_cast<uint64_t *>(ws + SW * WRAW);
     uint64_t *xfull = bars, *xempty = bars + GM_SX;
-    uint64_t *wfull = bars + 2 * GM_SX, *wempty = bars + 2 * GM_SX + GM_SW;
-    uint64_t *afull = bars + 2 * GM_SX + 2 * GM_SW, *aempty = afull + 2, *tfull = afull + 4;
+    uint64_t *wfull = bars + 2 * GM_SX, *wempty = bars + 2 * GM_SX + SW;
+    uint64_t *afull = bars + 2 * GM_SX + 2 * SW, *aempty = afull + 2, *tfull = afull + 4;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(tfull + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t rb = blockIdx.x;                       // 8 rowgroups = 128 rows
     const int n0 = blockIdx.y * GM_BN;                   // first token
-    const int nk = (int)nchunks;                         // weight tiles along k
+    const int nk = (int)((nchunks + CPS - 1) / CPS);     // stages along k
+    // chunks in stage kk, and the activation boxes it needs (none wholly past k)
+    auto chunks_of = [&](int kk) {
+        const int64_t c = nchunks - (int64_t)kk * CPS;
+        return c < CPS ? (int)c : CPS;
+    };
+    auto boxes_of = [&](int kk) {
+        const int64_t b = (kdim - (int64_t)kk * GM_KW + GM_BKX - 1) / GM_BKX;
+        return b < NBOX ? (int)b : NBOX;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < GM_SX; s++) {
             mbar_init(&xfull[s], 1);
             mbar_init(&xempty[s], 1);
         }
-        for (int s = 0; s < GM_SW; s++) {
+        for (int s = 0; s < SW; s++) {
             mbar_init(&wfull[s], 1);
             mbar_init(&wempty[s], 128);
         }
@@ -173,48 +193,54 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
         if (lane == 0) {   // ---------------------------------------- producer
             const int64_t nrg = rowgroups - rb * 8 < 8 ? rowgroups - rb * 8 : 8;
             int wi = 0, xi = 0;                          // copies issued
-            // weight tile kk -> stage kk % GM_SW (refilled once the dequant
-            // warps have read tile kk - GM_SW)
+            // weight stage kk -> slot kk % SW (refilled once the dequant
+            // warps have read stage kk - SW)
             auto issue_w = [&](int kk) {
-                const int sw = kk % GM_SW;
-                if (kk >= GM_SW) ok = mbar_wait(&wempty[sw], ((kk / GM_SW) - 1) & 1);
+                const int sw = kk % SW;
+                if (kk >= SW) ok = mbar_wait(&wempty[sw], ((kk / SW) - 1) & 1);
                 if (!ok) return;
-                mbar_expect_tx(&wfull[sw], (uint32_t)(nrg * TB));
+                const int nc = chunks_of(kk);
+                mbar_expect_tx(&wfull[sw], (uint32_t)(nrg * nc * TB));
                 for (int i = 0; i < nrg; i++)
-                    bulk_g2s(ws + sw * WRAW + i * TB, W + ((rb * 8 + i) * nchunks + kk) * TB, TB, &wfull[sw]);
+                    bulk_g2s(ws + sw * WRAW + i * (CPS * TB), W + ((rb * 8 + i) * nchunks + (int64_t)kk * CPS) * TB,
+                             (uint32_t)(nc * TB), &wfull[sw]);
                 wi++;
             };
-            for (int kk = 0; kk < GM_SW && kk < nk && ok; kk++) issue_w(kk);
+            for (int kk = 0; kk < SW && kk < nk && ok; kk++) issue_w(kk);
             for (int kk = 0; kk < nk && ok; kk++) {
-                for (int h = 0; h < NBOX && ok; h++) {
-                    const int xsi = NBOX * kk + h, sx = xsi % GM_SX;
-                    if (xsi >= GM_SX) ok = mbar_wait(&xempty[sx], ((xsi / GM_SX) - 1) & 1);
+                const int nb = boxes_of(kk);
+                for (int h = 0; h < nb && ok; h++) {
+                    const int sx = xi % GM_SX;
+                    if (xi >= GM_SX) ok = mbar_wait(&xempty[sx], ((xi / GM_SX) - 1) & 1);
                     if (!ok) break;
                     mbar_expect_tx(&xfull[sx], XBYTES);
-                    tma_2d(xs + sx * XBYTES, &xmap, kk * KW + h * GM_BKX, n0, &xfull[sx]);
+                    tma_2d(xs + sx * XBYTES, &xmap, kk * GM_KW + h * GM_BKX, n0, &xfull[sx]);
                     xi++;
                 }
-                if (ok && kk + GM_SW < nk) issue_w(kk + GM_SW);
+                if (ok && kk + SW < nk) issue_w(kk + SW);
             }
             if (!ok) {   // a wait gave up: let this thread's copies still in flight land first
-                for (int j = wi > GM_SW ? wi - GM_SW : 0; j < wi; j++)
-                    mbar_wait_bounded(&wfull[j % GM_SW], (j / GM_SW) & 1, GM_WAIT_LIMIT);
+                for (int j = wi > SW ? wi - SW : 0; j < wi; j++)
+                    mbar_wait_bounded(&wfull[j % SW], (j / SW) & 1, GM_WAIT_LIMIT);
                 for (int j = xi > GM_SX ? xi - GM_SX : 0; j < xi; j++)
                     mbar_wait_bounded(&xfull[j % GM_SX], (j / GM_SX) & 1, GM_WAIT_LIMIT);
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {   // --------------------------------------------- MMA
+            int xc = 0;                              // activation boxes consumed
             for (int kk = 0; kk < nk && ok; kk++) {
                 const int b = kk & 1;
                 ok = mbar_wait(&afull[b], (kk >> 1) & 1);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t abuf = tmem + GM_TMEM_A + ACOLS * b;
-                for (int h = 0; h < NBOX && ok; h++) {
-                    const int xsi = NBOX * kk + h, sx = xsi % GM_SX;
-                    ok = mbar_wait(&xfull[sx], (xsi / GM_SX) & 1);
+                const int nb = boxes_of(kk);
+                for (int h = 0; h < nb && ok; h++) {
+                    const int sx = xc % GM_SX;
+                    ok = mbar_wait(&xfull[sx], (xc / GM_SX) & 1);
                     if (!ok) break;
+                    xc++;
                     tc_fence_after();
                     const uint32_t b0 = smem_u32(xs + sx * XBYTES);
 #pragma unroll
@@ -228,8 +254,8 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
         }
     } else {
         // ------------------------ dequant (2 groups of 4 warps = 128 rows each)
-        // Group G = (warp - 2) / 4 handles the weight tiles kk = G, G+2, ...
-        // (A buffer G). Thread = weight row r = tensor-memory lane: warp w
+        // Group G = (warp - 2) / 4 handles the stages kk = G, G+2, ...
+        // (A buffer G), chunk by chunk. Thread = weight row r = tensor-memory lane: warp w
         // owns lanes 32*(w%4) .. +31. Row r of the tile is row g + 8hs of rowgroup r>>4;
         // its block t (32 quants) is two 16-byte parts of fragment lane 4g+t
         // and its f16 scale sits at 2048 + 4(4g+t) + 2hs. The four blocks are
@@ -241,12 +267,17 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
         const bool have = rb * 8 + rg_in < rowgroups;
         const uint32_t tlane = (uint32_t)(quad * 32) << 16;
         for (int kk = grp; kk < nk && ok; kk += 2) {
-            const int sw = kk % GM_SW, b = kk & 1;
-            ok = mbar_wait(&wfull[sw], (kk / GM_SW) & 1);
+            const int sw = kk % SW, b = kk & 1;
+            ok = mbar_wait(&wfull[sw], (kk / SW) & 1);
             if (ok && kk >= 2) ok = mbar_wait(&aempty[b], ((kk >> 1) - 1) & 1);
             if (!ok) break;
             tc_fence_after();
-            const uint8_t *T = ws + sw * WRAW + rg_in * TB;
+            const int nc = CPS == 1 ? 1 : chunks_of(kk);
+#pragma unroll 1
+            for (int ch = 0; ch < nc; ch++) {
+            const uint8_t *T = ws + sw * WRAW + rg_in * (CPS * TB) + ch * TB;
+            const uint32_t abuf = tmem + tlane + GM_TMEM_A + ACOLS * b + (CK / 2) * ch;
+            const bool last = ch == nc - 1;          // the stage's raw bytes are all in registers after this chunk's loads
             if constexpr (TYPE == EF_Q4_K) {
                 // Row r: header (d, dmin, scale_min_k4 bytes) at 2048 + 16 rl; the
                 // qs bytes [4t, 4t+4) and [16+4t, 16+4t+4) of group j in lane
@@ -262,8 +293,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                                                                            (4 * g + tt) * 16 + 8 * (j & 1))
                                          : make_uint2(0, 0);
                 if (have) hdr = *reinterpret_cast<const uint4 *>(T + SCO + 16 * rl);
-                mbar_arrive(&wempty[sw]);          // raw tile consumed (in registers)
-                const uint32_t abuf = tmem + tlane + GM_TMEM_A + ACOLS * b;
+                if (last) mbar_arrive(&wempty[sw]);          // raw stage consumed (in registers)
                 const uint32_t hw[4] = {hdr.x, hdr.y, hdr.z, hdr.w};
                 auto hbyte = [&](int i) { return (int)((hw[i >> 2] >> (8 * (i & 3))) & 0xFF); };
                 const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
@@ -304,9 +334,6 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                         tmem_st16(abuf + 32 * j + 16 * u, h);   // k = 64j + 32u .. +31 as 16 f16 pairs
                     }
                 }
-                asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
-                tc_fence_before();
-                mbar_arrive(&afull[b]);
             } else {
             // Q8_0: block t = parts 2hs, 2hs+1 of lane 4g+t; Q4_0: part hs of
             // lane 4g+t (word j = weights 8j..8j+7 at nibble slots 0,16,4,20,...)
@@ -329,8 +356,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                     sc[i] = 0;
                 }
             }
-            mbar_arrive(&wempty[sw]);          // raw tile consumed (in registers)
-            const uint32_t abuf = tmem + tlane + GM_TMEM_A + ACOLS * b;
+            if (last) mbar_arrive(&wempty[sw]);   // raw stage consumed (in registers)
             // tcgen05.st takes one column address for the whole warp: block t
             // is stored by all lanes at once, each picking it from the slot
             // its staggered load order put it in (i = (t - stagger) mod 4).
@@ -362,10 +388,11 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                 }
                 tmem_st16(abuf + 16 * t, h);   // k = 32t .. 32t+31 as 16 f16 pairs
             }
+            }
+            }
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             mbar_arrive(&afull[b]);
-            }
         }
         // ------------------------------------------------------------ epilogue
         if (ok) ok = mbar_wait(tfull, 0);
@@ -407,18 +434,18 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
 // f32 -> f16 activations (round to nearest even), for x given in f32.
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_q8_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
-                     int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
-    gemm_body<EF_Q8_0>(xmap, W, rowgroups, nchunks, rows, M, y);
+                     int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
+    gemm_body<EF_Q8_0>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_q4_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
-                     int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
-    gemm_body<EF_Q4_K>(xmap, W, rowgroups, nchunks, rows, M, y);
+                     int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
+    gemm_body<EF_Q4_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_q4_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
-                     int64_t nchunks, int64_t rows, int M, float *__restrict__ y) {
-    gemm_body<EF_Q4_0>(xmap, W, rowgroups, nchunks, rows, M, y);
+                     int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
+    gemm_body<EF_Q4_0>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 
 __global__ void f32_to_f16_kernel(const float *__restrict__ src, __half *__restrict__ dst, int64_t n) {
@@ -448,7 +475,8 @@ static EncodeTiledFn encode_fn() {
 }
 
 template <int TYPE> static size_t gemm_smem() {
-    return 1024 + (size_t)GM_SX * (GM_BN * 128) + (size_t)GM_SW * 8 * GmTile<TYPE>::BYTES + 256;
+    return 1024 + (size_t)GM_SX * (GM_BN * 128) +
+           (size_t)gm_sw<TYPE>() * 8 * (GM_KW / GmTile<TYPE>::CK) * GmTile<TYPE>::BYTES + 256;
 }
 
 template <int TYPE>
@@ -475,7 +503,7 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
     }
     dim3 grid((unsigned)((w->rowgroups + 7) / 8), (unsigned)((M + GM_BN - 1) / GM_BN));
     ctx->launches++;
-    kern<<<grid, GM_THREADS, smem, ctx->stream>>>(map, w->dev, w->rowgroups, w->nchunks, w->rows, M, y);
+    kern<<<grid, GM_THREADS, smem, ctx->stream>>>(map, w->dev, w->rowgroups, w->nchunks, w->rows, w->k, M, y);
     return check_cuda(ctx, cudaGetLastError(), "gemm launch");
 }
 

@@ -11,8 +11,9 @@ pytestmark = pytest.mark.gpu
 REL = 1e-3
 
 
-@pytest.mark.parametrize("t,rows,k", [("Q8_0", 256, 512), ("Q8_0", 48, 2048), ("Q4_0", 256, 512),
-                                      ("Q4_0", 40, 2048), ("Q4_K", 128, 1024), ("Q4_K", 37, 2304),
+@pytest.mark.parametrize("t,rows,k", [("Q8_0", 256, 512), ("Q8_0", 48, 2048), ("Q8_0", 64, 640),
+                                      ("Q8_0", 32, 4128), ("Q4_0", 256, 512), ("Q4_0", 40, 2048),
+                                      ("Q4_0", 40, 4128), ("Q4_K", 128, 1024), ("Q4_K", 37, 2304),
                                       ("Q6_K", 64, 512)])
 @pytest.mark.parametrize("M", [17, 64, 130])
 def test_gemm_f16x_vs_oracle(ops, oracle_mod, t, rows, k, M):
