@@ -394,6 +394,12 @@ int ef_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, f
     return launch_gemm(ctx, w, x, x_type, M, y);
 }
 
+int ef_gemm_status(ef_ctx *ctx) {
+    if (!ctx) return EF_ERR_INVALID;
+    if (int rc = use_device(ctx)) return rc;
+    return gemm_status(ctx);
+}
+
 int ef_matmul(ef_ctx *ctx, const ef_weight *w, const float *x, int tokens, float *y) {
     if (!ctx) return EF_ERR_INVALID;
     if (tokens <= 16) return ef_gemv(ctx, w, x, tokens, y);

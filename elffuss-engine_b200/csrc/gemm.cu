@@ -194,7 +194,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             const int64_t nrg = rowgroups - rb * 8 < 8 ? rowgroups - rb * 8 : 8;
             int wi = 0, xi = 0;                          // copies issued
             // weight stage kk -> slot kk % SW (refilled once the dequant
-            // warps have read stage kk - SW)
+            // warps have consumed stage kk - SW)
             auto issue_w = [&](int kk) {
                 const int sw = kk % SW;
                 if (kk >= SW) ok = mbar_wait(&wempty[sw], ((kk / SW) - 1) & 1);
@@ -277,7 +277,6 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             for (int ch = 0; ch < nc; ch++) {
             const uint8_t *T = ws + sw * WRAW + rg_in * (CPS * TB) + ch * TB;
             const uint32_t abuf = tmem + tlane + GM_TMEM_A + ACOLS * b + (CK / 2) * ch;
-            const bool last = ch == nc - 1;          // the stage's raw bytes are all in registers after this chunk's loads
             if constexpr (TYPE == EF_Q4_K) {
                 // Row r: header (d, dmin, scale_min_k4 bytes) at 2048 + 16 rl; the
                 // qs bytes [4t, 4t+4) and [16+4t, 16+4t+4) of group j in lane
@@ -293,7 +292,6 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                                                                            (4 * g + tt) * 16 + 8 * (j & 1))
                                          : make_uint2(0, 0);
                 if (have) hdr = *reinterpret_cast<const uint4 *>(T + SCO + 16 * rl);
-                if (last) mbar_arrive(&wempty[sw]);          // raw stage consumed (in registers)
                 const uint32_t hw[4] = {hdr.x, hdr.y, hdr.z, hdr.w};
                 auto hbyte = [&](int i) { return (int)((hw[i >> 2] >> (8 * (i & 3))) & 0xFF); };
                 const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
@@ -356,7 +354,6 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                     sc[i] = 0;
                 }
             }
-            if (last) mbar_arrive(&wempty[sw]);   // raw stage consumed (in registers)
             // tcgen05.st takes one column address for the whole warp: block t
             // is stored by all lanes at once, each picking it from the slot
             // its staggered load order put it in (i = (t - stagger) mod 4).
@@ -393,6 +390,12 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
             tc_fence_before();
             mbar_arrive(&afull[b]);
+            // The raw stage is released only after the tensor-memory stores
+            // that consume every value read from it. Released right after the
+            // shared loads, the next bulk copy into the stage may overtake
+            // loads that the compiler scheduled later (wrong Q4_K results when
+            // a weight producer of its own refilled stages at once).
+            mbar_arrive(&wempty[sw]);
         }
         // ------------------------------------------------------------ epilogue
         if (ok) ok = mbar_wait(tfull, 0);
@@ -505,6 +508,19 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
     ctx->launches++;
     kern<<<grid, GM_THREADS, smem, ctx->stream>>>(map, w->dev, w->rowgroups, w->nchunks, w->rows, w->k, M, y);
     return check_cuda(ctx, cudaGetLastError(), "gemm launch");
+}
+
+// Reads and clears the flag a bounded pipeline wait sets when it gives up.
+int gemm_status(ef_ctx *ctx) {
+    int flag = 0;
+    if (int rc = check_cuda(ctx, cudaStreamSynchronize(ctx->stream), "gemm status sync")) return rc;
+    if (int rc = check_cuda(ctx, cudaMemcpyFromSymbol(&flag, g_gemm_error, sizeof(int)), "gemm status read"))
+        return rc;
+    if (!flag) return EF_OK;
+    const int zero = 0;
+    if (int rc = check_cuda(ctx, cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int)), "gemm status clear"))
+        return rc;
+    return set_err(ctx, EF_ERR_TIMEOUT, "gemm: a pipeline wait gave up; outputs since the last check are invalid");
 }
 
 int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y) {

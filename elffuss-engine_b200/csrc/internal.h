@@ -120,6 +120,7 @@ int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight 
                 int64_t *ctas_out = nullptr);
 
 // gemm.cu
+int gemm_status(ef_ctx *ctx);
 int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y);
 
 }  // namespace ef

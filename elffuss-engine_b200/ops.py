@@ -198,6 +198,12 @@ class Gemm2Ops:
     def reproducible(self, type, rows, k, lote):
         return self.plan(type, rows, k, lote) is not None
 
+    def status(self):
+        """Synchronizes and raises EfError (EF_ERR_TIMEOUT) if a GEMM since the
+        last check gave up on a bounded pipeline wait (its output is invalid)."""
+        h = self._ops.ctx.bind()
+        check(lib().ef_gemm_status(h), h)
+
     def cola(self, type, w, x1, rows, k, lote):
         """One token with the batch's kernel (js/ops.gemm2.js:294-302)."""
         if self.plan(type, rows, k, lote) is None:

@@ -52,7 +52,7 @@ enum {
     EF_ERR_OOM = -5,         /* device allocation failed */
     EF_ERR_MISMATCH = -6,    /* weight handle does not match the call (js/repack.js:268-286) */
     EF_ERR_RANGE = -7,       /* offset/size outside a buffer, or a slice outside a tensor */
-    EF_ERR_TIMEOUT = -8      /* a tensor-parallel peer did not arrive within the wait limit */
+    EF_ERR_TIMEOUT = -8      /* a bounded device wait gave up (a tensor-parallel peer, a GEMM pipeline stage) */
 };
 
 /* GGUF tensor types (ggml ids, js/gguf.js:48-64). */
@@ -188,6 +188,14 @@ EF_API int ef_gemv_sections(ef_ctx *ctx, const ef_weight *const *ws, int n, cons
  * `flags` is reserved (0). */
 EF_API int ef_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y,
             uint32_t flags);
+
+/* Synchronizes the context's stream and reports whether a prefill GEMM gave up
+ * on one of its bounded pipeline waits (about a second each) since the last
+ * call: EF_ERR_TIMEOUT then (the flag is cleared; those GEMMs' outputs are
+ * invalid), else EF_OK. The kernel never spins without a limit; it stops
+ * issuing work, lets its own copies land and frees its tensor memory. No
+ * reference counterpart (WebGPU has no device-side waits). */
+EF_API int ef_gemm_status(ef_ctx *ctx);
 
 /* Decode GEMV that allocates nothing (no counterpart in the reference, which
  * is single-device and allocates through its own buffer pool). ef_gemv keeps

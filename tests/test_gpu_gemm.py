@@ -23,6 +23,7 @@ def test_gemm_f16x_vs_oracle(ops, oracle_mod, t, rows, k, M):
     xh = oracle_mod.f32_to_f16_bits(x)
     y = ops.gemm2.matmul(t, w, torch.from_numpy(xh.view(np.float16)).cuda(), rows, k, M, x_f16=True)
     y = y.cpu().numpy()
+    ops.gemm2.status()
     want = oracle_mod.matmul_f64(t, raw, rows, k, xh=xh, tokens=M, w16=True)
     tol = oracle_mod.tolerance(t, raw, rows, k, xh.view(np.float16).astype(np.float32), rel=REL)
     assert np.all(np.abs(y - want) <= tol)
@@ -36,6 +37,7 @@ def test_gemm_config2_vs_torch(ops, t, M, k, rows):
     wd = ops.dequant(t, w, rows * k // formats.block_info(t)[0]).reshape(rows, k)
     x = torch.randn(M, k, device="cuda").half()
     y = ops.gemm2.matmul(t, w, x, rows, k, M, x_f16=True)
+    ops.gemm2.status()
     ref = x.float() @ wd.half().float().T
     tol = REL * torch.linalg.norm(x.float(), dim=1)[:, None] * torch.linalg.norm(wd, dim=1)[None, :]
     assert bool(torch.all((y - ref).abs() <= tol))
@@ -50,3 +52,16 @@ def test_cola_matches_batch_row(ops):
     y1 = ops.gemm2.cola("Q8_0", w, x[-1:].clone(), rows, k, lote)
     assert ops.gemm2.reproducible("Q8_0", rows, k, lote)
     torch.testing.assert_close(y1[0], yb[-1], rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("t,M,k,rows", [("Q8_0", 512, 2048, 8192), ("Q4_K", 512, 4096, 4096)])
+def test_gemm_repeatable(ops, t, M, k, rows):
+    """The pipeline hands every weight stage back only after it is consumed:
+    back-to-back calls on the same inputs give bit-identical outputs."""
+    raw = formats.synth(t, rows, k, seed=3)
+    w = ops.load_weight(t, raw, rows, k)
+    x = torch.randn(M, k, device="cuda").half()
+    y0 = ops.gemm2.matmul(t, w, x, rows, k, M, x_f16=True)
+    for _ in range(10):
+        assert torch.equal(ops.gemm2.matmul(t, w, x, rows, k, M, x_f16=True), y0)
+    ops.gemm2.status()
