@@ -118,6 +118,7 @@ template <int TYPE> struct GmTile;
 template <> struct GmTile<EF_Q8_0> { static constexpr int BYTES = 2176, SC = 2048, CK = 128; };
 template <> struct GmTile<EF_Q4_0> { static constexpr int BYTES = 1152, SC = 1024, CK = 128; };
 template <> struct GmTile<EF_Q4_K> { static constexpr int BYTES = 2304, SC = 2048, CK = 256; };
+template <> struct GmTile<EF_Q6_K> { static constexpr int BYTES = 3360, SC = 3072, CK = 256; };
 // weight stages (each 8 rowgroups x GM_KW) that fit beside the activation ring, at most 4
 template <int TYPE> __host__ __device__ constexpr int gm_sw() {
     constexpr int per = 8 * (GM_KW / GmTile<TYPE>::CK) * GmTile<TYPE>::BYTES;
@@ -277,7 +278,53 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             for (int ch = 0; ch < nc; ch++) {
             const uint8_t *T = ws + sw * WRAW + rg_in * (CPS * TB) + ch * TB;
             const uint32_t abuf = tmem + tlane + GM_TMEM_A + ACOLS * b + (CK / 2) * ch;
-            if constexpr (TYPE == EF_Q4_K) {
+            if constexpr (TYPE == EF_Q6_K) {
+                // Row r = g + 8hs: for lane column t and step s (32 weights) a
+                // low-nibble word at part 2hs + (s>>2), offset 4(s&3) of lane
+                // 4g+t (byte b: k = 32s + 4t + b in bits 0-3, 32s + 16 + 4t + b
+                // in bits 4-7); for step pair sp a high-bit word at part 4 + hs,
+                // offset 4sp (byte b: bits 0-1 / 2-3 = halves 0 / 1 of step 2sp,
+                // 4-5 / 6-7 = those of step 2sp+1); 16 int8 scales at 3072 + 16 rl
+                // (one per 16 weights); f16 d at 3328 + 4g + 2hs.
+                uint4 lo[4][2], hi[4], scv = make_uint4(0, 0, 0, 0);
+                uint32_t dbits = 0;
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const uint8_t *P = T + (4 * g + t) * 16;
+                    lo[t][0] = have ? *reinterpret_cast<const uint4 *>(P + (2 * hs) * 512) : make_uint4(0, 0, 0, 0);
+                    lo[t][1] = have ? *reinterpret_cast<const uint4 *>(P + (2 * hs + 1) * 512) : make_uint4(0, 0, 0, 0);
+                    hi[t] = have ? *reinterpret_cast<const uint4 *>(P + (4 + hs) * 512) : make_uint4(0, 0, 0, 0);
+                }
+                if (have) {
+                    scv = *reinterpret_cast<const uint4 *>(T + SCO + 16 * rl);
+                    dbits = *reinterpret_cast<const unsigned short *>(T + 3328 + 4 * g + 2 * hs);
+                }
+                const float d = __half2float(__ushort_as_half((unsigned short)dbits));
+                const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+                auto wd = [](const uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; };
+#pragma unroll
+                for (int st = 0; st < 8; st++) {
+                    // f16(d * sc) of sub-blocks 2st (half 0) and 2st+1 (half 1)
+                    const int s0 = (int)(int8_t)((scw[st >> 1] >> (16 * (st & 1))) & 0xFF);
+                    const int s1 = (int)(int8_t)((scw[st >> 1] >> (16 * (st & 1) + 8)) & 0xFF);
+                    const uint32_t d0 = (uint32_t)__half_as_ushort(__float2half_rn(d * (float)s0)) * 0x10001u;
+                    const uint32_t d1 = (uint32_t)__half_as_ushort(__float2half_rn(d * (float)s1)) * 0x10001u;
+                    uint32_t h[16];
+#pragma unroll
+                    for (int t = 0; t < 4; t++) {
+                        const uint32_t w = wd(lo[t][st >> 2], st & 3), hw = wd(hi[t], st >> 1);
+                        const uint32_t g0 = (st & 1) ? hw : hw << 4, g1 = (st & 1) ? hw >> 2 : hw << 2;
+                        const uint32_t q0 = (w & 0x0F0F0F0Fu) | (g0 & 0x30303030u);          // k = 32st + 4t + b
+                        const uint32_t q1 = ((w >> 4) & 0x0F0F0F0Fu) | (g1 & 0x30303030u);   // k = 32st + 16 + 4t + b
+                        // (1024 + q) - (1024 + 32) = q - 32, exact in f16
+                        h[2 * t] = hmul2u(hsub2u(prmt(q0, 0x64646464u, 0x5140), 0x64206420u), d0);
+                        h[2 * t + 1] = hmul2u(hsub2u(prmt(q0, 0x64646464u, 0x7362), 0x64206420u), d0);
+                        h[8 + 2 * t] = hmul2u(hsub2u(prmt(q1, 0x64646464u, 0x5140), 0x64206420u), d1);
+                        h[9 + 2 * t] = hmul2u(hsub2u(prmt(q1, 0x64646464u, 0x7362), 0x64206420u), d1);
+                    }
+                    tmem_st16(abuf + 16 * st, h);   // k = 32st .. 32st+31 as 16 f16 pairs
+                }
+            } else if constexpr (TYPE == EF_Q4_K) {
                 // Row r: header (d, dmin, scale_min_k4 bytes) at 2048 + 16 rl; the
                 // qs bytes [4t, 4t+4) and [16+4t, 16+4t+4) of group j in lane
                 // 4g+t's part 2hs + (j>>1) at offset 8(j&1). Low nibbles of group
@@ -446,6 +493,11 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_body<EF_Q4_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_q6_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+                     int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
+    gemm_body<EF_Q6_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
+}
+__global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_q4_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q4_0>(xmap, W, rowgroups, nchunks, rows, k, M, y);
@@ -495,7 +547,10 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return set_err(ctx, EF_ERR_CUDA, "gemm: tensor map encode failed (%d)", (int)cr);
-    auto kern = TYPE == EF_Q8_0 ? gemm_q8_0_kernel : TYPE == EF_Q4_0 ? gemm_q4_0_kernel : gemm_q4_k_kernel;
+    auto kern = TYPE == EF_Q8_0   ? gemm_q8_0_kernel
+                : TYPE == EF_Q4_0 ? gemm_q4_0_kernel
+                : TYPE == EF_Q4_K ? gemm_q4_k_kernel
+                                  : gemm_q6_k_kernel;
     const size_t smem = gemm_smem<TYPE>();
     static unsigned long long configured = 0;
     if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
@@ -524,7 +579,7 @@ int gemm_status(ef_ctx *ctx) {
 }
 
 int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y) {
-    if ((w->type == EF_Q8_0 || w->type == EF_Q4_0 || w->type == EF_Q4_K) && w->k % 8 == 0) {
+    if ((w->type == EF_Q8_0 || w->type == EF_Q4_0 || w->type == EF_Q4_K || w->type == EF_Q6_K) && w->k % 8 == 0) {
         // tcgen05 path: activations as f16 [M][K] (converted from f32 if needed)
         const __half *xh = (const __half *)x;
         if (x_type == EF_F32) {
@@ -539,7 +594,8 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
         }
         if (w->type == EF_Q8_0) return launch_tc<EF_Q8_0>(ctx, w, xh, M, y);
         if (w->type == EF_Q4_0) return launch_tc<EF_Q4_0>(ctx, w, xh, M, y);
-        return launch_tc<EF_Q4_K>(ctx, w, xh, M, y);
+        if (w->type == EF_Q4_K) return launch_tc<EF_Q4_K>(ctx, w, xh, M, y);
+        return launch_tc<EF_Q6_K>(ctx, w, xh, M, y);
     }
     // Other types: the token dimension in groups of 16 through the GEMV
     // kernel (same numerics contract: f16 activations, f32 accumulation).
