@@ -17,8 +17,10 @@
 //   attention          softmax(q.k / sqrt(D)) with causal + window mask, times
 //                      v, times sigmoid(per-head gate) (kernels.nn.wgsl.js:
 //                      141-200, kernels.model.wgsl.js:89-105): split over the
-//                      keys for one new token per sequence, one CTA per query
-//                      row for a prompt
+//                      keys for one new token per sequence; for a prompt,
+//                      64-key tiles shared by 128 (head, token) rows with an
+//                      online softmax (one CTA per query row for head
+//                      groupings other than 1, 2, 4, 8)
 //   argmax             greedy token, strict '>' so the lowest index wins ties
 //                      (sample.js:95-99); advances the device-side position;
 //                      per-shard pairs and their selection for a sharded head
@@ -285,6 +287,193 @@ __global__ void __launch_bounds__(256) attention_kernel(const float *__restrict_
         o *= inv;
         if (gate) o = o / (1.0f + expf(-gate[(int64_t)r * H + h]));
         out[((int64_t)r * H + h) * D + d] = o;
+    }
+}
+
+// Prompt attention (several new tokens per sequence), tiled in the manner of
+// flash attention: CTA = (block of BQ = 128 / G consecutive query tokens of one
+// sequence, cache head kvh) for the G = H / KVH query heads that share the
+// cache head, so R = 128 (head, token) rows per CTA. The key range the rows
+// can see goes through shared memory in tiles of 64 keys (each K and V row
+// read once per CTA); per tile: scores S = Q K^T (a thread owns 8 rows x 4
+// keys), the causal / window mask, an online softmax per row (running max m,
+// running sum l, old output rescaled by exp(m_old - m_new)), and O += P V (a
+// thread owns 8 rows x 4 or 8 dimensions of O in registers). All f32; same
+// masking, scale, positions and gate as attention_kernel (kernels.nn.wgsl.js:
+// 141-200, kernels.model.wgsl.js:89-105). Rows of shared-memory tiles are
+// padded by 4 floats so that the 16-byte loads of different rows fall in
+// different banks. Query blocks are taken last to first: the longest key
+// ranges start first.
+constexpr int FA_R = 128, FA_BK = 64, FA_T = 256;
+template <int D> constexpr size_t fa_smem() {
+    return (size_t)(FA_R * (D + 4) + 2 * FA_BK * (D + 4) + FA_R * (FA_BK + 4) + 3 * FA_R) * sizeof(float);
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(FA_T, 1) attn_prompt_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
+                                                          const float *__restrict__ vcache,
+                                                          const float *__restrict__ gate, const int *__restrict__ pos,
+                                                          int tokens, int max_pos, int window, int H, int KVH,
+                                                          float *__restrict__ out) {
+    pdl_trigger();
+    pdl_wait();
+    constexpr int BQ = FA_R / G, LD = D + 4, LP = FA_BK + 4, C4 = D / 4, DV = D / 64;
+    extern __shared__ float4 fa_smem4[];
+    float *Qs = reinterpret_cast<float *>(fa_smem4);   // [R][LD], pre-scaled by 1/sqrt(D)
+    float *Ks = Qs + FA_R * LD;                          // [BK][LD]
+    float *Vs = Ks + FA_BK * LD;                         // [BK][LD]
+    float *Ps = Vs + FA_BK * LD;                         // [R][LP] scores, then probabilities
+    float *rm = Ps + FA_R * LP, *rl = rm + FA_R, *ra = rl + FA_R;   // running max, sum, rescale
+    const int tid = threadIdx.x;
+    const int qb = gridDim.x - 1 - blockIdx.x, kvh = blockIdx.y, sq = blockIdx.z;
+    const int t0 = qb * BQ, p0 = pos[sq];
+    const float scale = rsqrtf((float)D);
+    for (int e = tid; e < FA_R * C4; e += FA_T) {
+        const int i = e / C4, c = e - i * C4, tq = t0 + i % BQ;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (tq < tokens) {
+            v = *reinterpret_cast<const float4 *>(q + (((int64_t)sq * tokens + tq) * H + kvh * G + i / BQ) * D + 4 * c);
+            v.x *= scale;
+            v.y *= scale;
+            v.z *= scale;
+            v.w *= scale;
+        }
+        *reinterpret_cast<float4 *>(Qs + i * LD + 4 * c) = v;
+    }
+    for (int i = tid; i < FA_R; i += FA_T) {
+        rm[i] = -INFINITY;
+        rl[i] = 0.f;
+    }
+    // the keys any row of the block can see
+    const int tl = (t0 + BQ < tokens ? t0 + BQ : tokens) - 1;
+    const int qlo = p0 + t0 < max_pos ? p0 + t0 : max_pos - 1, qhi = p0 + tl < max_pos ? p0 + tl : max_pos - 1;
+    const int klo = window > 0 && qlo - window + 1 > 0 ? qlo - window + 1 : 0;
+    const int rg = tid >> 4, kg = tid & 15;   // S: rows 8rg.., keys kg + 16j; PV: rows 8rg.., dims 4kg.. (+64)
+    int qp[8];                                // each row's position, -1 past the prompt
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int tq = t0 + (8 * rg + i) % BQ, p = p0 + tq;
+        qp[i] = tq < tokens ? (p < max_pos ? p : max_pos - 1) : -1;
+    }
+    float o[8][4 * DV];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+#pragma unroll
+        for (int c = 0; c < 4 * DV; c++) o[i][c] = 0.f;
+    for (int kt = (klo / FA_BK) * FA_BK; kt <= qhi; kt += FA_BK) {
+        __syncthreads();   // the previous tile's K, V and P are no longer read
+        for (int e = tid; e < FA_BK * C4; e += FA_T) {
+            const int j = e / C4, c = e - j * C4, key = kt + j;
+            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+            if (key <= qhi) {   // qhi < max_pos: inside the caches
+                const int64_t off = (((int64_t)sq * max_pos + key) * KVH + kvh) * D + 4 * c;
+                kv = *reinterpret_cast<const float4 *>(kcache + off);
+                vv = *reinterpret_cast<const float4 *>(vcache + off);
+            }
+            *reinterpret_cast<float4 *>(Ks + j * LD + 4 * c) = kv;
+            *reinterpret_cast<float4 *>(Vs + j * LD + 4 * c) = vv;
+        }
+        __syncthreads();
+        float sc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) sc[i][j] = 0.f;
+#pragma unroll 4
+        for (int c = 0; c < D; c += 4) {
+            float4 kk[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) kk[j] = *reinterpret_cast<const float4 *>(Ks + (kg + 16 * j) * LD + c);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float4 qq = *reinterpret_cast<const float4 *>(Qs + (8 * rg + i) * LD + c);
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    sc[i][j] = fmaf(qq.w, kk[j].w, fmaf(qq.z, kk[j].z, fmaf(qq.y, kk[j].y, fmaf(qq.x, kk[j].x, sc[i][j]))));
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int key = kt + kg + 16 * j;
+                const bool vis = qp[i] >= 0 && key <= qp[i] && (window <= 0 || qp[i] - key < window);
+                Ps[(8 * rg + i) * LP + kg + 16 * j] = vis ? sc[i][j] : -INFINITY;
+            }
+        __syncthreads();
+        {   // online softmax: two threads per row, 32 keys each
+            const int row = tid >> 1, half = tid & 1;
+            float *pr = Ps + row * LP + 32 * half;
+            float mx = -INFINITY;
+#pragma unroll 8
+            for (int c = 0; c < 32; c++) mx = fmaxf(mx, pr[c]);
+            mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+            const float mold = rm[row], mnew = fmaxf(mold, mx);
+            float alpha = 1.f, sum = 0.f;
+            if (mnew != -INFINITY) {
+                alpha = expf(mold - mnew);   // 0 while nothing was visible before
+#pragma unroll 8
+                for (int c = 0; c < 32; c++) {
+                    const float e = expf(pr[c] - mnew);   // masked keys: exp(-inf) = 0
+                    pr[c] = e;
+                    sum += e;
+                }
+            } else {   // nothing visible so far: adds nothing
+#pragma unroll 8
+                for (int c = 0; c < 32; c++) pr[c] = 0.f;
+            }
+            sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+            if (half == 0) {
+                rm[row] = mnew;
+                rl[row] = rl[row] * alpha + sum;
+                ra[row] = alpha;
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            const float a = ra[8 * rg + i];
+#pragma unroll
+            for (int c = 0; c < 4 * DV; c++) o[i][c] *= a;
+        }
+#pragma unroll 2
+        for (int j = 0; j < FA_BK; j += 4) {
+            float4 pp[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) pp[i] = *reinterpret_cast<const float4 *>(Ps + (8 * rg + i) * LP + j);
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++) {
+                float4 v[DV];
+#pragma unroll
+                for (int u = 0; u < DV; u++) v[u] = *reinterpret_cast<const float4 *>(Vs + (j + jj) * LD + 64 * u + 4 * kg);
+#pragma unroll
+                for (int i = 0; i < 8; i++) {
+                    const float pv = jj == 0 ? pp[i].x : jj == 1 ? pp[i].y : jj == 2 ? pp[i].z : pp[i].w;
+#pragma unroll
+                    for (int u = 0; u < DV; u++) {
+                        o[i][4 * u] = fmaf(pv, v[u].x, o[i][4 * u]);
+                        o[i][4 * u + 1] = fmaf(pv, v[u].y, o[i][4 * u + 1]);
+                        o[i][4 * u + 2] = fmaf(pv, v[u].z, o[i][4 * u + 2]);
+                        o[i][4 * u + 3] = fmaf(pv, v[u].w, o[i][4 * u + 3]);
+                    }
+                }
+            }
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int row = 8 * rg + i, tq = t0 + row % BQ, h = kvh * G + row / BQ;
+        if (tq >= tokens) continue;
+        const float l = rl[row];
+        float f = l > 0.f ? 1.f / l : 0.f;
+        const int64_t r = (int64_t)sq * tokens + tq;
+        if (gate) f = f / (1.0f + expf(-gate[r * H + h]));
+#pragma unroll
+        for (int u = 0; u < DV; u++) {
+            const float4 w = make_float4(o[i][4 * u] * f, o[i][4 * u + 1] * f, o[i][4 * u + 2] * f, o[i][4 * u + 3] * f);
+            *reinterpret_cast<float4 *>(out + (r * H + h) * D + 64 * u + 4 * kg) = w;
+        }
     }
 }
 
@@ -724,6 +913,24 @@ static int part_launch(ef_ctx *ctx, dim3 grid, const float *q, const float *kcac
                      max_pos, window, heads, kv_heads, part);
 }
 
+template <int D, int G>
+static int prompt_attn_launch(ef_ctx *ctx, int seqs, const float *q, const float *kcache, const float *vcache,
+                              const float *gate, const int *pos, int tokens, int max_pos, int window, int heads,
+                              int kv_heads, float *out) {
+    constexpr size_t smem = fa_smem<D>();
+    static unsigned long long configured = 0;   // per instantiation, one bit per device
+    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(attn_prompt_kernel<D, G>,
+                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                                "prompt attention smem attribute"))
+            return rc;
+        configured |= 1ull << ctx->device;
+    }
+    const dim3 grid((unsigned)((tokens + FA_R / G - 1) / (FA_R / G)), (unsigned)kv_heads, (unsigned)seqs);
+    return launch_on(ctx, attn_prompt_kernel<D, G>, grid, FA_T, smem, "prompt attention launch", q, kcache, vcache,
+                     gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+}
+
 }  // namespace ef
 
 using namespace ef;
@@ -819,18 +1026,6 @@ static int attention_launch(ef_ctx *ctx, const float *q, const float *kcache, co
                             const float *head_gate, const int *pos, int seqs, int tokens, int max_pos, int window,
                             int heads, int kv_heads, int head_dim, float *out) {
     const int span = window > 0 && window < max_pos ? window : max_pos;
-    const size_t smem = (size_t)span * 4;
-    if (smem > 200 * 1024) return set_err(ctx, EF_ERR_RANGE, "attention: %d keys exceed shared memory", span);
-    static unsigned long long configured[2] = {0, 0};
-    const int di = head_dim == 64 ? 0 : 1;
-    if (ctx->device < 64 && !(configured[di] & (1ull << ctx->device))) {
-        cudaError_t e = di == 0 ? cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       200 * 1024)
-                                : cudaFuncSetAttribute(attention_kernel<128>,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (int rc = check_cuda(ctx, e, "attention smem attribute")) return rc;
-        configured[di] |= 1ull << ctx->device;
-    }
     const int G = heads / kv_heads;
     if (tokens == 1 && (G == 1 || G == 2 || G == 4 || G == 8)) {
         // one new token per sequence: the keys split over CTAs, then merged
@@ -868,6 +1063,32 @@ static int attention_launch(ef_ctx *ctx, const float *q, const float *kcache, co
                              (const float *)part, head_gate, heads, nsplit, out);
         return launch_on(ctx, attn_combine_kernel<128>, cg, CT, cs, "attention combine launch", (const float *)part,
                          head_gate, heads, nsplit, out);
+    }
+    if (G == 1 || G == 2 || G == 4 || G == 8) {
+        // several new tokens per sequence: key tiles shared by a block of queries
+        switch (head_dim * 16 + G) {
+        case 64 * 16 + 1: return prompt_attn_launch<64, 1>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 64 * 16 + 2: return prompt_attn_launch<64, 2>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 64 * 16 + 4: return prompt_attn_launch<64, 4>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 64 * 16 + 8: return prompt_attn_launch<64, 8>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 128 * 16 + 1: return prompt_attn_launch<128, 1>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 128 * 16 + 2: return prompt_attn_launch<128, 2>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 128 * 16 + 4: return prompt_attn_launch<128, 4>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        default: return prompt_attn_launch<128, 8>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        }
+    }
+    // other head groupings: a CTA per (head, query row), scores of all keys in shared memory
+    const size_t smem = (size_t)span * 4;
+    if (smem > 200 * 1024) return set_err(ctx, EF_ERR_RANGE, "attention: %d keys exceed shared memory", span);
+    static unsigned long long configured[2] = {0, 0};
+    const int di = head_dim == 64 ? 0 : 1;
+    if (ctx->device < 64 && !(configured[di] & (1ull << ctx->device))) {
+        cudaError_t e = di == 0 ? cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       200 * 1024)
+                                : cudaFuncSetAttribute(attention_kernel<128>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (int rc = check_cuda(ctx, e, "attention smem attribute")) return rc;
+        configured[di] |= 1ull << ctx->device;
     }
     const dim3 grid(heads, seqs * tokens);
     if (di == 0)

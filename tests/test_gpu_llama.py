@@ -87,6 +87,43 @@ def test_rope_cache_and_attention_batched(ops, D, mode, norm):
                     assert np.allclose(out[r].cpu().numpy().reshape(H, D)[hh], want, rtol=1e-4, atol=1e-5)
 
 
+@pytest.mark.parametrize("D,H,KV,S,T,pos,window,gated", [
+    (128, 32, 8, 1, 700, [0], 0, False),          # the 8B shape, G = 4
+    (64, 16, 2, 2, 300, [0, 50], 100, True),      # G = 8, a window, two sequences at different offsets
+    (128, 8, 8, 1, 257, [3], 0, True),            # G = 1
+    (64, 8, 4, 2, 130, [10, 0], 0, False),        # G = 2
+    (128, 16, 2, 1, 9, [0], 3, False),            # a short prompt, window smaller than a key tile
+])
+def test_prompt_attention_tiled(ops, D, H, KV, S, T, pos, window, gated):
+    """Several new tokens per sequence (the prompt path): key tiles shared by a
+    block of queries with an online softmax, against float64."""
+    L, h = lib(), ops.ctx.bind()
+    maxp = max(pos) + T + 5
+    g = torch.Generator("cuda").manual_seed(D + H + T)
+    kc = torch.randn(S, maxp, KV, D, device="cuda", generator=g)
+    vc = torch.randn(S, maxp, KV, D, device="cuda", generator=g)
+    q = torch.randn(S * T, H * D, device="cuda", generator=g) * 2
+    gate = torch.randn(S * T, H, device="cuda", generator=g) if gated else None
+    pd = torch.tensor(pos, dtype=torch.int32, device="cuda")
+    out = torch.empty(S * T, H * D, device="cuda")
+    check(L.ef_attention(h, P(q), P(kc), P(vc), P(gate), P(pd), S, T, maxp, window, H, KV, D, P(out)), h)
+    G = H // KV
+    for s in range(S):
+        Q = q[s * T:(s + 1) * T].double().reshape(T, H, D)
+        K = kc[s].double().repeat_interleave(G, dim=1)          # [maxp][H][D]
+        V = vc[s].double().repeat_interleave(G, dim=1)
+        sc = torch.einsum("thd,khd->htk", Q, K) / D ** 0.5
+        qp = torch.arange(T, device="cuda")[:, None] + pos[s]
+        key = torch.arange(maxp, device="cuda")[None, :]
+        vis = (key <= qp) & ((window == 0) | (qp - key < window))
+        sc = sc.masked_fill(~vis[None], float("-inf"))
+        want = torch.einsum("htk,khd->thd", torch.softmax(sc, dim=-1), V)
+        if gated:
+            want = want * torch.sigmoid(gate[s * T:(s + 1) * T].double())[:, :, None]
+        got = out[s * T:(s + 1) * T].double().reshape(T, H, D)
+        assert torch.allclose(got, want, rtol=1e-4, atol=1e-5), float((got - want).abs().max())
+
+
 @pytest.mark.parametrize("D,H,KV", [(128, 8, 2), (64, 32, 8), (128, 4, 4), (64, 16, 2)])
 def test_decode_attention_split_over_long_caches(ops, D, H, KV):
     """One new token per sequence: the keys split in ranges of 256 over CTAs,
