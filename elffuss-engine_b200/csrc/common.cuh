@@ -511,6 +511,26 @@ __device__ __forceinline__ uint32_t hmul2u(uint32_t a, uint32_t b) {
     __half2 r = __hmul2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b));
     return *reinterpret_cast<uint32_t *>(&r);
 }
+// word i of v (i < 4, after unrolling a compile-time constant)
+__device__ __forceinline__ uint32_t wsel(const uint4 &v, int i) {
+    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
+}
+// two f16 weights from the bytes of qbytes that `sel` picks (prmt selector
+// 0x5140: bytes 0,1; 0x7362: bytes 2,3): q as (1024 + q) - 1024 exactly, then
+// one f16 fma with the sub-block's f16(d * sc) and -f16(dmin * m)
+__device__ __forceinline__ uint32_t f16_pair_dm(uint32_t qbytes, uint32_t sel, uint32_t d2, uint32_t negm2) {
+    uint32_t r;
+    const uint32_t q = hsub2u(prmt(qbytes, 0x64646464u, sel), 0x64006400u);
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(q), "r"(d2), "r"(negm2));
+    return r;
+}
+// f32 -> f16x2 (v, v), round to nearest even
+__device__ __forceinline__ uint32_t f16x2_bcast(float v) {
+    const uint32_t h = __half_as_ushort(__float2half_rn(v));
+    return h | (h << 16);
+}
+// bit c of x (c < 4) to bit 8c
+__device__ __forceinline__ uint32_t spread4(uint32_t x) { return (x * 0x00204081u) & 0x01010101u; }
 __device__ __forceinline__ uint32_t hfma2u(uint32_t a, uint32_t b, uint32_t c) {
     __half2 r = __hfma2(*reinterpret_cast<__half2 *>(&a), *reinterpret_cast<__half2 *>(&b),
                         *reinterpret_cast<__half2 *>(&c));

@@ -119,6 +119,8 @@ template <> struct GmTile<EF_Q8_0> { static constexpr int BYTES = 2176, SC = 204
 template <> struct GmTile<EF_Q4_0> { static constexpr int BYTES = 1152, SC = 1024, CK = 128; };
 template <> struct GmTile<EF_Q4_K> { static constexpr int BYTES = 2304, SC = 2048, CK = 256; };
 template <> struct GmTile<EF_Q6_K> { static constexpr int BYTES = 3360, SC = 3072, CK = 256; };
+template <> struct GmTile<EF_Q5_K> { static constexpr int BYTES = 2816, SC = 2560, CK = 256; };
+template <> struct GmTile<EF_Q2_K> { static constexpr int BYTES = 1344, SC = 1024, CK = 256; };
 // weight stages (each 8 rowgroups x GM_KW) that fit beside the activation ring, at most 4
 template <int TYPE> __host__ __device__ constexpr int gm_sw() {
     constexpr int per = 8 * (GM_KW / GmTile<TYPE>::CK) * GmTile<TYPE>::BYTES;
@@ -324,6 +326,92 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                     }
                     tmem_st16(abuf + 16 * st, h);   // k = 32st .. 32st+31 as 16 f16 pairs
                 }
+            } else if constexpr (TYPE == EF_Q5_K) {
+                // Row r = g + 8hs: lane column t holds the 64 weights 64t..: qs
+                // bytes 0..31 at parts 2hs, 2hs+1 of lane 4g+t (low nibble:
+                // weight 64t + b, sub-block 2t; high nibble: 64t + 32 + b,
+                // sub-block 2t+1), their fifth bits as two words (bit l of
+                // weight 64t + l / 64t + 32 + l) at part 4, offset 8hs; the row's
+                // header (d, dmin, scale_min_k4 bytes) at 2560 + 16 rl.
+                uint4 qs[4][2], hdr = make_uint4(0, 0, 0, 0);
+                uint2 fb[4];
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    const uint8_t *P = T + (4 * g + t) * 16;
+                    qs[t][0] = have ? *reinterpret_cast<const uint4 *>(P + (2 * hs) * 512) : make_uint4(0, 0, 0, 0);
+                    qs[t][1] = have ? *reinterpret_cast<const uint4 *>(P + (2 * hs + 1) * 512) : make_uint4(0, 0, 0, 0);
+                    fb[t] = have ? *reinterpret_cast<const uint2 *>(P + 4 * 512 + 8 * hs) : make_uint2(0, 0);
+                }
+                if (have) hdr = *reinterpret_cast<const uint4 *>(T + SCO + 16 * rl);
+                const uint32_t hw[4] = {hdr.x, hdr.y, hdr.z, hdr.w};
+                auto hbyte = [&](int i) { return (int)((hw[i >> 2] >> (8 * (i & 3))) & 0xFF); };
+                const float d = __half2float(__ushort_as_half((unsigned short)(hdr.x & 0xFFFF)));
+                const float dmin = __half2float(__ushort_as_half((unsigned short)(hdr.x >> 16)));
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        const int sb = 2 * t + u;
+                        int sc, mn;
+                        if (sb < 4) {
+                            sc = hbyte(4 + sb) & 63;
+                            mn = hbyte(8 + sb) & 63;
+                        } else {
+                            sc = (hbyte(8 + sb) & 0xF) | ((hbyte(sb) >> 6) << 4);
+                            mn = (hbyte(8 + sb) >> 4) | ((hbyte(4 + sb) >> 6) << 4);
+                        }
+                        const uint32_t d2 = f16x2_bcast(d * (float)sc), m2 = f16x2_bcast(-(dmin * (float)mn));
+                        const uint32_t bits = u ? fb[t].y : fb[t].x;
+                        uint32_t h[16];
+#pragma unroll
+                        for (int w = 0; w < 8; w++) {   // weights 64t + 32u + 4w .. +3
+                            const uint32_t raw = wsel(qs[t][w >> 2], w & 3);
+                            const uint32_t q = ((u ? raw >> 4 : raw) & 0x0F0F0F0Fu) | (spread4((bits >> (4 * w)) & 0xF) << 4);
+                            h[2 * w] = f16_pair_dm(q, 0x5140, d2, m2);
+                            h[2 * w + 1] = f16_pair_dm(q, 0x7362, d2, m2);
+                        }
+                        tmem_st16(abuf + 32 * t + 16 * u, h);   // k = 64t + 32u .. +31 as 16 f16 pairs
+                    }
+                }
+            } else if constexpr (TYPE == EF_Q2_K) {
+                // Row r = g + 8hs: lane column t holds the 64 weights 64t.. =
+                // sub-blocks 4t..4t+3 of 16 weights: part hs of lane 4g+t, word
+                // w (sub-block 4t + w), byte c, bits 2s'..2s'+1 = the 2-bit q of
+                // weight 64t + 16w + 4s' + c; the sub-blocks' scale bytes (low
+                // nibble sc, high nibble m) at 1024 + 8(4g+t) + 4hs; the row's
+                // f16 d, dmin at 1280 + 4 rl.
+                uint4 qv[4];
+                uint32_t scb[4], dmw = 0;
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    qv[t] = have ? *reinterpret_cast<const uint4 *>(T + hs * 512 + (4 * g + t) * 16) : make_uint4(0, 0, 0, 0);
+                    scb[t] = have ? *reinterpret_cast<const uint32_t *>(T + SCO + 8 * (4 * g + t) + 4 * hs) : 0u;
+                }
+                if (have) dmw = *reinterpret_cast<const uint32_t *>(T + 1280 + 4 * rl);
+                const float d = __half2float(__ushort_as_half((unsigned short)(dmw & 0xFFFF)));
+                const float dmin = __half2float(__ushort_as_half((unsigned short)(dmw >> 16)));
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+#pragma unroll
+                    for (int hf = 0; hf < 2; hf++) {
+                        uint32_t h[16];
+#pragma unroll
+                        for (int ww = 0; ww < 2; ww++) {
+                            const int w = 2 * hf + ww;
+                            const uint32_t sc = (scb[t] >> (8 * w)) & 0xFF;
+                            const uint32_t d2 = f16x2_bcast(d * (float)(sc & 15));
+                            const uint32_t m2 = f16x2_bcast(-(dmin * (float)(sc >> 4)));
+                            const uint32_t word = wsel(qv[t], w);
+#pragma unroll
+                            for (int sp = 0; sp < 4; sp++) {   // weights 64t + 16w + 4sp .. +3
+                                const uint32_t q = (word >> (2 * sp)) & 0x03030303u;
+                                h[8 * ww + 2 * sp] = f16_pair_dm(q, 0x5140, d2, m2);
+                                h[8 * ww + 2 * sp + 1] = f16_pair_dm(q, 0x7362, d2, m2);
+                            }
+                        }
+                        tmem_st16(abuf + 32 * t + 16 * hf, h);   // k = 64t + 32hf .. +31
+                    }
+                }
             } else if constexpr (TYPE == EF_Q4_K) {
                 // Row r: header (d, dmin, scale_min_k4 bytes) at 2048 + 16 rl; the
                 // qs bytes [4t, 4t+4) and [16+4t, 16+4t+4) of group j in lane
@@ -498,6 +586,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_body<EF_Q6_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_q5_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+                     int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
+    gemm_body<EF_Q5_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
+}
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_q2_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+                     int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
+    gemm_body<EF_Q2_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
+}
+__global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_q4_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q4_0>(xmap, W, rowgroups, nchunks, rows, k, M, y);
@@ -550,6 +648,8 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
     auto kern = TYPE == EF_Q8_0   ? gemm_q8_0_kernel
                 : TYPE == EF_Q4_0 ? gemm_q4_0_kernel
                 : TYPE == EF_Q4_K ? gemm_q4_k_kernel
+                : TYPE == EF_Q5_K ? gemm_q5_k_kernel
+                : TYPE == EF_Q2_K ? gemm_q2_k_kernel
                                   : gemm_q6_k_kernel;
     const size_t smem = gemm_smem<TYPE>();
     static unsigned long long configured = 0;
@@ -579,7 +679,9 @@ int gemm_status(ef_ctx *ctx) {
 }
 
 int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y) {
-    if ((w->type == EF_Q8_0 || w->type == EF_Q4_0 || w->type == EF_Q4_K || w->type == EF_Q6_K) && w->k % 8 == 0) {
+    if ((w->type == EF_Q8_0 || w->type == EF_Q4_0 || w->type == EF_Q4_K || w->type == EF_Q6_K || w->type == EF_Q5_K ||
+         w->type == EF_Q2_K) &&
+        w->k % 8 == 0) {
         // tcgen05 path: activations as f16 [M][K] (converted from f32 if needed)
         const __half *xh = (const __half *)x;
         if (x_type == EF_F32) {
@@ -595,6 +697,8 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
         if (w->type == EF_Q8_0) return launch_tc<EF_Q8_0>(ctx, w, xh, M, y);
         if (w->type == EF_Q4_0) return launch_tc<EF_Q4_0>(ctx, w, xh, M, y);
         if (w->type == EF_Q4_K) return launch_tc<EF_Q4_K>(ctx, w, xh, M, y);
+        if (w->type == EF_Q5_K) return launch_tc<EF_Q5_K>(ctx, w, xh, M, y);
+        if (w->type == EF_Q2_K) return launch_tc<EF_Q2_K>(ctx, w, xh, M, y);
         return launch_tc<EF_Q6_K>(ctx, w, xh, M, y);
     }
     // Other types: the token dimension in groups of 16 through the GEMV

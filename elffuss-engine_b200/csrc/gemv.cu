@@ -65,7 +65,6 @@ __device__ const __align__(16) uint16_t g_grid_iq1s_f16[EF_GRID_IQ1S_ENTRIES * 8
 
 constexpr uint32_t H2_1152 = 0x64806480u;   // half2(1152, 1152)
 constexpr uint32_t H2_1032 = 0x64086408u;   // half2(1032, 1032)
-constexpr uint32_t H2_1024 = 0x64006400u;   // half2(1024, 1024)
 constexpr int GV_WARPS = 8;                 // rowgroups (warps) per CTA = one rowblock
 constexpr int MAX_XS_BYTES = 64 * 1024;     // shared memory for activation data
 
@@ -158,9 +157,6 @@ template <int TYPE> __host__ __device__ inline int i8_xbytes(int M) {
     return (i8_frag_bytes<TYPE>(M) + 4 * (subs + 1) * mp + 15) & ~15;
 }
 
-__device__ __forceinline__ uint32_t wsel(const uint4 &v, int i) {
-    return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w;
-}
 // Shared-memory reads (activation data).
 __device__ __forceinline__ uint4 lds128(const uint8_t *p) { return *reinterpret_cast<const uint4 *>(p); }
 __device__ __forceinline__ uint2 lds64(const uint8_t *p) { return *reinterpret_cast<const uint2 *>(p); }
@@ -288,21 +284,8 @@ __device__ __forceinline__ void compute(const RawQ40 &r, const uint8_t *xc, int 
 }
 
 // --------------------------------------------------------- Q5_K / Q2_K ---
-// f16 operands: q as (1024 + q) - 1024 exactly, then one f16 fma with the
-// sub-block's f16(d * sc) and -f16(dmin * m).
-__device__ __forceinline__ uint32_t f16_pair_dm(uint32_t qbytes, uint32_t sel, uint32_t d2, uint32_t negm2) {
-    uint32_t r;
-    const uint32_t q = hsub2u(prmt(qbytes, 0x64646464u, sel), H2_1024);
-    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(q), "r"(d2), "r"(negm2));
-    return r;
-}
-// two f32 -> f16x2 (d, d) and (-m, -m)
-__device__ __forceinline__ uint32_t f16x2_bcast(float v) {
-    const uint32_t h = __half_as_ushort(__float2half_rn(v));
-    return h | (h << 16);
-}
-// bit c of x (c < 4) to bit 8c
-__device__ __forceinline__ uint32_t spread4(uint32_t x) { return (x * 0x00204081u) & 0x01010101u; }
+// f16 operands: f16_pair_dm (common.cuh) -- q as (1024 + q) - 1024 exactly,
+// then one f16 fma with the sub-block's f16(d * sc) and -f16(dmin * m).
 
 // Q5_K, lane (g,t): parts 0,1 / 2,3 = qs bytes 32t.. of rows g / g+8, part 4 =
 // fifth-bit words (low, high sub-block) of both rows, the rows' verbatim
