@@ -9,8 +9,9 @@
 //
 //   producer (1 thread):  per stage of 256 k, one cp.async.bulk per rowgroup
 //                         of its repacked chunk tiles (2 x 2176 B for Q8_0,
-//                         2 x 1152 B for Q4_0, 1 x 2304 B for Q4_K: a
-//                         rowgroup's chunks are contiguous), 2-4 stages as
+//                         2 x 1152 B for Q4_0, one 256-k tile of 2304 /
+//                         3360 / 2816 / 1344 B for Q4_K / Q6_K / Q5_K / Q2_K:
+//                         a rowgroup's chunks are contiguous), 2-4 stages as
 //                         shared memory allows; and TMA loads (128B swizzle,
 //                         into this CTA only) of the f16 activations, 64 k x
 //                         256 tokens per box (4 boxes in flight);
