@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 
 #include "common.cuh"
+#include "gen/iq_grids.h"
 #include "internal.h"
 
 namespace ef {
@@ -47,6 +48,10 @@ constexpr int GM_THREADS = 320;   // producer, MMA, 2 x 4 dequant/epilogue warps
 constexpr uint32_t GM_WAIT_LIMIT = 1u << 24;   // try_wait polls before giving up (about a second)
 
 __device__ int g_gemm_error;   // nonzero after a bounded wait gave up
+
+// i-quant codebooks as f16 (8 weights of an entry per 16 bytes, in weight order)
+__device__ const __align__(16) uint16_t g_gm_grid_iq2xxs[EF_GRID_IQ2XXS_ENTRIES * 8] = {EF_GRID_IQ2XXS_F16_INIT};
+__device__ const __align__(16) uint16_t g_gm_grid_iq1s[EF_GRID_IQ1S_ENTRIES * 8] = {EF_GRID_IQ1S_F16_INIT};
 
 // ------------------------------------------------------------ PTX wrappers --
 // (mbarrier and bulk-copy helpers are in common.cuh)
@@ -122,10 +127,16 @@ template <> struct GmTile<EF_Q4_K> { static constexpr int BYTES = 2304, SC = 204
 template <> struct GmTile<EF_Q6_K> { static constexpr int BYTES = 3360, SC = 3072, CK = 256; };
 template <> struct GmTile<EF_Q5_K> { static constexpr int BYTES = 2816, SC = 2560, CK = 256; };
 template <> struct GmTile<EF_Q2_K> { static constexpr int BYTES = 1344, SC = 1024, CK = 256; };
+template <> struct GmTile<EF_IQ2_XXS> { static constexpr int BYTES = 1056, SC = 1024, CK = 256; };   // SC: d
+template <> struct GmTile<EF_IQ1_S> { static constexpr int BYTES = 800, SC = 768, CK = 256; };        // SC: d
+// shared-memory codebook bytes: IQ2_XXS grid (256 x 16) + sign masks (128 x 16); IQ1_S grid (2048 x 16)
+template <int TYPE> __host__ __device__ constexpr int gm_tab() {
+    return TYPE == EF_IQ2_XXS ? 384 * 16 : TYPE == EF_IQ1_S ? 2048 * 16 : 0;
+}
 // weight stages (each 8 rowgroups x GM_KW) that fit beside the activation ring, at most 4
 template <int TYPE> __host__ __device__ constexpr int gm_sw() {
     constexpr int per = 8 * (GM_KW / GmTile<TYPE>::CK) * GmTile<TYPE>::BYTES;
-    constexpr int n = (GM_SMEM_MAX - 1024 - GM_SX * GM_BN * 128 - 256) / per;
+    constexpr int n = (GM_SMEM_MAX - 1024 - GM_SX * GM_BN * 128 - 256 - gm_tab<TYPE>()) / per;
     return n > 4 ? 4 : n;
 }
 
@@ -150,6 +161,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
     uint64_t *wfull = bars + 2 * GM_SX, *wempty = bars + 2 * GM_SX + SW;
     uint64_t *afull = bars + 2 * GM_SX + 2 * SW, *aempty = afull + 2, *tfull = afull + 4;
     uint32_t *tslot = reinterpret_cast<uint32_t *>(tfull + 1);
+    uint4 *tab = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(bars) + 256);   // i-quant codebooks
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t rb = blockIdx.x;                       // 8 rowgroups = 128 rows
@@ -165,6 +177,20 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
         return b < NBOX ? (int)b : NBOX;
     };
 
+    if constexpr (TYPE == EF_IQ2_XXS) {   // grid, then the sign masks (7 stored bits + even parity)
+        const uint4 *src = reinterpret_cast<const uint4 *>(g_gm_grid_iq2xxs);
+        for (int i = threadIdx.x; i < 256; i += GM_THREADS) tab[i] = src[i];
+        for (int i = threadIdx.x; i < 128; i += GM_THREADS) {
+            const uint32_t s8 = (uint32_t)i | ((uint32_t)(__popc(i) & 1) << 7);
+            uint32_t w[4];
+#pragma unroll
+            for (int p = 0; p < 4; p++) w[p] = (((s8 >> (2 * p)) & 1u) << 15) | (((s8 >> (2 * p + 1)) & 1u) << 31);
+            tab[256 + i] = make_uint4(w[0], w[1], w[2], w[3]);
+        }
+    } else if constexpr (TYPE == EF_IQ1_S) {
+        const uint4 *src = reinterpret_cast<const uint4 *>(g_gm_grid_iq1s);
+        for (int i = threadIdx.x; i < 2048; i += GM_THREADS) tab[i] = src[i];
+    }
     if (threadIdx.x == 0) {
         for (int s = 0; s < GM_SX; s++) {
             mbar_init(&xfull[s], 1);
@@ -413,6 +439,74 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                         tmem_st16(abuf + 32 * t + 16 * hf, h);   // k = 64t + 32hf .. +31
                     }
                 }
+            } else if constexpr (TYPE == EF_IQ2_XXS) {
+                // Row r = g + 8hs: lane column t holds 32-blocks 2t, 2t+1
+                // (weights 64t..): their GGUF bytes at part hs of lane 4g+t, per
+                // block u a word of four grid indices and a word of four 7-bit
+                // sign indices with the 4-bit scale on top; f16 d at
+                // 1024 + 4g + 2hs. Weight 8l + j of a block = db * grid * sign
+                // (kernels.wgsl.js:368-396), db = f16(d * (0.5 + s) / 4).
+                uint4 qv[4];
+                uint32_t dbits = 0;
+#pragma unroll
+                for (int t = 0; t < 4; t++)
+                    qv[t] = have ? *reinterpret_cast<const uint4 *>(T + hs * 512 + (4 * g + t) * 16) : make_uint4(0, 0, 0, 0);
+                if (have) dbits = *reinterpret_cast<const unsigned short *>(T + SCO + 4 * g + 2 * hs);
+                const float d = __half2float(__ushort_as_half((unsigned short)dbits));
+                const uint4 *grid = tab, *sgn = tab + 256;
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        const uint32_t a0 = u ? qv[t].z : qv[t].x, a1 = u ? qv[t].w : qv[t].y;
+                        const uint32_t db = f16x2_bcast(d * (0.5f + (float)(a1 >> 28)) * 0.25f);
+                        uint32_t h[16];
+#pragma unroll
+                        for (int l = 0; l < 4; l++) {
+                            const uint4 G = grid[(a0 >> (8 * l)) & 0xFF], S = sgn[(a1 >> (7 * l)) & 127];
+                            h[4 * l] = hmul2u(G.x ^ S.x, db);
+                            h[4 * l + 1] = hmul2u(G.y ^ S.y, db);
+                            h[4 * l + 2] = hmul2u(G.z ^ S.z, db);
+                            h[4 * l + 3] = hmul2u(G.w ^ S.w, db);
+                        }
+                        tmem_st16(abuf + 32 * t + 16 * u, h);   // k = 64t + 32u .. +31
+                    }
+                }
+            } else if constexpr (TYPE == EF_IQ1_S) {
+                // Row r = g + 8hs: lane column t holds 32-blocks 2t, 2t+1: their
+                // qs bytes (one word per block) at 16(4g+t) + 8hs, their qh
+                // halves at 512 + 8(4g+t) + 4hs; f16 d at 768 + 4g + 2hs. Weight
+                // 8l + j = dl * (grid + delta) (kernels.wgsl.js:805-822), grid
+                // entry qs byte l | qh bits 3l..3l+2 << 8, delta -/+ 1/8 by qh
+                // bit 15, dl = f16(d * (2 * qh[12..14] + 1)).
+                uint2 qs[4];
+                uint32_t qh[4], dbits = 0;
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+                    qs[t] = have ? *reinterpret_cast<const uint2 *>(T + (4 * g + t) * 16 + 8 * hs) : make_uint2(0, 0);
+                    qh[t] = have ? *reinterpret_cast<const uint32_t *>(T + 512 + (4 * g + t) * 8 + 4 * hs) : 0u;
+                }
+                if (have) dbits = *reinterpret_cast<const unsigned short *>(T + SCO + 4 * g + 2 * hs);
+                const float d = __half2float(__ushort_as_half((unsigned short)dbits));
+#pragma unroll
+                for (int t = 0; t < 4; t++) {
+#pragma unroll
+                    for (int u = 0; u < 2; u++) {
+                        const uint32_t q = u ? qs[t].y : qs[t].x, hh = (qh[t] >> (16 * u)) & 0xFFFFu;
+                        const uint32_t del = (hh & 0x8000u) ? 0xB000B000u : 0x30003000u;   // -/+ 0.125
+                        const uint32_t dl = f16x2_bcast(d * (float)(2u * ((hh >> 12) & 7u) + 1u));
+                        uint32_t h[16];
+#pragma unroll
+                        for (int l = 0; l < 4; l++) {
+                            const uint4 G = tab[((q >> (8 * l)) & 0xFF) | (((hh >> (3 * l)) & 7) << 8)];
+                            h[4 * l] = hmul2u(hadd2u(G.x, del), dl);   // grid + delta exact in f16
+                            h[4 * l + 1] = hmul2u(hadd2u(G.y, del), dl);
+                            h[4 * l + 2] = hmul2u(hadd2u(G.z, del), dl);
+                            h[4 * l + 3] = hmul2u(hadd2u(G.w, del), dl);
+                        }
+                        tmem_st16(abuf + 32 * t + 16 * u, h);   // k = 64t + 32u .. +31
+                    }
+                }
             } else if constexpr (TYPE == EF_Q4_K) {
                 // Row r: header (d, dmin, scale_min_k4 bytes) at 2048 + 16 rl; the
                 // qs bytes [4t, 4t+4) and [16+4t, 16+4t+4) of group j in lane
@@ -597,6 +691,16 @@ __global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_body<EF_Q2_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_iq2_xxs_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+                        int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
+    gemm_body<EF_IQ2_XXS>(xmap, W, rowgroups, nchunks, rows, k, M, y);
+}
+__global__ void __launch_bounds__(GM_THREADS, 1)
+    gemm_iq1_s_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
+    gemm_body<EF_IQ1_S>(xmap, W, rowgroups, nchunks, rows, k, M, y);
+}
+__global__ void __launch_bounds__(GM_THREADS, 1)
     gemm_q4_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q4_0>(xmap, W, rowgroups, nchunks, rows, k, M, y);
@@ -630,7 +734,7 @@ static EncodeTiledFn encode_fn() {
 
 template <int TYPE> static size_t gemm_smem() {
     return 1024 + (size_t)GM_SX * (GM_BN * 128) +
-           (size_t)gm_sw<TYPE>() * 8 * (GM_KW / GmTile<TYPE>::CK) * GmTile<TYPE>::BYTES + 256;
+           (size_t)gm_sw<TYPE>() * 8 * (GM_KW / GmTile<TYPE>::CK) * GmTile<TYPE>::BYTES + 256 + gm_tab<TYPE>();
 }
 
 template <int TYPE>
@@ -651,7 +755,9 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
                 : TYPE == EF_Q4_K ? gemm_q4_k_kernel
                 : TYPE == EF_Q5_K ? gemm_q5_k_kernel
                 : TYPE == EF_Q2_K ? gemm_q2_k_kernel
-                                  : gemm_q6_k_kernel;
+                : TYPE == EF_IQ2_XXS ? gemm_iq2_xxs_kernel
+                : TYPE == EF_IQ1_S   ? gemm_iq1_s_kernel
+                                     : gemm_q6_k_kernel;
     const size_t smem = gemm_smem<TYPE>();
     static unsigned long long configured = 0;
     if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
@@ -680,9 +786,9 @@ int gemm_status(ef_ctx *ctx) {
 }
 
 int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y) {
-    if ((w->type == EF_Q8_0 || w->type == EF_Q4_0 || w->type == EF_Q4_K || w->type == EF_Q6_K || w->type == EF_Q5_K ||
-         w->type == EF_Q2_K) &&
-        w->k % 8 == 0) {
+    // The activation tensor map needs rows of a multiple of 16 bytes (k % 8 == 0),
+    // which every GGUF block size (32 or 256 weights) gives.
+    if (w->k % 8 == 0) {
         // tcgen05 path: activations as f16 [M][K] (converted from f32 if needed)
         const __half *xh = (const __half *)x;
         if (x_type == EF_F32) {
@@ -700,10 +806,12 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
         if (w->type == EF_Q4_K) return launch_tc<EF_Q4_K>(ctx, w, xh, M, y);
         if (w->type == EF_Q5_K) return launch_tc<EF_Q5_K>(ctx, w, xh, M, y);
         if (w->type == EF_Q2_K) return launch_tc<EF_Q2_K>(ctx, w, xh, M, y);
-        return launch_tc<EF_Q6_K>(ctx, w, xh, M, y);
+        if (w->type == EF_IQ2_XXS) return launch_tc<EF_IQ2_XXS>(ctx, w, xh, M, y);
+        if (w->type == EF_IQ1_S) return launch_tc<EF_IQ1_S>(ctx, w, xh, M, y);
+        if (w->type == EF_Q6_K) return launch_tc<EF_Q6_K>(ctx, w, xh, M, y);
     }
-    // Other types: the token dimension in groups of 16 through the GEMV
-    // kernel (same numerics contract: f16 activations, f32 accumulation).
+    // Otherwise the token dimension in groups of 16 through the GEMV kernel
+    // (same numerics contract: f16 activations, f32 accumulation).
     const float *xf = (const float *)x;
     if (x_type == EF_F16) {
         const int64_t n = (int64_t)M * w->k;

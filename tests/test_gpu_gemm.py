@@ -15,7 +15,9 @@ REL = 1e-3
                                       ("Q8_0", 32, 4128), ("Q4_0", 256, 512), ("Q4_0", 40, 2048),
                                       ("Q4_0", 40, 4128), ("Q4_K", 128, 1024), ("Q4_K", 37, 2304),
                                       ("Q6_K", 64, 512), ("Q6_K", 37, 2304), ("Q5_K", 48, 1024),
-                                      ("Q5_K", 37, 2304), ("Q2_K", 64, 512), ("Q2_K", 37, 2304)])
+                                      ("Q5_K", 37, 2304), ("Q2_K", 64, 512), ("Q2_K", 37, 2304),
+                                      ("IQ2_XXS", 64, 512), ("IQ2_XXS", 37, 2304), ("IQ1_S", 64, 512),
+                                      ("IQ1_S", 37, 2304)])
 @pytest.mark.parametrize("M", [17, 64, 130])
 def test_gemm_f16x_vs_oracle(ops, oracle_mod, t, rows, k, M):
     raw = formats.synth(t, rows, k, seed=M + rows)
@@ -33,7 +35,8 @@ def test_gemm_f16x_vs_oracle(ops, oracle_mod, t, rows, k, M):
 @pytest.mark.parametrize("t,M,k,rows", [("Q8_0", 512, 2048, 8192), ("Q8_0", 2048, 8192, 2048),
                                         ("Q4_0", 512, 2048, 8192), ("Q4_K", 512, 4096, 4096),
                                         ("Q6_K", 512, 4096, 4096), ("Q5_K", 512, 4096, 4096),
-                                        ("Q2_K", 512, 4096, 4096)])
+                                        ("Q2_K", 512, 4096, 4096), ("IQ2_XXS", 512, 4096, 4096),
+                                        ("IQ1_S", 512, 4096, 4096)])
 def test_gemm_config2_vs_torch(ops, t, M, k, rows):
     raw = formats.synth(t, rows, k, seed=2)
     w = ops.load_weight(t, raw, rows, k)
