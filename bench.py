@@ -244,6 +244,70 @@ def tp_comm(ops, args, world, rank):
     return _COMM["c"]
 
 
+def bench_sharded(ops, L, args, world, rank, barrier, capture, timed_replays):
+    """Config 1 at N > 1 as one matrix split by output rows: each rank runs the
+    GEMV (1 token) on its rows / N, and an all-gather (the library's
+    peer-memory kernel) assembles the whole y on every rank. Reported per
+    shape: the kernel time, the all-gather time and both in sequence, each the
+    max over ranks of graph-replayed calls on enough weight copies that every
+    replay reads HBM."""
+    import torch
+
+    from elffuss_engine_b200 import formats
+    from elffuss_engine_b200._lib import check
+    from elffuss_engine_b200.ops import _ptr
+    comm = tp_comm(ops, args, world, rank)
+    if comm is None:
+        return {"skipped": "--tp-comm nccl: the all-gather is measured with the library's peer kernel only"}
+    out = []
+    for t, n, k in [("Q4_K", 14336, 4096), ("Q6_K", 14336, 4096)]:
+        rows = n // world
+        raw = formats.synth(t, rows, k, seed=500 + rank)
+        sb = formats.tensor_bytes(t, rows, k)
+        copies = min(64, max(8, -(-2 * 126 * 2 ** 20 // sb)))    # > twice the L2 per replay
+        ws = [ops.load_weight(t, raw, rows, k) for _ in range(copies)]
+        del raw
+        x = torch.randn(1, k, device="cuda", generator=torch.Generator("cuda").manual_seed(5))
+        ys = torch.empty(1, rows, device="cuda")
+        yall = torch.empty(world * rows, device="cuda")
+
+        def gemvs():
+            h = ops.ctx.bind()
+            for wc in ws:
+                check(L.ef_gemv(h, wc.h, _ptr(x), 1, _ptr(ys)), h)
+
+        def gathers():
+            for _ in ws:
+                comm.all_gather(yall, ys)
+
+        def both():
+            h = ops.ctx.bind()
+            for wc in ws:
+                check(L.ef_gemv(h, wc.h, _ptr(x), 1, _ptr(ys)), h)
+                comm.all_gather(yall, ys)
+
+        res = {}
+        for name, fn in (("kernel_us", gemvs), ("allgather_us", gathers), ("total_us", both)):
+            barrier()
+            g = capture(fn)
+            barrier()
+            for _ in range(3):
+                g.replay()
+            res[name] = round(timed_replays(g, 20) * 1e3 / (20 * copies), 2)
+            del g
+        if comm.status() != 0:
+            raise RuntimeError("sharded GEMV: a peer did not arrive in time")
+        whole = formats.tensor_bytes(t, n, k)
+        out.append({"type": t, "rows": n, "k": k, "rows_per_rank": rows, "weight_copies": copies, **res,
+                    "GBps_whole_matrix": round(whole / (res["total_us"] * 1e-6) / 1e9, 1)})
+        for wc in ws:
+            wc.free()
+        torch.cuda.empty_cache()
+    return {"workload": f"config1 14336x4096 GEMV (1 token) split by output rows over {world} ranks, y "
+                        "assembled on every rank by the library's peer-memory all-gather",
+            "per_shape": out}
+
+
 def bench_decode(ops, args, world, rank, barrier, max_over_ranks):
     """Config 3: the synthetic LFM3-shaped decoder (lfm3.py), tensor-parallel
     over the ranks when world > 1: a 512-id prompt (all ids at once through
@@ -594,6 +658,8 @@ def run_ours(args):
 
     # ---- config 2: Q8_0 prefill GEMM on tcgen05 (tensor roofline) ----
     gemm = None if args.no_gemm else bench_gemm(ops, L, args, capture, timed_replays, rank)
+    sharded = (bench_sharded(ops, L, args, world, rank, barrier, capture, timed_replays)
+               if world > 1 and args.sharded else None)
     for wk in work:
         wk[4].free()                  # the sweep's weights (486 MB) are no longer needed
     torch.cuda.empty_cache()
@@ -640,6 +706,7 @@ def run_ours(args):
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "gemm": gemm,
+            "sharded_gemv": sharded,
             "config0": {"workload": "config0 Q8_0 GEMV 8192x2048, 1 token (8 weight copies back to back)",
                         "us": round(us0, 2), "GBps": round(b0 / (us0 * 1e-6) / 1e9, 1),
                         "frac": round(b0 / (us0 * 1e-6) / 1e9 / peak, 4), "algorithmic_bytes": b0},
@@ -665,6 +732,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-2 GEMM measurement")
+    ap.add_argument("--sharded", action="store_true",
+                    help="N > 1: also time one config-1 matrix split by rows plus the all-gather of y")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3/4 decode measurements")
     ap.add_argument("--tp-comm", default="peer", choices=["peer", "peer-separate", "nccl"],
                     help="tensor-parallel decode collectives: the library's peer-memory kernels with the "
