@@ -44,7 +44,6 @@ constexpr int GM_BM = 128;     // weight rows per CTA tile (MMA M)
 constexpr int GM_BN = 256;     // tokens per CTA tile (MMA N)
 constexpr int GM_BKX = 64;     // k per activation stage (one 128-byte swizzle atom)
 constexpr int GM_SX = 4;       // activation stages
-constexpr int GM_THREADS = 320;   // producer, MMA, 2 x 4 dequant/epilogue warps
 constexpr uint32_t GM_WAIT_LIMIT = 1u << 24;   // try_wait polls before giving up (about a second)
 
 __device__ int g_gemm_error;   // nonzero after a bounded wait gave up
@@ -133,6 +132,10 @@ template <> struct GmTile<EF_IQ1_S> { static constexpr int BYTES = 800, SC = 768
 template <int TYPE> __host__ __device__ constexpr int gm_tab() {
     return TYPE == EF_IQ2_XXS ? 384 * 16 : TYPE == EF_IQ1_S ? 2048 * 16 : 0;
 }
+// Threads: producer, MMA, and 2 x 4 dequant / epilogue warps per chunk tile of
+// a stage (two tiles of 128 k for Q8_0 / Q4_0, dequantised in parallel by the
+// two halves of each group; one 256-k tile for the other types).
+template <int TYPE> __host__ __device__ constexpr int gm_threads() { return 64 + 256 * (GM_KW / GmTile<TYPE>::CK); }
 // weight stages (each 8 rowgroups x GM_KW) that fit beside the activation ring, at most 4
 template <int TYPE> __host__ __device__ constexpr int gm_sw() {
     constexpr int per = 8 * (GM_KW / GmTile<TYPE>::CK) * GmTile<TYPE>::BYTES;
@@ -145,6 +148,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                                           int64_t nchunks, int64_t rows, int64_t kdim, int M, float *__restrict__ y) {
     constexpr int TB = GmTile<TYPE>::BYTES, SCO = GmTile<TYPE>::SC, CK = GmTile<TYPE>::CK;
     constexpr int CPS = GM_KW / CK;                      // chunks per stage (contiguous per rowgroup)
+    constexpr int NTHR = gm_threads<TYPE>();             // 2 x 4 dequant warps per chunk of a stage
     constexpr int SW = gm_sw<TYPE>();
     constexpr int NBOX = GM_KW / GM_BKX, ACOLS = GM_KW / 2;
     constexpr int WRAW = 8 * CPS * TB;                   // 8 rowgroups x CPS chunk tiles
@@ -179,8 +183,8 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
 
     if constexpr (TYPE == EF_IQ2_XXS) {   // grid, then the sign masks (7 stored bits + even parity)
         const uint4 *src = reinterpret_cast<const uint4 *>(g_gm_grid_iq2xxs);
-        for (int i = threadIdx.x; i < 256; i += GM_THREADS) tab[i] = src[i];
-        for (int i = threadIdx.x; i < 128; i += GM_THREADS) {
+        for (int i = threadIdx.x; i < 256; i += NTHR) tab[i] = src[i];
+        for (int i = threadIdx.x; i < 128; i += NTHR) {
             const uint32_t s8 = (uint32_t)i | ((uint32_t)(__popc(i) & 1) << 7);
             uint32_t w[4];
 #pragma unroll
@@ -189,7 +193,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
         }
     } else if constexpr (TYPE == EF_IQ1_S) {
         const uint4 *src = reinterpret_cast<const uint4 *>(g_gm_grid_iq1s);
-        for (int i = threadIdx.x; i < 2048; i += GM_THREADS) tab[i] = src[i];
+        for (int i = threadIdx.x; i < 2048; i += NTHR) tab[i] = src[i];
     }
     if (threadIdx.x == 0) {
         for (int s = 0; s < GM_SX; s++) {
@@ -198,10 +202,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
         }
         for (int s = 0; s < SW; s++) {
             mbar_init(&wfull[s], 1);
-            mbar_init(&wempty[s], 128);
+            mbar_init(&wempty[s], 128 * CPS);
         }
         for (int b = 0; b < 2; b++) {
-            mbar_init(&afull[b], 128);
+            mbar_init(&afull[b], 128 * CPS);
             mbar_init(&aempty[b], 1);
         }
         mbar_init(tfull, 1);
@@ -283,15 +287,16 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             umma_commit(tfull);                // accumulator complete
         }
     } else {
-        // ------------------------ dequant (2 groups of 4 warps = 128 rows each)
-        // Group G = (warp - 2) / 4 handles the stages kk = G, G+2, ...
-        // (A buffer G), chunk by chunk. Thread = weight row r = tensor-memory lane: warp w
+        // ------------------------ dequant (2 groups of 4 warps = 128 rows each,
+        // per chunk of a stage) Group G handles the stages kk = G, G+2, ... (A
+        // buffer G); with two chunks per stage, half h of the group the chunk h.
+        // Thread = weight row r = tensor-memory lane: warp w
         // owns lanes 32*(w%4) .. +31. Row r of the tile is row g + 8hs of rowgroup r>>4;
         // its block t (32 quants) is two 16-byte parts of fragment lane 4g+t
         // and its f16 scale sits at 2048 + 4(4g+t) + 2hs. The four blocks are
         // read in a lane-staggered order, so one 128-bit shared load by the 32
         // lanes touches each bank group four times (no conflicts).
-        const int quad = warp & 3, grp = (warp - 2) >> 2;
+        const int quad = warp & 3, grp = ((warp - 2) >> 2) & 1, half = (warp - 2) >> 3;
         const int r = quad * 32 + lane;
         const int rl = r & 15, g = rl & 7, hs = rl >> 3, rg_in = r >> 4;
         const bool have = rb * 8 + rg_in < rowgroups;
@@ -304,7 +309,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             tc_fence_after();
             const int nc = CPS == 1 ? 1 : chunks_of(kk);
 #pragma unroll 1
-            for (int ch = 0; ch < nc; ch++) {
+            for (int ch = half; ch < nc; ch += CPS) {
             const uint8_t *T = ws + sw * WRAW + rg_in * (CPS * TB) + ch * TB;
             const uint32_t abuf = tmem + tlane + GM_TMEM_A + ACOLS * b + (CK / 2) * ch;
             if constexpr (TYPE == EF_Q6_K) {
@@ -632,8 +637,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
         tc_fence_after();
         if (ok) {
             const int64_t row = rb * GM_BM + quad * 32 + lane;
+            constexpr int EC = GM_BN / (2 * CPS);   // accumulator columns per epilogue group
+            const int eg = grp + 2 * half;
 #pragma unroll 1
-            for (int c0 = grp * (GM_BN / 2); c0 < (grp + 1) * (GM_BN / 2); c0 += 32) {
+            for (int c0 = eg * EC; c0 < (eg + 1) * EC; c0 += 32) {
                 if (n0 + c0 >= M) break;
                 uint32_t v[32];
                 asm volatile(
@@ -665,42 +672,42 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
 }
 
 // f32 -> f16 activations (round to nearest even), for x given in f32.
-__global__ void __launch_bounds__(GM_THREADS, 1)
+__global__ void __launch_bounds__(gm_threads<EF_Q8_0>(), 1)
     gemm_q8_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q8_0>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
-__global__ void __launch_bounds__(GM_THREADS, 1)
+__global__ void __launch_bounds__(gm_threads<EF_Q4_K>(), 1)
     gemm_q4_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q4_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
-__global__ void __launch_bounds__(GM_THREADS, 1)
+__global__ void __launch_bounds__(gm_threads<EF_Q6_K>(), 1)
     gemm_q6_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q6_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
-__global__ void __launch_bounds__(GM_THREADS, 1)
+__global__ void __launch_bounds__(gm_threads<EF_Q5_K>(), 1)
     gemm_q5_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q5_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
-__global__ void __launch_bounds__(GM_THREADS, 1)
+__global__ void __launch_bounds__(gm_threads<EF_Q2_K>(), 1)
     gemm_q2_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q2_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
-__global__ void __launch_bounds__(GM_THREADS, 1)
+__global__ void __launch_bounds__(gm_threads<EF_IQ2_XXS>(), 1)
     gemm_iq2_xxs_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                         int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_IQ2_XXS>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
-__global__ void __launch_bounds__(GM_THREADS, 1)
+__global__ void __launch_bounds__(gm_threads<EF_IQ1_S>(), 1)
     gemm_iq1_s_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                       int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_IQ1_S>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
-__global__ void __launch_bounds__(GM_THREADS, 1)
+__global__ void __launch_bounds__(gm_threads<EF_Q4_0>(), 1)
     gemm_q4_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q4_0>(xmap, W, rowgroups, nchunks, rows, k, M, y);
@@ -768,7 +775,7 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
     }
     dim3 grid((unsigned)((w->rowgroups + 7) / 8), (unsigned)((M + GM_BN - 1) / GM_BN));
     ctx->launches++;
-    kern<<<grid, GM_THREADS, smem, ctx->stream>>>(map, w->dev, w->rowgroups, w->nchunks, w->rows, w->k, M, y);
+    kern<<<grid, gm_threads<TYPE>(), smem, ctx->stream>>>(map, w->dev, w->rowgroups, w->nchunks, w->rows, w->k, M, y);
     return check_cuda(ctx, cudaGetLastError(), "gemm launch");
 }
 
