@@ -659,7 +659,7 @@ def run_ours(args):
     # ---- config 2: Q8_0 prefill GEMM on tcgen05 (tensor roofline) ----
     gemm = None if args.no_gemm else bench_gemm(ops, L, args, capture, timed_replays, rank)
     sharded = (bench_sharded(ops, L, args, world, rank, barrier, capture, timed_replays)
-               if world > 1 and args.sharded else None)
+               if world > 1 and not args.no_sharded else None)
     for wk in work:
         wk[4].free()                  # the sweep's weights (486 MB) are no longer needed
     torch.cuda.empty_cache()
@@ -732,8 +732,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-2 GEMM measurement")
-    ap.add_argument("--sharded", action="store_true",
-                    help="N > 1: also time one config-1 matrix split by rows plus the all-gather of y")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="N > 1: skip timing one config-1 matrix split by rows plus the all-gather of y")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3/4 decode measurements")
     ap.add_argument("--tp-comm", default="peer", choices=["peer", "peer-separate", "nccl"],
                     help="tensor-parallel decode collectives: the library's peer-memory kernels with the "
