@@ -293,6 +293,25 @@ class QuantOps:
         check(lib().ef_dequant(h, w.h, 0, nrows, _ptr(out)), h)
         return out
 
+    def gather(self, type, w: Weight, ids, dim: int, tokens: int) -> torch.Tensor:
+        """Rows of a quantized table to f32, out[t] = dequant(W)[ids[t]] (js/ops.js:1104-1118, the
+        embedding lookup): f32 [tokens][dim], bit-exact; an id outside the table's rows gives a
+        zero row. dim must be the row length and a whole number of blocks, as in the reference."""
+        name = formats.type_name(type)
+        be, _ = formats.block_info(name)
+        if dim % be:
+            raise EfError(-3, f"gather {name}: dim={dim} is not a multiple of {be}")
+        self._check_weight(name, w, w.rows, dim)
+        if tokens < 1:
+            raise EfError(-3, f"gather: tokens={tokens}")
+        ids = torch.as_tensor(ids).reshape(-1)[:tokens].to(self.device, torch.int32).contiguous()
+        if ids.numel() < tokens:
+            raise EfError(-7, f"gather: {ids.numel()} ids < tokens = {tokens}")
+        out = torch.empty((tokens, dim), dtype=torch.float32, device=self.device)
+        h = self.ctx.bind()
+        check(lib().ef_gather(h, w.h, _ptr(ids), tokens, _ptr(out)), h)
+        return out
+
     def matmul(self, type, w: Weight, x, rows: int, k: int, tokens: int = 1) -> torch.Tensor:
         """Y[tokens][rows] = dequant(W) . X (js/ops.js:827-1101): GEMV up to 16 tokens,
         tensor-core GEMM above."""

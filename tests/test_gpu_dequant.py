@@ -66,3 +66,23 @@ def test_slice_load_is_the_sub_matrix(ops, oracle_mod):
     w = ops.load_weight_slice("Q6_K", raw, rows, k, 16, 24, 256, 512)
     got = ops.dequant("Q6_K", w, 24 * 2).cpu().numpy().reshape(24, 512)
     np.testing.assert_array_equal(got, full[16:40, 256:768])
+
+
+@pytest.mark.parametrize("t", ["Q8_0", "Q4_0", "Q2_K", "Q4_K", "Q5_K", "Q6_K", "IQ2_XXS", "IQ1_S"])
+def test_gather_operator_rows_of_dequant(ops, t):
+    """quant.gather (js/ops.js:1104-1118): the chosen rows of dequant(W), bit for
+    bit, repeated ids included; an id past the table gives a zero row; a dim that
+    is not a whole number of blocks is refused as the reference refuses it."""
+    from elffuss_engine_b200._lib import EfError
+    be, _ = formats.block_info(t)
+    rows, k = 40, 512
+    raw = formats.synth(t, rows, k, seed=9)
+    w = ops.load_weight(t, raw, rows, k)
+    wd = ops.dequant(t, w, rows * k // be).reshape(rows, k)
+    ids = [3, 0, 39, 3, 40]
+    out = ops.gather(t, w, ids, k, 5)
+    assert out.shape == (5, k)
+    assert torch.equal(out[:4], wd[[3, 0, 39, 3]])
+    assert torch.equal(out[4], torch.zeros(k, device=out.device))
+    with pytest.raises(EfError):
+        ops.gather(t, w, ids, k + 16, 5)
