@@ -57,6 +57,7 @@ _SIGS = {
     "ef_weight_load": ([_P, _I, _P, _I64, _I64, _PP], _I),
     "ef_weight_load_device": ([_P, _I, _P, _I64, _I64, _PP], _I),
     "ef_weight_load_slice": ([_P, _I, _P, _I64, _I64, _I64, _I64, _I64, _I64, _PP], _I),
+    "ef_weight_load_shard": ([_P, _I, _P, _I64, _I64, _I, _I, _I, _PP], _I),
     "ef_weight_free": ([_P, _P], _I),
     "ef_weight_info": ([_P, ctypes.POINTER(_I), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
                         ctypes.POINTER(_SZ)], _I),

@@ -295,6 +295,26 @@ int ef_weight_load_slice(ef_ctx *ctx, int type, const void *host_gguf, int64_t r
     return ef_weight_load(ctx, type, part.data(), nrows, nk, out);
 }
 
+int ef_weight_load_shard(ef_ctx *ctx, int type, const void *host_gguf, int64_t rows, int64_t k, int shard_axis,
+                         int rank, int nranks, ef_weight **out) {
+    if (!ctx || !host_gguf || !out) return EF_ERR_INVALID;
+    if (nranks < 1 || rank < 0 || rank >= nranks || (shard_axis != 0 && shard_axis != 1))
+        return set_err(ctx, EF_ERR_INVALID, "shard: axis %d, rank %d of %d", shard_axis, rank, nranks);
+    TypeGeo g;
+    if (int rc = check_shape(ctx, type, rows, k, g)) return rc;
+    if (shard_axis == 0) {   // column-parallel: a range of output rows
+        if (rows % nranks) return set_err(ctx, EF_ERR_SHAPE, "shard: %lld rows over %d ranks", (long long)rows, nranks);
+        const int64_t n = rows / nranks;
+        return ef_weight_load_slice(ctx, type, host_gguf, rows, k, rank * n, n, 0, k, out);
+    }
+    // row-parallel: a range of input columns, whole blocks
+    if (k % ((int64_t)nranks * g.block_elems))
+        return set_err(ctx, EF_ERR_SHAPE, "shard: k=%lld is not %d ranks x whole blocks of %d", (long long)k, nranks,
+                       g.block_elems);
+    const int64_t n = k / nranks;
+    return ef_weight_load_slice(ctx, type, host_gguf, rows, k, 0, rows, rank * n, n, out);
+}
+
 int ef_weight_free(ef_ctx *ctx, ef_weight *w) {
     if (!ctx || !w) return EF_ERR_INVALID;
     cudaSetDevice(ctx->device);

@@ -255,6 +255,18 @@ class QuantOps:
                                          row0, nrows, k0, nk, ctypes.byref(h)), c)
         return Weight(self.ctx, h, name, nrows, nk, label)
 
+    def load_weight_shard(self, type, raw, rows, k, axis, rank, nranks, label="") -> Weight:
+        """Rank `rank` of `nranks`'s shard of a host tensor: axis 0 splits the output
+        rows (column-parallel), axis 1 the input columns (row-parallel); even splits only."""
+        name = formats.type_name(type)
+        a = np.ascontiguousarray(np.asarray(raw, dtype=np.uint8).reshape(-1))
+        h = ctypes.c_void_p()
+        c = self.ctx.bind()
+        check(lib().ef_weight_load_shard(c, formats.type_id(name), a.ctypes.data_as(ctypes.c_void_p), rows, k,
+                                         axis, rank, nranks, ctypes.byref(h)), c)
+        return Weight(self.ctx, h, name, rows // nranks if axis == 0 else rows, k // nranks if axis == 1 else k,
+                      label)
+
     def _check_weight(self, tipo, w: Weight, rows, k):
         name = formats.type_name(tipo)
         if name not in formats.HOT_TYPES:

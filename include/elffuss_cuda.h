@@ -138,6 +138,14 @@ EF_API int ef_weight_load_device(ef_ctx *ctx, int type, const void *dev_gguf, in
  * block). No reference counterpart: the reference is single-device. */
 EF_API int ef_weight_load_slice(ef_ctx *ctx, int type, const void *host_gguf, int64_t rows, int64_t k,
                          int64_t row0, int64_t nrows, int64_t k0, int64_t nk, ef_weight **out);
+/* The shard of tensor-parallel rank `rank` of `nranks` of a host GGUF tensor
+ * of rows x k, as ef_weight_load_slice loads it: shard_axis 0 = column-
+ * parallel (rows / nranks consecutive output rows), 1 = row-parallel
+ * (k / nranks consecutive input columns, whole blocks). The split must be
+ * even (EF_ERR_SHAPE otherwise). The drop-in boundary's TP weight loader; no
+ * reference counterpart: the reference is single-device. */
+EF_API int ef_weight_load_shard(ef_ctx *ctx, int type, const void *host_gguf, int64_t rows, int64_t k,
+                                int shard_axis, int rank, int nranks, ef_weight **out);
 EF_API int ef_weight_free(ef_ctx *ctx, ef_weight *w);
 EF_API int ef_weight_info(const ef_weight *w, int *type, int64_t *rows, int64_t *k, size_t *dev_bytes);
 /* Inverse repack: write the original GGUF bytes (rows * k/elems * bytes) to

@@ -68,6 +68,25 @@ def test_slice_load_is_the_sub_matrix(ops, oracle_mod):
     np.testing.assert_array_equal(got, full[16:40, 256:768])
 
 
+@pytest.mark.parametrize("t,axis", [("Q8_0", 0), ("Q8_0", 1), ("Q4_K", 0), ("Q4_K", 1), ("Q6_K", 1)])
+def test_shard_load_is_the_rank_slice(ops, oracle_mod, t, axis):
+    """ef_weight_load_shard: rank r of 4 gets rows (axis 0) or columns (axis 1)
+    [r * n/4, (r+1) * n/4) of the tensor, bit-exact; uneven splits are refused."""
+    from elffuss_engine_b200._lib import EfError
+    rows, k, n = 64, 2048, 4
+    raw = formats.synth(t, rows, k, seed=12)
+    full = oracle_mod.dequant(t, raw).reshape(rows, k)
+    be, _ = formats.block_info(t)
+    for r in range(n):
+        w = ops.load_weight_shard(t, raw, rows, k, axis, r, n)
+        nr, nk = (rows // n, k) if axis == 0 else (rows, k // n)
+        got = ops.dequant(t, w, nr * nk // be).cpu().numpy().reshape(nr, nk)
+        want = full[r * nr:(r + 1) * nr] if axis == 0 else full[:, r * nk:(r + 1) * nk]
+        np.testing.assert_array_equal(got, want)
+    with pytest.raises(EfError):
+        ops.load_weight_shard(t, raw, rows, k, axis, 0, 3)   # 64 rows / 2048 columns do not split in 3
+
+
 @pytest.mark.parametrize("t", ["Q8_0", "Q4_0", "Q2_K", "Q4_K", "Q5_K", "Q6_K", "IQ2_XXS", "IQ1_S"])
 def test_gather_operator_rows_of_dequant(ops, t):
     """quant.gather (js/ops.js:1104-1118): the chosen rows of dequant(W), bit for
