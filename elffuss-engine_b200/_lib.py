@@ -94,6 +94,7 @@ _SIGS = {
     "ef_allgather": ([_P, _P, _P, ctypes.c_int64, _P], _I),
     "ef_tp_status": ([_P, _P], _I),
     "ef_gemm_status": ([_P], _I),
+    "ef_gemm_set_wait_limit": ([_P, _I], _I),
     "ef_gguf_open": ([ctypes.c_char_p, _P, ctypes.c_char_p, ctypes.c_size_t], _I),
     "ef_gguf_close": ([_P], _I),
     "ef_gguf_header": ([_P, _P, _P, _P, _P, _P], _I),

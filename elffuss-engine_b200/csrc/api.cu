@@ -33,6 +33,8 @@ int check_cuda(ef_ctx *ctx, cudaError_t e, const char *what) {
 
 int ensure_scratch(ef_ctx *ctx, int slot, size_t bytes, bool zero) {
     if (ctx->scratch_bytes[slot] >= bytes) return EF_OK;
+    if (ctx->no_alloc)
+        return set_err(ctx, EF_ERR_RANGE, "scratch: %zu bytes needed, more than the allocation-free array", bytes);
     if (ctx->scratch[slot]) {
         // Queued work or a CUDA graph captured earlier may still use the old
         // buffer: it is kept until the context is destroyed.
@@ -418,6 +420,12 @@ int ef_gemm_status(ef_ctx *ctx) {
     if (!ctx) return EF_ERR_INVALID;
     if (int rc = use_device(ctx)) return rc;
     return gemm_status(ctx);
+}
+
+int ef_gemm_set_wait_limit(ef_ctx *ctx, int polls) {
+    if (!ctx) return EF_ERR_INVALID;
+    if (int rc = use_device(ctx)) return rc;
+    return gemm_set_wait_limit(ctx, polls);
 }
 
 int ef_matmul(ef_ctx *ctx, const ef_weight *w, const float *x, int tokens, float *y) {

@@ -34,6 +34,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "gen/iq_grids.h"
 #include "internal.h"
@@ -47,6 +49,10 @@ constexpr int GM_SX = 4;       // activation stages
 constexpr uint32_t GM_WAIT_LIMIT = 1u << 24;   // try_wait polls before giving up (about a second)
 
 __device__ int g_gemm_error;   // nonzero after a bounded wait gave up
+// Polls a pipeline wait makes before it gives up (GM_WAIT_LIMIT unless a test
+// lowers it through ef_gemm_set_wait_limit). The waits that let a CTA's own
+// copies and MMAs drain before it exits always use GM_WAIT_LIMIT.
+__device__ uint32_t g_gemm_wait_limit = GM_WAIT_LIMIT;
 
 // i-quant codebooks as f16 (8 weights of an entry per 16 bytes, in weight order)
 __device__ const __align__(16) uint16_t g_gm_grid_iq2xxs[EF_GRID_IQ2XXS_ENTRIES * 8] = {EF_GRID_IQ2XXS_F16_INIT};
@@ -54,8 +60,8 @@ __device__ const __align__(16) uint16_t g_gm_grid_iq1s[EF_GRID_IQ1S_ENTRIES * 8]
 
 // ------------------------------------------------------------ PTX wrappers --
 // (mbarrier and bulk-copy helpers are in common.cuh)
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
-    if (mbar_wait_bounded(bar, parity, GM_WAIT_LIMIT)) return true;
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit) {
+    if (mbar_wait_bounded(bar, parity, limit)) return true;
     atomicExch(&g_gemm_error, 1);
     return false;
 }
@@ -221,6 +227,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
+    const uint32_t lim = g_gemm_wait_limit;
     bool ok = true;
 
     if (warp == 0) {
@@ -231,7 +238,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             // warps have consumed stage kk - SW)
             auto issue_w = [&](int kk) {
                 const int sw = kk % SW;
-                if (kk >= SW) ok = mbar_wait(&wempty[sw], ((kk / SW) - 1) & 1);
+                if (kk >= SW) ok = mbar_wait(&wempty[sw], ((kk / SW) - 1) & 1, lim);
                 if (!ok) return;
                 const int nc = chunks_of(kk);
                 mbar_expect_tx(&wfull[sw], (uint32_t)(nrg * nc * TB));
@@ -245,7 +252,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                 const int nb = boxes_of(kk);
                 for (int h = 0; h < nb && ok; h++) {
                     const int sx = xi % GM_SX;
-                    if (xi >= GM_SX) ok = mbar_wait(&xempty[sx], ((xi / GM_SX) - 1) & 1);
+                    if (xi >= GM_SX) ok = mbar_wait(&xempty[sx], ((xi / GM_SX) - 1) & 1, lim);
                     if (!ok) break;
                     mbar_expect_tx(&xfull[sx], XBYTES);
                     tma_2d(xs + sx * XBYTES, &xmap, kk * GM_KW + h * GM_BKX, n0, &xfull[sx]);
@@ -265,14 +272,14 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             int xc = 0;                              // activation boxes consumed
             for (int kk = 0; kk < nk && ok; kk++) {
                 const int b = kk & 1;
-                ok = mbar_wait(&afull[b], (kk >> 1) & 1);
+                ok = mbar_wait(&afull[b], (kk >> 1) & 1, lim);
                 if (!ok) break;
                 tc_fence_after();
                 const uint32_t abuf = tmem + GM_TMEM_A + ACOLS * b;
                 const int nb = boxes_of(kk);
                 for (int h = 0; h < nb && ok; h++) {
                     const int sx = xc % GM_SX;
-                    ok = mbar_wait(&xfull[sx], (xc / GM_SX) & 1);
+                    ok = mbar_wait(&xfull[sx], (xc / GM_SX) & 1, lim);
                     if (!ok) break;
                     xc++;
                     tc_fence_after();
@@ -285,6 +292,10 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                 umma_commit(&aempty[b]);       // A buffer reusable
             }
             umma_commit(tfull);                // accumulator complete
+            // Whether or not a wait gave up, every MMA issued above must finish
+            // before tensor memory is freed and the CTA's shared memory is
+            // released (the epilogue warps skip their wait after a failure).
+            mbar_wait_bounded(tfull, 0, GM_WAIT_LIMIT);
         }
     } else {
         // ------------------------ dequant (2 groups of 4 warps = 128 rows each,
@@ -303,8 +314,8 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
         const uint32_t tlane = (uint32_t)(quad * 32) << 16;
         for (int kk = grp; kk < nk && ok; kk += 2) {
             const int sw = kk % SW, b = kk & 1;
-            ok = mbar_wait(&wfull[sw], (kk / SW) & 1);
-            if (ok && kk >= 2) ok = mbar_wait(&aempty[b], ((kk >> 1) - 1) & 1);
+            ok = mbar_wait(&wfull[sw], (kk / SW) & 1, lim);
+            if (ok && kk >= 2) ok = mbar_wait(&aempty[b], ((kk >> 1) - 1) & 1, lim);
             if (!ok) break;
             tc_fence_after();
             const int nc = CPS == 1 ? 1 : chunks_of(kk);
@@ -633,7 +644,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
             mbar_arrive(&wempty[sw]);
         }
         // ------------------------------------------------------------ epilogue
-        if (ok) ok = mbar_wait(tfull, 0);
+        if (ok) ok = mbar_wait(tfull, 0, lim);
         tc_fence_after();
         if (ok) {
             const int64_t row = rb * GM_BM + quad * 32 + lane;
@@ -766,12 +777,12 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
                 : TYPE == EF_IQ1_S   ? gemm_iq1_s_kernel
                                      : gemm_q6_k_kernel;
     const size_t smem = gemm_smem<TYPE>();
-    static unsigned long long configured = 0;
-    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
+    static std::atomic<unsigned long long> configured{0};   // one bit per device
+    if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
         if (int rc = check_cuda(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                                 "gemm smem attribute"))
             return rc;
-        configured |= 1ull << ctx->device;
+        configured.fetch_or(1ull << ctx->device);
     }
     dim3 grid((unsigned)((w->rowgroups + 7) / 8), (unsigned)((M + GM_BN - 1) / GM_BN));
     ctx->launches++;
@@ -790,6 +801,14 @@ int gemm_status(ef_ctx *ctx) {
     if (int rc = check_cuda(ctx, cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int)), "gemm status clear"))
         return rc;
     return set_err(ctx, EF_ERR_TIMEOUT, "gemm: a pipeline wait gave up; outputs since the last check are invalid");
+}
+
+// Sets the poll count of the pipeline waits (negative: the default, about a
+// second; 0: every wait gives up without polling).
+int gemm_set_wait_limit(ef_ctx *ctx, int polls) {
+    const uint32_t v = polls < 0 ? GM_WAIT_LIMIT : (uint32_t)polls;
+    if (int rc = check_cuda(ctx, cudaStreamSynchronize(ctx->stream), "gemm wait limit sync")) return rc;
+    return check_cuda(ctx, cudaMemcpyToSymbol(g_gemm_wait_limit, &v, sizeof(v)), "gemm wait limit set");
 }
 
 int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y) {

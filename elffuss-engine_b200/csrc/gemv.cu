@@ -48,6 +48,7 @@
 #include <stdlib.h>
 
 #include <algorithm>
+#include <atomic>
 #include <map>
 #include <mutex>
 #include <tuple>
@@ -1339,11 +1340,11 @@ static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int64_t rowblocks, bool fused
     constexpr int KH = kh_of<TYPE, TQ, NT, SWIGLU>();
     constexpr int threads = GV_WARPS * KH * 32;
     auto kern = gemv_kernel<TYPE, TQ, NT, SWIGLU, FUSED, KH>;
-    static unsigned long long configured = 0;   // per instantiation, one bit per device
-    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
+    static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
+    if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
         if (e != cudaSuccess) return check_cuda(ctx, e, "gemv smem attribute");
-        configured |= 1ull << ctx->device;
+        configured.fetch_or(1ull << ctx->device);
     }
     // The widest k-split (at most 8 slices, a portable cluster) whose clusters
     // all fit on the device at once. Measured on B200 over 1024-12288 rows x
@@ -1560,6 +1561,7 @@ extern "C" int ef_gemv_noalloc(const ef_weight *w, const float *x, int M, float 
         return EF_ERR_CUDA;
     tmp.scratch[0] = addr[dev];
     tmp.scratch_bytes[0] = NOALLOC_SCRATCH_BYTES;
+    tmp.no_alloc = true;   // a size this file's check missed fails instead of allocating
     float *ys[1] = {y};
     const int rc = launch_gemv(&tmp, &w, 1, nullptr, x, M, ys);
     tmp.scratch[0] = nullptr;   // not the context's to free

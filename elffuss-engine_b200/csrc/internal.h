@@ -47,6 +47,9 @@ struct ef_ctx {
     // previous one on the stream finishes; it waits for that kernel's results
     // (griddepcontrol.wait) before reading them.
     bool pdl = false;
+    // Set only on the stack context of ef_gemv_noalloc: scratch must never
+    // grow (ensure_scratch reports EF_ERR_RANGE instead of allocating).
+    bool no_alloc = false;
 };
 
 namespace ef {
@@ -121,6 +124,7 @@ int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight 
 
 // gemm.cu
 int gemm_status(ef_ctx *ctx);
+int gemm_set_wait_limit(ef_ctx *ctx, int polls);
 int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int M, float *y);
 
 }  // namespace ef

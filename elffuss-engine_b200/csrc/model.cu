@@ -31,6 +31,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -901,13 +903,13 @@ template <int D, int G>
 static int part_launch(ef_ctx *ctx, dim3 grid, const float *q, const float *kcache, const float *vcache, const int *pos,
                        int tokens, int max_pos, int window, int heads, int kv_heads, float *part) {
     constexpr size_t smem = 2 * AK * D * sizeof(float);
-    static unsigned long long configured = 0;   // per instantiation, one bit per device
-    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
+    static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
+    if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
         if (int rc = check_cuda(ctx, cudaFuncSetAttribute(attn_part_kernel<D, G>,
                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                                 "attention smem attribute"))
             return rc;
-        configured |= 1ull << ctx->device;
+        configured.fetch_or(1ull << ctx->device);
     }
     return launch_on(ctx, attn_part_kernel<D, G>, grid, AT, smem, "attention launch", q, kcache, vcache, pos, tokens,
                      max_pos, window, heads, kv_heads, part);
@@ -918,13 +920,13 @@ static int prompt_attn_launch(ef_ctx *ctx, int seqs, const float *q, const float
                               const float *gate, const int *pos, int tokens, int max_pos, int window, int heads,
                               int kv_heads, float *out) {
     constexpr size_t smem = fa_smem<D>();
-    static unsigned long long configured = 0;   // per instantiation, one bit per device
-    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
+    static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
+    if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
         if (int rc = check_cuda(ctx, cudaFuncSetAttribute(attn_prompt_kernel<D, G>,
                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                                 "prompt attention smem attribute"))
             return rc;
-        configured |= 1ull << ctx->device;
+        configured.fetch_or(1ull << ctx->device);
     }
     const dim3 grid((unsigned)((tokens + FA_R / G - 1) / (FA_R / G)), (unsigned)kv_heads, (unsigned)seqs);
     return launch_on(ctx, attn_prompt_kernel<D, G>, grid, FA_T, smem, "prompt attention launch", q, kcache, vcache,
@@ -1080,15 +1082,15 @@ static int attention_launch(ef_ctx *ctx, const float *q, const float *kcache, co
     // other head groupings: a CTA per (head, query row), scores of all keys in shared memory
     const size_t smem = (size_t)span * 4;
     if (smem > 200 * 1024) return set_err(ctx, EF_ERR_RANGE, "attention: %d keys exceed shared memory", span);
-    static unsigned long long configured[2] = {0, 0};
+    static std::atomic<unsigned long long> configured[2] = {{0}, {0}};
     const int di = head_dim == 64 ? 0 : 1;
-    if (ctx->device < 64 && !(configured[di] & (1ull << ctx->device))) {
+    if (ctx->device < 64 && !(configured[di].load() & (1ull << ctx->device))) {
         cudaError_t e = di == 0 ? cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                        200 * 1024)
                                 : cudaFuncSetAttribute(attention_kernel<128>,
                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (int rc = check_cuda(ctx, e, "attention smem attribute")) return rc;
-        configured[di] |= 1ull << ctx->device;
+        configured[di].fetch_or(1ull << ctx->device);
     }
     const dim3 grid(heads, seqs * tokens);
     if (di == 0)
@@ -1129,12 +1131,12 @@ int ef_topk(ef_ctx *ctx, const float *logits, int rows, int n, int m, int *ids, 
     while (sort_n < nch * m) sort_n <<= 1;
     const size_t smem = (size_t)sort_n * 8;
     if (int rc = ensure_scratch(ctx, 3, (size_t)rows * nch * m * 8)) return rc;
-    static unsigned long long configured = 0;
-    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
+    static std::atomic<unsigned long long> configured{0};
+    if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
         if (int rc = check_cuda(ctx, cudaFuncSetAttribute(topk_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                           227 * 1024), "topk smem attribute"))
             return rc;
-        configured |= 1ull << ctx->device;
+        configured.fetch_or(1ull << ctx->device);
     }
     if (int rc = check_cuda(ctx, cudaMemsetAsync(flags, 0, (size_t)rows * sizeof(int), ctx->stream), "topk flags"))
         return rc;

@@ -8,6 +8,8 @@
 // tile layout.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "common.cuh"
 #include "gen/iq_grids.h"
 #include "internal.h"
@@ -199,12 +201,12 @@ int launch_gather_norm(ef_ctx *ctx, const ef_weight *w, const int *ids, int toke
     const size_t smem = (size_t)w->k * sizeof(float);
     if (smem > 200 * 1024) return set_err(ctx, EF_ERR_RANGE, "gather_rmsnorm: row of %lld exceeds shared memory",
                                           (long long)w->k);
-    static unsigned long long configured = 0;
-    if (ctx->device < 64 && !(configured & (1ull << ctx->device))) {
+    static std::atomic<unsigned long long> configured{0};
+    if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
         if (int rc = check_cuda(ctx, cudaFuncSetAttribute(gather_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                           200 * 1024), "gather_rmsnorm smem attribute"))
             return rc;
-        configured |= 1ull << ctx->device;
+        configured.fetch_or(1ull << ctx->device);
     }
     const int bpc = geo.chunk_k / geo.block_elems;
     const int64_t bpr = w->k / geo.block_elems;

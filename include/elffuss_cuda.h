@@ -205,15 +205,23 @@ EF_API int ef_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, i
  * reference counterpart (WebGPU has no device-side waits). */
 EF_API int ef_gemm_status(ef_ctx *ctx);
 
+/* Test hook for the bounded waits above: sets how many polls each pipeline
+ * wait of later GEMMs on the context's device makes before it gives up
+ * (negative restores the default, about a second; 0 makes every wait give up
+ * without polling, so the next GEMM stops at once and ef_gemm_status reports
+ * EF_ERR_TIMEOUT). The kernel still lets its own copies and tensor-core work
+ * drain before it exits. Synchronizes the context's stream. No reference
+ * counterpart. */
+EF_API int ef_gemm_set_wait_limit(ef_ctx *ctx, int polls);
+
 /* Decode GEMV that allocates nothing (no counterpart in the reference, which
  * is single-device and allocates through its own buffer pool). ef_gemv keeps
  * its per-call activation fragments in context scratch that it grows with
  * cudaMalloc on the first call of a larger shape; some callers cannot allow
- * that: code that runs while a stream is being captured into a CUDA graph
- * (cudaFree synchronizes and is not allowed there), decode loops that cannot
- * take the implicit device synchronization of an allocation, and hosts whose
- * device memory is owned entirely by another allocator (a framework's caching
- * allocator or a fixed arena). This variant uses a file-scope device array of
+ * that: hosts whose device memory is owned entirely by another allocator (a
+ * framework's caching allocator or a fixed arena), and decode loops that
+ * cannot take the implicit device synchronization of an allocation or a
+ * free. This variant uses a file-scope device array of
  * 1 MiB instead, held by every GPU that loads the library until the process
  * exits; it supports k up to the point where the activation data exceeds
  * 1 MiB (k up to about 30,000 for 9-16 tokens and 61,000 for 3-8 tokens;

@@ -72,3 +72,32 @@ def test_gemm_repeatable(ops, t, M, k, rows):
     for _ in range(10):
         assert torch.equal(ops.gemm2.matmul(t, w, x, rows, k, M, x_f16=True), y0)
     ops.gemm2.status()
+
+
+def test_gemm_wait_timeout_is_reported_and_recovers(ops, oracle_mod):
+    """Every pipeline wait given a limit of zero polls gives up at once: the
+    kernel still drains its own copies and MMAs, frees its tensor memory and
+    exits; ef_gemm_status reports EF_ERR_TIMEOUT; with the default limit back,
+    the next GEMM matches the oracle's GEMM2 contract."""
+    from elffuss_engine_b200._lib import EfError, check, lib
+    t, rows, k, M = "Q8_0", 256, 2048, 130
+    raw = formats.synth(t, rows, k, seed=11)
+    w = ops.load_weight(t, raw, rows, k)
+    x = np.random.default_rng(11).standard_normal((M, k)).astype(np.float32)
+    xh = oracle_mod.f32_to_f16_bits(x)
+    xd = torch.from_numpy(xh.view(np.float16)).cuda()
+    h = ops.ctx.bind()
+    try:
+        check(lib().ef_gemm_set_wait_limit(h, 0), h)   # zero polls: every pipeline wait gives up at once
+        ops.gemm2.matmul(t, w, xd, rows, k, M, x_f16=True)
+        with pytest.raises(EfError) as err:
+            ops.gemm2.status()
+        assert "EF_ERR_TIMEOUT" in str(err.value)
+    finally:
+        check(lib().ef_gemm_set_wait_limit(h, -1), h)   # the default limit again
+    ops.gemm2.status()   # cleared by the report above
+    y = ops.gemm2.matmul(t, w, xd, rows, k, M, x_f16=True).cpu().numpy()
+    ops.gemm2.status()
+    want = oracle_mod.matmul_f64(t, raw, rows, k, xh=xh, tokens=M, w16=True)
+    tol = oracle_mod.tolerance(t, raw, rows, k, xh.view(np.float16).astype(np.float32), rel=REL)
+    assert np.all(np.abs(y - want) <= tol)
