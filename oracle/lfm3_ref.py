@@ -23,7 +23,9 @@ f16(d*q), activations rounded to f16 -- so that the remaining difference to
 the GPU is f32 accumulation order, and greedy tokens can be compared exactly.
 With matmul="f32" (for the full-size model, whose f64 weights would not fit
 a test's memory) the products of those same f16 operands are summed in f32
-by the host BLAS; everything else stays f64.
+by the host BLAS; everything else stays f64. With matmul="exact" the products
+take the exact dequantised weights and unrounded activations, all f64 (the
+cross-check of oracle/forward_f32.py).
 Parity of this file with the reference's own code is unpinned: the reference
 ships no model tests and its CPU path (Node + WebAssembly) cannot run here; it
 is a restatement of the cited code.
@@ -74,6 +76,7 @@ class LFM3Oracle:
                  matmul: str = "f64"):
         self.cfg = cfg
         self.f32 = matmul == "f32"
+        self.exact = matmul == "exact"
         self.rank, self.world = rank, world
         self.allreduce = allreduce or (lambda v: v)
         self.allgather = allgather
@@ -82,7 +85,10 @@ class LFM3Oracle:
             if isinstance(val, tuple):
                 raw, rows, k = val
                 w = dequant_q8_0(raw, rows, k)
-                self.w16[name] = w.astype(np.float16).astype(np.float32 if self.f32 else np.float64)
+                if self.exact:
+                    self.w16[name] = w.astype(np.float64)
+                else:
+                    self.w16[name] = w.astype(np.float16).astype(np.float32 if self.f32 else np.float64)
                 if name == "token_embd":
                     self.embd = w if self.f32 else w.astype(np.float64)
             else:
@@ -99,6 +105,8 @@ class LFM3Oracle:
         self.pos = 0
 
     def mm(self, name: str, x: np.ndarray) -> np.ndarray:
+        if self.exact:
+            return self.w16[name] @ np.asarray(x, np.float64)
         if self.f32:
             return (self.w16[name] @ f16(x).astype(np.float32)).astype(np.float64)
         return self.w16[name] @ f16(x)
@@ -159,6 +167,7 @@ class LFM3Oracle:
         self.pos += 1
         if self.world == 1:
             logits = self.mm("token_embd", nrm)
+            self.last_logits = logits
             return int(np.argmax(logits))     # first maximum = lowest index wins ties
         logits = self.mm("output", nrm)       # this rank's vocabulary rows
         i = int(np.argmax(logits))

@@ -37,3 +37,21 @@ def ops():
         pytest.skip("no CUDA device")
     from elffuss_engine_b200.ops import QuantOps
     return QuantOps(0)
+
+
+_REPORT: dict = {}
+
+
+@pytest.fixture(scope="session")
+def parity_report():
+    """Measured error ratios and token agreements, written as JSON at the end
+    of the session to $EF_PARITY_REPORT when that is set (else only kept)."""
+    return _REPORT
+
+
+def pytest_sessionfinish(session, exitstatus):
+    path = os.environ.get("EF_PARITY_REPORT")
+    if path and _REPORT:
+        import json
+        with open(path, "w") as f:
+            json.dump(_REPORT, f, indent=1, sort_keys=True)

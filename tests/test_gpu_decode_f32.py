@@ -1,0 +1,150 @@
+"""North-star decode acceptance at the full benchmark shapes, against the
+reference GPU path's arithmetic: the f32 forward of oracle/forward_f32.py
+(exact f32 dequantised weights, f32 activations, f32 sums).
+
+  * config 3: the LFM3-shaped decoder with the bench's seeded weights and its
+    512-id prompt (one batched pass through the GEMM path), then 31 steps;
+  * config 4: the 8B-shaped Llama decoder with the bench's weights and its
+    4096-id context (4095 ids through the GEMM path, the last id as the first
+    step), 32 steps at batch 1 and at batch 16.
+
+The reference forward is teacher-forced on the CUDA decoder's own tokens, so
+every step is compared on the same history: the CUDA token must be the f32
+forward's greedy token, except where the f32 forward's top two logits are
+closer than the logit error the CUDA path's f16 / int8 operands cause (a
+near-tie: either token is a correct greedy pick within the acceptance
+tolerance). The first such step also ends the stretch over which the
+free-running sequences are identical; its index and margin are reported (to
+$EF_PARITY_REPORT when set). The logit error itself is bounded relative to
+the spread of the logits."""
+import numpy as np
+import pytest
+import torch
+
+from oracle.forward_f32 import F32Decoder
+
+pytestmark = pytest.mark.gpu
+# max |logit error| / std(logits) allowed at a step: twice the largest value
+# measured on B200 (0.049, config 4, where the 4095-token prompt runs through
+# the f16 GEMM); config 3 measured 0.020
+LOGIT_REL = 0.1
+
+
+def _compare(gpu_tok, gpu_logits, orc_logits):
+    """Per step and sequence: agreement, error and margins. gpu_tok [n][S],
+    gpu_logits / orc_logits [n][S][V] (CPU tensors)."""
+    rows = []
+    for i in range(len(gpu_tok)):
+        for s in range(len(gpu_tok[i])):
+            lo, lg = orc_logits[i][s].double(), gpu_logits[i][s].double()
+            g = int(gpu_tok[i][s])
+            top2 = torch.topk(lo, 2)
+            o = int(top2.indices[0])
+            err = float((lg - lo).abs().max())
+            rows.append(dict(step=i, seq=s, match=g == o, err_rel=err / float(lo.std()),
+                             gap=float(lo[o] - lo[g]), top2=float(top2.values[0] - top2.values[1]), err=err))
+    return rows
+
+
+def _summary(rows, S):
+    first = {}
+    for s in range(S):
+        mism = [r["step"] for r in rows if r["seq"] == s and not r["match"]]
+        first[s] = mism[0] if mism else None
+    return {"steps": max(r["step"] for r in rows) + 1, "sequences": S,
+            "tokens_matching": sum(r["match"] for r in rows), "tokens": len(rows),
+            "first_divergence_per_seq": first,
+            "divergences": [{k: (round(v, 6) if isinstance(v, float) else v) for k, v in r.items()}
+                            for r in rows if not r["match"]],
+            "max_err_rel": round(max(r["err_rel"] for r in rows), 6)}
+
+
+def _check(rows):
+    for r in rows:
+        assert r["err_rel"] <= LOGIT_REL, r
+        if not r["match"]:
+            # a different greedy pick only where the f32 forward's own logits of the
+            # two tokens are closer than twice the CUDA path's logit error
+            assert r["gap"] <= 2 * r["err"], r
+
+
+def test_config3_lfm3_512_prompt_vs_f32_forward(ops, parity_report):
+    from elffuss_engine_b200.lfm3 import LFM3Config, LFM3Decoder, synth_weights
+    cfg = LFM3Config()
+    n = 32
+    w = synth_weights(cfg, seed=0, device="cuda")
+    prompt = torch.randint(0, cfg.vocab, (512,), generator=torch.Generator().manual_seed(0), dtype=torch.int32)
+    dec = LFM3Decoder(ops, cfg, w)
+    dec.reset(out_base=prompt.numel())
+    dec.tok.copy_(prompt[:1].cuda())
+    dec.step()                                   # sizes the scratch (as generate() does)
+    torch.cuda.synchronize()
+    dec.reset(out_base=prompt.numel())
+    dec.prefill(prompt.cuda())
+    logits = [dec.logits.clone()]
+    dec.capture()
+    for _ in range(n - 1):
+        dec.run_step()
+        logits.append(dec.logits.clone())
+    torch.cuda.synchronize()
+    toks = dec.out_tokens[:n].cpu()
+    gpu_logits = [[lg.cpu()] for lg in logits]
+    dec.graph = None
+    del dec, logits
+    wc = {k: ((v[0].cpu(), v[1], v[2]) if isinstance(v, tuple) else v.cpu()) for k, v in w.items()}
+    del w
+    torch.cuda.empty_cache()
+    orc = F32Decoder("lfm3", cfg, wc, device="cuda")
+    orc.reset(1)
+    orc_logits = [orc.forward(prompt[None].long()).cpu()]
+    for i in range(n - 1):
+        orc_logits.append(orc.forward(toks[i].view(1, 1).long()).cpu())
+    del orc
+    torch.cuda.empty_cache()
+    rows = _compare([[int(t)] for t in toks], gpu_logits, orc_logits)
+    parity_report["decode config3 lfm3 512-id prompt vs f32 forward"] = _summary(rows, 1)
+    _check(rows)
+
+
+@pytest.fixture(scope="module")
+def llama8b():
+    """The bench's config-4 weights and ids, built once for both batch sizes."""
+    from elffuss_engine_b200.llama import LlamaConfig, synth_weights
+    cfg = LlamaConfig()
+    w = synth_weights(cfg, seed=0, device="cuda")
+    ids = torch.randint(0, cfg.vocab, (4096 + 15,), generator=torch.Generator().manual_seed(4), dtype=torch.int32)
+    yield cfg, w, ids
+    del w
+    torch.cuda.empty_cache()
+
+
+@pytest.mark.parametrize("B", [1, 16])
+def test_config4_llama8b_vs_f32_forward(ops, parity_report, llama8b, B):
+    from elffuss_engine_b200.llama import LlamaDecoder
+    cfg, w, ids = llama8b
+    n = 32
+    prompt = ids[:4096]
+    lasts = [int(prompt[-1])] + [int(t) for t in ids[4096:4096 + B - 1]]
+    dec = LlamaDecoder(ops, cfg, w, batch=B)
+    dec.start(prompt, lasts)
+    toks, gpu_logits = [], []
+    for _ in range(n):
+        dec.step()
+        toks.append(dec.tok.cpu().tolist())
+        gpu_logits.append(dec.logits.cpu())
+    del dec
+    torch.cuda.empty_cache()
+    wc = {k: ((v[0].cpu(),) + tuple(v[1:]) if isinstance(v, tuple) else v.cpu()) for k, v in w.items()}
+    orc = F32Decoder("llama", cfg, wc, device="cuda")
+    del wc
+    orc.reset(1)
+    orc.forward(prompt[None, :4095].long())
+    orc.fork(B)
+    orc_logits = [orc.forward(torch.tensor(lasts).view(B, 1)).cpu()]
+    for i in range(n - 1):
+        orc_logits.append(orc.forward(torch.tensor(toks[i]).view(B, 1)).cpu())
+    del orc
+    torch.cuda.empty_cache()
+    rows = _compare(toks, gpu_logits, orc_logits)
+    parity_report[f"decode config4 llama8b batch {B} vs f32 forward"] = _summary(rows, B)
+    _check(rows)
