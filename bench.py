@@ -1,29 +1,34 @@
 """Benchmark of the quantized GEMV hot path (BASELINE.json metric / config 1).
 
 Workload (config 1, the K-quant GEMV sweep): Q4_K and Q6_K weights of shapes
-14336x4096 and 4096x14336, activations M in {1, 4, 16} -- 12 GEMVs per step,
-each on its OWN copy of its weight tensor, so a step streams 486 MB of weights
-(> the 126 MB L2: every step reads HBM, no L2 flush needed). Synthetic seeded
-inputs with the BASELINE.json distributions (no dataset exists).
+14336x4096 and 4096x14336, activations M in {1, 4, 16} -- 12 GEMVs per round,
+each on its OWN copy of its weight tensor; a step is ROUNDS = 8 rounds on 8
+distinct copies (96 tensors, 3.9 GB: far more than the 126 MB L2, so every
+GEMV reads HBM and no flush is needed). Synthetic seeded inputs with the
+BASELINE.json distributions (no dataset exists).
 
-  value  = algorithmic bytes of all 12 GEMVs (weights + x + y) / device time
-           of the step: the step (12 x ef_gemv, each = activation prep kernel +
-           GEMV kernel) is captured once as a CUDA graph and replayed K times
-           back to back; CUDA events around the K replays, inputs resident;
+  value  = algorithmic bytes of the step's 96 GEMVs (weights + x + y) / device
+           time of the step: the step is captured once as a CUDA graph and
+           replayed K times back to back; CUDA events around the K replays,
+           inputs resident;
   e2e    = the same bytes through the public operator (QuantOps.gemv.matmul)
-           with x copied from pinned host memory and y copied back to pinned
-           host memory inside every step (captured and replayed the same way);
-  roofline: the GEMV's algorithmic bytes / its own duration (CUDA events
-           recorded between the kernels inside a captured step) against the
-           measured HBM copy bandwidth (MEASURED_PEAKS.json).
+           with the step's x copied from pinned host memory and all its y
+           copied back to pinned host memory inside every step;
+  roofline: each call's GEMV launched back to back on its 8 weight copies,
+           200 graph replays, against the measured HBM copy bandwidth
+           (MEASURED_PEAKS.json).
 
-N > 1 (torchrun, one rank per GPU): weak scaling -- every rank runs the same
-sweep on its own weights (independent tensors, no collective on the data path);
-the step time is the max over ranks and value counts all ranks' bytes.
+N > 1 (torchrun, one rank per GPU): strong scaling -- every matrix of the
+sweep is split by output rows over the ranks, each rank runs the GEMV on its
+rows and an all-gather (the library's peer-memory collective, or NCCL with
+--tp-comm nccl) assembles the whole y on every rank after every GEMV; value =
+whole-matrix bytes / the max over ranks of the step time. The weak-scaling
+figure (every rank streaming its own whole tensors) is reported beside it.
 
 --impl reference: the reference's CPU arithmetic restated in C (oracle/, the
 reference's own CPU path needs a JavaScript engine with WebAssembly, which is
-absent) on all host cores, on a bounded row sample of the same workload.
+absent here and on the GPU box) on all host cores, on a bounded row sample of
+the same workload.
 """
 from __future__ import annotations
 
@@ -90,7 +95,7 @@ class Clocks:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except OSError:
@@ -166,7 +171,7 @@ def run_reference(args):
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": WORKLOAD},
+            "data": "synthetic", "config": sweep_config(args.gpus, ROUNDS * sum(alg_bytes(*c) for c in calls())),
             "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                              "sample": desc},
             "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -226,7 +231,7 @@ def bench_gemm(ops, L, args, capture, timed_replays, rank):
                         "f16 activations, f32 out; 8 distinct weight tensors per shape",
             "per_shape": per_shape,
             "roofline": {"bound": "tensor", "achieved": round(ach, 1), "peak": peak, "unit": "TFLOP/s",
-                         "frac": round(ach / peak, 4), "peak_source": src, "kernel": "gemm_q8_0_kernel"}}
+                         "frac": round(ach / peak, 4), "peak_source": src, "kernel": "ef_gemm_q8_0_kernel"}}
 
 
 DECODE_PROMPT, DECODE_TOKENS = 512, 128
@@ -242,70 +247,6 @@ def tp_comm(ops, args, world, rank):
         from elffuss_engine_b200.tp import TPComm
         _COMM["c"] = TPComm(ops, rank, world, max_bytes=1 << 20)
     return _COMM["c"]
-
-
-def bench_sharded(ops, L, args, world, rank, barrier, capture, timed_replays):
-    """Config 1 at N > 1 as one matrix split by output rows: each rank runs the
-    GEMV (1 token) on its rows / N, and an all-gather (the library's
-    peer-memory kernel) assembles the whole y on every rank. Reported per
-    shape: the kernel time, the all-gather time and both in sequence, each the
-    max over ranks of graph-replayed calls on enough weight copies that every
-    replay reads HBM."""
-    import torch
-
-    from elffuss_engine_b200 import formats
-    from elffuss_engine_b200._lib import check
-    from elffuss_engine_b200.ops import _ptr
-    comm = tp_comm(ops, args, world, rank)
-    if comm is None:
-        return {"skipped": "--tp-comm nccl: the all-gather is measured with the library's peer kernel only"}
-    out = []
-    for t, n, k in [("Q4_K", 14336, 4096), ("Q6_K", 14336, 4096)]:
-        rows = n // world
-        raw = formats.synth(t, rows, k, seed=500 + rank)
-        sb = formats.tensor_bytes(t, rows, k)
-        copies = min(64, max(8, -(-2 * 126 * 2 ** 20 // sb)))    # > twice the L2 per replay
-        ws = [ops.load_weight(t, raw, rows, k) for _ in range(copies)]
-        del raw
-        x = torch.randn(1, k, device="cuda", generator=torch.Generator("cuda").manual_seed(5))
-        ys = torch.empty(1, rows, device="cuda")
-        yall = torch.empty(world * rows, device="cuda")
-
-        def gemvs():
-            h = ops.ctx.bind()
-            for wc in ws:
-                check(L.ef_gemv(h, wc.h, _ptr(x), 1, _ptr(ys)), h)
-
-        def gathers():
-            for _ in ws:
-                comm.all_gather(yall, ys)
-
-        def both():
-            h = ops.ctx.bind()
-            for wc in ws:
-                check(L.ef_gemv(h, wc.h, _ptr(x), 1, _ptr(ys)), h)
-                comm.all_gather(yall, ys)
-
-        res = {}
-        for name, fn in (("kernel_us", gemvs), ("allgather_us", gathers), ("total_us", both)):
-            barrier()
-            g = capture(fn)
-            barrier()
-            for _ in range(3):
-                g.replay()
-            res[name] = round(timed_replays(g, 20) * 1e3 / (20 * copies), 2)
-            del g
-        if comm.status() != 0:
-            raise RuntimeError("sharded GEMV: a peer did not arrive in time")
-        whole = formats.tensor_bytes(t, n, k)
-        out.append({"type": t, "rows": n, "k": k, "rows_per_rank": rows, "weight_copies": copies, **res,
-                    "GBps_whole_matrix": round(whole / (res["total_us"] * 1e-6) / 1e9, 1)})
-        for wc in ws:
-            wc.free()
-        torch.cuda.empty_cache()
-    return {"workload": f"config1 14336x4096 GEMV (1 token) split by output rows over {world} ranks, y "
-                        "assembled on every rank by the library's peer-memory all-gather",
-            "per_shape": out}
 
 
 def bench_decode(ops, args, world, rank, barrier, max_over_ranks):
@@ -470,6 +411,28 @@ def run_profile(args):
     return 0
 
 
+ROUNDS = 8          # weight copies per call: a step streams every call's matrix ROUNDS times
+REPLAYS = 200       # graph replays behind each per-call duration
+
+
+def sweep_config(world: int, step_bytes: int) -> dict:
+    """The `config` object of both arms' JSON lines (same keys)."""
+    return {"workload": WORKLOAD, "rounds_per_step": ROUNDS, "bytes_per_step": step_bytes,
+            "l2": f"inputs larger than L2: {ROUNDS} distinct weight tensors per call, "
+                  f"{ROUNDS * 12} per step ({ROUNDS * 486} MB at N = 1)",
+            "parallelism": "single GPU" if world == 1 else
+            f"row-sharded x{world}: every matrix split by output rows over the ranks, y assembled on every "
+            f"rank by an all-gather after each GEMV"}
+
+
+def shard_rows(raw, t: str, n: int, k: int, rank: int, world: int):
+    """Rows [rank * n / world, (rank + 1) * n / world) of a GGUF tensor's bytes."""
+    from elffuss_engine_b200 import formats
+    per_row = formats.tensor_bytes(t, 1, k)
+    r0, r1 = rank * n // world, (rank + 1) * n // world
+    return raw.reshape(-1)[r0 * per_row:r1 * per_row], r1 - r0
+
+
 def run_ours(args):
     import numpy as np
     import torch
@@ -489,47 +452,65 @@ def run_ours(args):
         from datetime import timedelta
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device(f"cuda:{local}"))
     ops = QuantOps(local)
-    stream = torch.cuda.current_stream()
+    L = lib()
+    comm = tp_comm(ops, args, world, rank) if world > 1 else None
 
-    # weights: one tensor per call (12 distinct tensors, > L2 per step), each
-    # drawn by the seeded host generator with the BASELINE distributions.
+    # weights: ROUNDS tensors per call (this rank's row shard of each at N > 1),
+    # each drawn by the seeded host generator with the BASELINE distributions;
+    # the same x per call in every round.
     work = []
     for i, (t, n, k, m) in enumerate(calls()):
-        raw = formats.synth(t, n, k, seed=1000 * rank + i)
-        w = ops.load_weight(t, raw, n, k)
-        x = torch.randn(m, k, device="cuda", generator=torch.Generator("cuda").manual_seed(i + 7 * rank))
-        y = torch.empty(m, n, device="cuda")
-        xh = torch.empty(m, k, dtype=torch.float32).pin_memory()
-        xh.copy_(x.cpu())
-        yh = torch.empty(m, n, dtype=torch.float32).pin_memory()
-        work.append((t, n, k, m, w, x, y, xh, yh, alg_bytes(t, n, k, m)))
-    del raw
-    step_bytes = sum(wk[-1] for wk in work)
-    L = lib()
-    # end-to-end buffers: all inputs of a step in one pinned host buffer (one
-    # host->device copy per step), all results gathered for one readback
-    x_elems = sum(m * k for (t, n, k, m, *_r) in work)
-    y_elems = sum(m * n for (t, n, k, m, *_r) in work)
-    xh_all = torch.cat([wk[7].view(-1) for wk in work]).pin_memory()
+        raw = formats.synth(t, n, k, seed=i)
+        part, rows = shard_rows(raw, t, n, k, rank, world) if world > 1 else (raw, n)
+        ws = [ops.load_weight(t, part, rows, k) for _ in range(ROUNDS)]
+        x = torch.randn(m, k, device="cuda", generator=torch.Generator("cuda").manual_seed(i))
+        y = torch.empty(m, rows, device="cuda")
+        yall = torch.empty(world * m * rows, device="cuda") if world > 1 else None
+        work.append(dict(t=t, n=n, k=k, m=m, rows=rows, ws=ws, x=x, y=y, yall=yall,
+                         bytes=alg_bytes(t, n, k, m), shard_bytes=alg_bytes(t, rows, k, m)))
+    del raw, part
+    step_bytes = ROUNDS * sum(wk["bytes"] for wk in work)        # whole matrices (all ranks together)
+
+    def gather(wk):
+        if world > 1:
+            if comm is not None:
+                comm.all_gather(wk["yall"], wk["y"])
+            else:
+                dist.all_gather_into_tensor(wk["yall"], wk["y"].view(-1))
+
+    def step_device():
+        h = ops.ctx.bind()
+        for r in range(ROUNDS):
+            for wk in work:
+                check(L.ef_gemv(h, wk["ws"][r].h, _ptr(wk["x"]), wk["m"], _ptr(wk["y"])), h)
+                gather(wk)
+
+    # end-to-end buffers: the step's inputs in one pinned host buffer (one
+    # host->device copy per step), all its results gathered for one readback
+    x_elems = sum(wk["m"] * wk["k"] for wk in work)
+    y_elems = ROUNDS * sum(wk["m"] * wk["rows"] * world for wk in work)
+    xh_all = torch.cat([wk["x"].view(-1).cpu() for wk in work]).pin_memory()
     x_all = torch.empty(x_elems, device="cuda")
     y_all = torch.empty(y_elems, device="cuda")
     yh_all = torch.empty(y_elems, dtype=torch.float32).pin_memory()
     x_views, off = [], 0
-    for (t, n, k, m, *_r) in work:
-        x_views.append(x_all[off:off + m * k].view(m, k))
-        off += m * k
-
-    def step_device():
-        h = ops.ctx.bind()
-        for (t, n, k, m, w, x, y, xh, yh, b) in work:
-            check(L.ef_gemv(h, w.h, _ptr(x), m, _ptr(y)), h)
+    for wk in work:
+        x_views.append(x_all[off:off + wk["m"] * wk["k"]].view(wk["m"], wk["k"]))
+        off += wk["m"] * wk["k"]
 
     def step_e2e():
-        x_all.copy_(xh_all, non_blocking=True)                      # the step's inputs, host -> device
-        outs = [ops.gemv.matmul(t, wt, xv, n, k, m)                  # public operator (allocates its output)
-                for (t, n, k, m, wt, *_r), xv in zip(work, x_views)]
-        torch.cat([o.view(-1) for o in outs], out=y_all)
-        yh_all.copy_(y_all, non_blocking=True)                       # the step's results, device -> host
+        x_all.copy_(xh_all, non_blocking=True)                  # the step's inputs, host -> device
+        outs = []
+        for r in range(ROUNDS):
+            for wk, xv in zip(work, x_views):
+                o = ops.gemv.matmul(wk["t"], wk["ws"][r], xv, wk["rows"], wk["k"], wk["m"])   # public operator
+                if world > 1:
+                    wk["y"].copy_(o)
+                    gather(wk)
+                    o = wk["yall"]
+                outs.append(o.view(-1))
+        torch.cat(outs, out=y_all)
+        yh_all.copy_(y_all, non_blocking=True)                   # the step's results, device -> host
 
     def barrier():
         torch.cuda.synchronize()
@@ -551,7 +532,7 @@ def run_ours(args):
         with torch.cuda.stream(cs):
             fn(*a)          # warm this stream (first-use attribute setup, scratch sizing)
         torch.cuda.synchronize()
-        with torch.cuda.graph(g, stream=cs):
+        with torch.cuda.graph(g, stream=cs, capture_error_mode="thread_local"):
             fn(*a)
         torch.cuda.synchronize()
         return g
@@ -582,132 +563,141 @@ def run_ours(args):
                               "warmup_launches": launches_per_step * args.warmup}), flush=True)
         return 0
 
-    # ---- device-resident timing: one captured step (12 GEMVs), replayed ----
-    g_dev = capture(step_device)
-    for _ in range(args.warmup):
-        g_dev.replay()
     with Clocks(local) as clk:
+        # ---- device-resident timing: one captured step, replayed K times ----
+        g_dev = capture(step_device)
+        for _ in range(args.warmup):
+            g_dev.replay()
         t_ms = timed_replays(g_dev, args.steps)
-    ms_step = t_ms / args.steps
-    value = world * step_bytes / (ms_step * 1e-3) / 1e9
+        ms_step = t_ms / args.steps
+        value = step_bytes / (ms_step * 1e-3) / 1e9
+        del g_dev
 
-    # ---- per-kernel durations: each call's GEMV launched back to back on 8
-    # distinct copies of its weight (more than L2 between reuses), CUDA events
-    # around the replays of that captured sequence ----
-    COPIES = 8
-    reps = max(3, min(args.steps, 20))
-    kern_ms = []
-    for i, (t, n, k, m, w, x, y, xh, yh, b) in enumerate(work):
-        raw = formats.synth(t, n, k, seed=1000 * rank + i)
-        ws = [w] + [ops.load_weight(t, raw, n, k) for _ in range(COPIES - 1)]
-        del raw
-
-        def seq(ws=ws, x=x, y=y, m=m):
-            h = ops.ctx.bind()
-            for wc in ws:
-                check(L.ef_gemv(h, wc.h, _ptr(x), m, _ptr(y)), h)
-        g_k = capture(seq)
-        g_k.replay()
-        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
-        ev0.record()
-        for _ in range(reps):
+        # ---- per-kernel durations: each call's GEMV launched back to back on
+        # its ROUNDS weight copies (more than L2 between reuses), CUDA events
+        # around REPLAYS replays of that captured sequence ----
+        kern_ms = []
+        for wk in work:
+            def seq(wk=wk):
+                h = ops.ctx.bind()
+                for wc in wk["ws"]:
+                    check(L.ef_gemv(h, wc.h, _ptr(wk["x"]), wk["m"], _ptr(wk["y"])), h)
+            g_k = capture(seq)
             g_k.replay()
-        ev1.record()
-        torch.cuda.synchronize()
-        kern_ms.append(ev0.elapsed_time(ev1) / (reps * COPIES))
-        del g_k
-        for wc in ws[1:]:
+            kern_ms.append(timed_replays(g_k, REPLAYS) / (REPLAYS * ROUNDS))
+            del g_k
+
+        # ---- config 0: Q8_0 GEMV 8192 x 2048, 1 token (the same back-to-back method) ----
+        raw0 = formats.synth("Q8_0", 8192, 2048, seed=77)
+        ws0 = [ops.load_weight("Q8_0", raw0, 8192, 2048) for _ in range(ROUNDS)]
+        del raw0
+        x0 = torch.randn(1, 2048, device="cuda", generator=torch.Generator("cuda").manual_seed(77))
+        y0 = torch.empty(1, 8192, device="cuda")
+
+        def seq0():
+            h = ops.ctx.bind()
+            for wc in ws0:
+                check(L.ef_gemv(h, wc.h, _ptr(x0), 1, _ptr(y0)), h)
+        g0 = capture(seq0)
+        g0.replay()
+        us0 = timed_replays(g0, REPLAYS) * 1e3 / (REPLAYS * ROUNDS)
+        b0 = formats.tensor_bytes("Q8_0", 8192, 2048) + 4 * 2048 + 4 * 8192
+        del g0
+        for wc in ws0:
             wc.free()
 
-    # ---- config 0: Q8_0 GEMV 8192 x 2048, 1 token (the same back-to-back method) ----
-    raw0 = formats.synth("Q8_0", 8192, 2048, seed=77 + rank)
-    ws0 = [ops.load_weight("Q8_0", raw0, 8192, 2048) for _ in range(COPIES)]
-    del raw0
-    x0 = torch.randn(1, 2048, device="cuda", generator=torch.Generator("cuda").manual_seed(77))
-    y0 = torch.empty(1, 8192, device="cuda")
+        # ---- end to end through the public operator, pinned host buffers ----
+        g_e2e = capture(step_e2e)
+        for _ in range(args.warmup):
+            g_e2e.replay()
+        e2e_ms = timed_replays(g_e2e, args.steps) / args.steps
+        e2e_val = step_bytes / (e2e_ms * 1e-3) / 1e9
+        h2d = 4 * x_elems
+        d2h = 4 * y_elems
+        del g_e2e
 
-    def seq0():
-        h = ops.ctx.bind()
-        for wc in ws0:
-            check(L.ef_gemv(h, wc.h, _ptr(x0), 1, _ptr(y0)), h)
-    g0 = capture(seq0)
-    g0.replay()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    ev0.record()
-    for _ in range(reps):
-        g0.replay()
-    ev1.record()
-    torch.cuda.synchronize()
-    us0 = ev0.elapsed_time(ev1) * 1e3 / (reps * COPIES)
-    b0 = formats.tensor_bytes("Q8_0", 8192, 2048) + 4 * 2048 + 4 * 8192
-    del g0
-    for wc in ws0:
-        wc.free()
+    # ---- N > 1: the same sweep with every rank streaming its own whole tensors
+    # (weak scaling, no collective), for comparison with the sharded value ----
+    weak = None
+    if world > 1:
+        full = []
+        for i, (t, n, k, m) in enumerate(calls()):
+            raw = formats.synth(t, n, k, seed=1000 * rank + i)
+            full.append((ops.load_weight(t, raw, n, k), torch.empty(m, n, device="cuda"), m, alg_bytes(t, n, k, m)))
+        del raw
 
-    # ---- end to end through the public operator, pinned host buffers ----
-    g_e2e = capture(step_e2e)
-    for _ in range(args.warmup):
-        g_e2e.replay()
-    e2e_ms = timed_replays(g_e2e, args.steps) / args.steps
-    e2e_val = world * step_bytes / (e2e_ms * 1e-3) / 1e9
-    h2d = 4 * x_elems
-    d2h = 4 * y_elems
-    del g_dev, g_e2e
+        def step_weak():
+            h = ops.ctx.bind()
+            for (w, y, m, b), wk in zip(full, work):
+                check(L.ef_gemv(h, w.h, _ptr(wk["x"]), m, _ptr(y)), h)
+        g_w = capture(step_weak)
+        for _ in range(3):
+            g_w.replay()
+        wms = timed_replays(g_w, 10 * args.steps) / (10 * args.steps)
+        weak = {"value": round(world * sum(b for *_, b in full) / (wms * 1e-3) / 1e9, 2), "unit": "GB/s",
+                "ms_per_step": round(wms, 4), "scaling": "weak",
+                "what": "every rank streams its own whole 12 tensors of the sweep, no collective; whole-job GB/s"}
+        del g_w
+        for w, *_ in full:
+            w.free()
 
     # ---- config 2: Q8_0 prefill GEMM on tcgen05 (tensor roofline) ----
     gemm = None if args.no_gemm else bench_gemm(ops, L, args, capture, timed_replays, rank)
-    sharded = (bench_sharded(ops, L, args, world, rank, barrier, capture, timed_replays)
-               if world > 1 and not args.no_sharded else None)
     for wk in work:
-        wk[4].free()                  # the sweep's weights (486 MB) are no longer needed
+        for w in wk["ws"]:
+            w.free()
     torch.cuda.empty_cache()
 
     # ---- config 3: LFM3-shaped decode, tensor-parallel over the ranks ----
     decode = None if args.no_decode else bench_decode(ops, args, world, rank, barrier, max_over_ranks)
     decode8b = None if args.no_decode else bench_llama(ops, args, world, rank, barrier, max_over_ranks)
 
-    # ---- roofline of the dominant kernel (the GEMV) ----
+    # ---- roofline of the dominant kernel (the GEMV, on this rank's rows) ----
     peak, peak_kind = peaks()
+    shard_step = sum(wk["shard_bytes"] for wk in work)
     kern_total_ms = sum(kern_ms)
-    achieved = step_bytes / (kern_total_ms * 1e-3) / 1e9
-    per_call = [{"type": t, "rows": n, "k": k, "M": m, "us": round(kern_ms[j] * 1e3, 2),
-                 "GBps": round(b / (kern_ms[j] * 1e-3) / 1e9, 1)}
-                for j, (t, n, k, m, w, x, y, xh, yh, b) in enumerate(work)]
+    achieved = shard_step / (kern_total_ms * 1e-3) / 1e9
+    per_call = [{"type": wk["t"], "rows": wk["rows"], "k": wk["k"], "M": wk["m"], "us": round(kern_ms[j] * 1e3, 2),
+                 "GBps": round(wk["shard_bytes"] / (kern_ms[j] * 1e-3) / 1e9, 1)} for j, wk in enumerate(work)]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         import oracle
         oracle.build()
-        v, desc = cpu_sample(os.cpu_count() or 1, budget_s=args.cpu_seconds)
-        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": os.cpu_count() or 1, "kind": "port",
-               "sample": desc}
+        cores = os.cpu_count() or 1
+        v, desc = cpu_sample(cores, budget_s=args.cpu_seconds)
+        capped = max(1, min(8, cores // 2))
+        vc, _ = cpu_sample(capped, budget_s=args.cpu_seconds / 2)
+        cpu = {"value": round(v, 3), "unit": "GB/s", "cores": cores, "kind": "port", "sample": desc,
+               "reference_thread_cap": {"threads": capped, "value": round(vc, 3),
+                                        "rule": "min(8, cores / 2), the reference CPU pool's own cap "
+                                                "(js/cpu.js:107-113)"}}
 
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "f16 operands, f32 accumulate (Q4_K/Q6_K weights)", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "per_rank_bytes_per_step": step_bytes,
-                       "l2": "inputs larger than L2: 12 distinct weight tensors, 486 MB per step",
-                       "parallelism": f"weak x{world} (independent tensors per rank)"},
+            "higher_is_better": True, "scaling": "weak" if world == 1 else "strong", "vs_baseline": None,
+            "dtype": "s8 x u8 -> s32 (Q4_K/Q6_K weights, x as two int8 planes per 256-block), f32 scales",
+            "data": "synthetic",
+            "config": sweep_config(world, step_bytes),
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "traffic": profile_traffic(), "algorithmic_bytes": step_bytes,
-                         "per": "the 12 calls of a step: sum of their algorithmic bytes / sum of their average "
-                                "launch durations (each call launched back to back on 8 weight copies; for M > 2 "
-                                "the duration includes the call's activation-prep kernel)",
-                         "kernel": "gemv_kernel"},
+                         "traffic": profile_traffic() if world == 1 else None, "algorithmic_bytes": shard_step,
+                         "per": f"the 12 calls of a round on this rank's rows: sum of their algorithmic bytes / "
+                                f"sum of their average launch durations (each call launched back to back on its "
+                                f"{ROUNDS} weight copies, {REPLAYS} graph replays; for M > 2 the duration "
+                                f"includes the call's activation-prep kernel)",
+                         "kernel": "ef_gemv_kernel"},
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps * launches_per_step,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
+            "weak_scaling": weak,
             "gemm": gemm,
-            "sharded_gemv": sharded,
-            "config0": {"workload": "config0 Q8_0 GEMV 8192x2048, 1 token (8 weight copies back to back)",
+            "config0": {"workload": f"config0 Q8_0 GEMV 8192x2048, 1 token ({ROUNDS} weight copies back to back, "
+                                    f"{REPLAYS} graph replays)",
                         "us": round(us0, 2), "GBps": round(b0 / (us0 * 1e-6) / 1e9, 1),
                         "frac": round(b0 / (us0 * 1e-6) / 1e9 / peak, 4), "algorithmic_bytes": b0},
             "decode": decode,
@@ -732,8 +722,6 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--no-gemm", action="store_true", help="skip the config-2 GEMM measurement")
-    ap.add_argument("--no-sharded", action="store_true",
-                    help="N > 1: skip timing one config-1 matrix split by rows plus the all-gather of y")
     ap.add_argument("--no-decode", action="store_true", help="skip the config-3/4 decode measurements")
     ap.add_argument("--tp-comm", default="peer", choices=["peer", "peer-separate", "nccl"],
                     help="tensor-parallel decode collectives: the library's peer-memory kernels with the "

@@ -24,7 +24,7 @@
 // Fused form (ef_gemv_allreduce_norm): the row-parallel GEMV itself stores its
 // output rows into slot [parity][rank] of a second data region of every rank
 // and each of its CTAs adds 1 to counter [parity][rank] of every rank
-// (gemv.cu, GemvPush); tp_norm_kernel waits until every rank's counter has
+// (gemv.cu, GemvPush); ef_tp_norm_kernel waits until every rank's counter has
 // reached the GEMV's CTA count, sums the slots in rank order and applies the
 // post-norm + residual + next norm of the decoder. Its last CTA clears the
 // parity's counters and advances the call counter that gives the parity. A
@@ -93,7 +93,7 @@ __device__ __forceinline__ uint64_t global_ns() {
 // SUM: dst[i] = sum over ranks r (in order) of rank r's src[i], n floats.
 // !SUM: dst[r * n + i] = rank r's src[i], n 4-byte words.
 template <bool SUM>
-__global__ void __launch_bounds__(256) tp_kernel(const TpArgs a, const uint32_t *__restrict__ src, int64_t n,
+__global__ void __launch_bounds__(256) ef_tp_kernel(const TpArgs a, const uint32_t *__restrict__ src, int64_t n,
                                                  uint32_t *__restrict__ dst) {
     pdl_trigger();
     pdl_wait();
@@ -166,9 +166,9 @@ __global__ void __launch_bounds__(256) tp_kernel(const TpArgs a, const uint32_t 
 
 // Consumer of the fused row-parallel GEMV: row blockIdx.x of o = sum over
 // ranks (in order) of the slots; then x += rmsnorm(o) * w_post (or += o without
-// w_post) and nrm = rmsnorm(x) * w_next, as norm_add_norm_kernel.
+// w_post) and nrm = rmsnorm(x) * w_next, as ef_norm_add_norm_kernel.
 template <int V>
-__global__ void __launch_bounds__(256) tp_norm_kernel(const TpArgs a, uint32_t expected,
+__global__ void __launch_bounds__(256) ef_tp_norm_kernel(const TpArgs a, uint32_t expected,
                                                       const float *__restrict__ w_post, float *__restrict__ x,
                                                       const float *__restrict__ w_next, int n, float eps,
                                                       float *__restrict__ nrm) {
@@ -281,9 +281,9 @@ static int tp_launch(ef_ctx *ctx, ef_tp *tp, bool sum, const void *src, int64_t 
     a.data_bytes = (int64_t)tp->data_bytes;
     a.timeout_ns = tp->timeout_ns;
     if (sum)
-        return launch_on(ctx, tp_kernel<true>, TP_CTAS, 256, 0, "allreduce launch", a, (const uint32_t *)src, words,
+        return launch_on(ctx, ef_tp_kernel<true>, TP_CTAS, 256, 0, "allreduce launch", a, (const uint32_t *)src, words,
                          (uint32_t *)dst);
-    return launch_on(ctx, tp_kernel<false>, TP_CTAS, 256, 0, "allgather launch", a, (const uint32_t *)src, words,
+    return launch_on(ctx, ef_tp_kernel<false>, TP_CTAS, 256, 0, "allgather launch", a, (const uint32_t *)src, words,
                      (uint32_t *)dst);
 }
 
@@ -389,13 +389,13 @@ int ef_gemv_allreduce_norm(ef_ctx *ctx, ef_tp *tp, const ef_weight *w, const flo
     if (int rc = launch_gemv(ctx, &w, 1, nullptr, x, M, ys, &push, &ctas)) return rc;
     const uint32_t expected = (uint32_t)ctas;
     switch (v) {
-    case 1: return launch_on(ctx, tp_norm_kernel<1>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
+    case 1: return launch_on(ctx, ef_tp_norm_kernel<1>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
                              (int)w->rows, eps, nrm);
-    case 2: return launch_on(ctx, tp_norm_kernel<2>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
+    case 2: return launch_on(ctx, ef_tp_norm_kernel<2>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
                              (int)w->rows, eps, nrm);
-    case 4: return launch_on(ctx, tp_norm_kernel<4>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
+    case 4: return launch_on(ctx, ef_tp_norm_kernel<4>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
                              (int)w->rows, eps, nrm);
-    default: return launch_on(ctx, tp_norm_kernel<8>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid,
+    default: return launch_on(ctx, ef_tp_norm_kernel<8>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid,
                               w_next, (int)w->rows, eps, nrm);
     }
 }

@@ -684,51 +684,51 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
 
 // f32 -> f16 activations (round to nearest even), for x given in f32.
 __global__ void __launch_bounds__(gm_threads<EF_Q8_0>(), 1)
-    gemm_q8_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+    ef_gemm_q8_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q8_0>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(gm_threads<EF_Q4_K>(), 1)
-    gemm_q4_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+    ef_gemm_q4_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q4_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(gm_threads<EF_Q6_K>(), 1)
-    gemm_q6_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+    ef_gemm_q6_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q6_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(gm_threads<EF_Q5_K>(), 1)
-    gemm_q5_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+    ef_gemm_q5_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q5_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(gm_threads<EF_Q2_K>(), 1)
-    gemm_q2_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+    ef_gemm_q2_k_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q2_K>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(gm_threads<EF_IQ2_XXS>(), 1)
-    gemm_iq2_xxs_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+    ef_gemm_iq2_xxs_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                         int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_IQ2_XXS>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(gm_threads<EF_IQ1_S>(), 1)
-    gemm_iq1_s_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+    ef_gemm_iq1_s_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                       int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_IQ1_S>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 __global__ void __launch_bounds__(gm_threads<EF_Q4_0>(), 1)
-    gemm_q4_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
+    ef_gemm_q4_0_kernel(const __grid_constant__ CUtensorMap xmap, const uint8_t *__restrict__ W, int64_t rowgroups,
                      int64_t nchunks, int64_t rows, int64_t k, int M, float *__restrict__ y) {
     gemm_body<EF_Q4_0>(xmap, W, rowgroups, nchunks, rows, k, M, y);
 }
 
-__global__ void f32_to_f16_kernel(const float *__restrict__ src, __half *__restrict__ dst, int64_t n) {
+__global__ void ef_f32_to_f16_kernel(const float *__restrict__ src, __half *__restrict__ dst, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         dst[i] = __float2half_rn(src[i]);
 }
-__global__ void f16_to_f32_kernel(const __half *__restrict__ src, float *__restrict__ dst, int64_t n) {
+__global__ void ef_f16_to_f32_kernel(const __half *__restrict__ src, float *__restrict__ dst, int64_t n) {
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
         dst[i] = __half2float(src[i]);
 }
@@ -768,14 +768,14 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (cr != CUDA_SUCCESS) return set_err(ctx, EF_ERR_CUDA, "gemm: tensor map encode failed (%d)", (int)cr);
-    auto kern = TYPE == EF_Q8_0   ? gemm_q8_0_kernel
-                : TYPE == EF_Q4_0 ? gemm_q4_0_kernel
-                : TYPE == EF_Q4_K ? gemm_q4_k_kernel
-                : TYPE == EF_Q5_K ? gemm_q5_k_kernel
-                : TYPE == EF_Q2_K ? gemm_q2_k_kernel
-                : TYPE == EF_IQ2_XXS ? gemm_iq2_xxs_kernel
-                : TYPE == EF_IQ1_S   ? gemm_iq1_s_kernel
-                                     : gemm_q6_k_kernel;
+    auto kern = TYPE == EF_Q8_0   ? ef_gemm_q8_0_kernel
+                : TYPE == EF_Q4_0 ? ef_gemm_q4_0_kernel
+                : TYPE == EF_Q4_K ? ef_gemm_q4_k_kernel
+                : TYPE == EF_Q5_K ? ef_gemm_q5_k_kernel
+                : TYPE == EF_Q2_K ? ef_gemm_q2_k_kernel
+                : TYPE == EF_IQ2_XXS ? ef_gemm_iq2_xxs_kernel
+                : TYPE == EF_IQ1_S   ? ef_gemm_iq1_s_kernel
+                                     : ef_gemm_q6_k_kernel;
     const size_t smem = gemm_smem<TYPE>();
     static std::atomic<unsigned long long> configured{0};   // one bit per device
     if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
@@ -823,7 +823,7 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
             int64_t blocks = (n + 255) / 256;
             if (blocks > 148 * 32) blocks = 148 * 32;
             ctx->launches++;
-            f32_to_f16_kernel<<<(int)blocks, 256, 0, ctx->stream>>>((const float *)x, (__half *)ctx->scratch[1], n);
+            ef_f32_to_f16_kernel<<<(int)blocks, 256, 0, ctx->stream>>>((const float *)x, (__half *)ctx->scratch[1], n);
             if (int rc = check_cuda(ctx, cudaGetLastError(), "gemm f32->f16")) return rc;
             xh = (const __half *)ctx->scratch[1];
         }
@@ -845,7 +845,7 @@ int launch_gemm(ef_ctx *ctx, const ef_weight *w, const void *x, int x_type, int 
         int64_t blocks = (n + 255) / 256;
         if (blocks > 148 * 32) blocks = 148 * 32;
         ctx->launches++;
-        f16_to_f32_kernel<<<(int)blocks, 256, 0, ctx->stream>>>((const __half *)x, (float *)ctx->scratch[1], n);
+        ef_f16_to_f32_kernel<<<(int)blocks, 256, 0, ctx->stream>>>((const __half *)x, (float *)ctx->scratch[1], n);
         if (int rc = check_cuda(ctx, cudaGetLastError(), "gemm f16->f32")) return rc;
         xf = (const float *)ctx->scratch[1];
     }

@@ -86,7 +86,7 @@ struct GemvArgs {
     int xs_bytes;             // shared memory for activation data
     int xs_half;              // offset of the second phase buffer
     int xb;                   // bytes of activation data per chunk
-    const uint8_t *xf;        // activation data from gemv_xprep (3..16 tokens)
+    const uint8_t *xf;        // activation data from ef_gemv_xprep (3..16 tokens)
     const float *x;           // f32 activations [M][K] (1..2 tokens: staged by each CTA)
     int64_t K;
     GemvPush push;            // tensor-parallel row-parallel output (push.n = 0: write y)
@@ -967,7 +967,7 @@ __device__ __forceinline__ void stage_x(const float *x, int M, int64_t K, int64_
 // once, and waits for the kernel before it (which may have produced x, or
 // still read the scratch) before touching memory.
 template <int TYPE>
-__global__ void gemv_xprep(const float *__restrict__ x, int M, int64_t K, int64_t nchunks, int xb,
+__global__ void ef_gemv_xprep(const float *__restrict__ x, int M, int64_t K, int64_t nchunks, int xb,
                            uint8_t *__restrict__ xf) {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -1050,7 +1050,7 @@ static size_t gemv_smem(int xs_bytes, bool cluster) {
 // CTA stages its own activation data from f32 x (1-2 tokens); KH: warps per
 // rowgroup (1 or 2).
 template <int TYPE, int TQ, int NT, bool SWIGLU, bool FUSED, int KH>
-__global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) gemv_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const GemvArgs a) {
     using TR = Tr<TYPE>;
     using Raw = typename RawOf<TYPE>::T;
     constexpr int W = GV_WARPS;
@@ -1339,7 +1339,7 @@ template <int TYPE, int TQ, int NT, bool SWIGLU, bool FUSED>
 static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int64_t rowblocks, bool fused) {
     constexpr int KH = kh_of<TYPE, TQ, NT, SWIGLU>();
     constexpr int threads = GV_WARPS * KH * 32;
-    auto kern = gemv_kernel<TYPE, TQ, NT, SWIGLU, FUSED, KH>;
+    auto kern = ef_gemv_kernel<TYPE, TQ, NT, SWIGLU, FUSED, KH>;
     static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
@@ -1425,7 +1425,7 @@ static int launch_t(ef_ctx *ctx, GemvArgs &a, const ef_weight *const *ws, int n,
         cfg.attrs = attr;
         cfg.numAttrs = ctx->pdl ? 1 : 0;
         ctx->launches++;
-        if (int rc = check_cuda(ctx, cudaLaunchKernelEx(&cfg, gemv_xprep<TYPE>, x, a.M, a.K, a.nchunks, a.xb,
+        if (int rc = check_cuda(ctx, cudaLaunchKernelEx(&cfg, ef_gemv_xprep<TYPE>, x, a.M, a.K, a.nchunks, a.xb,
                                                         (uint8_t *)ctx->scratch[0]), "gemv xprep launch"))
             return rc;
     } else {

@@ -43,7 +43,7 @@ namespace ef {
 // the row in registers (all loads issued before the first reduction),
 // n = 4 * T * V.
 template <int V>
-__global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
+__global__ void __launch_bounds__(256) ef_rmsnorm_kernel(const float *__restrict__ x, const float *__restrict__ w,
                                                       int n, float eps, float *__restrict__ y) {
     pdl_trigger();
     pdl_wait();
@@ -68,9 +68,9 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const float *__restrict__ 
 }
 
 // x += rmsnorm(o) * w_post (or += o without a post-norm); nrm = rmsnorm(x) * w_next.
-// Same shape rules as rmsnorm_kernel.
+// Same shape rules as ef_rmsnorm_kernel.
 template <int V>
-__global__ void __launch_bounds__(256) norm_add_norm_kernel(const float *__restrict__ o,
+__global__ void __launch_bounds__(256) ef_norm_add_norm_kernel(const float *__restrict__ o,
                                                             const float *__restrict__ w_post, float *__restrict__ x,
                                                             const float *__restrict__ w_next, int n, float eps,
                                                             float *__restrict__ nrm) {
@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(256) norm_add_norm_kernel(const float *__restr
 // One thread per channel; tokens in order. bcx [T][3C] = B | C | x;
 // state [K-1][C] (oldest first); w [C][K] in temporal order (r = 0 oldest).
 template <int K>
-__global__ void shortconv_kernel(const float *__restrict__ bcx, const float *__restrict__ w, float *__restrict__ state,
+__global__ void ef_shortconv_kernel(const float *__restrict__ bcx, const float *__restrict__ w, float *__restrict__ state,
                                  int tokens, int C, float *__restrict__ y) {
     pdl_trigger();
     pdl_wait();
@@ -154,7 +154,7 @@ __global__ void shortconv_kernel(const float *__restrict__ bcx, const float *__r
 // theta = position * base^(-2p/D) (kernels.nn.wgsl.js:87-139). With wq / wk,
 // the per-head RMSNorm comes first (model.js:877-917).
 template <int D, bool NEOX>
-__global__ void rope_cache_kernel(float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
+__global__ void ef_rope_cache_kernel(float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
                                   const float *__restrict__ wq, const float *__restrict__ wk,
                                   const int *__restrict__ pos, int seqs, int tokens, int max_pos, int H, int KVH,
                                   float theta_scale, float eps, float *__restrict__ kcache,
@@ -218,14 +218,14 @@ __global__ void rope_cache_kernel(float *__restrict__ q, const float *__restrict
 }
 
 // CTA per (head h = blockIdx.x, query row r = blockIdx.y); rows as in
-// rope_cache_kernel. The query at position qp sees keys 0..qp of its
+// ef_rope_cache_kernel. The query at position qp sees keys 0..qp of its
 // sequence's caches, those with qp - key < window (window 0 = all); scale
 // 1/sqrt(D); grouped heads (H / KVH queries per cache head); times
 // sigmoid(gate[r][h]) when gate is given (kernels.nn.wgsl.js:141-200,
 // kernels.model.wgsl.js:89-105). Scores in shared memory; the weighted sum of
 // v rows is split over blockDim / D groups of keys, then added in group order.
 template <int D>
-__global__ void __launch_bounds__(256) attention_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
+__global__ void __launch_bounds__(256) ef_attention_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
                                                         const float *__restrict__ vcache,
                                                         const float *__restrict__ gate, const int *__restrict__ pos,
                                                         int tokens, int max_pos, int window, int H, int KVH,
@@ -301,7 +301,7 @@ __global__ void __launch_bounds__(256) attention_kernel(const float *__restrict_
 // keys), the causal / window mask, an online softmax per row (running max m,
 // running sum l, old output rescaled by exp(m_old - m_new)), and O += P V (a
 // thread owns 8 rows x 4 or 8 dimensions of O in registers). All f32; same
-// masking, scale, positions and gate as attention_kernel (kernels.nn.wgsl.js:
+// masking, scale, positions and gate as ef_attention_kernel (kernels.nn.wgsl.js:
 // 141-200, kernels.model.wgsl.js:89-105). Rows of shared-memory tiles are
 // padded by 4 floats so that the 16-byte loads of different rows fall in
 // different banks. Query blocks are taken last to first: the longest key
@@ -312,7 +312,7 @@ template <int D> constexpr size_t fa_smem() {
 }
 
 template <int D, int G>
-__global__ void __launch_bounds__(FA_T, 1) attn_prompt_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
+__global__ void __launch_bounds__(FA_T, 1) ef_attn_prompt_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
                                                           const float *__restrict__ vcache,
                                                           const float *__restrict__ gate, const int *__restrict__ pos,
                                                           int tokens, int max_pos, int window, int H, int KVH,
@@ -486,14 +486,14 @@ __global__ void __launch_bounds__(FA_T, 1) attn_prompt_kernel(const float *__res
 // together; small CTAs so that several load while others compute), then: a
 // warp per key with the lanes across the head dimension for the G scores;
 // per head the range's max m and sum l of exp(s - m); a thread per dimension
-// for the unnormalised sums of exp(s - m) * v. attn_combine_kernel merges the
-// ranges. Same masking and scale as attention_kernel.
+// for the unnormalised sums of exp(s - m) * v. ef_attn_combine_kernel merges the
+// ranges. Same masking and scale as ef_attention_kernel.
 constexpr int AK = 32;         // keys per range
 constexpr int AT = 128;        // threads per CTA
 static_assert(AK == 32, "the softmax step holds one key per lane");
 
 template <int D, int G>
-__global__ void __launch_bounds__(AT) attn_part_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
+__global__ void __launch_bounds__(AT) ef_attn_part_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
                                                        const float *__restrict__ vcache, const int *__restrict__ pos,
                                                        int tokens, int max_pos, int window, int H, int KVH,
                                                        float *__restrict__ part) {
@@ -614,7 +614,7 @@ __global__ void __launch_bounds__(AT) attn_part_kernel(const float *__restrict__
 constexpr int CT = 512;
 
 template <int D>
-__global__ void __launch_bounds__(CT) attn_combine_kernel(const float *__restrict__ part,
+__global__ void __launch_bounds__(CT) ef_attn_combine_kernel(const float *__restrict__ part,
                                                           const float *__restrict__ gate, int H, int nsplit,
                                                           float *__restrict__ out) {
     pdl_trigger();
@@ -697,7 +697,7 @@ __device__ void bitonic_desc(unsigned long long *a, int n) {
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(512) topk_chunk_kernel(const float *__restrict__ logits, int n, int m,
+__global__ void __launch_bounds__(512) ef_topk_chunk_kernel(const float *__restrict__ logits, int n, int m,
                                                          unsigned long long *__restrict__ cand,
                                                          int *__restrict__ flags) {
     pdl_trigger();
@@ -726,7 +726,7 @@ __global__ void __launch_bounds__(512) topk_chunk_kernel(const float *__restrict
     if (threadIdx.x == 0 && nan_seen) atomicOr(flags + row, 2);
 }
 
-__global__ void __launch_bounds__(1024) topk_final_kernel(const float *__restrict__ logits, int n, int m, int nch,
+__global__ void __launch_bounds__(1024) ef_topk_final_kernel(const float *__restrict__ logits, int n, int m, int nch,
                                                           int sort_n, const unsigned long long *__restrict__ cand,
                                                           int *__restrict__ ids, float *__restrict__ vals) {
     pdl_trigger();
@@ -751,7 +751,7 @@ __global__ void __launch_bounds__(1024) topk_final_kernel(const float *__restric
 
 // out = g * sigmoid(g) * u, elementwise (kernels.nn.wgsl.js swiglu; the same
 // expression as the fused SwiGLU GEMV's epilogue).
-__global__ void swiglu_kernel(const float *__restrict__ g, const float *__restrict__ u, int64_t n,
+__global__ void ef_swiglu_kernel(const float *__restrict__ g, const float *__restrict__ u, int64_t n,
                               float *__restrict__ out) {
     pdl_trigger();
     pdl_wait();
@@ -778,7 +778,7 @@ __device__ __forceinline__ void finish_step(int tok, int *token, int *pos, int *
 // tensor-parallel head): the row's pair[0] = the best value's bits, pair[1] =
 // its index + offset, for argmax_select over the shards.
 template <bool PAIR>
-__global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ logits, int n,
+__global__ void __launch_bounds__(1024) ef_argmax_kernel(const float *__restrict__ logits, int n,
                                                       int *__restrict__ token, int *__restrict__ pos,
                                                       int *__restrict__ out_tokens, int out_base, int out_cap,
                                                       int offset, int *__restrict__ pair) {
@@ -866,7 +866,7 @@ __global__ void __launch_bounds__(1024) argmax_kernel(const float *__restrict__ 
 // Row blockIdx.x: the winner over the shards' (value, index) pairs (pairs
 // [nranks][rows][2]), in the same order as one argmax over the whole
 // vocabulary: larger value, then lower index.
-__global__ void argmax_select_kernel(const int *__restrict__ pairs, int npairs, int *__restrict__ token,
+__global__ void ef_argmax_select_kernel(const int *__restrict__ pairs, int npairs, int *__restrict__ token,
                                      int *__restrict__ pos, int *__restrict__ out_tokens, int out_base,
                                      int out_cap) {
     pdl_trigger();
@@ -905,13 +905,13 @@ static int part_launch(ef_ctx *ctx, dim3 grid, const float *q, const float *kcac
     constexpr size_t smem = 2 * AK * D * sizeof(float);
     static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
-        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(attn_part_kernel<D, G>,
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(ef_attn_part_kernel<D, G>,
                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                                 "attention smem attribute"))
             return rc;
         configured.fetch_or(1ull << ctx->device);
     }
-    return launch_on(ctx, attn_part_kernel<D, G>, grid, AT, smem, "attention launch", q, kcache, vcache, pos, tokens,
+    return launch_on(ctx, ef_attn_part_kernel<D, G>, grid, AT, smem, "attention launch", q, kcache, vcache, pos, tokens,
                      max_pos, window, heads, kv_heads, part);
 }
 
@@ -922,14 +922,14 @@ static int prompt_attn_launch(ef_ctx *ctx, int seqs, const float *q, const float
     constexpr size_t smem = fa_smem<D>();
     static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
-        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(attn_prompt_kernel<D, G>,
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(ef_attn_prompt_kernel<D, G>,
                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                                 "prompt attention smem attribute"))
             return rc;
         configured.fetch_or(1ull << ctx->device);
     }
     const dim3 grid((unsigned)((tokens + FA_R / G - 1) / (FA_R / G)), (unsigned)kv_heads, (unsigned)seqs);
-    return launch_on(ctx, attn_prompt_kernel<D, G>, grid, FA_T, smem, "prompt attention launch", q, kcache, vcache,
+    return launch_on(ctx, ef_attn_prompt_kernel<D, G>, grid, FA_T, smem, "prompt attention launch", q, kcache, vcache,
                      gate, pos, tokens, max_pos, window, heads, kv_heads, out);
 }
 
@@ -947,10 +947,10 @@ int ef_rmsnorm(ef_ctx *ctx, const float *x, const float *w, int rows, int n, flo
     if (!v) return set_err(ctx, EF_ERR_SHAPE, "rmsnorm: n=%d (a multiple of 128 up to 8192, power-of-2 blocks)", n);
     int rc = EF_OK;
     switch (v) {
-    case 1: rc = launch_on(ctx, rmsnorm_kernel<1>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
-    case 2: rc = launch_on(ctx, rmsnorm_kernel<2>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
-    case 4: rc = launch_on(ctx, rmsnorm_kernel<4>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
-    default: rc = launch_on(ctx, rmsnorm_kernel<8>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
+    case 1: rc = launch_on(ctx, ef_rmsnorm_kernel<1>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
+    case 2: rc = launch_on(ctx, ef_rmsnorm_kernel<2>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
+    case 4: rc = launch_on(ctx, ef_rmsnorm_kernel<4>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
+    default: rc = launch_on(ctx, ef_rmsnorm_kernel<8>, rows, th, 0, "rmsnorm launch", x, w, n, eps, y); break;
     }
     return rc;
 }
@@ -964,10 +964,10 @@ int ef_norm_add_norm(ef_ctx *ctx, const float *o, const float *w_post, float *x,
     if (!v) return set_err(ctx, EF_ERR_SHAPE, "norm_add_norm: n=%d (a multiple of 128 up to 8192, power-of-2 blocks)", n);
     int rc = EF_OK;
     switch (v) {
-    case 1: rc = launch_on(ctx, norm_add_norm_kernel<1>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
-    case 2: rc = launch_on(ctx, norm_add_norm_kernel<2>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
-    case 4: rc = launch_on(ctx, norm_add_norm_kernel<4>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
-    default: rc = launch_on(ctx, norm_add_norm_kernel<8>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
+    case 1: rc = launch_on(ctx, ef_norm_add_norm_kernel<1>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
+    case 2: rc = launch_on(ctx, ef_norm_add_norm_kernel<2>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
+    case 4: rc = launch_on(ctx, ef_norm_add_norm_kernel<4>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
+    default: rc = launch_on(ctx, ef_norm_add_norm_kernel<8>, rows, th, 0, "norm_add_norm launch", o, w_post, x, w_next, n, eps, nrm); break;
     }
     return rc;
 }
@@ -977,7 +977,7 @@ int ef_shortconv(ef_ctx *ctx, const float *bcx, const float *conv_w, float *stat
     if (!ctx || !bcx || !conv_w || !state || !y || tokens < 1 || channels < 1)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "shortconv: bad arguments") : EF_ERR_INVALID;
     if (kernel != 3) return set_err(ctx, EF_ERR_SHAPE, "shortconv: kernel %d (3 supported)", kernel);
-    return launch_on(ctx, shortconv_kernel<3>, grid1d(channels, 256), 256, 0, "shortconv launch", bcx, conv_w,
+    return launch_on(ctx, ef_shortconv_kernel<3>, grid1d(channels, 256), 256, 0, "shortconv launch", bcx, conv_w,
                      state, tokens, channels, y);
 }
 
@@ -988,7 +988,7 @@ static int rope_launch(ef_ctx *ctx, float *q, const float *k, const float *v, co
     const int64_t warps = (int64_t)seqs * tokens * (heads + kv_heads);
     const int grid = (int)((warps + 7) / 8);
 #define EF_ROPE(DD, NX)                                                                                     \
-    return launch_on(ctx, rope_cache_kernel<DD, NX>, grid, 256, 0, "rope_cache launch", q, k, v, wq, wk, pos, \
+    return launch_on(ctx, ef_rope_cache_kernel<DD, NX>, grid, 256, 0, "rope_cache launch", q, k, v, wq, wk, pos, \
                      seqs, tokens, max_pos, heads, kv_heads, theta_scale, eps, kcache, vcache)
     if (head_dim == 64) {
         if (neox) EF_ROPE(64, true);
@@ -1061,9 +1061,9 @@ static int attention_launch(ef_ctx *ctx, const float *q, const float *kcache, co
         const size_t cs = (size_t)nsplit * sizeof(float);
         if (cs > 48 * 1024) return set_err(ctx, EF_ERR_RANGE, "attention: %d key ranges", nsplit);
         if (head_dim == 64)
-            return launch_on(ctx, attn_combine_kernel<64>, cg, CT, cs, "attention combine launch",
+            return launch_on(ctx, ef_attn_combine_kernel<64>, cg, CT, cs, "attention combine launch",
                              (const float *)part, head_gate, heads, nsplit, out);
-        return launch_on(ctx, attn_combine_kernel<128>, cg, CT, cs, "attention combine launch", (const float *)part,
+        return launch_on(ctx, ef_attn_combine_kernel<128>, cg, CT, cs, "attention combine launch", (const float *)part,
                          head_gate, heads, nsplit, out);
     }
     if (G == 1 || G == 2 || G == 4 || G == 8) {
@@ -1085,18 +1085,18 @@ static int attention_launch(ef_ctx *ctx, const float *q, const float *kcache, co
     static std::atomic<unsigned long long> configured[2] = {{0}, {0}};
     const int di = head_dim == 64 ? 0 : 1;
     if (ctx->device < 64 && !(configured[di].load() & (1ull << ctx->device))) {
-        cudaError_t e = di == 0 ? cudaFuncSetAttribute(attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaError_t e = di == 0 ? cudaFuncSetAttribute(ef_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                        200 * 1024)
-                                : cudaFuncSetAttribute(attention_kernel<128>,
+                                : cudaFuncSetAttribute(ef_attention_kernel<128>,
                                                        cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         if (int rc = check_cuda(ctx, e, "attention smem attribute")) return rc;
         configured[di].fetch_or(1ull << ctx->device);
     }
     const dim3 grid(heads, seqs * tokens);
     if (di == 0)
-        return launch_on(ctx, attention_kernel<64>, grid, 256, smem, "attention launch", q, kcache, vcache,
+        return launch_on(ctx, ef_attention_kernel<64>, grid, 256, smem, "attention launch", q, kcache, vcache,
                          head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
-    return launch_on(ctx, attention_kernel<128>, grid, 256, smem, "attention launch", q, kcache, vcache, head_gate,
+    return launch_on(ctx, ef_attention_kernel<128>, grid, 256, smem, "attention launch", q, kcache, vcache, head_gate,
                      pos, tokens, max_pos, window, heads, kv_heads, out);
 }
 
@@ -1133,7 +1133,7 @@ int ef_topk(ef_ctx *ctx, const float *logits, int rows, int n, int m, int *ids, 
     if (int rc = ensure_scratch(ctx, 3, (size_t)rows * nch * m * 8)) return rc;
     static std::atomic<unsigned long long> configured{0};
     if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
-        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(topk_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(ef_topk_final_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                           227 * 1024), "topk smem attribute"))
             return rc;
         configured.fetch_or(1ull << ctx->device);
@@ -1141,9 +1141,9 @@ int ef_topk(ef_ctx *ctx, const float *logits, int rows, int n, int m, int *ids, 
     if (int rc = check_cuda(ctx, cudaMemsetAsync(flags, 0, (size_t)rows * sizeof(int), ctx->stream), "topk flags"))
         return rc;
     unsigned long long *cand = (unsigned long long *)ctx->scratch[3];
-    if (int rc = launch_on(ctx, topk_chunk_kernel, dim3(nch, rows), 512, 0, "topk launch", logits, n, m, cand, flags))
+    if (int rc = launch_on(ctx, ef_topk_chunk_kernel, dim3(nch, rows), 512, 0, "topk launch", logits, n, m, cand, flags))
         return rc;
-    return launch_on(ctx, topk_final_kernel, rows, 1024, smem, "topk launch", logits, n, m, nch, sort_n,
+    return launch_on(ctx, ef_topk_final_kernel, rows, 1024, smem, "topk launch", logits, n, m, nch, sort_n,
                      (const unsigned long long *)cand, ids, vals);
 }
 
@@ -1152,7 +1152,7 @@ int ef_swiglu(ef_ctx *ctx, const float *gate, const float *up, int64_t n, float 
         return ctx ? set_err(ctx, EF_ERR_INVALID, "swiglu: bad arguments") : EF_ERR_INVALID;
     int64_t blocks = (n + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
-    return launch_on(ctx, swiglu_kernel, (int)blocks, 256, 0, "swiglu launch", gate, up, n, out);
+    return launch_on(ctx, ef_swiglu_kernel, (int)blocks, 256, 0, "swiglu launch", gate, up, n, out);
 }
 
 int ef_argmax_step(ef_ctx *ctx, const float *logits, int n, int *token, int *pos, int *out_tokens, int out_base,
@@ -1164,14 +1164,14 @@ int ef_argmax_rows(ef_ctx *ctx, const float *logits, int rows, int n, int *token
                    int out_base, int out_cap) {
     if (!ctx || !logits || !tokens || !pos || n < 1 || rows < 1 || rows > 65535)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "argmax: bad arguments") : EF_ERR_INVALID;
-    return launch_on(ctx, argmax_kernel<false>, rows, 1024, 0, "argmax launch", logits, n, tokens, pos, out_tokens,
+    return launch_on(ctx, ef_argmax_kernel<false>, rows, 1024, 0, "argmax launch", logits, n, tokens, pos, out_tokens,
                      out_base, out_cap, 0, (int *)nullptr);
 }
 
 int ef_argmax_partial(ef_ctx *ctx, const float *logits, int rows, int n, int offset, int *pairs) {
     if (!ctx || !logits || !pairs || n < 1 || offset < 0 || rows < 1 || rows > 65535)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "argmax_partial: bad arguments") : EF_ERR_INVALID;
-    return launch_on(ctx, argmax_kernel<true>, rows, 1024, 0, "argmax_partial launch", logits, n, (int *)nullptr,
+    return launch_on(ctx, ef_argmax_kernel<true>, rows, 1024, 0, "argmax_partial launch", logits, n, (int *)nullptr,
                      (int *)nullptr, (int *)nullptr, 0, 0, offset, pairs);
 }
 
@@ -1179,7 +1179,7 @@ int ef_argmax_select(ef_ctx *ctx, const int *pairs, int nranks, int rows, int *t
                      int out_base, int out_cap) {
     if (!ctx || !pairs || !tokens || !pos || nranks < 1 || rows < 1 || rows > 65535)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "argmax_select: bad arguments") : EF_ERR_INVALID;
-    return launch_on(ctx, argmax_select_kernel, rows, 32, 0, "argmax_select launch", pairs, nranks, tokens, pos,
+    return launch_on(ctx, ef_argmax_select_kernel, rows, 32, 0, "argmax_select launch", pairs, nranks, tokens, pos,
                      out_tokens, out_base, out_cap);
 }
 

@@ -21,7 +21,7 @@ __device__ const int8_t g_grid_iq1s_i8[EF_GRID_IQ1S_ENTRIES * 8] = {EF_GRID_IQ1S
 
 // Thread per GGUF block of the padded tensor (rowgroups*16 rows x
 // nchunks*blocks_per_chunk blocks). Padding blocks are written as zeros.
-__global__ void repack_kernel(int type, const uint8_t *__restrict__ src, int64_t rows, int64_t bpr,
+__global__ void ef_repack_kernel(int type, const uint8_t *__restrict__ src, int64_t rows, int64_t bpr,
                               int64_t rowgroups, int64_t nchunks, int bpc, int bb, int tile_bytes,
                               uint8_t *__restrict__ dst) {
     const int64_t bpr_pad = nchunks * bpc;
@@ -43,7 +43,7 @@ __global__ void repack_kernel(int type, const uint8_t *__restrict__ src, int64_t
 }
 
 // Thread per GGUF block of the logical tensor: gather back the original bytes.
-__global__ void unpack_kernel(int type, const uint8_t *__restrict__ src, int64_t rows, int64_t bpr,
+__global__ void ef_unpack_kernel(int type, const uint8_t *__restrict__ src, int64_t rows, int64_t bpr,
                               int64_t nchunks, int bpc, int bb, int tile_bytes,
                               uint8_t *__restrict__ dst) {
     const int64_t total = rows * bpr;
@@ -61,7 +61,7 @@ __global__ void unpack_kernel(int type, const uint8_t *__restrict__ src, int64_t
 
 // Thread per GGUF block of rows [row0, row0+nrows): gather, then decode with
 // the reference's f32 arithmetic (common.cuh decode_block).
-__global__ void dequant_kernel(int type, const uint8_t *__restrict__ src, int64_t row0, int64_t nrows,
+__global__ void ef_dequant_kernel(int type, const uint8_t *__restrict__ src, int64_t row0, int64_t nrows,
                                int64_t bpr, int64_t nchunks, int bpc, int bb, int be, int tile_bytes,
                                int64_t k, float *__restrict__ out) {
     const int8_t *grid = type == EF_IQ2_XXS ? g_grid_iq2xxs_i8 : g_grid_iq1s_i8;
@@ -84,7 +84,7 @@ __global__ void dequant_kernel(int type, const uint8_t *__restrict__ src, int64_
 // reference's quant.gather, js/ops.js:1104-1118 / gatherShader
 // kernels.wgsl.js:1199): out[t][:] = dequant(W)[ids[t]][:]. Ids outside
 // [0, rows) produce a row of zeros.
-__global__ void gather_kernel(int type, const uint8_t *__restrict__ src, const int *__restrict__ ids, int tokens,
+__global__ void ef_gather_kernel(int type, const uint8_t *__restrict__ src, const int *__restrict__ ids, int tokens,
                               int64_t rows, int64_t bpr, int64_t nchunks, int bpc, int bb, int be, int tile_bytes,
                               int64_t k, float *__restrict__ out) {
     pdl_trigger();
@@ -111,9 +111,9 @@ __global__ void gather_kernel(int type, const uint8_t *__restrict__ src, const i
 }
 
 // F2 (js/ops.fusion.js:152-165, kernels.fusion.wgsl.js:143-200): CTA per
-// token: the embedding row as gather_kernel decodes it (same blocks, same
+// token: the embedding row as ef_gather_kernel decodes it (same blocks, same
 // bits) into shared memory and x, then nrm = x * rsqrt(mean(x^2) + eps) * w.
-__global__ void gather_norm_kernel(int type, const uint8_t *__restrict__ src, const int *__restrict__ ids,
+__global__ void ef_gather_norm_kernel(int type, const uint8_t *__restrict__ src, const int *__restrict__ ids,
                                    int64_t rows, int64_t bpr, int64_t nchunks, int bpc, int be, int tile_bytes,
                                    int64_t k, const float *__restrict__ wn, float eps, float *__restrict__ x,
                                    float *__restrict__ nrm) {
@@ -164,7 +164,7 @@ int launch_repack(ef_ctx *ctx, int type, const uint8_t *dev_gguf, int64_t rows, 
     const int64_t bpr = k / geo.block_elems;
     const int64_t total = w->rowgroups * RG_ROWS * w->nchunks * bpc;
     ctx->launches++;
-    repack_kernel<<<grid_for(total), 256, 0, ctx->stream>>>(type, dev_gguf, rows, bpr, w->rowgroups,
+    ef_repack_kernel<<<grid_for(total), 256, 0, ctx->stream>>>(type, dev_gguf, rows, bpr, w->rowgroups,
                                                             w->nchunks, bpc, geo.block_bytes,
                                                             geo.tile_bytes, w->dev);
     return check_cuda(ctx, cudaGetLastError(), "repack launch");
@@ -176,7 +176,7 @@ int launch_unpack(ef_ctx *ctx, const ef_weight *w, uint8_t *dev_gguf) {
     const int bpc = geo.chunk_k / geo.block_elems;
     const int64_t bpr = w->k / geo.block_elems;
     ctx->launches++;
-    unpack_kernel<<<grid_for(w->rows * bpr), 256, 0, ctx->stream>>>(
+    ef_unpack_kernel<<<grid_for(w->rows * bpr), 256, 0, ctx->stream>>>(
         w->type, w->dev, w->rows, bpr, w->nchunks, bpc, geo.block_bytes, geo.tile_bytes, dev_gguf);
     return check_cuda(ctx, cudaGetLastError(), "unpack launch");
 }
@@ -188,7 +188,7 @@ int launch_dequant(ef_ctx *ctx, const ef_weight *w, int64_t row0, int64_t nrows,
     const int64_t bpr = w->k / geo.block_elems;
     // 256 f32 + 256 bytes of local state per thread: keep blocks small.
     ctx->launches++;
-    dequant_kernel<<<grid_for(nrows * bpr), 128, 0, ctx->stream>>>(
+    ef_dequant_kernel<<<grid_for(nrows * bpr), 128, 0, ctx->stream>>>(
         w->type, w->dev, row0, nrows, bpr, w->nchunks, bpc, geo.block_bytes, geo.block_elems,
         geo.tile_bytes, w->k, out);
     return check_cuda(ctx, cudaGetLastError(), "dequant launch");
@@ -203,14 +203,14 @@ int launch_gather_norm(ef_ctx *ctx, const ef_weight *w, const int *ids, int toke
                                           (long long)w->k);
     static std::atomic<unsigned long long> configured{0};
     if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
-        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(gather_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(ef_gather_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                           200 * 1024), "gather_rmsnorm smem attribute"))
             return rc;
         configured.fetch_or(1ull << ctx->device);
     }
     const int bpc = geo.chunk_k / geo.block_elems;
     const int64_t bpr = w->k / geo.block_elems;
-    return launch_on(ctx, gather_norm_kernel, tokens, 256, smem, "gather_rmsnorm launch", w->type,
+    return launch_on(ctx, ef_gather_norm_kernel, tokens, 256, smem, "gather_rmsnorm launch", w->type,
                      (const uint8_t *)w->dev, ids, w->rows, bpr, w->nchunks, bpc, geo.block_elems, geo.tile_bytes, w->k,
                      wn, eps, x, nrm);
 }
@@ -220,7 +220,7 @@ int launch_gather(ef_ctx *ctx, const ef_weight *w, const int *ids, int tokens, f
     geo_of(w->type, geo);
     const int bpc = geo.chunk_k / geo.block_elems;
     const int64_t bpr = w->k / geo.block_elems;
-    return launch_on(ctx, gather_kernel, grid_for((int64_t)tokens * bpr), 128, 0, "gather launch", w->type,
+    return launch_on(ctx, ef_gather_kernel, grid_for((int64_t)tokens * bpr), 128, 0, "gather launch", w->type,
                      (const uint8_t *)w->dev, ids, tokens, w->rows, bpr, w->nchunks, bpc, geo.block_bytes,
                      geo.block_elems, geo.tile_bytes, w->k, out);
 }
