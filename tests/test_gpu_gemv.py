@@ -69,15 +69,20 @@ def test_swiglu_vs_oracle(ops, oracle_mod, t, M):
 
 
 @pytest.mark.parametrize("t", ["Q8_0", "Q4_K"])
-def test_sections_equal_single(ops, t):
+@pytest.mark.parametrize("M", [2, 4])
+def test_sections_equal_single(ops, oracle_mod, t, M):
+    """Several matrices in one launch give each matrix's product: within the
+    bound against the oracle, and bit-equal to single calls."""
     k = 1024
     shapes = [512, 128, 128, 32]
     raws = [formats.synth(t, r, k, seed=i) for i, r in enumerate(shapes)]
     ws = [ops.load_weight(t, raw, r, k) for raw, r in zip(raws, shapes)]
-    x = torch.randn(2, k, device="cuda")
-    ys = ops.gemv.secciones(t, ws, x, shapes, k, 2)
-    for w, r, y in zip(ws, shapes, ys):
-        single = ops.gemv.matmul(t, w, x, r, k, 2)
+    x = torch.randn(M, k, device="cuda", generator=torch.Generator("cuda").manual_seed(M))
+    ys = ops.gemv.secciones(t, ws, x, shapes, k, M)
+    xn = x.cpu().numpy()
+    for w, raw, r, y in zip(ws, raws, shapes, ys):
+        _check(oracle_mod, t, raw, r, k, xn, y.cpu().numpy())
+        single = ops.gemv.matmul(t, w, x, r, k, M)
         torch.testing.assert_close(y, single, rtol=0, atol=0)
     assert ops.gemv.despachados()["secciones"] >= 1
 
@@ -112,3 +117,4 @@ def test_wrong_weight_raises(ops):
         ops.matmul("Q4_K", w, torch.randn(1, 256, device="cuda"), 32, 256, 1)
     with pytest.raises(EfError):
         ops.matmul("Q4_0X", w, torch.randn(1, 256, device="cuda"), 16, 256, 1)
+
