@@ -316,7 +316,8 @@ def bench_llama(ops, args, world, rank, barrier, max_over_ranks):
     tensor-parallel over the ranks when world > 1: a 4096-id context (its
     first 4095 ids through the GEMM path once), then greedy decode steps at
     batch 1 and at batch 16 (16 sequences sharing the first 4095 ids, each
-    with its own last id), each step one CUDA-graph replay."""
+    with its own last id), each step one CUDA-graph replay; batch 16 again
+    with f16 KV caches (the reference's kvF16 option)."""
     import torch
 
     from elffuss_engine_b200.llama import LlamaConfig, LlamaDecoder, shard_weights, synth_weights
@@ -332,9 +333,10 @@ def bench_llama(ops, args, world, rank, barrier, max_over_ranks):
                        f"{LLAMA_CONTEXT}-id context, {LLAMA_STEPS} greedy steps per batch size",
            "parallelism": f"tp{world} ({args.tp_comm} collectives)" if world > 1 else "single GPU",
            "weight_bytes_per_step_per_gpu": cfg.step_weight_bytes() // world}
-    for B in (1, 16):
-        dec = LlamaDecoder(ops, cfg, w, batch=B, rank=rank, world=world, comm=tp_comm(ops, args, world, rank),
-                           fused=world > 1 and args.tp_comm == "peer")
+    import dataclasses
+    for B, kv16 in ((1, False), (16, False), (16, True)):
+        dec = LlamaDecoder(ops, dataclasses.replace(cfg, kv_f16=kv16), w, batch=B, rank=rank, world=world,
+                           comm=tp_comm(ops, args, world, rank), fused=world > 1 and args.tp_comm == "peer")
         lasts = [int(prompt[-1])] + [int(t) for t in ids[LLAMA_CONTEXT:LLAMA_CONTEXT + B - 1]]
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
         barrier()
@@ -357,7 +359,7 @@ def bench_llama(ops, args, world, rank, barrier, max_over_ranks):
         barrier()
         ms = max_over_ranks(ev[1].elapsed_time(ev[2])) / LLAMA_STEPS
         toks = dec.out_tokens[:, :4].cpu().tolist()
-        out[f"batch{B}"] = {"tok_s": round(B * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
+        out[f"batch{B}" + ("_kv_f16" if kv16 else "")] = {"tok_s": round(B * 1e3 / ms, 1), "ms_per_step": round(ms, 4),
                             "weight_GBps_per_gpu": round(cfg.step_weight_bytes() / world / (ms * 1e-3) / 1e9, 1),
                             "prefill_4095_ms": round(prefill_ms, 1), "first_tokens": toks[0][:4],
                             "distinct_first_tokens": len({t[0] for t in toks})}

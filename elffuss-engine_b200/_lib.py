@@ -85,6 +85,12 @@ _SIGS = {
     "ef_rope_cache": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, ctypes.c_float,
                        _P, _P], _I),
     "ef_attention": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
+    "ef_qk_norm_rope_cache_f16": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, ctypes.c_float, ctypes.c_float,
+                                   _P, _P], _I),
+    "ef_attn_decode_f16": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
+    "ef_rope_cache_f16": ([_P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, ctypes.c_float, ctypes.c_float,
+                           _P, _P], _I),
+    "ef_attention_f16": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _I, _P], _I),
     "ef_swiglu": ([_P, _P, _P, ctypes.c_int64, _P], _I),
     "ef_topk": ([_P, _P, _I, _I, _I, _P, _P, _P], _I),
     "ef_tp_create": ([_P, _I, _I, ctypes.c_size_t, ctypes.c_double, _P], _I),

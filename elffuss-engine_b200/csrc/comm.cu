@@ -8,28 +8,31 @@
 // the sharded head's argmax pairs gathered).
 //
 // Design: every rank maps every other rank's exchange buffer (CUDA IPC, plain
-// peer stores -- no multicast). A call is TP_CTAS CTAs per GPU, CTA b owning
-// one contiguous part of the data: it stores its part into slot
-// [parity][rank] of every rank's buffer (its own included), publishes it with
-// a system-scope release store of its epoch into each rank's flag [b][rank],
-// waits (bounded) until every rank's flag [b][.] in its own buffer has
-// reached that epoch (acquire), then reads the slots in rank order -- the sum
-// is the same on every rank, bit for bit. Epochs count calls per CTA index
-// and live in device memory, so calls can be captured in a CUDA graph and
-// replayed. Two slot parities: a CTA can be at most one call ahead of the
-// same CTA on any other rank, so it never overwrites words still being read.
-// A wait that runs out sets the buffer's error word, skips the read and
-// returns; every later call returns at once, and the host reads the status.
+// peer stores -- no multicast). Every word travels stamped: one 8-byte store
+// of (epoch << 32 | word), so the data is its own flag -- the reader polls
+// the words themselves until each carries this call's epoch, with no release
+// fence and no separate flag store after the data (one NVLink crossing per
+// exchange instead of data + fence round trip + flag). A call is TP_CTAS
+// CTAs per GPU, CTA b owning one contiguous part of the data: it stores its
+// part, stamped, into slot [parity][rank] of every other rank's buffer, then
+// reads every other rank's slot words of its part (bounded wait on each
+// stamp) and combines them with its own source words in rank order -- the
+// sum is the same on every rank, bit for bit. Epochs count calls per CTA
+// index (every call runs every CTA, so they are all equal) and live in device
+// memory, so calls can be captured in a CUDA graph and replayed. Two slot
+// parities: a rank that writes call e+2 into a slot has seen every rank's
+// data of call e+1, which each rank wrote only after its call e had ended,
+// so no word is overwritten while it is still read; a stale word carries an
+// older epoch and is never taken for a new one. A wait that runs out sets the
+// buffer's error word, skips the output and returns; every later call
+// returns at once, and the host reads the status.
 //
 // Fused form (ef_gemv_allreduce_norm): the row-parallel GEMV itself stores its
-// output rows into slot [parity][rank] of a second data region of every rank
-// and each of its CTAs adds 1 to counter [parity][rank] of every rank
-// (gemv.cu, GemvPush); ef_tp_norm_kernel waits until every rank's counter has
-// reached the GEMV's CTA count, sums the slots in rank order and applies the
-// post-norm + residual + next norm of the decoder. Its last CTA clears the
-// parity's counters and advances the call counter that gives the parity. A
-// rank can be at most one call ahead of another here too, so it only ever
-// writes the other parity's slots and counters.
+// output rows, stamped with the fused call counter, into slot [parity][rank]
+// of a second data region of every rank (gemv.cu, GemvPush);
+// ef_tp_norm_kernel waits until every word of its row carries that counter,
+// sums the slots in rank order and applies the post-norm + residual + next
+// norm of the decoder. Its last CTA advances the call counter.
 #include <cuda_runtime.h>
 #include <stdint.h>
 #include <string.h>
@@ -42,11 +45,10 @@ constexpr size_t TP_CTRL_BYTES = 4096;
 
 struct ef_tp {
     int rank = 0, nranks = 1, device = 0;
-    size_t slot_bytes = 0;           // per rank per parity
-    size_t data_bytes = 0;           // 2 * nranks * slot_bytes
-    // [2][nranks][slot_bytes] data (collectives) | [2][nranks][slot_bytes] data (fused GEMV) | control:
-    // flags u32 [TP_CTAS][nranks] | epoch u32 [TP_CTAS] | error u32 | counters u32 [2][nranks] |
-    // fused call counter u32 | CTAs done u32
+    size_t slot_bytes = 0;           // payload bytes per rank per parity (stamped: twice that)
+    size_t data_bytes = 0;           // 2 * nranks * 2 * slot_bytes
+    // [2][nranks][2 * slot_bytes] data (collectives) | [2][nranks][2 * slot_bytes] data (fused GEMV) |
+    // control: epoch u32 [TP_CTAS] | error u32 | fused call counter u32 | CTAs done u32
     uint8_t *buf = nullptr;
     uint8_t *peer[EF_TP_MAX_RANKS] = {};
     bool opened[EF_TP_MAX_RANKS] = {};
@@ -58,36 +60,55 @@ namespace ef {
 struct TpArgs {
     uint8_t *peer[EF_TP_MAX_RANKS];
     int rank, nranks;
-    int64_t slot_bytes, data_bytes, timeout_ns;   // the control block is at 2 * data_bytes
+    int64_t slot_bytes, data_bytes, timeout_ns;   // stamped slot bytes; the control block is at 2 * data_bytes
 };
 
 // control block words of a rank's buffer
 struct TpCtl {
-    uint32_t *flags, *epoch, *error, *ctr, *fepoch, *fdone;
+    uint32_t *epoch, *error, *fepoch, *fdone;
 };
-__host__ __device__ inline TpCtl tp_ctl(uint8_t *buf, int64_t data_bytes, int nranks) {
+__host__ __device__ inline TpCtl tp_ctl(uint8_t *buf, int64_t data_bytes) {
     TpCtl c;
-    c.flags = reinterpret_cast<uint32_t *>(buf + 2 * data_bytes);
-    c.epoch = c.flags + TP_CTAS * nranks;
+    c.epoch = reinterpret_cast<uint32_t *>(buf + 2 * data_bytes);
     c.error = c.epoch + TP_CTAS;
-    c.ctr = c.error + 1;
-    c.fepoch = c.ctr + 2 * nranks;
+    c.fepoch = c.error + 1;
     c.fdone = c.fepoch + 1;
     return c;
 }
 
-__device__ __forceinline__ void st_release_sys(uint32_t *p, uint32_t v) {
-    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+// stamped words: (epoch << 32 | word), one single-copy-atomic 8-byte access each
+__device__ __forceinline__ void st_stamped(uint64_t *p, uint32_t w, uint32_t ep) {
+    asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(((uint64_t)ep << 32) | w) : "memory");
 }
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t *p) {
-    uint32_t v;
-    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+__device__ __forceinline__ void st_stamped2(uint64_t *p, uint32_t w0, uint32_t w1, uint32_t ep) {
+    asm volatile("st.relaxed.sys.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(((uint64_t)ep << 32) | w0),
+                 "l"(((uint64_t)ep << 32) | w1)
+                 : "memory");
+}
+__device__ __forceinline__ uint64_t ld_stamped(const uint64_t *p) {
+    uint64_t v;
+    asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
+}
+__device__ __forceinline__ void ld_stamped2(const uint64_t *p, uint64_t &v0, uint64_t &v1) {
+    asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "l"(p) : "memory");
 }
 __device__ __forceinline__ uint64_t global_ns() {
     uint64_t t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
+}
+
+// The word at p once its stamp is ep. Bounded: once `late` is set (by this
+// wait or an earlier one of the thread) it returns at once.
+__device__ __forceinline__ uint32_t wait_stamped(const uint64_t *p, uint32_t ep, uint64_t t0, int64_t limit,
+                                                 bool &late) {
+    uint64_t v = ld_stamped(p);
+    while ((uint32_t)(v >> 32) != ep && !late) {
+        if ((int64_t)(global_ns() - t0) > limit) late = true;
+        v = ld_stamped(p);
+    }
+    return (uint32_t)v;
 }
 
 // SUM: dst[i] = sum over ranks r (in order) of rank r's src[i], n floats.
@@ -100,117 +121,122 @@ __global__ void __launch_bounds__(256) ef_tp_kernel(const TpArgs a, const uint32
     __shared__ uint32_t ep, bad;
     const int cb = blockIdx.x;
     uint8_t *mine = a.peer[a.rank];
-    const TpCtl ctl = tp_ctl(mine, a.data_bytes, a.nranks);
-    uint32_t *flags = ctl.flags, *epoch = ctl.epoch, *error = ctl.error;
+    const TpCtl ctl = tp_ctl(mine, a.data_bytes);
     if (threadIdx.x == 0) {
-        bad = *(volatile uint32_t *)error;
-        ep = *(volatile uint32_t *)(epoch + cb) + 1;
+        bad = *(volatile uint32_t *)ctl.error;
+        ep = *(volatile uint32_t *)(ctl.epoch + cb) + 1;
     }
     __syncthreads();
     if (bad) return;
+    const uint32_t e = ep;
     // this CTA's part: [i0, i1), in whole 16-byte pieces except at the end
     const int64_t per = ((n + TP_CTAS - 1) / TP_CTAS + 3) / 4 * 4;
     const int64_t i0 = cb * per < n ? cb * per : n, i1 = i0 + per < n ? i0 + per : n;
-    const int parity = ep & 1;
+    const int parity = e & 1;
     const int64_t off = ((int64_t)parity * a.nranks + a.rank) * a.slot_bytes;
     const bool vec = ((uintptr_t)src % 16) == 0;
     for (int r = 0; r < a.nranks; r++) {
-        uint32_t *d = reinterpret_cast<uint32_t *>(a.peer[r] + off);
+        if (r == a.rank) continue;
+        uint64_t *d = reinterpret_cast<uint64_t *>(a.peer[r] + off);
         int64_t i = i0;
         if (vec) {
             const int64_t nv = (i1 - i0) / 4;
-            for (int64_t j = threadIdx.x; j < nv; j += blockDim.x)
-                reinterpret_cast<uint4 *>(d + i0)[j] = reinterpret_cast<const uint4 *>(src + i0)[j];
+            for (int64_t j = threadIdx.x; j < nv; j += blockDim.x) {
+                const uint4 v = reinterpret_cast<const uint4 *>(src + i0)[j];
+                st_stamped2(d + i0 + 4 * j, v.x, v.y, e);
+                st_stamped2(d + i0 + 4 * j + 2, v.z, v.w, e);
+            }
             i = i0 + 4 * nv;
         }
-        for (int64_t j = i + threadIdx.x; j < i1; j += blockDim.x) d[j] = src[j];
+        for (int64_t j = i + threadIdx.x; j < i1; j += blockDim.x) st_stamped(d + j, src[j], e);
     }
-    // the CTA barrier orders every thread's stores before the flag stores,
-    // and a release is cumulative over what happens before it
+    // every thread's reads of src above before any thread's writes of dst (in place)
     __syncthreads();
-    if (threadIdx.x < a.nranks) {
-        uint32_t *f = tp_ctl(a.peer[threadIdx.x], a.data_bytes, a.nranks).flags + cb * a.nranks + a.rank;
-        st_release_sys(f, ep);
-    }
-    // wait for every rank's part of this call (bounded)
-    if (threadIdx.x < a.nranks) {
-        const uint64_t t0 = global_ns();
-        while ((int32_t)(ld_acquire_sys(flags + cb * a.nranks + threadIdx.x) - ep) < 0) {
-            if ((int64_t)(global_ns() - t0) > a.timeout_ns) {
-                atomicExch(error, 1u + threadIdx.x);
-                bad = 1;
-                break;
-            }
-            __nanosleep(20);
-        }
-    }
-    __syncthreads();
-    if (bad) return;
-    const uint8_t *slots = mine + (int64_t)parity * a.nranks * a.slot_bytes;
+    const uint64_t t0 = global_ns();
+    bool late = false;
+    int who = -1;                           // the first rank whose words did not arrive in time
+    const uint64_t *slots = reinterpret_cast<const uint64_t *>(mine + (int64_t)parity * a.nranks * a.slot_bytes);
+    const int64_t sw = a.slot_bytes / 8;    // stamped words per slot
     if (SUM) {
         float *df = reinterpret_cast<float *>(dst);
         for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
             float s = 0.f;
-            for (int r = 0; r < a.nranks; r++) s += reinterpret_cast<const float *>(slots + r * a.slot_bytes)[i];
-            df[i] = s;
+            for (int r = 0; r < a.nranks; r++) {
+                s += __uint_as_float(r == a.rank ? src[i] : wait_stamped(slots + r * sw + i, e, t0, a.timeout_ns, late));
+                if (late && who < 0) who = r;
+            }
+            if (!late) df[i] = s;
         }
     } else {
-        for (int r = 0; r < a.nranks; r++) {
-            const uint32_t *sr = reinterpret_cast<const uint32_t *>(slots + r * a.slot_bytes);
-            for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) dst[r * n + i] = sr[i];
-        }
+        for (int r = 0; r < a.nranks; r++)
+            for (int64_t i = i0 + threadIdx.x; i < i1; i += blockDim.x) {
+                const uint32_t w = r == a.rank ? src[i] : wait_stamped(slots + r * sw + i, e, t0, a.timeout_ns, late);
+                if (late && who < 0) who = r;
+                if (!late) dst[r * n + i] = w;
+            }
     }
-    __syncthreads();
-    if (threadIdx.x == 0) *(volatile uint32_t *)(epoch + cb) = ep;
+    if (__syncthreads_or(late)) {
+        if (late) atomicExch(ctl.error, 1u + (uint32_t)who);
+        return;
+    }
+    if (threadIdx.x == 0) *(volatile uint32_t *)(ctl.epoch + cb) = e;
+}
+
+// The four words at p (16-byte aligned) once every stamp is ep; bounded like
+// wait_stamped.
+__device__ __forceinline__ float4 wait_stamped4(const uint64_t *p, uint32_t ep, uint64_t t0, int64_t limit,
+                                                bool &late) {
+    uint64_t v0, v1, v2, v3;
+    for (;;) {
+        ld_stamped2(p, v0, v1);
+        ld_stamped2(p + 2, v2, v3);
+        const bool ok = (uint32_t)(v0 >> 32) == ep && (uint32_t)(v1 >> 32) == ep && (uint32_t)(v2 >> 32) == ep &&
+                        (uint32_t)(v3 >> 32) == ep;
+        if (ok || late) break;
+        if ((int64_t)(global_ns() - t0) > limit) late = true;
+    }
+    return make_float4(__uint_as_float((uint32_t)v0), __uint_as_float((uint32_t)v1), __uint_as_float((uint32_t)v2),
+                       __uint_as_float((uint32_t)v3));
 }
 
 // Consumer of the fused row-parallel GEMV: row blockIdx.x of o = sum over
 // ranks (in order) of the slots; then x += rmsnorm(o) * w_post (or += o without
 // w_post) and nrm = rmsnorm(x) * w_next, as ef_norm_add_norm_kernel.
 template <int V>
-__global__ void __launch_bounds__(256) ef_tp_norm_kernel(const TpArgs a, uint32_t expected,
-                                                      const float *__restrict__ w_post, float *__restrict__ x,
-                                                      const float *__restrict__ w_next, int n, float eps,
-                                                      float *__restrict__ nrm) {
+__global__ void __launch_bounds__(256) ef_tp_norm_kernel(const TpArgs a, const float *__restrict__ w_post,
+                                                      float *__restrict__ x, const float *__restrict__ w_next, int n,
+                                                      float eps, float *__restrict__ nrm) {
     pdl_trigger();
     pdl_wait();
     __shared__ float red[32];
-    __shared__ uint32_t par, ep, bad;
+    __shared__ uint32_t ep, bad;
     uint8_t *mine = a.peer[a.rank];
-    const TpCtl ctl = tp_ctl(mine, a.data_bytes, a.nranks);
+    const TpCtl ctl = tp_ctl(mine, a.data_bytes);
     if (threadIdx.x == 0) {
         bad = *(volatile uint32_t *)ctl.error;
-        ep = *(volatile uint32_t *)ctl.fepoch;
-        par = ep & 1;
+        ep = *(volatile uint32_t *)ctl.fepoch + 1;   // this call's number (the GEMV's stamp)
     }
     __syncthreads();
     if (bad) return;
-    if (threadIdx.x < a.nranks) {
-        const uint32_t *c = ctl.ctr + par * a.nranks + threadIdx.x;
-        const uint64_t t0 = global_ns();
-        while (ld_acquire_sys(c) < expected) {
-            if ((int64_t)(global_ns() - t0) > a.timeout_ns) {
-                atomicExch(ctl.error, 1u + threadIdx.x);
-                bad = 1;
-                break;
-            }
-            __nanosleep(20);
-        }
-    }
-    __syncthreads();
-    if (bad) return;
+    const uint32_t e = ep;
     const int64_t row = (int64_t)blockIdx.x * (n / 4);
-    const uint8_t *slots = mine + a.data_bytes + (int64_t)par * a.nranks * a.slot_bytes;
+    const uint64_t *slots =
+        reinterpret_cast<const uint64_t *>(mine + a.data_bytes + (int64_t)(e & 1) * a.nranks * a.slot_bytes);
+    const int64_t sw = a.slot_bytes / 8;    // stamped words per slot
     float4 *x4 = reinterpret_cast<float4 *>(x) + row;
     float4 *n4 = reinterpret_cast<float4 *>(nrm) + row;
     const float4 *wp = reinterpret_cast<const float4 *>(w_post), *wn = reinterpret_cast<const float4 *>(w_next);
+    const uint64_t t0 = global_ns();
+    bool late = false;
+    int who = -1;
     float4 ov[V], xv[V];
 #pragma unroll
     for (int j = 0; j < V; j++) {
         const int i = threadIdx.x + blockDim.x * j;
         float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
         for (int r = 0; r < a.nranks; r++) {
-            const float4 v = reinterpret_cast<const float4 *>(slots + r * a.slot_bytes)[row + i];
+            const float4 v = wait_stamped4(slots + r * sw + 4 * (row + i), e, t0, a.timeout_ns, late);
+            if (late && who < 0) who = r;
             s.x += v.x;
             s.y += v.y;
             s.z += v.z;
@@ -218,6 +244,10 @@ __global__ void __launch_bounds__(256) ef_tp_norm_kernel(const TpArgs a, uint32_
         }
         ov[j] = s;
         xv[j] = x4[i];
+    }
+    if (__syncthreads_or(late)) {
+        if (late) atomicExch(ctl.error, 1u + (uint32_t)who);
+        return;
     }
     float s1 = 1.f;
     if (w_post) {
@@ -245,15 +275,12 @@ __global__ void __launch_bounds__(256) ef_tp_norm_kernel(const TpArgs a, uint32_
         const float4 w4 = wn[i];
         n4[i] = make_float4(xv[j].x * s2 * w4.x, xv[j].y * s2 * w4.y, xv[j].z * s2 * w4.z, xv[j].w * s2 * w4.w);
     }
-    // the last CTA clears this parity's counters and advances the call counter
+    // the last CTA advances the call counter
     __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
         if (atomicAdd(ctl.fdone, 1u) == gridDim.x - 1) {
-            for (int r = 0; r < a.nranks; r++) ctl.ctr[par * a.nranks + r] = 0;
             *ctl.fdone = 0;
-            __threadfence();
-            *(volatile uint32_t *)ctl.fepoch = ep + 1;
+            *(volatile uint32_t *)ctl.fepoch = e;
         }
     }
 }
@@ -263,23 +290,21 @@ static TpArgs tp_args(ef_tp *tp) {
     for (int r = 0; r < tp->nranks; r++) a.peer[r] = tp->peer[r];
     a.rank = tp->rank;
     a.nranks = tp->nranks;
-    a.slot_bytes = (int64_t)tp->slot_bytes;
+    a.slot_bytes = 2 * (int64_t)tp->slot_bytes;
     a.data_bytes = (int64_t)tp->data_bytes;
     a.timeout_ns = tp->timeout_ns;
     return a;
 }
 
-static int tp_launch(ef_ctx *ctx, ef_tp *tp, bool sum, const void *src, int64_t words, void *dst) {
-    TpArgs a = {};
-    for (int r = 0; r < tp->nranks; r++) {
+static int tp_connected(ef_ctx *ctx, const ef_tp *tp) {
+    for (int r = 0; r < tp->nranks; r++)
         if (!tp->peer[r]) return set_err(ctx, EF_ERR_INVALID, "tp: rank %d is not connected", r);
-        a.peer[r] = tp->peer[r];
-    }
-    a.rank = tp->rank;
-    a.nranks = tp->nranks;
-    a.slot_bytes = (int64_t)tp->slot_bytes;
-    a.data_bytes = (int64_t)tp->data_bytes;
-    a.timeout_ns = tp->timeout_ns;
+    return EF_OK;
+}
+
+static int tp_launch(ef_ctx *ctx, ef_tp *tp, bool sum, const void *src, int64_t words, void *dst) {
+    if (int rc = tp_connected(ctx, tp)) return rc;
+    const TpArgs a = tp_args(tp);
     if (sum)
         return launch_on(ctx, ef_tp_kernel<true>, TP_CTAS, 256, 0, "allreduce launch", a, (const uint32_t *)src, words,
                          (uint32_t *)dst);
@@ -303,7 +328,7 @@ int ef_tp_create(ef_ctx *ctx, int rank, int nranks, size_t max_bytes, double tim
     tp->nranks = nranks;
     tp->device = ctx->device;
     tp->slot_bytes = (max_bytes + 255) / 256 * 256;
-    tp->data_bytes = 2 * (size_t)nranks * tp->slot_bytes;
+    tp->data_bytes = 2 * (size_t)nranks * 2 * tp->slot_bytes;
     tp->timeout_ns = (int64_t)(timeout_s * 1e9);
     const size_t total = 2 * tp->data_bytes + TP_CTRL_BYTES;
     int rc = check_cuda(ctx, cudaMalloc(&tp->buf, total), "tp buffer alloc");
@@ -364,8 +389,7 @@ int ef_gemv_allreduce_norm(ef_ctx *ctx, ef_tp *tp, const ef_weight *w, const flo
                            float *x_resid, const float *w_next, float eps, float *nrm) {
     if (!ctx || !tp || !w || !x || !x_resid || !w_next || !nrm || M < 1 || M > 16)
         return ctx ? set_err(ctx, EF_ERR_INVALID, "gemv_allreduce_norm: bad arguments") : EF_ERR_INVALID;
-    for (int r = 0; r < tp->nranks; r++)
-        if (!tp->peer[r]) return set_err(ctx, EF_ERR_INVALID, "tp: rank %d is not connected", r);
+    if (int rc = tp_connected(ctx, tp)) return rc;
     if ((size_t)M * w->rows * 4 > tp->slot_bytes)
         return set_err(ctx, EF_ERR_RANGE, "gemv_allreduce_norm: %d x %lld floats exceed the %zu-byte slot", M,
                        (long long)w->rows, tp->slot_bytes);
@@ -378,32 +402,27 @@ int ef_gemv_allreduce_norm(ef_ctx *ctx, ef_tp *tp, const ef_weight *w, const flo
     GemvPush push;
     push.n = tp->nranks;
     push.rank = tp->rank;
-    push.slot_bytes = (int64_t)tp->slot_bytes;
-    for (int r = 0; r < tp->nranks; r++) {
-        push.data[r] = tp->peer[r] + tp->data_bytes;
-        push.ctr[r] = tp_ctl(tp->peer[r], (int64_t)tp->data_bytes, tp->nranks).ctr;
-    }
-    push.epoch = tp_ctl(tp->buf, (int64_t)tp->data_bytes, tp->nranks).fepoch;
-    int64_t ctas = 0;
+    push.slot_bytes = a.slot_bytes;
+    for (int r = 0; r < tp->nranks; r++) push.data[r] = tp->peer[r] + tp->data_bytes;
+    push.epoch = tp_ctl(tp->buf, (int64_t)tp->data_bytes).fepoch;
     float *ys[1] = {nrm};    // (not written: the output goes to the ranks' slots)
-    if (int rc = launch_gemv(ctx, &w, 1, nullptr, x, M, ys, &push, &ctas)) return rc;
-    const uint32_t expected = (uint32_t)ctas;
+    if (int rc = launch_gemv(ctx, &w, 1, nullptr, x, M, ys, &push)) return rc;
     switch (v) {
-    case 1: return launch_on(ctx, ef_tp_norm_kernel<1>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
+    case 1: return launch_on(ctx, ef_tp_norm_kernel<1>, M, th, 0, "tp norm launch", a, w_post, x_resid, w_next,
                              (int)w->rows, eps, nrm);
-    case 2: return launch_on(ctx, ef_tp_norm_kernel<2>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
+    case 2: return launch_on(ctx, ef_tp_norm_kernel<2>, M, th, 0, "tp norm launch", a, w_post, x_resid, w_next,
                              (int)w->rows, eps, nrm);
-    case 4: return launch_on(ctx, ef_tp_norm_kernel<4>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid, w_next,
+    case 4: return launch_on(ctx, ef_tp_norm_kernel<4>, M, th, 0, "tp norm launch", a, w_post, x_resid, w_next,
                              (int)w->rows, eps, nrm);
-    default: return launch_on(ctx, ef_tp_norm_kernel<8>, M, th, 0, "tp norm launch", a, expected, w_post, x_resid,
-                              w_next, (int)w->rows, eps, nrm);
+    default: return launch_on(ctx, ef_tp_norm_kernel<8>, M, th, 0, "tp norm launch", a, w_post, x_resid, w_next,
+                              (int)w->rows, eps, nrm);
     }
 }
 
 int ef_tp_status(ef_ctx *ctx, const ef_tp *tp) {
     if (!ctx || !tp) return ctx ? set_err(ctx, EF_ERR_INVALID, "tp_status: bad arguments") : EF_ERR_INVALID;
     uint32_t err = 0;
-    const TpCtl c = tp_ctl(tp->buf, (int64_t)tp->data_bytes, tp->nranks);
+    const TpCtl c = tp_ctl(tp->buf, (int64_t)tp->data_bytes);
     if (int rc = check_cuda(ctx, cudaMemcpy(&err, c.error, 4, cudaMemcpyDeviceToHost), "tp status read"))
         return rc;
     if (err) return set_err(ctx, EF_ERR_TIMEOUT, "tp: rank %d did not arrive in time", (int)err - 1);

@@ -1209,16 +1209,22 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const Ge
     const int M = a.M;
     const int64_t rows = a.rows[m];
     float *y = a.y[m];
-    // output element [tok][r]: y, or every rank's exchange slot (tensor parallel)
+    // output element [tok][r]: y, or every rank's exchange slot (tensor
+    // parallel), stamped with this call's number
     const int npush = a.push.n;
-    const int64_t slot_off = npush ? ((int64_t)((*(volatile const uint32_t *)a.push.epoch) & 1) * npush +
-                                      a.push.rank) * a.push.slot_bytes : 0;
+    const uint32_t call = npush ? *(volatile const uint32_t *)a.push.epoch + 1 : 0;
+    const int64_t slot_off = ((int64_t)(call & 1) * npush + a.push.rank) * a.push.slot_bytes;
     auto put = [&](int tok, int64_t r, float v) {
         const int64_t idx = (int64_t)tok * rows + r;
         if (!npush) {
             y[idx] = v;
         } else {
-            for (int p = 0; p < npush; p++) reinterpret_cast<float *>(a.push.data[p] + slot_off)[idx] = v;
+            const uint64_t word = ((uint64_t)call << 32) | __float_as_uint(v);
+            for (int p = 0; p < npush; p++)
+                asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(
+                                 reinterpret_cast<uint64_t *>(a.push.data[p] + slot_off) + idx),
+                             "l"(word)
+                             : "memory");
         }
     };
     if (kh == 0 && active) {
@@ -1256,16 +1262,6 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const Ge
             }
         }
         cluster.sync();              // keep this CTA's shared memory alive until all ranks have read it
-    }
-    if (npush) {
-        // this CTA's stores, then one count per rank (the barrier orders every
-        // thread's stores before the release, which is cumulative)
-        __syncthreads();
-        if (threadIdx.x < npush) {
-            const int parity = (int)((*(volatile const uint32_t *)a.push.epoch) & 1);
-            uint32_t *c = a.push.ctr[threadIdx.x] + parity * npush + a.push.rank;
-            asm volatile("red.release.sys.global.add.u32 [%0], 1;" ::"l"(c) : "memory");
-        }
     }
 }
 
@@ -1460,7 +1456,7 @@ static int launch_sw(ef_ctx *ctx, GemvArgs &a, bool sw, const ef_weight *const *
 }
 
 int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight *w_up, const float *x, int M,
-                float *const *ys, const GemvPush *push, int64_t *ctas_out) {
+                float *const *ys, const GemvPush *push) {
     GemvArgs a = {};
     if (push) a.push = *push;
     const ef_weight *w0 = ws[0];
@@ -1487,7 +1483,6 @@ int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight 
     case EF_IQ1_S: rc = launch_sw<EF_IQ1_S>(ctx, a, sw, ws, n, x); break;
     default: return set_err(ctx, EF_ERR_TYPE, "gemv: unsupported type %d", w0->type);
     }
-    if (ctas_out) *ctas_out = a.ctas;
     return rc;
 }
 

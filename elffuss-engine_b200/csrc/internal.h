@@ -99,15 +99,14 @@ inline int norm_v(int n, int &threads) {
 
 // gemv.cu
 // Row-parallel output of a tensor-parallel GEMV (comm.cu): instead of y, the
-// kernel stores its rows into slot [parity][rank] of every rank's exchange
-// data region (parity = *epoch & 1) and each CTA then adds 1 (release, system
-// scope) to counter [parity][rank] of every rank.
+// kernel stores its rows, each word stamped with this call's number
+// e = *epoch + 1 as one 8-byte store (e << 32 | word), into slot
+// [e & 1][rank] of every rank's exchange data region.
 struct GemvPush {
     int n = 0, rank = 0;                      // ranks (0 = off), this rank
-    int64_t slot_bytes = 0;
+    int64_t slot_bytes = 0;                   // bytes of a stamped slot
     uint8_t *data[EF_TP_MAX_RANKS] = {};      // each rank's data region [2][n][slot_bytes]
-    uint32_t *ctr[EF_TP_MAX_RANKS] = {};      // each rank's counters [2][n]
-    const uint32_t *epoch = nullptr;          // this rank's call counter
+    const uint32_t *epoch = nullptr;          // this rank's count of finished calls
 };
 struct GemvPlan {
     int64_t ctas;      // rowblocks x kslices
@@ -119,8 +118,7 @@ struct GemvPlan {
 };
 GemvPlan gemv_plan(int64_t rowblocks, int64_t nchunks, int xb, bool fused, int ks);
 int launch_gemv(ef_ctx *ctx, const ef_weight *const *ws, int n, const ef_weight *w_up,
-                const float *x, int M, float *const *ys, const GemvPush *push = nullptr,
-                int64_t *ctas_out = nullptr);
+                const float *x, int M, float *const *ys, const GemvPush *push = nullptr);
 
 // gemm.cu
 int gemm_status(ef_ctx *ctx);

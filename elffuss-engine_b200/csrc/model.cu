@@ -28,6 +28,10 @@
 //   swiglu             g * sigmoid(g) * u for the prompt's FFN
 // Positions and tokens live in device memory, so one decode step can be
 // captured as a CUDA graph and replayed with no host round trip.
+// The KV caches hold f32, or f16 (the reference's kvF16 option,
+// kernels.attn.wgsl.js:51-55, model.js:906-946: k after its norm and RoPE and v
+// rounded to f16 when stored, to nearest even; q, the scores and every sum
+// stay f32). Half the cache bytes, which decode attention reads whole.
 #include <cuda_runtime.h>
 #include <math.h>
 
@@ -37,6 +41,21 @@
 #include "internal.h"
 
 namespace ef {
+
+// cache element loads and stores (f32 or f16 caches)
+__device__ __forceinline__ float kv_f(float x) { return x; }
+__device__ __forceinline__ float kv_f(__half x) { return __half2float(x); }
+__device__ __forceinline__ void kv_put(float *p, float v) { *p = v; }
+__device__ __forceinline__ void kv_put(__half *p, float v) { *p = __float2half_rn(v); }
+__device__ __forceinline__ float4 kv_ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+__device__ __forceinline__ float4 kv_ld4(const __half *p) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(p);
+    const float2 a = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 b = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ float2 kv_ld2(const float *p) { return *reinterpret_cast<const float2 *>(p); }
+__device__ __forceinline__ float2 kv_ld2(const __half *p) { return __half22float2(*reinterpret_cast<const __half2 *>(p)); }
 
 
 // One CTA per row of T = min(256, n/4) threads; each thread keeps V float4 of
@@ -153,12 +172,12 @@ __global__ void ef_shortconv_kernel(const float *__restrict__ bcx, const float *
 // (j < D/64): NEOX pairs elements (p, p + D/2), NORM pairs (2p, 2p + 1);
 // theta = position * base^(-2p/D) (kernels.nn.wgsl.js:87-139). With wq / wk,
 // the per-head RMSNorm comes first (model.js:877-917).
-template <int D, bool NEOX>
+template <int D, bool NEOX, typename KV>
 __global__ void ef_rope_cache_kernel(float *__restrict__ q, const float *__restrict__ k, const float *__restrict__ v,
                                   const float *__restrict__ wq, const float *__restrict__ wk,
                                   const int *__restrict__ pos, int seqs, int tokens, int max_pos, int H, int KVH,
-                                  float theta_scale, float eps, float *__restrict__ kcache,
-                                  float *__restrict__ vcache) {
+                                  float theta_scale, float eps, KV *__restrict__ kcache,
+                                  KV *__restrict__ vcache) {
     pdl_trigger();
     pdl_wait();
     constexpr int J = D / 64;
@@ -194,7 +213,7 @@ __global__ void ef_rope_cache_kernel(float *__restrict__ q, const float *__restr
         }
     }
     const bool store = !isq && p >= 0 && p < max_pos;   // (a position past the caches is not stored)
-    float *kc = kcache + (((int64_t)sq * max_pos + p) * KVH + hh) * D;
+    KV *kc = kcache + (((int64_t)sq * max_pos + p) * KVH + hh) * D;
 #pragma unroll
     for (int j = 0; j < J; j++) {
         const float theta = (float)p * powf(theta_scale, (float)(lane + 32 * j));
@@ -205,15 +224,15 @@ __global__ void ef_rope_cache_kernel(float *__restrict__ q, const float *__restr
             qrow[i0[j]] = r0;
             qrow[i1[j]] = r1;
         } else if (store) {
-            kc[i0[j]] = r0;
-            kc[i1[j]] = r1;
+            kv_put(kc + i0[j], r0);
+            kv_put(kc + i1[j], r1);
         }
     }
     if (store) {
         const float *vr = v + ((int64_t)r * KVH + hh) * D;
-        float *vc = vcache + (((int64_t)sq * max_pos + p) * KVH + hh) * D;
+        KV *vc = vcache + (((int64_t)sq * max_pos + p) * KVH + hh) * D;
 #pragma unroll
-        for (int j = 0; j < D / 32; j++) vc[lane + 32 * j] = vr[lane + 32 * j];
+        for (int j = 0; j < D / 32; j++) kv_put(vc + lane + 32 * j, vr[lane + 32 * j]);
     }
 }
 
@@ -224,9 +243,9 @@ __global__ void ef_rope_cache_kernel(float *__restrict__ q, const float *__restr
 // sigmoid(gate[r][h]) when gate is given (kernels.nn.wgsl.js:141-200,
 // kernels.model.wgsl.js:89-105). Scores in shared memory; the weighted sum of
 // v rows is split over blockDim / D groups of keys, then added in group order.
-template <int D>
-__global__ void __launch_bounds__(256) ef_attention_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
-                                                        const float *__restrict__ vcache,
+template <int D, typename KV>
+__global__ void __launch_bounds__(256) ef_attention_kernel(const float *__restrict__ q, const KV *__restrict__ kcache,
+                                                        const KV *__restrict__ vcache,
                                                         const float *__restrict__ gate, const int *__restrict__ pos,
                                                         int tokens, int max_pos, int window, int H, int KVH,
                                                         float *__restrict__ out) {
@@ -240,18 +259,18 @@ __global__ void __launch_bounds__(256) ef_attention_kernel(const float *__restri
     const int sq = r / tokens, t = r - sq * tokens;
     const int nkv = min(pos[sq] + t + 1, max_pos), qpos = nkv - 1;   // never past the caches
     const int k0 = window > 0 && qpos - window + 1 > 0 ? qpos - window + 1 : 0;
-    const float *kb = kcache + (int64_t)sq * max_pos * KVH * D;
-    const float *vb = vcache + (int64_t)sq * max_pos * KVH * D;
+    const KV *kb = kcache + (int64_t)sq * max_pos * KVH * D;
+    const KV *vb = vcache + (int64_t)sq * max_pos * KVH * D;
     const float *qr = q + ((int64_t)r * H + h) * D;
     for (int i = threadIdx.x; i < D; i += blockDim.x) qs[i] = qr[i] * rsqrtf((float)D);
     __syncthreads();
     float mx = -1e30f;
     for (int kk = k0 + threadIdx.x; kk < nkv; kk += blockDim.x) {
-        const float4 *kr = reinterpret_cast<const float4 *>(kb + ((int64_t)kk * KVH + kvh) * D);
+        const KV *kr = kb + ((int64_t)kk * KVH + kvh) * D;
         float s = 0.f;
 #pragma unroll
         for (int i = 0; i < D / 4; i++) {
-            const float4 kv = kr[i];
+            const float4 kv = kv_ld4(kr + 4 * i);
             s += qs[4 * i] * kv.x + qs[4 * i + 1] * kv.y + qs[4 * i + 2] * kv.z + qs[4 * i + 3] * kv.w;
         }
         sc[kk - k0] = s;
@@ -279,7 +298,7 @@ __global__ void __launch_bounds__(256) ef_attention_kernel(const float *__restri
     constexpr int G = 256 / D;   // key groups
     const int d = threadIdx.x % D, g = threadIdx.x / D;
     float acc = 0.f;
-    for (int kk = k0 + g; kk < nkv; kk += G) acc += sc[kk - k0] * vb[((int64_t)kk * KVH + kvh) * D + d];
+    for (int kk = k0 + g; kk < nkv; kk += G) acc += sc[kk - k0] * kv_f(vb[((int64_t)kk * KVH + kvh) * D + d]);
     part[threadIdx.x] = acc;
     __syncthreads();
     if (threadIdx.x < D) {
@@ -311,9 +330,9 @@ template <int D> constexpr size_t fa_smem() {
     return (size_t)(FA_R * (D + 4) + 2 * FA_BK * (D + 4) + FA_R * (FA_BK + 4) + 3 * FA_R) * sizeof(float);
 }
 
-template <int D, int G>
-__global__ void __launch_bounds__(FA_T, 1) ef_attn_prompt_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
-                                                          const float *__restrict__ vcache,
+template <int D, int G, typename KV>
+__global__ void __launch_bounds__(FA_T, 1) ef_attn_prompt_kernel(const float *__restrict__ q, const KV *__restrict__ kcache,
+                                                          const KV *__restrict__ vcache,
                                                           const float *__restrict__ gate, const int *__restrict__ pos,
                                                           int tokens, int max_pos, int window, int H, int KVH,
                                                           float *__restrict__ out) {
@@ -369,8 +388,8 @@ __global__ void __launch_bounds__(FA_T, 1) ef_attn_prompt_kernel(const float *__
             float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
             if (key <= qhi) {   // qhi < max_pos: inside the caches
                 const int64_t off = (((int64_t)sq * max_pos + key) * KVH + kvh) * D + 4 * c;
-                kv = *reinterpret_cast<const float4 *>(kcache + off);
-                vv = *reinterpret_cast<const float4 *>(vcache + off);
+                kv = kv_ld4(kcache + off);
+                vv = kv_ld4(vcache + off);
             }
             *reinterpret_cast<float4 *>(Ks + j * LD + 4 * c) = kv;
             *reinterpret_cast<float4 *>(Vs + j * LD + 4 * c) = vv;
@@ -492,14 +511,14 @@ constexpr int AK = 32;         // keys per range
 constexpr int AT = 128;        // threads per CTA
 static_assert(AK == 32, "the softmax step holds one key per lane");
 
-template <int D, int G>
-__global__ void __launch_bounds__(AT) ef_attn_part_kernel(const float *__restrict__ q, const float *__restrict__ kcache,
-                                                       const float *__restrict__ vcache, const int *__restrict__ pos,
+template <int D, int G, typename KV>
+__global__ void __launch_bounds__(AT) ef_attn_part_kernel(const float *__restrict__ q, const KV *__restrict__ kcache,
+                                                       const KV *__restrict__ vcache, const int *__restrict__ pos,
                                                        int tokens, int max_pos, int window, int H, int KVH,
                                                        float *__restrict__ part) {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ __align__(16) float kv_s[];   // k rows [AK][D], then v rows [AK][D]
+    extern __shared__ __align__(16) uint8_t kv_raw[];   // k rows [AK][D], then v rows [AK][D] (cache type)
     __shared__ float sc[G][AK];
     __shared__ float ml[G][2];
     const int split = blockIdx.x, kvh = blockIdx.y, r = blockIdx.z, nsplit = gridDim.x;
@@ -516,15 +535,16 @@ __global__ void __launch_bounds__(AT) ef_attn_part_kernel(const float *__restric
         return;
     }
     const int n = b - a;
-    float *ks = kv_s, *vs = kv_s + AK * D;
+    KV *ks = reinterpret_cast<KV *>(kv_raw), *vs = ks + AK * D;
     {
-        const float *kb = kcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
-        const float *vb = vcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
-        constexpr int C = D / 4;     // 16-byte pieces per row
+        const KV *kb = kcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
+        const KV *vb = vcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
+        constexpr int EP = 16 / sizeof(KV);   // elements per 16-byte piece
+        constexpr int C = D / EP;             // 16-byte pieces per row
         for (int i = threadIdx.x; i < n * C; i += AT) {
             const int j = i / C, c = i - j * C;
-            cp_async16(ks + j * D + 4 * c, kb + (int64_t)j * KVH * D + 4 * c);
-            cp_async16(vs + j * D + 4 * c, vb + (int64_t)j * KVH * D + 4 * c);
+            cp_async16(ks + j * D + EP * c, kb + (int64_t)j * KVH * D + EP * c);
+            cp_async16(vs + j * D + EP * c, vb + (int64_t)j * KVH * D + EP * c);
         }
         cp_commit();
     }
@@ -541,10 +561,10 @@ __global__ void __launch_bounds__(AT) ef_attn_part_kernel(const float *__restric
     for (int j = warp; j < n; j += AT / 32) {
         float kr[E];
         if constexpr (E == 4) {
-            const float4 v4 = *reinterpret_cast<const float4 *>(ks + j * D + lane * 4);
+            const float4 v4 = kv_ld4(ks + j * D + lane * 4);
             kr[0] = v4.x; kr[1] = v4.y; kr[2] = v4.z; kr[3] = v4.w;
         } else {
-            const float2 v2 = *reinterpret_cast<const float2 *>(ks + j * D + lane * 2);
+            const float2 v2 = kv_ld2(ks + j * D + lane * 2);
             kr[0] = v2.x; kr[1] = v2.y;
         }
         float s[G];
@@ -587,7 +607,7 @@ __global__ void __launch_bounds__(AT) ef_attn_part_kernel(const float *__restric
     for (int jj = 0; jj < GJ; jj++) acc[jj] = 0.f;
 #pragma unroll 4
     for (int j = 0; j < n; j++) {
-        const float v = vs[j * D + d];
+        const float v = kv_f(vs[j * D + d]);
 #pragma unroll
         for (int jj = 0; jj < GJ; jj++)
             if (g0 + jj * GS < G) acc[jj] += sc[g0 + jj * GS][j] * v;
@@ -899,38 +919,184 @@ __global__ void ef_argmax_select_kernel(const int *__restrict__ pairs, int npair
 
 static int grid1d(int64_t n, int b) { return (int)((n + b - 1) / b); }
 
-template <int D, int G>
-static int part_launch(ef_ctx *ctx, dim3 grid, const float *q, const float *kcache, const float *vcache, const int *pos,
+template <int D, int G, typename KV>
+static int part_launch(ef_ctx *ctx, dim3 grid, const float *q, const KV *kcache, const KV *vcache, const int *pos,
                        int tokens, int max_pos, int window, int heads, int kv_heads, float *part) {
-    constexpr size_t smem = 2 * AK * D * sizeof(float);
+    constexpr size_t smem = 2 * AK * D * sizeof(KV);
     static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
-        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(ef_attn_part_kernel<D, G>,
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(ef_attn_part_kernel<D, G, KV>,
                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                                 "attention smem attribute"))
             return rc;
         configured.fetch_or(1ull << ctx->device);
     }
-    return launch_on(ctx, ef_attn_part_kernel<D, G>, grid, AT, smem, "attention launch", q, kcache, vcache, pos, tokens,
-                     max_pos, window, heads, kv_heads, part);
+    return launch_on(ctx, ef_attn_part_kernel<D, G, KV>, grid, AT, smem, "attention launch", q, kcache, vcache, pos,
+                     tokens, max_pos, window, heads, kv_heads, part);
 }
 
-template <int D, int G>
-static int prompt_attn_launch(ef_ctx *ctx, int seqs, const float *q, const float *kcache, const float *vcache,
+template <int D, int G, typename KV>
+static int prompt_attn_launch(ef_ctx *ctx, int seqs, const float *q, const KV *kcache, const KV *vcache,
                               const float *gate, const int *pos, int tokens, int max_pos, int window, int heads,
                               int kv_heads, float *out) {
     constexpr size_t smem = fa_smem<D>();
     static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
-        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(ef_attn_prompt_kernel<D, G>,
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(ef_attn_prompt_kernel<D, G, KV>,
                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                                 "prompt attention smem attribute"))
             return rc;
         configured.fetch_or(1ull << ctx->device);
     }
     const dim3 grid((unsigned)((tokens + FA_R / G - 1) / (FA_R / G)), (unsigned)kv_heads, (unsigned)seqs);
-    return launch_on(ctx, ef_attn_prompt_kernel<D, G>, grid, FA_T, smem, "prompt attention launch", q, kcache, vcache,
-                     gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+    return launch_on(ctx, ef_attn_prompt_kernel<D, G, KV>, grid, FA_T, smem, "prompt attention launch", q, kcache,
+                     vcache, gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+}
+
+template <typename KV>
+static int rope_launch(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
+                       const int *pos, int seqs, int tokens, int max_pos, int heads, int kv_heads, int head_dim,
+                       int neox, float theta_base, float eps, KV *kcache, KV *vcache) {
+    const float theta_scale = powf(theta_base, -2.0f / (float)head_dim);
+    const int64_t warps = (int64_t)seqs * tokens * (heads + kv_heads);
+    const int grid = (int)((warps + 7) / 8);
+#define EF_ROPE(DD, NX)                                                                                          \
+    return launch_on(ctx, ef_rope_cache_kernel<DD, NX, KV>, grid, 256, 0, "rope_cache launch", q, k, v, wq, wk, pos, \
+                     seqs, tokens, max_pos, heads, kv_heads, theta_scale, eps, kcache, vcache)
+    if (head_dim == 64) {
+        if (neox) EF_ROPE(64, true);
+        EF_ROPE(64, false);
+    }
+    if (neox) EF_ROPE(128, true);
+    EF_ROPE(128, false);
+#undef EF_ROPE
+}
+
+template <typename KV>
+static int qk_norm_rope_cache(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
+                              const int *pos, int max_pos, int heads, int kv_heads, int head_dim, float theta_base,
+                              float eps, KV *kcache, KV *vcache) {
+    if (!ctx || !q || !k || !v || !wq || !wk || !pos || !kcache || !vcache || heads < 1 || kv_heads < 1)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "qk_norm_rope_cache: bad arguments") : EF_ERR_INVALID;
+    if (head_dim != 64) return set_err(ctx, EF_ERR_SHAPE, "qk_norm_rope_cache: head_dim %d (64 supported)", head_dim);
+    return rope_launch(ctx, q, k, v, wq, wk, pos, 1, 1, max_pos, heads, kv_heads, 64, 1, theta_base, eps, kcache,
+                       vcache);
+}
+
+template <typename KV>
+static int rope_cache(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
+                      const int *pos, int seqs, int tokens, int max_pos, int heads, int kv_heads, int head_dim,
+                      int rope_mode, float theta_base, float eps, KV *kcache, KV *vcache) {
+    if (!ctx || !q || !k || !v || !pos || !kcache || !vcache || heads < 1 || kv_heads < 1 || seqs < 1 ||
+        tokens < 1 || max_pos < 1 || (!wq) != (!wk))
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "rope_cache: bad arguments") : EF_ERR_INVALID;
+    if (head_dim != 64 && head_dim != 128)
+        return set_err(ctx, EF_ERR_SHAPE, "rope_cache: head_dim %d (64 or 128 supported)", head_dim);
+    if (rope_mode != EF_ROPE_NORM && rope_mode != EF_ROPE_NEOX)
+        return set_err(ctx, EF_ERR_INVALID, "rope_cache: unknown RoPE mode %d", rope_mode);
+    if ((int64_t)seqs * tokens > 65535) return set_err(ctx, EF_ERR_RANGE, "rope_cache: more than 65535 rows");
+    return rope_launch(ctx, q, k, v, wq, wk, pos, seqs, tokens, max_pos, heads, kv_heads, head_dim,
+                       rope_mode == EF_ROPE_NEOX, theta_base, eps, kcache, vcache);
+}
+
+template <typename KV>
+static int attention_launch(ef_ctx *ctx, const float *q, const KV *kcache, const KV *vcache,
+                            const float *head_gate, const int *pos, int seqs, int tokens, int max_pos, int window,
+                            int heads, int kv_heads, int head_dim, float *out) {
+    const int span = window > 0 && window < max_pos ? window : max_pos;
+    const int G = heads / kv_heads;
+    if (tokens == 1 && (G == 1 || G == 2 || G == 4 || G == 8)) {
+        // one new token per sequence: the keys split over CTAs, then merged
+        const int nsplit = (span + AK - 1) / AK;
+        const int64_t rows = seqs;
+        const size_t bytes = (size_t)rows * heads * nsplit * (head_dim + 2) * sizeof(float);
+        if (int rc = ensure_scratch(ctx, 2, bytes)) return rc;
+        float *part = (float *)ctx->scratch[2];
+        const dim3 pg(nsplit, kv_heads, (unsigned)rows);
+#define EF_PART(DD, GG)                                                                                          \
+    rc = part_launch<DD, GG, KV>(ctx, pg, q, kcache, vcache, pos, tokens, max_pos, window, heads, kv_heads, part)
+        int rc;
+        if (head_dim == 64) {
+            switch (G) {
+            case 1: EF_PART(64, 1); break;
+            case 2: EF_PART(64, 2); break;
+            case 4: EF_PART(64, 4); break;
+            default: EF_PART(64, 8); break;
+            }
+        } else {
+            switch (G) {
+            case 1: EF_PART(128, 1); break;
+            case 2: EF_PART(128, 2); break;
+            case 4: EF_PART(128, 4); break;
+            default: EF_PART(128, 8); break;
+            }
+        }
+#undef EF_PART
+        if (rc) return rc;
+        const dim3 cg(heads, (unsigned)rows);
+        const size_t cs = (size_t)nsplit * sizeof(float);
+        if (cs > 48 * 1024) return set_err(ctx, EF_ERR_RANGE, "attention: %d key ranges", nsplit);
+        if (head_dim == 64)
+            return launch_on(ctx, ef_attn_combine_kernel<64>, cg, CT, cs, "attention combine launch",
+                             (const float *)part, head_gate, heads, nsplit, out);
+        return launch_on(ctx, ef_attn_combine_kernel<128>, cg, CT, cs, "attention combine launch", (const float *)part,
+                         head_gate, heads, nsplit, out);
+    }
+    if (G == 1 || G == 2 || G == 4 || G == 8) {
+        // several new tokens per sequence: key tiles shared by a block of queries
+        switch (head_dim * 16 + G) {
+        case 64 * 16 + 1: return prompt_attn_launch<64, 1, KV>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 64 * 16 + 2: return prompt_attn_launch<64, 2, KV>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 64 * 16 + 4: return prompt_attn_launch<64, 4, KV>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 64 * 16 + 8: return prompt_attn_launch<64, 8, KV>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 128 * 16 + 1: return prompt_attn_launch<128, 1, KV>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 128 * 16 + 2: return prompt_attn_launch<128, 2, KV>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        case 128 * 16 + 4: return prompt_attn_launch<128, 4, KV>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        default: return prompt_attn_launch<128, 8, KV>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+        }
+    }
+    // other head groupings: a CTA per (head, query row), scores of all keys in shared memory
+    const size_t smem = (size_t)span * 4;
+    if (smem > 200 * 1024) return set_err(ctx, EF_ERR_RANGE, "attention: %d keys exceed shared memory", span);
+    static std::atomic<unsigned long long> configured[2] = {{0}, {0}};
+    const int di = head_dim == 64 ? 0 : 1;
+    if (ctx->device < 64 && !(configured[di].load() & (1ull << ctx->device))) {
+        cudaError_t e = di == 0 ? cudaFuncSetAttribute(ef_attention_kernel<64, KV>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                       200 * 1024)
+                                : cudaFuncSetAttribute(ef_attention_kernel<128, KV>,
+                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        if (int rc = check_cuda(ctx, e, "attention smem attribute")) return rc;
+        configured[di].fetch_or(1ull << ctx->device);
+    }
+    const dim3 grid(heads, seqs * tokens);
+    if (di == 0)
+        return launch_on(ctx, ef_attention_kernel<64, KV>, grid, 256, smem, "attention launch", q, kcache, vcache,
+                         head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
+    return launch_on(ctx, ef_attention_kernel<128, KV>, grid, 256, smem, "attention launch", q, kcache, vcache, head_gate,
+                     pos, tokens, max_pos, window, heads, kv_heads, out);
+}
+
+template <typename KV>
+static int attn_decode(ef_ctx *ctx, const float *q, const KV *kcache, const KV *vcache, const float *head_gate,
+                       const int *pos, int max_pos, int window, int heads, int kv_heads, int head_dim, float *out) {
+    if (!ctx || !q || !kcache || !vcache || !pos || !out || heads < 1 || kv_heads < 1 || heads % kv_heads)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "attn_decode: bad arguments") : EF_ERR_INVALID;
+    if (head_dim != 64) return set_err(ctx, EF_ERR_SHAPE, "attn_decode: head_dim %d (64 supported)", head_dim);
+    return attention_launch(ctx, q, kcache, vcache, head_gate, pos, 1, 1, max_pos, window, heads, kv_heads, 64, out);
+}
+
+template <typename KV>
+static int attention(ef_ctx *ctx, const float *q, const KV *kcache, const KV *vcache, const float *head_gate,
+                     const int *pos, int seqs, int tokens, int max_pos, int window, int heads, int kv_heads,
+                     int head_dim, float *out) {
+    if (!ctx || !q || !kcache || !vcache || !pos || !out || heads < 1 || kv_heads < 1 || heads % kv_heads ||
+        seqs < 1 || tokens < 1 || max_pos < 1 || window < 0)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "attention: bad arguments") : EF_ERR_INVALID;
+    if (head_dim != 64 && head_dim != 128)
+        return set_err(ctx, EF_ERR_SHAPE, "attention: head_dim %d (64 or 128 supported)", head_dim);
+    if ((int64_t)seqs * tokens > 65535) return set_err(ctx, EF_ERR_RANGE, "attention: more than 65535 rows");
+    return attention_launch(ctx, q, kcache, vcache, head_gate, pos, seqs, tokens, max_pos, window, heads, kv_heads,
+                            head_dim, out);
 }
 
 }  // namespace ef
@@ -981,144 +1147,58 @@ int ef_shortconv(ef_ctx *ctx, const float *bcx, const float *conv_w, float *stat
                      state, tokens, channels, y);
 }
 
-static int rope_launch(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
-                       const int *pos, int seqs, int tokens, int max_pos, int heads, int kv_heads, int head_dim,
-                       int neox, float theta_base, float eps, float *kcache, float *vcache) {
-    const float theta_scale = powf(theta_base, -2.0f / (float)head_dim);
-    const int64_t warps = (int64_t)seqs * tokens * (heads + kv_heads);
-    const int grid = (int)((warps + 7) / 8);
-#define EF_ROPE(DD, NX)                                                                                     \
-    return launch_on(ctx, ef_rope_cache_kernel<DD, NX>, grid, 256, 0, "rope_cache launch", q, k, v, wq, wk, pos, \
-                     seqs, tokens, max_pos, heads, kv_heads, theta_scale, eps, kcache, vcache)
-    if (head_dim == 64) {
-        if (neox) EF_ROPE(64, true);
-        EF_ROPE(64, false);
-    }
-    if (neox) EF_ROPE(128, true);
-    EF_ROPE(128, false);
-#undef EF_ROPE
-}
-
 int ef_qk_norm_rope_cache(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
                           const int *pos, int max_pos, int heads, int kv_heads, int head_dim, float theta_base,
                           float eps, float *kcache, float *vcache) {
-    if (!ctx || !q || !k || !v || !wq || !wk || !pos || !kcache || !vcache || heads < 1 || kv_heads < 1)
-        return ctx ? set_err(ctx, EF_ERR_INVALID, "qk_norm_rope_cache: bad arguments") : EF_ERR_INVALID;
-    if (head_dim != 64) return set_err(ctx, EF_ERR_SHAPE, "qk_norm_rope_cache: head_dim %d (64 supported)", head_dim);
-    return rope_launch(ctx, q, k, v, wq, wk, pos, 1, 1, max_pos, heads, kv_heads, 64, 1, theta_base, eps, kcache,
-                       vcache);
+    return qk_norm_rope_cache(ctx, q, k, v, wq, wk, pos, max_pos, heads, kv_heads, head_dim, theta_base, eps, kcache,
+                              vcache);
+}
+
+int ef_qk_norm_rope_cache_f16(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
+                              const int *pos, int max_pos, int heads, int kv_heads, int head_dim, float theta_base,
+                              float eps, uint16_t *kcache, uint16_t *vcache) {
+    return qk_norm_rope_cache(ctx, q, k, v, wq, wk, pos, max_pos, heads, kv_heads, head_dim, theta_base, eps,
+                              reinterpret_cast<__half *>(kcache), reinterpret_cast<__half *>(vcache));
 }
 
 int ef_rope_cache(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
                   const int *pos, int seqs, int tokens, int max_pos, int heads, int kv_heads, int head_dim,
                   int rope_mode, float theta_base, float eps, float *kcache, float *vcache) {
-    if (!ctx || !q || !k || !v || !pos || !kcache || !vcache || heads < 1 || kv_heads < 1 || seqs < 1 ||
-        tokens < 1 || max_pos < 1 || (!wq) != (!wk))
-        return ctx ? set_err(ctx, EF_ERR_INVALID, "rope_cache: bad arguments") : EF_ERR_INVALID;
-    if (head_dim != 64 && head_dim != 128)
-        return set_err(ctx, EF_ERR_SHAPE, "rope_cache: head_dim %d (64 or 128 supported)", head_dim);
-    if (rope_mode != EF_ROPE_NORM && rope_mode != EF_ROPE_NEOX)
-        return set_err(ctx, EF_ERR_INVALID, "rope_cache: unknown RoPE mode %d", rope_mode);
-    if ((int64_t)seqs * tokens > 65535) return set_err(ctx, EF_ERR_RANGE, "rope_cache: more than 65535 rows");
-    return rope_launch(ctx, q, k, v, wq, wk, pos, seqs, tokens, max_pos, heads, kv_heads, head_dim,
-                       rope_mode == EF_ROPE_NEOX, theta_base, eps, kcache, vcache);
+    return rope_cache(ctx, q, k, v, wq, wk, pos, seqs, tokens, max_pos, heads, kv_heads, head_dim, rope_mode,
+                      theta_base, eps, kcache, vcache);
 }
 
-static int attention_launch(ef_ctx *ctx, const float *q, const float *kcache, const float *vcache,
-                            const float *head_gate, const int *pos, int seqs, int tokens, int max_pos, int window,
-                            int heads, int kv_heads, int head_dim, float *out) {
-    const int span = window > 0 && window < max_pos ? window : max_pos;
-    const int G = heads / kv_heads;
-    if (tokens == 1 && (G == 1 || G == 2 || G == 4 || G == 8)) {
-        // one new token per sequence: the keys split over CTAs, then merged
-        const int nsplit = (span + AK - 1) / AK;
-        const int64_t rows = seqs;
-        const size_t bytes = (size_t)rows * heads * nsplit * (head_dim + 2) * sizeof(float);
-        if (int rc = ensure_scratch(ctx, 2, bytes)) return rc;
-        float *part = (float *)ctx->scratch[2];
-        const dim3 pg(nsplit, kv_heads, (unsigned)rows);
-#define EF_PART(DD, GG)                                                                                          \
-    rc = part_launch<DD, GG>(ctx, pg, q, kcache, vcache, pos, tokens, max_pos, window, heads, kv_heads, part)
-        int rc;
-        if (head_dim == 64) {
-            switch (G) {
-            case 1: EF_PART(64, 1); break;
-            case 2: EF_PART(64, 2); break;
-            case 4: EF_PART(64, 4); break;
-            default: EF_PART(64, 8); break;
-            }
-        } else {
-            switch (G) {
-            case 1: EF_PART(128, 1); break;
-            case 2: EF_PART(128, 2); break;
-            case 4: EF_PART(128, 4); break;
-            default: EF_PART(128, 8); break;
-            }
-        }
-#undef EF_PART
-        if (rc) return rc;
-        const dim3 cg(heads, (unsigned)rows);
-        const size_t cs = (size_t)nsplit * sizeof(float);
-        if (cs > 48 * 1024) return set_err(ctx, EF_ERR_RANGE, "attention: %d key ranges", nsplit);
-        if (head_dim == 64)
-            return launch_on(ctx, ef_attn_combine_kernel<64>, cg, CT, cs, "attention combine launch",
-                             (const float *)part, head_gate, heads, nsplit, out);
-        return launch_on(ctx, ef_attn_combine_kernel<128>, cg, CT, cs, "attention combine launch", (const float *)part,
-                         head_gate, heads, nsplit, out);
-    }
-    if (G == 1 || G == 2 || G == 4 || G == 8) {
-        // several new tokens per sequence: key tiles shared by a block of queries
-        switch (head_dim * 16 + G) {
-        case 64 * 16 + 1: return prompt_attn_launch<64, 1>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
-        case 64 * 16 + 2: return prompt_attn_launch<64, 2>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
-        case 64 * 16 + 4: return prompt_attn_launch<64, 4>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
-        case 64 * 16 + 8: return prompt_attn_launch<64, 8>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
-        case 128 * 16 + 1: return prompt_attn_launch<128, 1>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
-        case 128 * 16 + 2: return prompt_attn_launch<128, 2>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
-        case 128 * 16 + 4: return prompt_attn_launch<128, 4>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
-        default: return prompt_attn_launch<128, 8>(ctx, seqs, q, kcache, vcache, head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
-        }
-    }
-    // other head groupings: a CTA per (head, query row), scores of all keys in shared memory
-    const size_t smem = (size_t)span * 4;
-    if (smem > 200 * 1024) return set_err(ctx, EF_ERR_RANGE, "attention: %d keys exceed shared memory", span);
-    static std::atomic<unsigned long long> configured[2] = {{0}, {0}};
-    const int di = head_dim == 64 ? 0 : 1;
-    if (ctx->device < 64 && !(configured[di].load() & (1ull << ctx->device))) {
-        cudaError_t e = di == 0 ? cudaFuncSetAttribute(ef_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                       200 * 1024)
-                                : cudaFuncSetAttribute(ef_attention_kernel<128>,
-                                                       cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
-        if (int rc = check_cuda(ctx, e, "attention smem attribute")) return rc;
-        configured[di].fetch_or(1ull << ctx->device);
-    }
-    const dim3 grid(heads, seqs * tokens);
-    if (di == 0)
-        return launch_on(ctx, ef_attention_kernel<64>, grid, 256, smem, "attention launch", q, kcache, vcache,
-                         head_gate, pos, tokens, max_pos, window, heads, kv_heads, out);
-    return launch_on(ctx, ef_attention_kernel<128>, grid, 256, smem, "attention launch", q, kcache, vcache, head_gate,
-                     pos, tokens, max_pos, window, heads, kv_heads, out);
+int ef_rope_cache_f16(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
+                      const int *pos, int seqs, int tokens, int max_pos, int heads, int kv_heads, int head_dim,
+                      int rope_mode, float theta_base, float eps, uint16_t *kcache, uint16_t *vcache) {
+    return rope_cache(ctx, q, k, v, wq, wk, pos, seqs, tokens, max_pos, heads, kv_heads, head_dim, rope_mode,
+                      theta_base, eps, reinterpret_cast<__half *>(kcache), reinterpret_cast<__half *>(vcache));
 }
 
 int ef_attn_decode(ef_ctx *ctx, const float *q, const float *kcache, const float *vcache, const float *head_gate,
                    const int *pos, int max_pos, int window, int heads, int kv_heads, int head_dim, float *out) {
-    if (!ctx || !q || !kcache || !vcache || !pos || !out || heads < 1 || kv_heads < 1 || heads % kv_heads)
-        return ctx ? set_err(ctx, EF_ERR_INVALID, "attn_decode: bad arguments") : EF_ERR_INVALID;
-    if (head_dim != 64) return set_err(ctx, EF_ERR_SHAPE, "attn_decode: head_dim %d (64 supported)", head_dim);
-    return attention_launch(ctx, q, kcache, vcache, head_gate, pos, 1, 1, max_pos, window, heads, kv_heads, 64, out);
+    return attn_decode(ctx, q, kcache, vcache, head_gate, pos, max_pos, window, heads, kv_heads, head_dim, out);
+}
+
+int ef_attn_decode_f16(ef_ctx *ctx, const float *q, const uint16_t *kcache, const uint16_t *vcache,
+                       const float *head_gate, const int *pos, int max_pos, int window, int heads, int kv_heads,
+                       int head_dim, float *out) {
+    return attn_decode(ctx, q, reinterpret_cast<const __half *>(kcache), reinterpret_cast<const __half *>(vcache),
+                       head_gate, pos, max_pos, window, heads, kv_heads, head_dim, out);
 }
 
 int ef_attention(ef_ctx *ctx, const float *q, const float *kcache, const float *vcache, const float *head_gate,
                  const int *pos, int seqs, int tokens, int max_pos, int window, int heads, int kv_heads, int head_dim,
                  float *out) {
-    if (!ctx || !q || !kcache || !vcache || !pos || !out || heads < 1 || kv_heads < 1 || heads % kv_heads ||
-        seqs < 1 || tokens < 1 || max_pos < 1 || window < 0)
-        return ctx ? set_err(ctx, EF_ERR_INVALID, "attention: bad arguments") : EF_ERR_INVALID;
-    if (head_dim != 64 && head_dim != 128)
-        return set_err(ctx, EF_ERR_SHAPE, "attention: head_dim %d (64 or 128 supported)", head_dim);
-    if ((int64_t)seqs * tokens > 65535) return set_err(ctx, EF_ERR_RANGE, "attention: more than 65535 rows");
-    return attention_launch(ctx, q, kcache, vcache, head_gate, pos, seqs, tokens, max_pos, window, heads, kv_heads,
-                            head_dim, out);
+    return attention(ctx, q, kcache, vcache, head_gate, pos, seqs, tokens, max_pos, window, heads, kv_heads, head_dim,
+                     out);
+}
+
+int ef_attention_f16(ef_ctx *ctx, const float *q, const uint16_t *kcache, const uint16_t *vcache,
+                     const float *head_gate, const int *pos, int seqs, int tokens, int max_pos, int window, int heads,
+                     int kv_heads, int head_dim, float *out) {
+    return attention(ctx, q, reinterpret_cast<const __half *>(kcache), reinterpret_cast<const __half *>(vcache),
+                     head_gate, pos, seqs, tokens, max_pos, window, heads, kv_heads, head_dim, out);
 }
 
 int ef_topk(ef_ctx *ctx, const float *logits, int rows, int n, int m, int *ids, float *vals, int *flags) {

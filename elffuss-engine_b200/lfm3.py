@@ -58,6 +58,7 @@ class LFM3Config:
     window: int = 4096              # sliding window of every other attention layer (the first, third, ...)
     eps: float = 1e-5
     max_pos: int = 4096 + 1024      # KV-cache capacity
+    kv_f16: bool = False            # f16 KV caches (the reference's kvF16 option), f32 by default
 
     def windows(self) -> dict:
         """window per attention layer (0 = global): alternating, starting with a sliding one."""
@@ -228,8 +229,14 @@ class LFM3Decoder:
         self.pair = torch.zeros(2, dtype=torch.int32, device=dev)
         self.pairs = torch.zeros(2 * world, dtype=torch.int32, device=dev)
         self.state = {l: z(cfg.conv_k - 1, self.Ec) for l in range(cfg.layers) if l not in cfg.attn_layers}
-        self.kc = {l: z(cfg.max_pos, KV, D) for l in cfg.attn_layers}
-        self.vc = {l: z(cfg.max_pos, KV, D) for l in cfg.attn_layers}
+        kvt = torch.float16 if cfg.kv_f16 else torch.float32
+        self.kc = {l: torch.zeros(cfg.max_pos, KV, D, dtype=kvt, device=dev) for l in cfg.attn_layers}
+        self.vc = {l: torch.zeros(cfg.max_pos, KV, D, dtype=kvt, device=dev) for l in cfg.attn_layers}
+        sfx = "_f16" if cfg.kv_f16 else ""
+        self._qk_rope = getattr(self.L, "ef_qk_norm_rope_cache" + sfx)
+        self._attn_dec = getattr(self.L, "ef_attn_decode" + sfx)
+        self._rope = getattr(self.L, "ef_rope_cache" + sfx)
+        self._attn = getattr(self.L, "ef_attention" + sfx)
         self.tok = torch.zeros(1, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(1, dtype=torch.int32, device=dev)
         self.out_tokens = torch.full((cfg.max_pos,), -1, dtype=torch.int32, device=dev)
@@ -296,10 +303,10 @@ class LFM3Decoder:
                 ys = (ctypes.c_void_p * 4)(self.q.data_ptr(), self.k.data_ptr(), self.v.data_ptr(), self.g.data_ptr())
                 check(L.ef_gemv_sections(h, ctypes.cast(ws, ctypes.POINTER(ctypes.c_void_p)), 4, _p(self.nrm), 1,
                                          ctypes.cast(ys, ctypes.POINTER(ctypes.c_void_p))), h)
-                check(L.ef_qk_norm_rope_cache(h, _p(self.q), _p(self.k), _p(self.v), _p(f[p + "attn_q_norm"]),
+                check(self._qk_rope(h, _p(self.q), _p(self.k), _p(self.v), _p(f[p + "attn_q_norm"]),
                                               _p(f[p + "attn_k_norm"]), _p(self.pos), cfg.max_pos, H, KV, D,
                                               ctypes.c_float(cfg.rope_theta), eps, _p(self.kc[l]), _p(self.vc[l])), h)
-                check(L.ef_attn_decode(h, _p(self.q), _p(self.kc[l]), _p(self.vc[l]), _p(self.g), _p(self.pos),
+                check(self._attn_dec(h, _p(self.q), _p(self.kc[l]), _p(self.vc[l]), _p(self.g), _p(self.pos),
                                        cfg.max_pos, self.windows[l], H, KV, D, _p(self.att)), h)
                 out_w, out_x = W[p + "attn_output"], self.att
             else:
@@ -391,10 +398,10 @@ class LFM3Decoder:
                 gemm(p + "attn_k", nrm, k)
                 gemm(p + "attn_v", nrm, v)
                 gemm(p + "attn_gate", nrm, g)
-                check(L.ef_rope_cache(h, _p(q), _p(k), _p(v), _p(f[p + "attn_q_norm"]), _p(f[p + "attn_k_norm"]),
+                check(self._rope(h, _p(q), _p(k), _p(v), _p(f[p + "attn_q_norm"]), _p(f[p + "attn_k_norm"]),
                                       _p(self.pos), 1, T, cfg.max_pos, H, KV, D, 2, ctypes.c_float(cfg.rope_theta),
                                       eps, _p(self.kc[l]), _p(self.vc[l])), h)
-                check(L.ef_attention(h, _p(q), _p(self.kc[l]), _p(self.vc[l]), _p(g), _p(self.pos), 1, T,
+                check(self._attn(h, _p(q), _p(self.kc[l]), _p(self.vc[l]), _p(g), _p(self.pos), 1, T,
                                      cfg.max_pos, self.windows[l], H, KV, D, _p(att)), h)
                 gemm(p + "attn_output", att, o)
             else:

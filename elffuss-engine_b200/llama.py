@@ -52,6 +52,7 @@ class LlamaConfig:
     rope_theta: float = 5e5
     eps: float = 1e-5
     max_pos: int = 4096 + 256     # KV-cache capacity per sequence
+    kv_f16: bool = False          # f16 KV caches (the reference's kvF16 option), f32 by default
 
     def weight_type(self, name: str) -> str:
         short = name.split(".", 2)[-1] if name.startswith("blk.") else name
@@ -191,8 +192,12 @@ class LlamaDecoder:
         self.logits = z(B, self.Vl)
         self.pairs1 = torch.zeros(B, 2, dtype=torch.int32, device=dev)
         self.pairs = torch.zeros(world * B * 2, dtype=torch.int32, device=dev)
-        self.kc = [z(B, cfg.max_pos, KVl, D) for _ in range(cfg.layers)]
-        self.vc = [z(B, cfg.max_pos, KVl, D) for _ in range(cfg.layers)]
+        kvt = torch.float16 if cfg.kv_f16 else torch.float32
+        self.kc = [torch.zeros(B, cfg.max_pos, KVl, D, dtype=kvt, device=dev) for _ in range(cfg.layers)]
+        self.vc = [torch.zeros(B, cfg.max_pos, KVl, D, dtype=kvt, device=dev) for _ in range(cfg.layers)]
+        sfx = "_f16" if cfg.kv_f16 else ""
+        self._rope = getattr(self.L, "ef_rope_cache" + sfx)
+        self._attn = getattr(self.L, "ef_attention" + sfx)
         self.tok = torch.zeros(B, dtype=torch.int32, device=dev)
         self.pos = torch.zeros(B, dtype=torch.int32, device=dev)
         self.out_tokens = torch.full((B, out_cap), -1, dtype=torch.int32, device=dev)
@@ -261,10 +266,10 @@ class LlamaDecoder:
             check(L.ef_gemv_sections(h, _pp([W[p + "attn_q"].h.value, W[p + "attn_k"].h.value]), 2, _p(self.nrm),
                                      B, _pp([self.q, self.k])), h)
             check(L.ef_gemv(h, W[p + "attn_v"].h, _p(self.nrm), B, _p(self.v)), h)
-            check(L.ef_rope_cache(h, _p(self.q), _p(self.k), _p(self.v), None, None, _p(self.pos), B, 1,
+            check(self._rope(h, _p(self.q), _p(self.k), _p(self.v), None, None, _p(self.pos), B, 1,
                                   cfg.max_pos, self.Hl, self.KVl, D, ROPE_NORM, ctypes.c_float(cfg.rope_theta), eps,
                                   _p(self.kc[l]), _p(self.vc[l])), h)
-            check(L.ef_attention(h, _p(self.q), _p(self.kc[l]), _p(self.vc[l]), None, _p(self.pos), B, 1,
+            check(self._attn(h, _p(self.q), _p(self.kc[l]), _p(self.vc[l]), None, _p(self.pos), B, 1,
                                  cfg.max_pos, 0, self.Hl, self.KVl, D, _p(self.att)), h)
             self._rowpar(h, W[p + "attn_output"], self.att, self.o, f[p + "ffn_norm"])
             check(L.ef_gemv_swiglu(h, W[p + "ffn_gate"].h, W[p + "ffn_up"].h, _p(self.nrm), B, _p(self.sw)), h)
@@ -312,10 +317,10 @@ class LlamaDecoder:
             gemm(p + "attn_q", nrm, q)
             gemm(p + "attn_k", nrm, k)
             gemm(p + "attn_v", nrm, v)
-            check(L.ef_rope_cache(h, _p(q), _p(k), _p(v), None, None, _p(pos0), 1, T, cfg.max_pos, self.Hl,
+            check(self._rope(h, _p(q), _p(k), _p(v), None, None, _p(pos0), 1, T, cfg.max_pos, self.Hl,
                                   self.KVl, D, ROPE_NORM, ctypes.c_float(cfg.rope_theta), eps, _p(self.kc[l]),
                                   _p(self.vc[l])), h)
-            check(L.ef_attention(h, _p(q), _p(self.kc[l]), _p(self.vc[l]), None, _p(pos0), 1, T, cfg.max_pos, 0,
+            check(self._attn(h, _p(q), _p(self.kc[l]), _p(self.vc[l]), None, _p(pos0), 1, T, cfg.max_pos, 0,
                                  self.Hl, self.KVl, D, _p(att)), h)
             gemm(p + "attn_output", att, o)
             self._reduce(o)

@@ -287,6 +287,17 @@ EF_API int ef_attn_decode(ef_ctx *ctx, const float *q, const float *kcache, cons
                           const float *head_gate, const int *pos, int max_pos, int window, int heads, int kv_heads,
                           int head_dim, float *out);
 
+/* The same three with f16 caches (the reference's kvF16 option,
+ * js/kernels.attn.wgsl.js:51-55, js/model.js:906-946): k (after its norm and
+ * RoPE) and v are rounded to f16, to nearest even, when stored; q, the scores
+ * and every sum stay f32. Caches are f16 bit patterns, same layout. */
+EF_API int ef_qk_norm_rope_cache_f16(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq,
+                                     const float *wk, const int *pos, int max_pos, int heads, int kv_heads,
+                                     int head_dim, float theta_base, float eps, uint16_t *kcache, uint16_t *vcache);
+EF_API int ef_attn_decode_f16(ef_ctx *ctx, const float *q, const uint16_t *kcache, const uint16_t *vcache,
+                              const float *head_gate, const int *pos, int max_pos, int window, int heads,
+                              int kv_heads, int head_dim, float *out);
+
 /* Greedy sampling (js/sample.js:95-99): *token = argmax of n logits (strict
  * '>', the lowest index wins ties); *pos += 1; when out_tokens is not NULL the
  * token is also stored at out_tokens[new *pos - out_base] if that index is in
@@ -340,6 +351,15 @@ EF_API int ef_rope_cache(ef_ctx *ctx, float *q, const float *k, const float *v, 
 EF_API int ef_attention(ef_ctx *ctx, const float *q, const float *kcache, const float *vcache,
                         const float *head_gate, const int *pos, int seqs, int tokens, int max_pos, int window,
                         int heads, int kv_heads, int head_dim, float *out);
+
+/* ef_rope_cache / ef_attention with f16 caches (f16 bit patterns, same
+ * layout; rounding as ef_qk_norm_rope_cache_f16). */
+EF_API int ef_rope_cache_f16(ef_ctx *ctx, float *q, const float *k, const float *v, const float *wq, const float *wk,
+                             const int *pos, int seqs, int tokens, int max_pos, int heads, int kv_heads, int head_dim,
+                             int rope_mode, float theta_base, float eps, uint16_t *kcache, uint16_t *vcache);
+EF_API int ef_attention_f16(ef_ctx *ctx, const float *q, const uint16_t *kcache, const uint16_t *vcache,
+                            const float *head_gate, const int *pos, int seqs, int tokens, int max_pos, int window,
+                            int heads, int kv_heads, int head_dim, float *out);
 
 /* Sampling candidates on the device (kernels.topk.wgsl.js, topk.js): for each
  * of `rows` rows of n logits, the m first in the sampler's order -- larger

@@ -102,6 +102,10 @@ class F32Decoder:
 
     def __init__(self, arch: str, cfg, weights: dict, device="cpu", dtype=torch.float32):
         self.arch, self.cfg, self.dev, self.dt = arch, cfg, torch.device(device), dtype
+        # f16 KV caches (cfg.kv_f16, the reference's kvF16: js/model.js:906-946,
+        # kernels.attn.wgsl.js:51-55): k after its norm and RoPE and v are
+        # rounded f32 -> f16 (to nearest even) when stored; all else unchanged
+        self.kv16 = bool(getattr(cfg, "kv_f16", False))
         self.w, self.f = {}, {}
         for name, val in weights.items():
             if isinstance(val, tuple):
@@ -164,6 +168,8 @@ class F32Decoder:
                         q = _rmsnorm(q, f[p + "attn_q_norm"], c.eps)
                         k = _rmsnorm(k, f[p + "attn_k_norm"], c.eps)
                     q, k = _rope(q, pos, c.rope_theta, lfm), _rope(k, pos, c.rope_theta, lfm)
+                    if self.kv16:
+                        k, v = k.float().half().to(self.dt), v.float().half().to(self.dt)
                     self.kc[l].append(k)
                     self.vc[l].append(v)
                     K = torch.cat(self.kc[l], dim=1)                             # [S][n][KV][D]

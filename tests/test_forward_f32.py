@@ -73,3 +73,25 @@ def test_f32_tokens_equal_f64_tokens_small_models():
                 lg = dec.forward(torch.tensor([[out[-1]]]))
             toks[dt] = out
         assert toks[torch.float32] == toks[torch.float64]
+
+
+def test_f16_kv_cache_rounds_every_stored_entry():
+    """cfg.kv_f16: the f32 forward keeps k and v in its caches as f16 values
+    (round to nearest even from the f32 values); the logits stay close to the
+    f32-cache forward's."""
+    import dataclasses
+    for arch, cfg in (("lfm3", LFM3Config(**LSMALL)), ("llama", LlamaConfig(**MSMALL))):
+        w = _np(lfm3_weights(cfg, seed=7) if arch == "lfm3" else llama_weights(cfg, seed=7))
+        ids = torch.tensor(np.random.default_rng(5).integers(0, cfg.vocab, 6)[None, :])
+        out = {}
+        for kv16 in (False, True):
+            dec = F32Decoder(arch, dataclasses.replace(cfg, kv_f16=kv16), w)
+            dec.reset(1)
+            out[kv16] = dec.forward(ids)
+            if kv16:
+                for d in (dec.kc, dec.vc):
+                    for ts in d.values():
+                        t = torch.cat(ts, dim=1)
+                        assert torch.equal(t, t.half().float())
+        lo, lh = out[False][0].double(), out[True][0].double()
+        assert float((lo - lh).abs().max()) < 0.05 * float(lo.std())

@@ -6,7 +6,9 @@ reference GPU path's arithmetic: the f32 forward of oracle/forward_f32.py
     512-id prompt (one batched pass through the GEMM path), then 31 steps;
   * config 4: the 8B-shaped Llama decoder with the bench's weights and its
     4096-id context (4095 ids through the GEMM path, the last id as the first
-    step), 32 steps at batch 1 and at batch 16.
+    step), 32 steps at batch 1 and at batch 16;
+  * both again with f16 KV caches (LFM3, and the 8B at batch 16) against the
+    f32 forward that rounds its cache entries to f16 the same way.
 
 The reference forward is teacher-forced on the CUDA decoder's own tokens, so
 every step is compared on the same history: the CUDA token must be the f32
@@ -68,9 +70,10 @@ def _check(rows):
             assert r["gap"] <= 2 * r["err"], r
 
 
-def test_config3_lfm3_512_prompt_vs_f32_forward(ops, parity_report):
+@pytest.mark.parametrize("kv_f16", [False, True])
+def test_config3_lfm3_512_prompt_vs_f32_forward(ops, parity_report, kv_f16):
     from elffuss_engine_b200.lfm3 import LFM3Config, LFM3Decoder, synth_weights
-    cfg = LFM3Config()
+    cfg = LFM3Config(kv_f16=kv_f16)
     n = 32
     w = synth_weights(cfg, seed=0, device="cuda")
     prompt = torch.randint(0, cfg.vocab, (512,), generator=torch.Generator().manual_seed(0), dtype=torch.int32)
@@ -102,7 +105,8 @@ def test_config3_lfm3_512_prompt_vs_f32_forward(ops, parity_report):
     del orc
     torch.cuda.empty_cache()
     rows = _compare([[int(t)] for t in toks], gpu_logits, orc_logits)
-    parity_report["decode config3 lfm3 512-id prompt vs f32 forward"] = _summary(rows, 1)
+    kv = ", f16 KV cache" if kv_f16 else ""
+    parity_report[f"decode config3 lfm3 512-id prompt vs f32 forward{kv}"] = _summary(rows, 1)
     _check(rows)
 
 
@@ -118,10 +122,12 @@ def llama8b():
     torch.cuda.empty_cache()
 
 
-@pytest.mark.parametrize("B", [1, 16])
-def test_config4_llama8b_vs_f32_forward(ops, parity_report, llama8b, B):
+@pytest.mark.parametrize("B,kv_f16", [(1, False), (16, False), (16, True)])
+def test_config4_llama8b_vs_f32_forward(ops, parity_report, llama8b, B, kv_f16):
+    import dataclasses
     from elffuss_engine_b200.llama import LlamaDecoder
     cfg, w, ids = llama8b
+    cfg = dataclasses.replace(cfg, kv_f16=kv_f16)
     n = 32
     prompt = ids[:4096]
     lasts = [int(prompt[-1])] + [int(t) for t in ids[4096:4096 + B - 1]]
@@ -146,5 +152,6 @@ def test_config4_llama8b_vs_f32_forward(ops, parity_report, llama8b, B):
     del orc
     torch.cuda.empty_cache()
     rows = _compare(toks, gpu_logits, orc_logits)
-    parity_report[f"decode config4 llama8b batch {B} vs f32 forward"] = _summary(rows, B)
+    kv = ", f16 KV cache" if kv_f16 else ""
+    parity_report[f"decode config4 llama8b batch {B} vs f32 forward{kv}"] = _summary(rows, B)
     _check(rows)

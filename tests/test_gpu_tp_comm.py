@@ -91,8 +91,9 @@ def _rank_main(rank, world, init, q, mode):
         inputs = [x.clone() for x in xs]
         for x in xs:
             comm.all_reduce(x)
-        pair = torch.tensor([rank * 10 + 1, rank * 10 + 2], dtype=torch.int32, device="cuda")
-        gathered = torch.zeros(2 * world, dtype=torch.int32, device="cuda")
+        # any 4-byte word travels unchanged (-1 is all ones, 0x7fc00001 a NaN payload)
+        pair = torch.tensor([rank * 10 + 1, -1 - rank, 0x7fc00001], dtype=torch.int32, device="cuda")
+        gathered = torch.zeros(3 * world, dtype=torch.int32, device="cuda")
         comm.all_gather(gathered, pair)
         # the same calls replayed from a graph
         gx = torch.zeros(2048, device="cuda")
@@ -131,7 +132,7 @@ def test_allreduce_allgather_exact_and_graph_replay():
         for j in range(3):
             want = got[0][1][j] + got[1][1][j]            # rank order: rank 0 + rank 1
             assert torch.equal(outs[j], want)
-        assert gathered == [1, 2, 11, 12]
+        assert gathered == [1, -1, 0x7fc00001, 11, -2, 0x7fc00001]
         for k in range(3):
             # two all-reduces of (1 + k) and (2 + k): (3 + 2k) * 2
             assert replays[k] == [float((3 + 2 * k) * 2)] * 4
