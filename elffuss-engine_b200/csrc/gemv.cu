@@ -1037,13 +1037,13 @@ template <bool SWIGLU> __device__ __forceinline__ float out_value(float gate, fl
 template <int NT, int KH> struct CombineBytes {
     static constexpr int v = KH == 2 ? GV_WARPS * 32 * NT * 4 * 4 : 0;
 };
-// cluster reduction: [rowgroup slot][matrix][token][16 rows] f32
-template <bool SW> struct ReduceBytes { static constexpr int v = GV_WARPS * (SW ? 2 : 1) * 16 * 16 * 4; };
+// cluster reduction: [rowgroup slot][k-slice][matrix][token][16 rows] f32
+template <bool SW> constexpr int reduce_bytes(int ks) { return GV_WARPS * ks * (SW ? 2 : 1) * 16 * 16 * 4; }
 // Shared memory: [activation data: the slice's chunks, or one or two phase
 // buffers][codebooks][pair-combine buffer][cluster-reduction buffer].
 template <int TYPE, int NT, bool SWIGLU, int KH>
-static size_t gemv_smem(int xs_bytes, bool cluster) {
-    return (size_t)xs_bytes + TableBytes<TYPE>::v + CombineBytes<NT, KH>::v + (cluster ? ReduceBytes<SWIGLU>::v : 0);
+static size_t gemv_smem(int xs_bytes, int ks) {
+    return (size_t)xs_bytes + TableBytes<TYPE>::v + CombineBytes<NT, KH>::v + (ks > 1 ? reduce_bytes<SWIGLU>(ks) : 0);
 }
 
 // TQ: Q4_K column layout (8 for the f16 types); NT: 8-token tiles; FUSED: the
@@ -1093,6 +1093,10 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const Ge
     while (m + 1 < a.nmat && rb >= a.rb_end[m]) m++;
     int64_t rg = (int64_t)(rb - (m ? a.rb_end[m - 1] : 0)) * W + wr;
     const bool active = rg < a.rowgroups[m];
+
+    // every rank of the cluster has started once this barrier phase completes
+    // (waited for before the first distributed shared memory store)
+    if (ks > 1) asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
 
     // ---- weight stream: this warp's chunks c0+kh, c0+kh+KH, ... < c1, each
     // tile loaded into registers one tile ahead of the math
@@ -1238,22 +1242,33 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const Ge
                 if (tok < M && r < rows) put(tok, r, out_value<SWIGLU>(acc[nt][i], acc2[nt][i]));
             });
     } else {
-        // ---- k-slices of this rowblock: one cluster, added in rank order ----
-        float *mine = red + wr * NMAT * 16 * 16;
+        // ---- k-slices of this rowblock (one cluster), added in rank order:
+        // rowgroup wr is finished by rank wr % ks; every slice stores its
+        // partial sums into slot [wr][its rank] of that rank's shared memory
+        // (distributed shared memory stores), one cluster barrier (release /
+        // acquire) makes them visible, and the owner reads only its own
+        // shared memory after it -- so no rank touches another's shared
+        // memory once the barrier is passed, and each may exit when done.
+        // (The barrier at the start of the kernel guarantees every rank has
+        // started before its shared memory is written.)
+        cg::cluster_group cluster = cg::this_cluster();
+        const int owner = wr % ks;
+        float *slot = red + ((size_t)wr * ks + ksi) * NMAT * 256;
+        float *dst = owner == ksi ? slot : cluster.map_shared_rank(slot, owner);
+        asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
         if (kh == 0 && active)
             for_owned<TQ, NT>(lane, [&](int nt, int i, int row, int tok) {
                 if (tok < M) {
-                    mine[tok * 16 + row] = acc[nt][i];
-                    if (SWIGLU) mine[256 + tok * 16 + row] = acc2[nt][i];
+                    dst[tok * 16 + row] = acc[nt][i];
+                    if (SWIGLU) dst[256 + tok * 16 + row] = acc2[nt][i];
                 }
             });
-        cg::cluster_group cluster = cg::this_cluster();
         cluster.sync();
-        if (kh == 0 && active && wr % ks == ksi) {   // rowgroup wr is finished by rank wr % ks
+        if (kh == 0 && active && owner == ksi) {
             for (int i = lane; i < 16 * M; i += 32) {
                 float s1 = 0.f, s2 = 0.f;
                 for (int rk = 0; rk < ks; rk++) {
-                    const float *src = cluster.map_shared_rank(mine, rk);
+                    const float *src = red + ((size_t)wr * ks + rk) * NMAT * 256;
                     s1 += src[i];
                     if (SWIGLU) s2 += src[256 + i];
                 }
@@ -1261,7 +1276,6 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const Ge
                 if (r < rows) put(i >> 4, r, out_value<SWIGLU>(s1, s2));
             }
         }
-        cluster.sync();              // keep this CTA's shared memory alive until all ranks have read it
     }
 }
 
@@ -1350,7 +1364,7 @@ static int launch_kernel(ef_ctx *ctx, GemvArgs &a, int64_t rowblocks, bool fused
     size_t smem = 0;
     for (int ks = (int)std::min<int64_t>(8, a.nchunks); ks >= 1; ks--) {
         p = gemv_plan(rowblocks, a.nchunks, a.xb, fused, ks);
-        smem = gemv_smem<TYPE, NT, SWIGLU, KH>(p.xs_bytes, ks > 1);
+        smem = gemv_smem<TYPE, NT, SWIGLU, KH>(p.xs_bytes, ks);
         if (ks == 1 || (smem <= 227 * 1024 && rowblocks <= max_active_clusters(ctx, (const void *)kern, threads, smem, ks)))
             break;
     }
