@@ -371,6 +371,87 @@ def bench_llama(ops, args, world, rank, barrier, max_over_ranks):
     return out
 
 
+TRACE_SHAPES = [("Q4_K", 14336, 4096, 1), ("Q4_K", 4096, 14336, 1), ("Q6_K", 14336, 4096, 1),
+                ("Q6_K", 4096, 14336, 1), ("Q8_0", 8192, 2048, 1), ("Q8_0", 2048, 2048, 1)]
+
+
+def run_gemv_trace(args):
+    """Launch phases of the GEMV kernel (needs `build.py --trace`): for each
+    shape, ROUNDS weight copies launched back to back in a CUDA graph (as
+    per_call), one replay traced. Per launch: the gap between the previous
+    launch's last CTA exit and this launch's wait release, and per CTA (SM
+    cycle counts, median over CTAs and launches 1..) the time before the wait
+    returns, the activation staging, the weight stream and the epilogue.
+    Prints one JSON line."""
+    import ctypes
+
+    import numpy as np
+    import torch
+
+    import elffuss_engine_b200._lib as _libmod
+    _libmod.LIB_PATH = os.path.join(os.path.dirname(_libmod.LIB_PATH), "libelffuss_cuda_trace.so")
+    from elffuss_engine_b200 import formats
+    from elffuss_engine_b200._lib import check, lib
+    from elffuss_engine_b200.ops import QuantOps, _ptr
+    L = lib()
+    L.ef_gemv_trace_set.argtypes = [ctypes.c_void_p, ctypes.c_uint]
+    L.ef_gemv_trace_set.restype = ctypes.c_int
+    ops = QuantOps(0)
+    cap = 1 << 14
+    buf = torch.zeros(cap * 12, dtype=torch.int64, device="cuda")
+    ghz = torch.cuda.get_device_properties(0).clock_rate / 1e6 if hasattr(torch.cuda.get_device_properties(0),
+                                                                           "clock_rate") else 1.965
+    out = []
+    for t, n, k, m in TRACE_SHAPES:
+        raw = formats.synth(t, n, k, seed=5)
+        ws = [ops.load_weight(t, raw, n, k) for _ in range(ROUNDS)]
+        x = torch.randn(m, k, device="cuda", generator=torch.Generator("cuda").manual_seed(1))
+        y = torch.empty(m, n, device="cuda")
+
+        def seq():
+            h = ops.ctx.bind()
+            for wc in ws:
+                check(L.ef_gemv(h, wc.h, _ptr(x), m, _ptr(y)), h)
+        cs = torch.cuda.Stream()
+        cs.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(cs):
+            seq()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=cs):
+            seq()
+        for _ in range(20):
+            g.replay()
+        buf.zero_()
+        torch.cuda.synchronize()
+        assert L.ef_gemv_trace_set(ctypes.c_void_p(buf.data_ptr()), cap) == 0
+        g.replay()
+        torch.cuda.synchronize()
+        assert L.ef_gemv_trace_set(None, 0) == 0
+        tr = buf.view(cap, 12).cpu().numpy()
+        tr = tr[tr[:, 2] > 0]
+        tr = tr[np.lexsort((tr[:, 2], tr[:, 0]))]
+        launch = np.zeros(len(tr), dtype=int)
+        for b in np.unique(tr[:, 0]):
+            idx = np.where(tr[:, 0] == b)[0]
+            launch[idx] = np.arange(len(idx))
+        ctas = len(tr) // ROUNDS
+        cyc = lambda a, b: float(np.median((tr[launch >= 1, 7 + b] - tr[launch >= 1, 7 + a]) / ghz / 1e3))
+        ends = [tr[launch == i, 6].max() for i in range(ROUNDS)]
+        waits = [tr[launch == i, 3].min() for i in range(ROUNDS)]
+        period = (tr[launch == ROUNDS - 1, 2].min() - tr[launch == 1, 2].min()) / (ROUNDS - 2) / 1e3
+        out.append({"shape": f"{t} {n}x{k} M={m}", "ctas": ctas, "period_us": round(period, 2),
+                    "release_after_prev_exit_us": round(float(np.median(
+                        [(waits[i + 1] - ends[i]) / 1e3 for i in range(ROUNDS - 1)])), 2),
+                    "before_wait_us": round(cyc(0, 1), 2), "staging_us": round(cyc(1, 2), 2),
+                    "stream_us": round(cyc(2, 3), 2), "epilogue_us": round(cyc(3, 4), 2)})
+        del g
+        for wc in ws:
+            wc.free()
+    print(json.dumps({"gemv_trace": out, "sm_ghz": ghz}), flush=True)
+    return 0
+
+
 def run_profile(args):
     """Profiling drivers for ncu (no timing): --ncu-gemm runs config 2's first
     GEMM shape (M=512, K=2048, N=8192) on 4 weight copies, eagerly, 3 times;
@@ -732,6 +813,8 @@ def main():
     ap.add_argument("--ncu-step", action="store_true",
                     help="profiling mode for ncu: eager warm-up steps plus one eager step, no timing")
     ap.add_argument("--ncu-gemm", action="store_true", help="profiling mode for ncu: config-2 GEMM calls only")
+    ap.add_argument("--gemv-trace", action="store_true",
+                    help="launch phases of the GEMV kernel from the trace library (build.py --trace)")
     ap.add_argument("--ncu-decode", action="store_true",
                     help="profiling mode for ncu: config-3 decode steps, the last in an NVTX range 'step'")
     args = ap.parse_args()
@@ -743,6 +826,8 @@ def main():
         return run_reference(args)
     if args.ncu_gemm or args.ncu_decode:
         return run_profile(args)
+    if args.gemv_trace:
+        return run_gemv_trace(args)
     return run_ours(args)
 
 

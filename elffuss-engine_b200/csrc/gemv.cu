@@ -1049,8 +1049,34 @@ static size_t gemv_smem(int xs_bytes, int ks) {
 // TQ: Q4_K column layout (8 for the f16 types); NT: 8-token tiles; FUSED: the
 // CTA stages its own activation data from f32 x (1-2 tokens); KH: warps per
 // rowgroup (1 or 2).
+// Launch-phase trace (only in builds with -DEF_GEMV_TRACE, a separate library
+// for measurement): thread 0 of each CTA records the global timer and its
+// SM's cycle counter at kernel entry, after the wait for the previous kernel,
+// once the activation data is staged, after the weight stream and at exit,
+// into the buffer set by ef_gemv_trace_set (12 words per CTA: block, SM, 5
+// times in ns, 5 cycle counts).
+#ifdef EF_GEMV_TRACE
+__device__ unsigned long long *g_trace = nullptr;
+__device__ unsigned int g_trace_n = 0, g_trace_cap = 0;
+#define EF_TRACE_MARK(i)                                               \
+    do {                                                               \
+        if (threadIdx.x == 0) {                                        \
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(tg[i]));  \
+            tc[i] = clock64();                                         \
+        }                                                              \
+    } while (0)
+#else
+#define EF_TRACE_MARK(i) \
+    do {                 \
+    } while (0)
+#endif
+
 template <int TYPE, int TQ, int NT, bool SWIGLU, bool FUSED, int KH>
 __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const GemvArgs a) {
+#ifdef EF_GEMV_TRACE
+    unsigned long long tg[5] = {}, tc[5] = {};
+#endif
+    EF_TRACE_MARK(0);
     using TR = Tr<TYPE>;
     using Raw = typename RawOf<TYPE>::T;
     constexpr int W = GV_WARPS;
@@ -1123,6 +1149,7 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const Ge
     // in place). x is produced by the kernel before this one: with
     // programmatic dependent launch, wait for it only now.
     asm volatile("griddepcontrol.wait;" ::: "memory");
+    EF_TRACE_MARK(1);
     auto copy_phase = [&](int c, uint8_t *dst) {   // prep buffer -> shared, async
         const int len = min(a.phase_chunks, c1 - c);
         const uint8_t *src = a.xf + (int64_t)c * FB;
@@ -1143,6 +1170,7 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const Ge
 #pragma unroll
         for (int i = 0; i < 4; i++) acc[nt][i] = acc2[nt][i] = 0.f;
 
+    EF_TRACE_MARK(2);                // (phases: staging continues inside the stream)
 #pragma unroll 1
     for (int p0 = c0; p0 < c1;) {    // activation phases
         int p1;
@@ -1187,6 +1215,7 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const Ge
         p0 = p1;
     }
     if (!FUSED) cp_wait<0>();
+    EF_TRACE_MARK(3);
     // The weight stream is done: with programmatic dependent launch the next
     // kernel may start now.
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -1277,6 +1306,24 @@ __global__ void __launch_bounds__(GV_WARPS * KH * 32, 1) ef_gemv_kernel(const Ge
             }
         }
     }
+#ifdef EF_GEMV_TRACE
+    __syncthreads();
+    EF_TRACE_MARK(4);
+    if (threadIdx.x == 0) {
+        const unsigned slot = atomicAdd(&g_trace_n, 1u);
+        if (g_trace && slot < g_trace_cap) {
+            unsigned long long *o = g_trace + (size_t)slot * 12;
+            unsigned sm;
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
+            o[0] = blockIdx.x;
+            o[1] = sm;
+            for (int i = 0; i < 5; i++) {
+                o[2 + i] = tg[i];
+                o[7 + i] = tc[i];
+            }
+        }
+    }
+#endif
 }
 
 // ------------------------------------------------------------------ host ---
@@ -1576,3 +1623,17 @@ extern "C" int ef_gemv_noalloc(const ef_weight *w, const float *x, int M, float 
     tmp.scratch[0] = nullptr;   // not the context's to free
     return rc;
 }
+
+#ifdef EF_GEMV_TRACE
+// Sets the launch-phase trace buffer (cap records of 12 u64; null: off) and
+// restarts its record count. Trace builds only; synchronizes the device.
+extern "C" __attribute__((visibility("default"))) int ef_gemv_trace_set(void *buf, unsigned cap) {
+    unsigned long long *p = (unsigned long long *)buf;
+    const unsigned zero = 0;
+    if (cudaDeviceSynchronize() != cudaSuccess) return EF_ERR_CUDA;
+    if (cudaMemcpyToSymbol(ef::g_trace, &p, sizeof(p)) != cudaSuccess) return EF_ERR_CUDA;
+    if (cudaMemcpyToSymbol(ef::g_trace_cap, &cap, sizeof(cap)) != cudaSuccess) return EF_ERR_CUDA;
+    if (cudaMemcpyToSymbol(ef::g_trace_n, &zero, sizeof(zero)) != cudaSuccess) return EF_ERR_CUDA;
+    return EF_OK;
+}
+#endif
