@@ -35,6 +35,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <algorithm>
 #include <atomic>
 
 #include "common.cuh"
@@ -498,34 +499,63 @@ __global__ void __launch_bounds__(FA_T, 1) ef_attn_prompt_kernel(const float *__
     }
 }
 
-// Decode attention split over the keys (one new token per row): CTA =
-// (key range `split` of AK keys, cache head kvh, row r) for all G = H / KVH
-// query heads that share the cache head. The range's k and v rows are copied
-// into shared memory at once (asynchronous 16-byte copies, all in flight
-// together; small CTAs so that several load while others compute), then: a
-// warp per key with the lanes across the head dimension for the G scores;
-// per head the range's max m and sum l of exp(s - m); a thread per dimension
-// for the unnormalised sums of exp(s - m) * v. ef_attn_combine_kernel merges the
-// ranges. Same masking and scale as ef_attention_kernel.
-constexpr int AK = 32;         // keys per range
-constexpr int AT = 128;        // threads per CTA
-static_assert(AK == 32, "the softmax step holds one key per lane");
+// Decode attention split over the keys (one new token per row), in the
+// manner of flash decoding: CTA = (key range `split` of cpc * AK keys, cache
+// head kvh, row r) for all G = H / KVH query heads that share the cache head,
+// AW warps, each on its own groups of KG keys of the range (groups w, w + AW,
+// ...) with no CTA barrier until the end. A warp streams its groups' k and v
+// rows into its own NB shared-memory slots (asynchronous 16-byte copies, NB - 1
+// groups in flight). Per group: each lane takes E = D / 32 dimensions of the
+// KG keys x G heads dot products, the KG * G partial sums are reduced over the
+// lanes by one transposing butterfly (after it lane L holds the score of key
+// (L % V) / G, head L % G, V = KG * G); the warp's running max m and sum l of
+// exp(s - m) per head (online softmax) and, each lane for its dimensions, the
+// running unnormalised sum of exp(s - m) * v, rescaled by exp(m_old - m_new).
+// At the end the AW warps' (sum, m, l) are merged in warp order and the
+// range's go to `part`; ef_attn_combine_kernel merges the ranges. Same masking
+// and scale as ef_attention_kernel.
+constexpr int AK = 32;         // keys per range unit (a range is cpc units)
+constexpr int AW = 4;          // warps per CTA
+constexpr int AT = AW * 32;    // threads per CTA
+constexpr int ANB = 3;         // shared-memory slots per warp (groups in flight + 1)
+template <int G> constexpr int akg() { return G >= 4 ? 32 / G : 8; }   // keys per group
+
+// v[i] summed over the 32 lanes; afterwards lane L holds, in v[0], the sum of
+// index L % V (plain butterfly over the lane bits >= log2(V), then a
+// transposing one over the lower bits).
+template <int V>
+__device__ __forceinline__ void xreduce(float (&v)[V], int lane) {
+#pragma unroll
+    for (int s = 16; s >= V; s >>= 1)
+#pragma unroll
+        for (int i = 0; i < V; i++) v[i] += __shfl_xor_sync(0xffffffffu, v[i], s);
+#pragma unroll
+    for (int s = V / 2; s >= 1; s >>= 1) {
+        const bool up = lane & s;
+#pragma unroll
+        for (int i = 0; i < s; i++) {
+            const float send = up ? v[i] : v[i + s], keep = up ? v[i + s] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, s);
+        }
+    }
+}
 
 template <int D, int G, typename KV>
 __global__ void __launch_bounds__(AT) ef_attn_part_kernel(const float *__restrict__ q, const KV *__restrict__ kcache,
                                                        const KV *__restrict__ vcache, const int *__restrict__ pos,
-                                                       int tokens, int max_pos, int window, int H, int KVH,
+                                                       int tokens, int max_pos, int window, int H, int KVH, int cpc,
                                                        float *__restrict__ part) {
     pdl_trigger();
     pdl_wait();
-    extern __shared__ __align__(16) uint8_t kv_raw[];   // k rows [AK][D], then v rows [AK][D] (cache type)
-    __shared__ float sc[G][AK];
-    __shared__ float ml[G][2];
+    constexpr int KG = akg<G>(), V = KG * G, E = D / 32;
+    extern __shared__ __align__(16) uint8_t kv_raw[];   // per warp: k [ANB][KG][D], then v [ANB][KG][D]
+    __shared__ float wm[AW][G], wl[AW][G];
+    __shared__ __align__(16) float wacc[AW][G][D];
     const int split = blockIdx.x, kvh = blockIdx.y, r = blockIdx.z, nsplit = gridDim.x;
     const int sq = r / tokens, t = r - sq * tokens;
     const int nkv = min(pos[sq] + t + 1, max_pos), qpos = nkv - 1;
     const int k0 = window > 0 && qpos - window + 1 > 0 ? qpos - window + 1 : 0;
-    const int a = k0 + split * AK, b = min(nkv, a + AK);
+    const int a = k0 + split * cpc * AK, b = min(nkv, a + cpc * AK);
     float *pr = part + (((int64_t)r * H + kvh * G) * nsplit + split) * (D + 2);   // head g at + g * nsplit * (D+2)
     if (a >= b) {                    // an empty range: weight 0 in the merge
         for (int i = threadIdx.x; i < G * (D + 2); i += AT) {
@@ -534,94 +564,142 @@ __global__ void __launch_bounds__(AT) ef_attn_part_kernel(const float *__restric
         }
         return;
     }
-    const int n = b - a;
-    KV *ks = reinterpret_cast<KV *>(kv_raw), *vs = ks + AK * D;
-    {
-        const KV *kb = kcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
-        const KV *vb = vcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
-        constexpr int EP = 16 / sizeof(KV);   // elements per 16-byte piece
-        constexpr int C = D / EP;             // 16-byte pieces per row
-        for (int i = threadIdx.x; i < n * C; i += AT) {
-            const int j = i / C, c = i - j * C;
-            cp_async16(ks + j * D + EP * c, kb + (int64_t)j * KVH * D + EP * c);
-            cp_async16(vs + j * D + EP * c, vb + (int64_t)j * KVH * D + EP * c);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    KV *ks = reinterpret_cast<KV *>(kv_raw) + (size_t)warp * 2 * ANB * KG * D, *vs = ks + ANB * KG * D;
+    const KV *kb = kcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
+    const KV *vb = vcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
+    const int ngroups = (b - a + KG - 1) / KG;
+    const int mine = ngroups > warp ? (ngroups - warp + AW - 1) / AW : 0;   // this warp's groups
+    auto issue = [&](int t) {        // this warp's t-th group -> slot t % ANB (an empty commit past the end)
+        if (t < mine) {
+            constexpr int EP = 16 / sizeof(KV), C = D / EP;   // elements per 16-byte piece, pieces per row
+            const int j0 = (warp + AW * t) * KG, n = min(KG, b - a - j0);
+            KV *kd = ks + (t % ANB) * KG * D, *vd = vs + (t % ANB) * KG * D;
+            for (int i = lane; i < n * C; i += 32) {
+                const int j = i / C, cc = i - j * C;
+                cp_async16(kd + j * D + EP * cc, kb + (int64_t)(j0 + j) * KVH * D + EP * cc);
+                cp_async16(vd + j * D + EP * cc, vb + (int64_t)(j0 + j) * KVH * D + EP * cc);
+            }
         }
         cp_commit();
-    }
-    const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
-    constexpr int E = D / 32;        // head-dimension elements per lane
+    };
+#pragma unroll
+    for (int t0 = 0; t0 < ANB - 1; t0++) issue(t0);
     float qv[G][E];
     const float qscale = rsqrtf((float)D);
 #pragma unroll
     for (int g = 0; g < G; g++)
 #pragma unroll
         for (int e = 0; e < E; e++) qv[g][e] = q[((int64_t)r * H + kvh * G + g) * D + lane * E + e] * qscale;
-    cp_wait<0>();
-    __syncthreads();
-    for (int j = warp; j < n; j += AT / 32) {
-        float kr[E];
-        if constexpr (E == 4) {
-            const float4 v4 = kv_ld4(ks + j * D + lane * 4);
-            kr[0] = v4.x; kr[1] = v4.y; kr[2] = v4.z; kr[3] = v4.w;
-        } else {
-            const float2 v2 = kv_ld2(ks + j * D + lane * 2);
-            kr[0] = v2.x; kr[1] = v2.y;
+    const int mg = lane % G;         // the head whose running max / sum this lane keeps
+    float m = -INFINITY, l = 0.f;
+    float acc[G][E];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < E; e++) acc[g][e] = 0.f;
+    for (int t = 0; t < mine; t++) {
+        issue(t + ANB - 1);
+        cp_wait<ANB - 1>();
+        __syncwarp();
+        const int n = min(KG, b - a - (warp + AW * t) * KG);
+        const KV *kg = ks + (t % ANB) * KG * D, *vg = vs + (t % ANB) * KG * D;
+        // partial scores of the KG keys x G heads over this lane's dimensions
+        float sv[V];
+#pragma unroll
+        for (int j = 0; j < KG; j++) {
+            float kr[E];
+            if (j < n) {
+                if constexpr (E == 4) {
+                    const float4 v4 = kv_ld4(kg + j * D + lane * 4);
+                    kr[0] = v4.x; kr[1] = v4.y; kr[2] = v4.z; kr[3] = v4.w;
+                } else {
+                    const float2 v2 = kv_ld2(kg + j * D + lane * 2);
+                    kr[0] = v2.x; kr[1] = v2.y;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < E; e++) kr[e] = 0.f;
+            }
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float s = 0.f;
+#pragma unroll
+                for (int e = 0; e < E; e++) s += qv[g][e] * kr[e];
+                sv[j * G + g] = s;
+            }
         }
-        float s[G];
+        xreduce<V>(sv, lane);
+        const int ji = (lane % V) / G;                // this lane's key of the group
+        const float sc = ji < n ? sv[0] : -INFINITY;
+        // online softmax per head over the group's keys (lanes of one head differ in bits log2 G .. log2 V - 1)
+        float gm = sc;
+#pragma unroll
+        for (int s = G; s < V; s <<= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, s));
+        const float mnew = fmaxf(m, gm);
+        const float p = ji < n ? expf(sc - mnew) : 0.f;
+        float ps = p;
+#pragma unroll
+        for (int s = G; s < V; s <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, s);
+        const float alpha = expf(m - mnew);           // 0 for the first group (m = -inf)
+        m = mnew;
+        l = l * alpha + ps;
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            s[g] = 0.f;
+            const float ag = __shfl_sync(0xffffffffu, alpha, g);
 #pragma unroll
-            for (int e = 0; e < E; e++) s[g] += qv[g][e] * kr[e];
+            for (int e = 0; e < E; e++) acc[g][e] *= ag;
         }
 #pragma unroll
-        for (int o = 16; o; o >>= 1)
+        for (int j = 0; j < KG; j++) {
+            if (j < n) {
+                float vr[E];
+                if constexpr (E == 4) {
+                    const float4 v4 = kv_ld4(vg + j * D + lane * 4);
+                    vr[0] = v4.x; vr[1] = v4.y; vr[2] = v4.z; vr[3] = v4.w;
+                } else {
+                    const float2 v2 = kv_ld2(vg + j * D + lane * 2);
+                    vr[0] = v2.x; vr[1] = v2.y;
+                }
 #pragma unroll
-            for (int g = 0; g < G; g++) s[g] += __shfl_xor_sync(0xffffffffu, s[g], o);
-        if (lane == 0)
+                for (int g = 0; g < G; g++) {
+                    const float pg = __shfl_sync(0xffffffffu, p, j * G + g);
 #pragma unroll
-            for (int g = 0; g < G; g++) sc[g][j] = s[g];
-    }
-    __syncthreads();
-    for (int g = warp; g < G; g += AT / 32) {
-        const float v = lane < n ? sc[g][lane] : -1e30f;      // AK == 32: a key per lane
-        float m = v;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        const float e = lane < n ? expf(v - m) : 0.f;
-        if (lane < n) sc[g][lane] = e;
-        float l = e;
-#pragma unroll
-        for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
-        if (lane == 0) {
-            ml[g][0] = m;
-            ml[g][1] = l;
-        }
-    }
-    __syncthreads();
-    constexpr int GS = AT / D;       // head groups side by side (1 for D = 128, 2 for D = 64)
-    constexpr int GJ = (G + GS - 1) / GS;
-    const int d = threadIdx.x % D, g0 = threadIdx.x / D;
-    float acc[GJ];
-#pragma unroll
-    for (int jj = 0; jj < GJ; jj++) acc[jj] = 0.f;
-#pragma unroll 4
-    for (int j = 0; j < n; j++) {
-        const float v = kv_f(vs[j * D + d]);
-#pragma unroll
-        for (int jj = 0; jj < GJ; jj++)
-            if (g0 + jj * GS < G) acc[jj] += sc[g0 + jj * GS][j] * v;
-    }
-#pragma unroll
-    for (int jj = 0; jj < GJ; jj++) {
-        const int g = g0 + jj * GS;
-        if (g < G) {
-            float *o = pr + (int64_t)g * nsplit * (D + 2);
-            o[d] = acc[jj];
-            if (d == 0) {
-                o[D] = ml[g][0];
-                o[D + 1] = ml[g][1];
+                    for (int e = 0; e < E; e++) acc[g][e] += pg * vr[e];
+                }
             }
+        }
+        __syncwarp();                // the slot is reissued ANB - 1 groups later
+    }
+    cp_wait<0>();
+    // merge the warps, in warp order
+    if (lane < G) {
+        wm[warp][lane] = m;          // (lane < G: mg == lane)
+        wl[warp][lane] = l;
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < E; e++) wacc[warp][g][lane * E + e] = acc[g][e];
+    (void)mg;
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * D; i += AT) {
+        const int g = i / D, d = i - g * D;
+        float M = wm[0][g];
+#pragma unroll
+        for (int w = 1; w < AW; w++) M = fmaxf(M, wm[w][g]);
+        float o = 0.f, L = 0.f;
+#pragma unroll
+        for (int w = 0; w < AW; w++) {
+            const float f = expf(wm[w][g] - M);       // 0 for a warp without keys (m = -inf)
+            o += f * wacc[w][g][d];
+            L += f * wl[w][g];
+        }
+        float *op = pr + (int64_t)g * nsplit * (D + 2);
+        op[d] = o;
+        if (d == 0) {
+            op[D] = M;
+            op[D + 1] = L;
         }
     }
 }
@@ -921,8 +999,8 @@ static int grid1d(int64_t n, int b) { return (int)((n + b - 1) / b); }
 
 template <int D, int G, typename KV>
 static int part_launch(ef_ctx *ctx, dim3 grid, const float *q, const KV *kcache, const KV *vcache, const int *pos,
-                       int tokens, int max_pos, int window, int heads, int kv_heads, float *part) {
-    constexpr size_t smem = 2 * AK * D * sizeof(KV);
+                       int tokens, int max_pos, int window, int heads, int kv_heads, int cpc, float *part) {
+    constexpr size_t smem = (size_t)AW * 2 * ANB * akg<G>() * D * sizeof(KV);
     static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
         if (int rc = check_cuda(ctx, cudaFuncSetAttribute(ef_attn_part_kernel<D, G, KV>,
@@ -932,7 +1010,7 @@ static int part_launch(ef_ctx *ctx, dim3 grid, const float *q, const KV *kcache,
         configured.fetch_or(1ull << ctx->device);
     }
     return launch_on(ctx, ef_attn_part_kernel<D, G, KV>, grid, AT, smem, "attention launch", q, kcache, vcache, pos,
-                     tokens, max_pos, window, heads, kv_heads, part);
+                     tokens, max_pos, window, heads, kv_heads, cpc, part);
 }
 
 template <int D, int G, typename KV>
@@ -1006,15 +1084,19 @@ static int attention_launch(ef_ctx *ctx, const float *q, const KV *kcache, const
     const int span = window > 0 && window < max_pos ? window : max_pos;
     const int G = heads / kv_heads;
     if (tokens == 1 && (G == 1 || G == 2 || G == 4 || G == 8)) {
-        // one new token per sequence: the keys split over CTAs, then merged
-        const int nsplit = (span + AK - 1) / AK;
+        // one new token per sequence: the keys split over CTAs (ranges of cpc
+        // chunks, as few as keep about 8 CTAs per SM in the grid), then merged
         const int64_t rows = seqs;
+        const int chunks = (span + AK - 1) / AK;
+        const int64_t want = (8LL * ctx->sm_count + rows * kv_heads - 1) / (rows * kv_heads);
+        const int cpc = (int)((chunks + std::min<int64_t>(chunks, want) - 1) / std::min<int64_t>(chunks, want));
+        const int nsplit = (chunks + cpc - 1) / cpc;
         const size_t bytes = (size_t)rows * heads * nsplit * (head_dim + 2) * sizeof(float);
         if (int rc = ensure_scratch(ctx, 2, bytes)) return rc;
         float *part = (float *)ctx->scratch[2];
         const dim3 pg(nsplit, kv_heads, (unsigned)rows);
 #define EF_PART(DD, GG)                                                                                          \
-    rc = part_launch<DD, GG, KV>(ctx, pg, q, kcache, vcache, pos, tokens, max_pos, window, heads, kv_heads, part)
+    rc = part_launch<DD, GG, KV>(ctx, pg, q, kcache, vcache, pos, tokens, max_pos, window, heads, kv_heads, cpc, part)
         int rc;
         if (head_dim == 64) {
             switch (G) {
