@@ -452,6 +452,67 @@ def run_gemv_trace(args):
     return 0
 
 
+def run_attn_probe(args):
+    """Decode attention alone at config 4's batch-16 shape (16 sequences at
+    position 4095, 32 query / 8 cache heads of 128, caches of LlamaConfig's
+    capacity), f32 and f16 caches: 8 layers' calls (distinct caches) captured
+    in a CUDA graph, 20 replays; per call time and K/V bytes read per second.
+    Prints one JSON line."""
+    import ctypes
+
+    import torch
+
+    from elffuss_engine_b200._lib import check, lib
+    from elffuss_engine_b200.llama import LlamaConfig
+    from elffuss_engine_b200.ops import QuantOps
+    cfg = LlamaConfig()
+    ops = QuantOps(0)
+    L = lib()
+    S, H, KV, D, maxp, layers = 16, cfg.heads, cfg.kv_heads, cfg.head_dim, cfg.max_pos, 8
+    P = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+    out = {}
+    for kv16 in (False, True):
+        dt = torch.float16 if kv16 else torch.float32
+        g = torch.Generator("cuda").manual_seed(1)
+        kc = [torch.randn(S, maxp, KV, D, device="cuda", generator=g).to(dt) for _ in range(layers)]
+        vc = [torch.randn(S, maxp, KV, D, device="cuda", generator=g).to(dt) for _ in range(layers)]
+        q = torch.randn(S, H * D, device="cuda", generator=g)
+        pos = torch.full((S,), LLAMA_CONTEXT - 1, dtype=torch.int32, device="cuda")
+        o = torch.empty(S, H * D, device="cuda")
+        fn = L.ef_attention_f16 if kv16 else L.ef_attention
+
+        def seq():
+            h = ops.ctx.bind()
+            for i in range(layers):
+                check(fn(h, P(q), P(kc[i]), P(vc[i]), None, P(pos), S, 1, maxp, 0, H, KV, D, P(o)), h)
+        seq()
+        torch.cuda.synchronize()
+        cs = torch.cuda.Stream()
+        cs.wait_stream(torch.cuda.current_stream())
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr, stream=cs):
+            seq()
+        for _ in range(3):
+            gr.replay()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(20):
+            gr.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / (20 * layers) * 1e3
+        kv_bytes = 2 * S * LLAMA_CONTEXT * KV * D * (2 if kv16 else 4)
+        out["f16" if kv16 else "f32"] = {"us_per_layer": round(us, 1), "kv_bytes": kv_bytes,
+                                         "GBps": round(kv_bytes / us / 1e3, 1),
+                                         "ms_per_step_32_layers": round(us * cfg.layers / 1e3, 3)}
+        del gr, kc, vc
+        torch.cuda.empty_cache()
+    print(json.dumps({"attn_probe": out, "shape": f"S={S} pos={LLAMA_CONTEXT - 1} H={H} KVH={KV} D={D}"}),
+          flush=True)
+    return 0
+
+
 def run_profile(args):
     """Profiling drivers for ncu (no timing): --ncu-gemm runs config 2's first
     GEMM shape (M=512, K=2048, N=8192) on 4 weight copies, eagerly, 3 times;
@@ -813,6 +874,8 @@ def main():
     ap.add_argument("--ncu-step", action="store_true",
                     help="profiling mode for ncu: eager warm-up steps plus one eager step, no timing")
     ap.add_argument("--ncu-gemm", action="store_true", help="profiling mode for ncu: config-2 GEMM calls only")
+    ap.add_argument("--attn-probe", action="store_true",
+                    help="decode attention alone at config 4's batch-16 shape, f32 and f16 caches")
     ap.add_argument("--gemv-trace", action="store_true",
                     help="launch phases of the GEMV kernel from the trace library (build.py --trace)")
     ap.add_argument("--ncu-decode", action="store_true",
@@ -828,6 +891,8 @@ def main():
         return run_profile(args)
     if args.gemv_trace:
         return run_gemv_trace(args)
+    if args.attn_probe:
+        return run_attn_probe(args)
     return run_ours(args)
 
 
