@@ -173,6 +173,12 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
     uint32_t *tslot = reinterpret_cast<uint32_t *>(tfull + 1);
     uint4 *tab = reinterpret_cast<uint4 *>(reinterpret_cast<uint8_t *>(bars) + 256);   // i-quant codebooks
 
+    // Programmatic dependent launch: the next kernel may be scheduled at once
+    // (it cannot share this CTA's SM, whose shared memory this one fills);
+    // the previous kernel's results are read (activations, by the producer's
+    // TMA) and y is written (epilogue) only after griddepcontrol.wait. The
+    // set-up, the weight copies and their dequantisation do not depend on it.
+    pdl_trigger();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int64_t rb = blockIdx.x;                       // 8 rowgroups = 128 rows
     const int n0 = blockIdx.y * GM_BN;                   // first token
@@ -248,6 +254,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
                 wi++;
             };
             for (int kk = 0; kk < SW && kk < nk && ok; kk++) issue_w(kk);
+            pdl_wait();                                  // the activations come from the kernel before
             for (int kk = 0; kk < nk && ok; kk++) {
                 const int nb = boxes_of(kk);
                 for (int h = 0; h < nb && ok; h++) {
@@ -646,6 +653,7 @@ __device__ __forceinline__ void gemm_body(const CUtensorMap &xmap, const uint8_t
         // ------------------------------------------------------------ epilogue
         if (ok) ok = mbar_wait(tfull, 0, lim);
         tc_fence_after();
+        pdl_wait();                  // (long since satisfied: y is written after the kernel before)
         if (ok) {
             const int64_t row = rb * GM_BM + quad * 32 + lane;
             constexpr int EC = GM_BN / (2 * CPS);   // accumulator columns per epilogue group
@@ -785,9 +793,8 @@ static int launch_tc(ef_ctx *ctx, const ef_weight *w, const __half *xh, int M, f
         configured.fetch_or(1ull << ctx->device);
     }
     dim3 grid((unsigned)((w->rowgroups + 7) / 8), (unsigned)((M + GM_BN - 1) / GM_BN));
-    ctx->launches++;
-    kern<<<grid, gm_threads<TYPE>(), smem, ctx->stream>>>(map, w->dev, w->rowgroups, w->nchunks, w->rows, w->k, M, y);
-    return check_cuda(ctx, cudaGetLastError(), "gemm launch");
+    return launch_on(ctx, kern, grid, dim3(gm_threads<TYPE>()), smem, "gemm launch", map, (const uint8_t *)w->dev,
+                     w->rowgroups, w->nchunks, w->rows, w->k, M, y);
 }
 
 // Reads and clears the flag a bounded pipeline wait sets when it gives up.
