@@ -185,8 +185,8 @@ GEMM_SHAPES = [(512, 2048, 8192), (2048, 8192, 2048)]   # (tokens M, k, weight r
 
 
 def bench_gemm(ops, L, args, capture, timed_replays, rank):
-    """Config 2: f16 activations x Q8_0 weights through ef_gemm, graph-replayed;
-    8 distinct weight tensors per shape (more than L2 per replay)."""
+    """Config 2: f16 activations x Q8_0 weights through ef_gemm, graph-replayed
+    REPLAYS times; 8 distinct weight tensors per shape (more than L2 per replay)."""
     import torch
 
     from elffuss_engine_b200 import formats
@@ -215,8 +215,7 @@ def bench_gemm(ops, L, args, capture, timed_replays, rank):
         g = capture(step)
         for _ in range(args.warmup):
             g.replay()
-        reps = max(3, min(args.steps, 10))
-        ms = timed_replays(g, reps) / (reps * len(ws))
+        ms = timed_replays(g, REPLAYS) / (REPLAYS * len(ws))
         del g
         flop = 2.0 * m * n * k
         tot_flop += flop

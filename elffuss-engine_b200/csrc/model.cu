@@ -37,6 +37,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 
 #include "common.cuh"
 #include "internal.h"
@@ -704,6 +705,220 @@ __global__ void __launch_bounds__(AT) ef_attn_part_kernel(const float *__restric
     }
 }
 
+// The same split with f16 caches and up to 4 query heads per cache head, on
+// the tensor cores (mma.sync m16n8k16, f16 operands, f32 accumulate). Each
+// warp takes groups of 16 keys. Scores: S[key][col] = K[key][:] . Q'[:][col],
+// K from shared memory by ldmatrix, Q' the G query heads (pre-scaled by
+// 1/sqrt(D)) each split into two f16 columns, hi = f16(q) and lo = f16(q - hi),
+// so that hi + lo carries q to about 22 bits and the f32 sum of the exact
+// f16 x f16 products keeps f32 accuracy; score = S[.][2h] + S[.][2h+1].
+// Online softmax per head as in the kernel above (lane (g, t) holds keys g
+// and g + 8 of head t). Values: out^T[d][col] += V^T[d][key] . P'[key][col],
+// V^T by ldmatrix.trans, P' the probabilities split the same way (gathered
+// from their lanes by shuffles), out = out^T[.][2h] + out^T[.][2h+1]. K and V
+// rows sit in shared memory with 16 bytes of padding per row (the 8 rows of
+// an ldmatrix read fall in different banks).
+constexpr int AHK = 16;        // keys per group (one MMA row tile)
+constexpr int AHNB = 3;        // shared-memory slots per warp
+
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void *p) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"((uint32_t)__cvta_generic_to_shared(p)));
+}
+// (hi, lo) f16 split of v, packed as the pair (first, second) of a b16x2 register half
+__device__ __forceinline__ __half split_part(float v, int lo) {
+    const __half h = __float2half_rn(v);
+    return lo ? __float2half_rn(v - __half2float(h)) : h;
+}
+__device__ __forceinline__ uint32_t pack_h2(__half a, __half b) {
+    return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+}
+
+template <int D, int G>
+__global__ void __launch_bounds__(AT) ef_attn_part_h_kernel(const float *__restrict__ q,
+                                                         const __half *__restrict__ kcache,
+                                                         const __half *__restrict__ vcache,
+                                                         const int *__restrict__ pos, int tokens, int max_pos,
+                                                         int window, int H, int KVH, int cpc,
+                                                         float *__restrict__ part) {
+    static_assert(G <= 4, "two f16 columns per query head, 8 columns per MMA");
+    pdl_trigger();
+    pdl_wait();
+    constexpr int LD = D + 8;        // padded row (halves)
+    constexpr int KS = D / 16;       // MMA k-steps of the scores, m-tiles of the values
+    extern __shared__ __align__(16) uint8_t kv_raw[];   // per warp: k [AHNB][AHK][LD], then v [AHNB][AHK][LD]
+    __shared__ float wm[AW][G], wl[AW][G];
+    __shared__ __align__(16) float wacc[AW][G][D];
+    const int split = blockIdx.x, kvh = blockIdx.y, r = blockIdx.z, nsplit = gridDim.x;
+    const int sq = r / tokens, t0k = r - sq * tokens;
+    const int nkv = min(pos[sq] + t0k + 1, max_pos), qpos = nkv - 1;
+    const int k0 = window > 0 && qpos - window + 1 > 0 ? qpos - window + 1 : 0;
+    const int a = k0 + split * cpc * AK, b = min(nkv, a + cpc * AK);
+    float *pr = part + (((int64_t)r * H + kvh * G) * nsplit + split) * (D + 2);
+    if (a >= b) {
+        for (int i = threadIdx.x; i < G * (D + 2); i += AT) {
+            const int g = i / (D + 2), c = i - g * (D + 2);
+            pr[(int64_t)g * nsplit * (D + 2) + c] = c == D ? -1e30f : 0.f;
+        }
+        return;
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t = lane & 3;
+    __half *ks = reinterpret_cast<__half *>(kv_raw) + (size_t)warp * 2 * AHNB * AHK * LD, *vs = ks + AHNB * AHK * LD;
+    const __half *kb = kcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
+    const __half *vb = vcache + (((int64_t)sq * max_pos + a) * KVH + kvh) * D;
+    const int ngroups = (b - a + AHK - 1) / AHK;
+    const int mine = ngroups > warp ? (ngroups - warp + AW - 1) / AW : 0;
+    auto issue = [&](int it) {
+        if (it < mine) {
+            constexpr int C = D / 8;     // 16-byte pieces per row
+            const int j0 = (warp + AW * it) * AHK, n = min(AHK, b - a - j0);
+            __half *kd = ks + (it % AHNB) * AHK * LD, *vd = vs + (it % AHNB) * AHK * LD;
+            for (int i = lane; i < n * C; i += 32) {
+                const int j = i / C, cc = i - j * C;
+                cp_async16(kd + j * LD + 8 * cc, kb + (int64_t)(j0 + j) * KVH * D + 8 * cc);
+                cp_async16(vd + j * LD + 8 * cc, vb + (int64_t)(j0 + j) * KVH * D + 8 * cc);
+            }
+        }
+        cp_commit();
+    };
+#pragma unroll
+    for (int i = 0; i < AHNB - 1; i++) issue(i);
+    // B fragments of Q' for the KS k-steps: column g = head g / 2, part g % 2
+    uint32_t qb[KS][2];
+    {
+        const int hg = g >> 1, lo = g & 1;
+        const float qscale = rsqrtf((float)D);
+        const float *qh = q + ((int64_t)r * H + kvh * G + (hg < G ? hg : 0)) * D;
+#pragma unroll
+        for (int s = 0; s < KS; s++) {
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (hg < G) {
+                v[0] = qh[s * 16 + 2 * t] * qscale;
+                v[1] = qh[s * 16 + 2 * t + 1] * qscale;
+                v[2] = qh[s * 16 + 2 * t + 8] * qscale;
+                v[3] = qh[s * 16 + 2 * t + 9] * qscale;
+            }
+            qb[s][0] = pack_h2(split_part(v[0], lo), split_part(v[1], lo));
+            qb[s][1] = pack_h2(split_part(v[2], lo), split_part(v[3], lo));
+        }
+    }
+    const bool head = t < G;         // this lane's softmax head is t
+    float m = -INFINITY, l = 0.f;
+    float acc[KS][4];
+#pragma unroll
+    for (int i = 0; i < KS; i++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) acc[i][e] = 0.f;
+    const int lr = (lane & 7) + ((lane >> 3) & 1) * 8, lc = (lane >> 4) * 8;   // ldmatrix A rows / cols
+    const int vk = (lane & 7) + (lane >> 4) * 8, vd = ((lane >> 3) & 1) * 8;   // ldmatrix.trans: key / dim
+    for (int it = 0; it < mine; it++) {
+        issue(it + AHNB - 1);
+        cp_wait<AHNB - 1>();
+        __syncwarp();
+        const int n = min(AHK, b - a - (warp + AW * it) * AHK);
+        const __half *kg = ks + (it % AHNB) * AHK * LD, *vg = vs + (it % AHNB) * AHK * LD;
+        // scores
+        float sc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int s = 0; s < KS; s++) {
+            uint32_t af[4];
+            ldsm_x4(af, kg + lr * LD + s * 16 + lc);
+            mma_f16_16816(sc, af[0], af[1], af[2], af[3], qb[s][0], qb[s][1]);
+        }
+        // lane (g, t): keys g and g + 8 of head t (columns 2t, 2t + 1); keys past n masked
+        // (their rows in shared memory are stale or unset: their scores are never used)
+        const float s0 = head && g < n ? sc[0] + sc[1] : -INFINITY;
+        const float s1 = head && g + 8 < n ? sc[2] + sc[3] : -INFINITY;
+        float gm = fmaxf(s0, s1);
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) gm = fmaxf(gm, __shfl_xor_sync(0xffffffffu, gm, o));
+        const float mnew = head ? fmaxf(m, gm) : 0.f;
+        const float p0 = head && g < n ? expf(s0 - mnew) : 0.f;
+        const float p1 = head && g + 8 < n ? expf(s1 - mnew) : 0.f;
+        float ps = p0 + p1;
+#pragma unroll
+        for (int o = 4; o < 32; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+        const float alpha = head ? expf(m - mnew) : 1.f;   // 0 for the first group (m = -inf)
+        if (head) {
+            m = mnew;
+            l = l * alpha + ps;
+        }
+        // P' B fragment: rows (keys) 2t, 2t+1, 2t+8, 2t+9 of column g (head g / 2, part g % 2)
+        const int hg = g >> 1, lo = g & 1;
+        const float q0 = __shfl_sync(0xffffffffu, p0, 8 * t + hg), q1 = __shfl_sync(0xffffffffu, p0, 8 * t + 4 + hg);
+        const float q2 = __shfl_sync(0xffffffffu, p1, 8 * t + hg), q3 = __shfl_sync(0xffffffffu, p1, 8 * t + 4 + hg);
+        const uint32_t pb0 = hg < G ? pack_h2(split_part(q0, lo), split_part(q1, lo)) : 0u;
+        const uint32_t pb1 = hg < G ? pack_h2(split_part(q2, lo), split_part(q3, lo)) : 0u;
+        // values: rescale, then add V^T P' (keys past n have p = 0; their V rows are
+        // zero-filled below so that stale data cannot be Inf or NaN)
+        if (n < AHK) {
+            __half *vw = const_cast<__half *>(vg);
+            for (int i = lane; i < (AHK - n) * (D / 2); i += 32) {
+                const int j = n + i / (D / 2), c = i - (j - n) * (D / 2);
+                reinterpret_cast<uint32_t *>(vw + j * LD)[c] = 0u;
+            }
+            __syncwarp();
+        }
+#pragma unroll
+        for (int i = 0; i < KS; i++) {
+            acc[i][0] *= alpha;
+            acc[i][1] *= alpha;
+            acc[i][2] *= alpha;
+            acc[i][3] *= alpha;
+            uint32_t af[4];
+            ldsm_x4_t(af, vg + vk * LD + i * 16 + vd);
+            mma_f16_16816(acc[i], af[0], af[1], af[2], af[3], pb0, pb1);
+        }
+        __syncwarp();                // the slot is reissued AHNB - 1 groups later
+    }
+    cp_wait<0>();
+    // merge the warps, in warp order: lane (g, t) holds out[16 i + g] and out[16 i + g + 8] of head t
+    if (head && g == 0) {
+        wm[warp][t] = m;
+        wl[warp][t] = l;
+    }
+    if (head)
+#pragma unroll
+        for (int i = 0; i < KS; i++) {
+            wacc[warp][t][16 * i + g] = acc[i][0] + acc[i][1];
+            wacc[warp][t][16 * i + g + 8] = acc[i][2] + acc[i][3];
+        }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * D; i += AT) {
+        const int h = i / D, d = i - h * D;
+        float M = wm[0][h];
+#pragma unroll
+        for (int w = 1; w < AW; w++) M = fmaxf(M, wm[w][h]);
+        float o = 0.f, L = 0.f;
+#pragma unroll
+        for (int w = 0; w < AW; w++) {
+            const float f = expf(wm[w][h] - M);
+            o += f * wacc[w][h][d];
+            L += f * wl[w][h];
+        }
+        float *op = pr + (int64_t)h * nsplit * (D + 2);
+        op[d] = o;
+        if (d == 0) {
+            op[D] = M;
+            op[D + 1] = L;
+        }
+    }
+}
+
 // out[r][h] = sum over ranges of exp(m_s - M) acc_s / sum of exp(m_s - M) l_s
 // (M = the largest m_s); times sigmoid(gate[r][h]) when given. CTA (head,
 // row) of CT threads = CT / D groups of ranges x D dimensions: the ranges'
@@ -997,9 +1212,29 @@ __global__ void ef_argmax_select_kernel(const int *__restrict__ pairs, int npair
 
 static int grid1d(int64_t n, int b) { return (int)((n + b - 1) / b); }
 
+template <int D, int G>
+static int part_h_launch(ef_ctx *ctx, dim3 grid, const float *q, const __half *kcache, const __half *vcache,
+                         const int *pos, int tokens, int max_pos, int window, int heads, int kv_heads, int cpc,
+                         float *part) {
+    constexpr size_t smem = (size_t)AW * 2 * AHNB * AHK * (D + 8) * sizeof(__half);
+    static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
+    if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
+        if (int rc = check_cuda(ctx, cudaFuncSetAttribute(ef_attn_part_h_kernel<D, G>,
+                                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                                "attention smem attribute"))
+            return rc;
+        configured.fetch_or(1ull << ctx->device);
+    }
+    return launch_on(ctx, ef_attn_part_h_kernel<D, G>, grid, AT, smem, "attention launch", q, kcache, vcache, pos,
+                     tokens, max_pos, window, heads, kv_heads, cpc, part);
+}
+
 template <int D, int G, typename KV>
 static int part_launch(ef_ctx *ctx, dim3 grid, const float *q, const KV *kcache, const KV *vcache, const int *pos,
                        int tokens, int max_pos, int window, int heads, int kv_heads, int cpc, float *part) {
+    if constexpr (std::is_same<KV, __half>::value && G <= 4)   // f16 caches: the tensor-core version
+        return part_h_launch<D, G>(ctx, grid, q, kcache, vcache, pos, tokens, max_pos, window, heads, kv_heads, cpc,
+                                   part);
     constexpr size_t smem = (size_t)AW * 2 * ANB * akg<G>() * D * sizeof(KV);
     static std::atomic<unsigned long long> configured{0};   // per instantiation, one bit per device
     if (ctx->device < 64 && !(configured.load() & (1ull << ctx->device))) {
