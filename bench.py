@@ -645,10 +645,13 @@ def run_ours(args):
         x_views.append(x_all[off:off + wk["m"] * wk["k"]].view(wk["m"], wk["k"]))
         off += wk["m"] * wk["k"]
 
+    copy_stream = torch.cuda.Stream()
+    round_elems = y_elems // ROUNDS
+
     def step_e2e():
         x_all.copy_(xh_all, non_blocking=True)                  # the step's inputs, host -> device
-        outs = []
         for r in range(ROUNDS):
+            outs = []
             for wk, xv in zip(work, x_views):
                 o = ops.gemv.matmul(wk["t"], wk["ws"][r], xv, wk["rows"], wk["k"], wk["m"])   # public operator
                 if world > 1:
@@ -656,8 +659,15 @@ def run_ours(args):
                     gather(wk)
                     o = wk["yall"]
                 outs.append(o.view(-1))
-        torch.cat(outs, out=y_all)
-        yh_all.copy_(y_all, non_blocking=True)                   # the step's results, device -> host
+            seg = y_all[r * round_elems:(r + 1) * round_elems]
+            torch.cat(outs, out=seg)
+            # this round's results, device -> host, on a copy stream while the next round computes
+            done = torch.cuda.Event()
+            done.record()
+            copy_stream.wait_event(done)
+            with torch.cuda.stream(copy_stream):
+                yh_all[r * round_elems:(r + 1) * round_elems].copy_(seg, non_blocking=True)
+        torch.cuda.current_stream().wait_stream(copy_stream)   # the step ends with its results on the host
 
     def barrier():
         torch.cuda.synchronize()

@@ -37,11 +37,14 @@ class Context:
         if rc < 0:
             raise EfError(rc, f"cannot create a context on cuda:{self.device}")
         self.h = h
+        self._stream = None     # the stream last handed to the library (only bind() sets it)
 
     def bind(self):
         """Queue subsequent library work on torch's current stream of this device."""
         s = torch.cuda.current_stream(self.device).cuda_stream
-        lib().ef_ctx_set_stream(self.h, ctypes.c_void_p(s))
+        if s != self._stream:
+            lib().ef_ctx_set_stream(self.h, ctypes.c_void_p(s))
+            self._stream = s
         return self.h
 
     def sync(self):
@@ -279,6 +282,10 @@ class QuantOps:
             raise EfError(-6, f"{name}: the weight ({got}) does not serve rows={rows} k={k}")
 
     def _activations(self, x, k, tokens):
+        n = tokens * k
+        if (isinstance(x, torch.Tensor) and x.is_cuda and x.dtype == torch.float32 and x.numel() == n
+                and x.is_contiguous()):
+            return x.view(tokens, k)       # already the operand: no copy, no reshape chain
         if not isinstance(x, torch.Tensor):
             x = torch.as_tensor(np.asarray(x, np.float32))
         if x.dtype != torch.float32:
