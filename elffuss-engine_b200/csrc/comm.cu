@@ -202,12 +202,18 @@ __device__ __forceinline__ float4 wait_stamped4(const uint64_t *p, uint32_t ep, 
 // Consumer of the fused row-parallel GEMV: row blockIdx.x of o = sum over
 // ranks (in order) of the slots; then x += rmsnorm(o) * w_post (or += o without
 // w_post) and nrm = rmsnorm(x) * w_next, as ef_norm_add_norm_kernel.
+// It works as soon as it is scheduled, without waiting for the GEMV's grid to
+// complete (which includes the acknowledgement of the GEMV's stores to the
+// other ranks): the GEMV's rows arrive stamped, and everything else it reads
+// (the call counter, x, the norm weights) was written by kernels that had
+// completed before the GEMV passed its own wait, which it does before it lets
+// this kernel be scheduled. It waits for the GEMV's completion only before it
+// exits, so that completion stays transitive for the kernels after it.
 template <int V>
 __global__ void __launch_bounds__(256) ef_tp_norm_kernel(const TpArgs a, const float *__restrict__ w_post,
                                                       float *__restrict__ x, const float *__restrict__ w_next, int n,
                                                       float eps, float *__restrict__ nrm) {
     pdl_trigger();
-    pdl_wait();
     __shared__ float red[32];
     __shared__ uint32_t ep, bad;
     uint8_t *mine = a.peer[a.rank];
@@ -217,7 +223,10 @@ __global__ void __launch_bounds__(256) ef_tp_norm_kernel(const TpArgs a, const f
         ep = *(volatile uint32_t *)ctl.fepoch + 1;   // this call's number (the GEMV's stamp)
     }
     __syncthreads();
-    if (bad) return;
+    if (bad) {
+        pdl_wait();
+        return;
+    }
     const uint32_t e = ep;
     const int64_t row = (int64_t)blockIdx.x * (n / 4);
     const uint64_t *slots =
@@ -247,6 +256,7 @@ __global__ void __launch_bounds__(256) ef_tp_norm_kernel(const TpArgs a, const f
     }
     if (__syncthreads_or(late)) {
         if (late) atomicExch(ctl.error, 1u + (uint32_t)who);
+        pdl_wait();
         return;
     }
     float s1 = 1.f;
@@ -283,6 +293,7 @@ __global__ void __launch_bounds__(256) ef_tp_norm_kernel(const TpArgs a, const f
             *(volatile uint32_t *)ctl.fepoch = e;
         }
     }
+    pdl_wait();                      // the GEMV has completed before this kernel does
 }
 
 static TpArgs tp_args(ef_tp *tp) {
