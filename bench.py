@@ -569,7 +569,7 @@ def sweep_config(world: int, step_bytes: int) -> dict:
                   f"{ROUNDS * 12} per step ({ROUNDS * 486} MB at N = 1)",
             "parallelism": "single GPU" if world == 1 else
             f"row-sharded x{world}: every matrix split by output rows over the ranks, y assembled on every "
-            f"rank by an all-gather after each GEMV"}
+            f"rank by an all-gather of each GEMV's output (fused into the GEMV with the peer collectives)"}
 
 
 def shard_rows(raw, t: str, n: int, k: int, rank: int, world: int):
@@ -629,8 +629,11 @@ def run_ours(args):
         h = ops.ctx.bind()
         for r in range(ROUNDS):
             for wk in work:
-                check(L.ef_gemv(h, wk["ws"][r].h, _ptr(wk["x"]), wk["m"], _ptr(wk["y"])), h)
-                gather(wk)
+                if world > 1 and comm is not None:   # the GEMV and its all-gather fused
+                    check(L.ef_gemv_allgather(h, comm.tp, wk["ws"][r].h, _ptr(wk["x"]), wk["m"], _ptr(wk["yall"])), h)
+                else:
+                    check(L.ef_gemv(h, wk["ws"][r].h, _ptr(wk["x"]), wk["m"], _ptr(wk["y"])), h)
+                    gather(wk)
 
     # end-to-end buffers: the step's inputs in one pinned host buffer (one
     # host->device copy per step), all its results gathered for one readback

@@ -111,6 +111,7 @@ _SIGS = {
     "ef_gguf_meta": ([_P, ctypes.c_int64, _P, _P, _P, _P, _P], _I),
     "ef_gguf_load_weight": ([_P, _P, ctypes.c_char_p, _P], _I),
     "ef_gemv_allreduce_norm": ([_P, _P, _P, _P, _I, _P, _P, _P, ctypes.c_float, _P], _I),
+    "ef_gemv_allgather": ([_P, _P, _P, _P, _I, _P], _I),
     "ef_tp_destroy": ([_P, _P], _I),
 }
 

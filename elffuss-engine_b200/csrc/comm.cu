@@ -37,6 +37,8 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "internal.h"
 
@@ -296,6 +298,56 @@ __global__ void __launch_bounds__(256) ef_tp_norm_kernel(const TpArgs a, const f
     pdl_wait();                      // the GEMV has completed before this kernel does
 }
 
+// Consumer of the fused row-sharded GEMV (ef_gemv_allgather): dst[r * n + i]
+// = rank r's y[i] (n = M x its rows), read from the ranks' stamped slots of
+// the fused region; bounded waits as above. Like ef_tp_norm_kernel it works as
+// soon as it is scheduled and waits for the GEMV's completion only before it
+// exits; its last CTA advances the fused call counter.
+__global__ void __launch_bounds__(256) ef_tp_gather_kernel(const TpArgs a, int64_t n, float *__restrict__ dst) {
+    pdl_trigger();
+    __shared__ uint32_t ep, bad;
+    uint8_t *mine = a.peer[a.rank];
+    const TpCtl ctl = tp_ctl(mine, a.data_bytes);
+    if (threadIdx.x == 0) {
+        bad = *(volatile uint32_t *)ctl.error;
+        ep = *(volatile uint32_t *)ctl.fepoch + 1;   // this call's number (the GEMV's stamp)
+    }
+    __syncthreads();
+    if (bad) {
+        pdl_wait();
+        return;
+    }
+    const uint32_t e = ep;
+    const uint64_t *slots =
+        reinterpret_cast<const uint64_t *>(mine + a.data_bytes + (int64_t)(e & 1) * a.nranks * a.slot_bytes);
+    const int64_t sw = a.slot_bytes / 8;    // stamped words per slot
+    const uint64_t t0 = global_ns();
+    bool late = false;
+    int who = -1;
+    const int64_t total = (int64_t)a.nranks * n;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / n);
+        const uint32_t w = wait_stamped(slots + r * sw + (i - (int64_t)r * n), e, t0, a.timeout_ns, late);
+        if (late) {
+            if (who < 0) who = r;
+            break;
+        }
+        dst[i] = __uint_as_float(w);
+    }
+    if (__syncthreads_or(late)) {
+        if (late) atomicExch(ctl.error, 1u + (uint32_t)who);
+        pdl_wait();
+        return;
+    }
+    if (threadIdx.x == 0) {
+        if (atomicAdd(ctl.fdone, 1u) == gridDim.x - 1) {
+            *ctl.fdone = 0;
+            *(volatile uint32_t *)ctl.fepoch = e;
+        }
+    }
+    pdl_wait();                      // the GEMV has completed before this kernel does
+}
+
 static TpArgs tp_args(ef_tp *tp) {
     TpArgs a = {};
     for (int r = 0; r < tp->nranks; r++) a.peer[r] = tp->peer[r];
@@ -428,6 +480,28 @@ int ef_gemv_allreduce_norm(ef_ctx *ctx, ef_tp *tp, const ef_weight *w, const flo
     default: return launch_on(ctx, ef_tp_norm_kernel<8>, M, th, 0, "tp norm launch", a, w_post, x_resid, w_next,
                               (int)w->rows, eps, nrm);
     }
+}
+
+int ef_gemv_allgather(ef_ctx *ctx, ef_tp *tp, const ef_weight *w, const float *x, int M, float *yall) {
+    if (!ctx || !tp || !w || !x || !yall || M < 1 || M > 16)
+        return ctx ? set_err(ctx, EF_ERR_INVALID, "gemv_allgather: bad arguments") : EF_ERR_INVALID;
+    if (int rc = tp_connected(ctx, tp)) return rc;
+    const int64_t n = (int64_t)M * w->rows;
+    if ((size_t)n * 4 > tp->slot_bytes)
+        return set_err(ctx, EF_ERR_RANGE, "gemv_allgather: %d x %lld floats exceed the %zu-byte slot", M,
+                       (long long)w->rows, tp->slot_bytes);
+    const TpArgs a = tp_args(tp);
+    GemvPush push;
+    push.n = tp->nranks;
+    push.rank = tp->rank;
+    push.slot_bytes = a.slot_bytes;
+    for (int r = 0; r < tp->nranks; r++) push.data[r] = tp->peer[r] + tp->data_bytes;
+    push.epoch = tp_ctl(tp->buf, (int64_t)tp->data_bytes).fepoch;
+    float *ys[1] = {yall};   // (not written by the GEMV: its output goes to the ranks' slots)
+    if (int rc = launch_gemv(ctx, &w, 1, nullptr, x, M, ys, &push)) return rc;
+    const int64_t total = (int64_t)tp->nranks * n;
+    const int ctas = (int)std::min<int64_t>(128, std::max<int64_t>(1, (total + 2047) / 2048));
+    return launch_on(ctx, ef_tp_gather_kernel, ctas, 256, 0, "tp gather launch", a, n, yall);
 }
 
 int ef_tp_status(ef_ctx *ctx, const ef_tp *tp) {

@@ -438,6 +438,15 @@ EF_API int ef_allgather(ef_ctx *ctx, ef_tp *tp, const void *src, int64_t bytes, 
  * M <= 16, M * n * 4 bytes within max_bytes. */
 EF_API int ef_gemv_allreduce_norm(ef_ctx *ctx, ef_tp *tp, const ef_weight *w, const float *x, int M,
                                   const float *w_post, float *x_resid, const float *w_next, float eps, float *nrm);
+/* A row-sharded GEMV with the all-gather of its output, fused: y = W x (this
+ * rank's rows of the whole matrix, M tokens) is stored by the GEMV kernel
+ * straight into every rank's exchange buffer over NVLink, then yall[r * n + i]
+ * = rank r's y[i] (n = M x this rank's rows, the same on every rank) -- the
+ * same as ef_gemv followed by ef_allgather, with one launch and one exchange
+ * fewer. M <= 16, M * rows * 4 bytes within max_bytes. Shares the fused call
+ * counter with ef_gemv_allreduce_norm (calls on one stream, in order). No
+ * reference counterpart: the reference is single-device. */
+EF_API int ef_gemv_allgather(ef_ctx *ctx, ef_tp *tp, const ef_weight *w, const float *x, int M, float *yall);
 EF_API int ef_tp_status(ef_ctx *ctx, const ef_tp *tp);
 EF_API int ef_tp_destroy(ef_ctx *ctx, ef_tp *tp);
 

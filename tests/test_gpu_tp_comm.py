@@ -47,6 +47,40 @@ def _rank_main(rank, world, init, q, mode):
             comm.close()
             return
         comm = TPComm(ops, rank, world, max_bytes=1 << 16)
+        if mode == "gather":
+            import ctypes
+            from elffuss_engine_b200 import formats
+            from elffuss_engine_b200._lib import check, lib
+            L, h = lib(), ops.ctx.bind()
+            P = lambda t: ctypes.c_void_p(t.data_ptr()) if t is not None else None
+            out = []
+            for n, k, M, t in ((256, 512, 1, "Q8_0"), (512, 1024, 3, "Q4_K"), (384, 512, 16, "Q8_0")):
+                raw = formats.synth(t, n, k, seed=20 + rank + n)    # this rank's rows of the whole matrix
+                w = ops.load_weight(t, raw, n, k)
+                x = torch.randn(M, k, device="cuda", generator=torch.Generator("cuda").manual_seed(5))
+                y = torch.empty(M, n, device="cuda")
+                ref = torch.empty(world * M * n, device="cuda")
+                check(L.ef_gemv(h, w.h, P(x), M, P(y)), h)
+                comm.all_gather(ref, y)
+                got = []
+                for rep in range(3):                 # repeated, and interleaved with the fused all-reduce
+                    ya = torch.full((world * M * n,), float("nan"), device="cuda")
+                    check(L.ef_gemv_allgather(h, comm.tp, w.h, P(x), M, P(ya)), h)
+                    if rep == 1:
+                        xr, nrm = torch.zeros(1, n, device="cuda"), torch.empty(1, n, device="cuda")
+                        wn = torch.ones(n, device="cuda")
+                        check(L.ef_gemv_allreduce_norm(h, comm.tp, w.h, P(x), 1, None, P(xr), P(wn),
+                                                       ctypes.c_float(1e-5), P(nrm)), h)
+                    got.append(ya)
+                torch.cuda.synchronize()
+                # numpy arrays travel through the queue by value (tensors would be shared
+                # through file descriptors of a process that may already have exited)
+                out.append((ref.cpu().numpy(), [g.cpu().numpy() for g in got]))
+                w.free()
+            q.put((rank, comm.status(), out))
+            dist.barrier()
+            comm.close()
+            return
         if mode == "fused":
             import ctypes
             import numpy as np
@@ -156,3 +190,14 @@ def test_missing_rank_times_out_with_status():
     st, y = got[0]
     assert st == -8                      # EF_ERR_TIMEOUT
     assert y == [0, 2, 4, 6]
+
+
+def test_fused_gemv_allgather_equals_gemv_then_allgather():
+    got = _run("gather")
+    for r in range(2):
+        st, out = got[r]
+        assert st == 0
+        for ref, reps in out:
+            for g in reps:
+                assert (g.view("u4") == ref.view("u4")).all()             # the same bits
+        assert all((a[0].view("u4") == b[0].view("u4")).all() for a, b in zip(got[0][1], got[1][1]))
